@@ -1,0 +1,13 @@
+"""Parameters of the binning stress fixtures, shared by the generator and the tests."""
+STRESS_CASES = [
+    # (name, seed, G, H, W, R, K, stress_mu2d keyword arguments)
+    ("tiny_k8", 11, 400, 48, 64, 1, 8, dict(n_clusters=4, sigma_px=5.0)),
+    ("ties_k32", 12, 3000, 64, 64, 1, 32, dict(n_clusters=6, sigma_px=4.0, quantise=True)),
+    ("special_k16", 13, 2000, 64, 96, 1, 16, dict(n_clusters=5, sigma_px=8.0, n_special=24)),
+    ("r2_k64", 14, 5000, 96, 128, 2, 64, dict(n_clusters=10, sigma_px=6.0)),
+    ("sparse_k128", 15, 300, 256, 256, 1, 128, dict(n_clusters=30, sigma_px=20.0, frac_off=0.3)),
+    ("allout_k4", 16, 200, 32, 32, 1, 4, dict(n_clusters=2, sigma_px=3.0, frac_drop=1.0)),
+]
+
+BIG_CASE = dict(seed=31, G=1_000_000, H=1072, W=1920, R=1, K=256,
+                kw=dict(n_clusters=64, sigma_px=30.0, frac_off=0.05, frac_drop=0.02))
