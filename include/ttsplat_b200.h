@@ -1,0 +1,166 @@
+/*
+ * tt-splat B200 — C ABI of the matrix-native 3DGS render/train hot path (sm_100a).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (as void*, NULL = the
+ * legacy default stream), launches asynchronously on that stream, performs no host<->device
+ * synchronisation and no allocation, and returns a status code (TTS_OK = 0).  On failure,
+ * tts_last_error() describes the problem (thread-local).  Scratch memory is passed in by the
+ * caller; each *_workspace_bytes() function gives the size an entry point needs.
+ *
+ * Data layout (all fp32 unless stated, row-major, views outermost):
+ *   params   [59*G + 1]   means3d[G,3] | log_scales[G,3] | quats[G,4] (w,x,y,z) | opacity_raw[G]
+ *                         | color_dc[G,3] | color_rest[G,15,3] | w_b_raw
+ *            (the GaussianModel parameters of spike/model.py:28-47, flattened)
+ *   cams     [V][TTS_CAM_FLOATS]   R_v[9], t_v[3], fx, fy, cx, cy, centre[3], pad
+ *   proj     [V][G][TTS_PROJ_FLOATS] mu2d.x, mu2d.y, conic a, b, c, color_o r, g, b, keo, depth, 0, 0
+ *   mu2d     [V][G][2], keep [V][G] (uint8)
+ *   tiles    T = (H/16)*(W/16), tile t = ty*(W/16) + tx, H and W multiples of 16
+ *   idx      [V][T][K] int32 gaussian id per slot in canonical order, -1 when unused
+ *   count    [V][T] int32 = min(cand, K);  cand [V][T] int32 = candidates (overflow = cand-K)
+ *   inv      [V][G][(2R+1)^2] int32 flat slot t*K+k of gaussian g at stencil offset j, or -1
+ *   slots    [V][T][K][TTS_SLOT_FLOATS]  theta_u[6] (tile-local), color_o[3], o_col, 0, 0
+ *   img      [V][H][W][3], den [V][H][W], gimg like img
+ *   slot_grads [V][T][K][TTS_SLOT_GRAD_FLOATS]  gtheta_u[6], gcolor_o[3], go_col
+ */
+#ifndef TTSPLAT_B200_H
+#define TTSPLAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTS_OK 0
+#define TTS_ERR_INVALID 1   /* bad argument (size, alignment, range) */
+#define TTS_ERR_CUDA 2      /* a CUDA launch or runtime call failed */
+#define TTS_ERR_CAPACITY 3  /* workspace too small */
+
+#define TTS_CAM_FLOATS 20
+#define TTS_PROJ_FLOATS 12
+#define TTS_SLOT_FLOATS 12
+#define TTS_SLOT_GRAD_FLOATS 10
+#define TTS_PARAM_FLOATS 59
+
+int tts_version(void);
+const char* tts_last_error(void);
+
+/* Device status word written by kernels instead of trapping (bounded waits that gave up). */
+int tts_read_status(int* status_host);      /* synchronous read + clear; diagnostic only */
+
+/* ---- geometry + SH colour + activations --------------------------------------------------
+ * Replaces spike/geometry.py:10-57 (quat_to_rotmat, cov3d, project_ewa), spike/sh.py:49-72
+ * (eval_sh_color on means - camera centre, spike/render.py:22-25) and the activations of
+ * _operands, tools/m4_train_binned.py:194-202 (o = sigmoid, keo = keep*o, color_o = keo*colour).
+ * Also counts kept gaussians per home cell into cell_count[V][T] (must be zeroed) and writes
+ * each gaussian's (cell, rank-in-cell) into cell_rank[V][G][2] for the binning scatter. */
+int tts_project(const float* params, int G, int sh_degree, const float* cams, int V, int H, int W,
+                float blur, float near_plane, float* proj, float* mu2d, uint8_t* keep,
+                int32_t* cell_count, int32_t* cell_rank, void* stream);
+
+/* ---- spatial-hash binning ----------------------------------------------------------------
+ * Replaces assign_bins, tools/m4_train_binned.py:75-127 (canonical = stable order of its key
+ * tile*2048 + clamp(long(dist2),0,2047), ties by stencil offset j then gaussian id), plus the
+ * inverse table of tools/m9_scatter_oracle.py:20-35 (indexed by stencil offset) and, when
+ * proj/slots are given, the operand gather of _operands :207-211 with theta_u_gathered
+ * :130-143.  G < 2^31, K <= 256, R <= 3. */
+size_t tts_bin_workspace_bytes(int G, int V, int H, int W);
+int tts_bin_from_mu2d(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W, int R,
+                      int K, int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv,
+                      void* workspace, size_t workspace_bytes, void* stream);
+int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float* proj,
+                 const int32_t* cell_count, const int32_t* cell_rank, int G, int V, int H, int W,
+                 int R, int K, float k_poly, int32_t* idx, int32_t* count, int32_t* cand,
+                 int32_t* inv, float* slots, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- operands in the reference layout -> slot rows ---------------------------------------
+ * Packs theta_u[V*T,6,K], color_o[V*T,K,3], o_col[V*T,K,1] (the operands of
+ * _DevRenderBinned.apply, tools/m4_train_binned.py:154-166) into slot rows, and the
+ * per-slot grads back into the reference layout. */
+int tts_pack_operands(const float* theta_u, const float* color_o, const float* o_col, int VT, int K,
+                      float* slots, void* stream);
+int tts_unpack_slot_grads(const float* slot_grads, int VT, int K, float* gtheta_u, float* gcolor_o,
+                          float* go_col, void* stream);
+
+/* ---- fused per-tile forward ----------------------------------------------------------------
+ * Replaces _DevRenderBinned.forward, tools/m4_train_binned.py:156-166 (= render_binned_cpu
+ * :226-230, WSRPolySplatHot.forward spike/backward.py:28-41): Q = Phi.theta_u per tile,
+ * w = relu(Q)^2, C = (sum w color_o + w_b c_b) / (sum w o_col + w_b); img[gidx] = C.
+ * slots_bf16 != 0 reads slot rows stored as bf16 (bf16 in, fp32 accumulate).
+ * The background weight is read on the device: w_b = softplus(*w_b) when w_b_is_raw != 0
+ * (the model's w_b_raw), else *w_b as given (the activated operand of _DevRenderBinned). */
+int tts_render_fwd(const void* slots, int slots_bf16, const int32_t* count, int V, int H, int W,
+                   int K, const float* w_b, int w_b_is_raw, const float* c_b, float* img,
+                   float* den, void* stream);
+
+/* ---- fused per-tile backward -------------------------------------------------------------
+ * Replaces _DevRenderBinned.backward, tools/m4_train_binned.py:169-186 (= WSRPolySplatHot
+ * .backward, spike/backward.py:43-58): per slot gtheta_u = Phi^T (2 relu(Q) gw),
+ * gcolor_o = w^T gnum, go_col = w^T gden; per tile partial gw_b = sum(gnum c_b + gden). */
+int tts_render_bwd(const float* slots, const int32_t* count, int V, int H, int W, int K,
+                   const float* c_b, const float* img, const float* den, const float* gimg,
+                   float* slot_grads, float* gwb_partial, void* stream);
+
+/* ---- photometric loss ------------------------------------------------------------------
+ * Replaces metrics.loss_fn, spike/metrics.py:26-28 ((1-l) L1 + l (1-SSIM), SSIM on inputs
+ * clamped to [0,1], 11-tap sigma-1.5 window shrunk for small images :15-19) with the manual
+ * gradient of tools/loss_manual.py:78-105.  gimg = grad_scale * dloss/dimg; loss[v] written. */
+size_t tts_loss_workspace_bytes(int V, int H, int W);
+int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W, float lambda,
+                     float grad_scale, float* gimg, float* loss, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ---- slot -> gaussian reduction + geometry/SH/activation backward ------------------------
+ * Replaces the index_add of tools/operands_manual.py:94-98 (= build_inv/gather_reduce,
+ * tools/m9_scatter_oracle.py), _theta_bwd :65-80, geom_bwd.bwd tools/geom_bwd.py:67-152, the
+ * activation grads of operands_manual.bwd_manual :103-110 and the SH colour backward; sums
+ * over the V views in view order; adds the reg_loss gradient (spike/mcmc.py:18-22) and the
+ * w_b_raw gradient from the per-tile partials.  grads has the params layout (overwritten). */
+int tts_backward_params(const float* params, int G, int sh_degree, const float* cams, int V,
+                        int H, int W, int R, int K, float k_poly, float blur, float near_plane,
+                        const int32_t* inv, const float* slot_grads, const float* gwb_partial,
+                        float lambda_o, float lambda_s, float* grads, void* stream);
+
+/* ---- Adam + SGLD ----------------------------------------------------------------------
+ * torch.optim.Adam step (spike/train.py:19,29; groups spike/model.py:82-95) over the flat
+ * params, then add_sgld_noise (spike/mcmc.py:25-34) when noise_lr > 0.  lr[7] = means,
+ * log_scales, quats, opacity_raw, color_dc, color_rest, w_b_raw.  The step number is read from
+ * *step (device int, already incremented for this step).  eps_noise [G,3] injects the
+ * Gaussian draw; when NULL a Philox4x32-10 stream keyed by (seed, step) is used. */
+int tts_adam_sgld(float* params, const float* grads, float* m, float* v, int G, int sh_degree,
+                  const int32_t* step, const double* lr7, double beta1, double beta2, double eps,
+                  float noise_lr, const float* eps_noise, uint64_t seed, void* stream);
+int tts_step_begin(int32_t* step, void* stream);
+/* add_sgld_noise alone (spike/mcmc.py:25-34) with lr = lr_means; same noise stream/injection. */
+int tts_sgld(float* params, int G, double lr_means, float noise_lr, const float* eps_noise,
+             const int32_t* step, uint64_t seed, void* stream);
+
+/* ---- MCMC relocation ---------------------------------------------------------------------
+ * relocate + reset_adam_state (spike/mcmc.py:41-87): dead = o < thr, targets drawn with
+ * replacement proportional to o over the alive set, target opacity split o/(n+1), dead slots
+ * take the target's parameters (+ offset * N(0,1) on means), moments of every touched
+ * gaussian zeroed.  thr = dead_thr when dead_frac <= 0, else the torch.quantile of o at
+ * dead_frac.  targets_in [n_dead] / offset_noise_in [n_dead,3] inject the draws (NULL: Philox
+ * keyed by (seed, step)).  n_dead_out receives the number moved (device int). */
+size_t tts_relocate_workspace_bytes(int G);
+int tts_relocate(float* params, float* m, float* v, int G, float dead_thr, float dead_frac,
+                 float offset, const int32_t* targets_in, const float* offset_noise_in,
+                 const int32_t* step, uint64_t seed, int32_t* n_dead_out, int32_t* targets_out,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- dense WSR (spike/backward.py:61-63, wsr_polysplat) -----------------------------------
+ * C[P,3] from theta_u[G,6], o[G], color[G,3], w_b (device scalar), Phi[P,6], c_b[3], keep[G]
+ * (fp32 0/1, may be NULL), and its backward. */
+int tts_wsr_dense_fwd(const float* theta_u, const float* o, const float* color, const float* w_b,
+                      const float* Phi, const float* c_b, const float* keep, int P, int G,
+                      float* C, float* den, void* stream);
+int tts_wsr_dense_bwd(const float* theta_u, const float* o, const float* color, const float* w_b,
+                      const float* Phi, const float* c_b, const float* keep, int P, int G,
+                      const float* C, const float* den, const float* gC, float* gtheta, float* go,
+                      float* gcolor, float* gw_b_partial, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,110 @@
+"""Device binning vs the reference's tables (golden fixtures) and the oracle: bit-exact."""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cam_from, golden
+from oracle import binning
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def gpu_bins(mu2d, keep, H, W, R, K):
+    from tt_splat_b200 import ops
+    idx, count, cand, inv = ops.bin_from_mu2d(torch.from_numpy(np.ascontiguousarray(mu2d)).to(DEV),
+                                             torch.from_numpy(np.asarray(keep).astype(np.uint8)).to(DEV), H, W, R, K)
+    torch.cuda.synchronize()
+    return idx[0].cpu().numpy(), count[0].cpu().numpy(), cand[0].cpu().numpy(), inv[0].cpu().numpy()
+
+
+def check(idx, count, cand, idx_ref, valid_ref, cand_ref):
+    ref = np.where(valid_ref, idx_ref, -1)
+    assert np.array_equal(idx, ref), f"{int((idx != ref).any(1).sum())} tiles differ"
+    assert np.array_equal(count, valid_ref.sum(1))
+    assert np.array_equal(cand, cand_ref)
+
+
+def test_config0_scene_bit_exact_vs_reference(pkg):
+    z = golden("bins_config0.npz")
+    cam = cam_from(z)
+    idx, count, cand, _ = gpu_bins(z["mu2d"], z["keep"], cam["H"], cam["W"], 1, 128)
+    check(idx, count, cand, z["idx_stable"], z["valid_stable"], z["cand"])
+    assert (cand > 128).sum() > 0            # the scene overflows
+
+
+@pytest.mark.parametrize("case", [c[0] for c in __import__("make_golden_cases").STRESS_CASES])
+def test_stress_bit_exact_vs_reference(case, pkg):
+    import make_golden_cases as mg
+    name, seed, G, H, W, R, K, kw = next(c for c in mg.STRESS_CASES if c[0] == case)
+    z = golden("bins_stress.npz")
+    mu, keep = pkg.synthetic.stress_mu2d(seed, G, H, W, **kw)
+    idx, count, cand, _ = gpu_bins(mu, keep, H, W, R, K)
+    check(idx, count, cand, z[f"{name}__idx_stable"], z[f"{name}__valid_stable"], z[f"{name}__cand"])
+
+
+def digest(idx, count, cand):
+    h = hashlib.sha256()
+    h.update(np.ascontiguousarray(idx.astype(np.int32)).tobytes())
+    h.update(np.ascontiguousarray(count.astype(np.int32)).tobytes())
+    h.update(np.ascontiguousarray(cand.astype(np.int32)).tobytes())
+    return h.hexdigest()
+
+
+def test_config1_digest_vs_reference(pkg):
+    z = golden("bins_config1.npz")
+    cam = cam_from(z)
+    idx, count, cand, _ = gpu_bins(z["mu2d"], z["keep"], cam["H"], cam["W"], 1, 128)
+    assert np.array_equal(cand, z["cand"])
+    assert digest(idx, count, cand) == str(z["digest"])
+
+
+def test_million_gaussians_digest_and_overflow_vs_reference(pkg):
+    """1M gaussians, 1920x1072, K=256: the radix-select path (tiles with more than 4096
+    candidates) and the overflow counts, bit-exact."""
+    import make_golden_cases as mg
+    c = mg.BIG_CASE
+    z = golden("bins_big.npz")
+    mu, keep = pkg.synthetic.stress_mu2d(c["seed"], c["G"], c["H"], c["W"], **c["kw"])
+    idx, count, cand, _ = gpu_bins(mu, keep, c["H"], c["W"], c["R"], c["K"])
+    assert np.array_equal(cand, z["cand"])
+    assert int(np.maximum(cand - c["K"], 0).sum()) == int(z["overflow"])
+    assert int((cand > 4096).sum()) > 0
+    assert digest(idx, count, cand) == str(z["digest"])
+
+
+def test_inverse_table_vs_oracle(pkg):
+    z = golden("bins_config0.npz")
+    cam = cam_from(z)
+    tm = binning.tile_map(cam["H"], cam["W"])
+    b = binning.assign_bins(z["mu2d"], z["keep"], tm, 1, 128)
+    _, _, _, inv = gpu_bins(z["mu2d"], z["keep"], cam["H"], cam["W"], 1, 128)
+    assert np.array_equal(inv, binning.stencil_inv(b, z["mu2d"].shape[0], 1))
+
+
+def test_batched_views_and_determinism(pkg):
+    from tt_splat_b200 import ops
+    mus, keeps = [], []
+    for s in range(3):
+        mu, keep = pkg.synthetic.stress_mu2d(100 + s, 4000, 128, 160, n_clusters=8, sigma_px=7.0)
+        mus.append(mu)
+        keeps.append(keep)
+    mu_t = torch.from_numpy(np.stack(mus)).to(DEV)
+    kp_t = torch.from_numpy(np.stack(keeps).astype(np.uint8)).to(DEV)
+    a = [t.cpu() for t in ops.bin_from_mu2d(mu_t, kp_t, 128, 160, 1, 64)]
+    b = [t.cpu() for t in ops.bin_from_mu2d(mu_t, kp_t, 128, 160, 1, 64)]
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    tm = binning.tile_map(128, 160)
+    for v in range(3):
+        r = binning.assign_bins(mus[v], keeps[v], tm, 1, 64)
+        assert np.array_equal(a[0][v].numpy(), np.where(r.valid, r.idx, -1))
+        assert np.array_equal(a[2][v].numpy(), r.cand)
+
+
+def test_no_kept_gaussians(pkg):
+    mu = np.zeros((50, 2), np.float32)
+    idx, count, cand, inv = gpu_bins(mu, np.zeros(50, bool), 32, 32, 1, 8)
+    assert (idx == -1).all() and (count == 0).all() and (cand == 0).all() and (inv == -1).all()

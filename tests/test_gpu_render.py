@@ -1,0 +1,133 @@
+"""Fused per-tile forward/backward and the full render pipeline vs the reference and the oracle.
+Tolerances (north star): images 1e-3 max abs in fp32 (bf16 slot rows 1e-2), gradients 1e-3
+relative L2."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import cam_from, golden, params_from, rel_l2
+from oracle import binning, pipeline, render as orender
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def test_render_on_reference_operands(pkg):
+    """_DevRenderBinned on the reference's own operands reproduces its image and operand grads."""
+    from tt_splat_b200 import binned
+    z = golden("render_config0.npz")
+    cam = cam_from(z)
+    tm = binned.TileMap(cam["H"], cam["W"])
+    th = torch.from_numpy(z["theta_u"]).to(DEV).requires_grad_(True)
+    col = torch.from_numpy(z["col"]).to(DEV).requires_grad_(True)
+    oc = torch.from_numpy(z["oc"]).to(DEV).requires_grad_(True)
+    wb = torch.tensor(float(z["w_b"]), device=DEV, requires_grad=True)
+    img = binned._DevRenderBinned.apply(th, col, oc, wb, tm.Phi, tm.gidx, torch.ones(3, device=DEV), cam["H"], cam["W"])
+    assert np.abs(img.detach().cpu().numpy() - z["img"]).max() < 1e-5
+    tgt = torch.from_numpy(z["target"]).to(DEV)
+    (img - tgt).abs().mean().backward()
+    assert rel_l2(th.grad.cpu().numpy(), z["gtheta"]) < 1e-4
+    assert rel_l2(col.grad.cpu().numpy(), z["gcol"]) < 1e-4
+    assert rel_l2(oc.grad.cpu().numpy(), z["goc"]) < 1e-4
+    assert abs(float(wb.grad) - float(z["gw_b"])) < 1e-4 * abs(float(z["gw_b"]))
+
+
+def _model(pkg, p):
+    return pkg.model.GaussianModel.from_arrays(p, device=DEV)
+
+
+@pytest.mark.parametrize("fixture,deg", [("render_config0.npz", 0), ("render_sh3.npz", 3)])
+def test_pipeline_vs_reference_and_oracle(fixture, deg, pkg):
+    from tt_splat_b200 import camera, render
+    z = golden(fixture)
+    cam = cam_from(z)
+    p = params_from(z)
+    K = int(z["K"])
+    m = _model(pkg, p)
+    img = render.render(m, camera.Camera.from_dict(cam), "A", sh_degree=deg, K=K)
+    fw = pipeline.render_view(p, deg, cam, K=K)
+    out = img.detach().cpu().numpy()
+    assert np.abs(out - fw["img"]).max() < 1e-3
+    assert np.abs(out - z["img"]).max() < 1e-3
+    tgt = torch.from_numpy(z["target"]).to(DEV)
+    (img - tgt).abs().mean().backward()
+    g = m.flat.grad
+    G = p["means3d"].shape[0]
+    from tt_splat_b200.model import view
+    gimg = (np.sign(fw["img"] - z["target"]) / fw["img"].size).astype(np.float32)
+    go = pipeline.backward_view(fw, gimg, p, deg)
+    names = ["means3d", "log_scales", "quats", "opacity_raw", "color_dc"] + (["color_rest"] if deg else [])
+    for n in names:
+        mine = view(g, G, n).cpu().numpy()
+        assert rel_l2(mine, z["grad_" + n]) < 1e-3, (n, rel_l2(mine, z["grad_" + n]))
+        assert rel_l2(mine, go[n]) < 1e-3, (n, rel_l2(mine, go[n]))
+    assert abs(float(view(g, G, "w_b_raw")) - float(z["grad_w_b_raw"])) < 1e-3 * abs(float(z["grad_w_b_raw"]))
+
+
+def test_slot_rows_bit_exact_given_projection(pkg):
+    """theta_u rows of the pack epilogue are the reference's fp32 expression bit for bit,
+    given the device's own mu2d/conic (tools/m4_train_binned.py:130-143)."""
+    from tt_splat_b200 import camera, ops
+    from tt_splat_b200.model import pack_arrays
+    sc = pkg.synthetic.config0(seed=3, G=1500, res=96)
+    flat = pack_arrays(sc["params"]).to(DEV)
+    cams = camera.pack_cameras([camera.Camera.from_dict(sc["cams"][0])], DEV)
+    pj = ops.project(flat, 1500, 0, cams, 96, 96)
+    bp = ops.bin_pack(pj, 1500, 96, 96, 1, 64)
+    proj = pj["proj"][0].cpu().numpy()
+    idx = bp["idx"][0].cpu().numpy()
+    valid = idx >= 0
+    tm = binning.tile_map(96, 96)
+    ii = np.where(valid, idx, 0)
+    th = orender.theta_u_gathered(proj[ii][..., 2:5], proj[ii][..., 0:2], tm.origins, 4.0) * valid[:, None, :]
+    rows = bp["slots"][0].cpu().numpy()
+    assert np.array_equal(np.transpose(rows[..., :6], (0, 2, 1))[np.broadcast_to(valid[:, None, :], th.shape)],
+                          th[np.broadcast_to(valid[:, None, :], th.shape)])
+    assert np.array_equal(rows[..., 6:9][valid], proj[ii][..., 5:8][valid])
+
+
+def test_bf16_slot_rows(pkg):
+    from tt_splat_b200 import camera, render
+    sc = pkg.synthetic.config1(seed=4, G=3000, res=128)
+    m = _model(pkg, sc["params"])
+    cam = camera.Camera.from_dict(sc["cams"][0])
+    a = render.render(m, cam, sh_degree=3).detach()
+    b = render.render(m, cam, sh_degree=3, bf16=True).detach()
+    assert (a - b).abs().max().item() < 1e-2
+
+
+def test_multi_view_batch_equals_single_views(pkg):
+    from tt_splat_b200 import camera, render
+    sc = pkg.synthetic.config2(seed=5, G=5000, H=64, W=96, n_views=3)
+    m = _model(pkg, sc["params"])
+    cams = [camera.Camera.from_dict(c) for c in sc["cams"]]
+    batch = render.render_views(m, cams, sh_degree=3).detach()
+    for v, c in enumerate(cams):
+        assert torch.equal(batch[v], render.render(m, c, sh_degree=3).detach())
+
+
+def test_dense_wsr_polysplat_vs_oracle(pkg):
+    from tt_splat_b200 import backward
+    rng = np.random.default_rng(0)
+    G, P = 37, 300
+    th = rng.standard_normal((G, 6)).astype(np.float32) * np.array([0.02, 0.02, 0.02, 0.3, 0.3, 0.5], np.float32)
+    th[:, 5] += 0.5
+    o = rng.uniform(0.1, 0.9, G).astype(np.float32)
+    col = rng.uniform(0, 1, (G, 3)).astype(np.float32)
+    px = rng.uniform(0, 16, P)
+    py = rng.uniform(0, 16, P)
+    Phi = np.stack([px * px, py * py, px * py, px, py, np.ones(P)], -1).astype(np.float32)
+    keep = (rng.random(G) > 0.2).astype(np.float32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV).requires_grad_(True)  # noqa: E731
+    tth, to, tcol = t(th), t(o), t(col)
+    wb = torch.tensor(0.05, device=DEV, requires_grad=True)
+    C = backward.wsr_polysplat(tth, to, tcol, wb, t(Phi).detach(), torch.ones(3, device=DEV), t(keep).detach())
+    ref = orender.wsr_dense_fwd(th, o, col, 0.05, Phi, np.ones(3), keep)
+    assert np.abs(C.detach().cpu().numpy() - ref).max() < 1e-5
+    gC = rng.standard_normal((P, 3)).astype(np.float32)
+    C.backward(torch.from_numpy(gC).to(DEV))
+    gth, go, gcol, gwb = orender.wsr_dense_bwd(gC, th, o, col, 0.05, Phi, np.ones(3), keep)
+    assert rel_l2(tth.grad.cpu().numpy(), gth) < 1e-4
+    assert rel_l2(to.grad.cpu().numpy(), go) < 1e-4
+    assert rel_l2(tcol.grad.cpu().numpy(), gcol) < 1e-4
+    assert abs(float(wb.grad) - gwb) < 1e-4 * abs(gwb)

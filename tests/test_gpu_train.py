@@ -1,0 +1,70 @@
+"""The graph-captured train step vs the oracle step, graph replay vs eager, and training."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_l2
+from oracle import pipeline
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _setup(pkg, seed=0, G=3000, res=64, views=2, deg=3):
+    sc = pkg.synthetic.config2(seed=seed, G=G, H=res, W=res + 32, n_views=views)
+    return sc
+
+
+def test_one_step_vs_oracle(pkg):
+    """Loss, gradient and the Adam update of one device step vs the oracle step."""
+    from tt_splat_b200 import camera, model, train
+    sc = _setup(pkg)
+    p = sc["params"]
+    m = model.GaussianModel.from_arrays(p, device=DEV)
+    st = train.TrainStep(m, [camera.Camera.from_dict(c) for c in sc["cams"]],
+                         [torch.from_numpy(t) for t in sc["targets"]], sh_degree=3, lr={"means": 1.6e-4},
+                         lambda_o=0.01, lambda_s=0.01, use_graph=False)
+    st.step()
+    total, losses, grads = pipeline.loss_and_grads(p, sc["cams"], sc["targets"], 3, lambda_o=0.01, lambda_s=0.01)
+    assert abs(st.mean_loss_value() - total) < 1e-5
+    G = p["means3d"].shape[0]
+    for n in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc", "color_rest"):
+        assert rel_l2(model.view(st.grads, G, n).cpu().numpy(), grads[n]) < 1e-3, n
+    ref = pipeline.copy_params(p)
+    pipeline.adam_step(ref, grads, {}, 1, {**train.DEFAULT_LR, "means": 1.6e-4}, 3)
+    for n in ("means3d", "log_scales", "opacity_raw", "color_rest"):
+        d = np.abs(model.view(m.flat.data, G, n).cpu().numpy() - ref[n]).max()
+        assert d < 2e-4, (n, d)     # Adam steps are ~lr: a sign flip of a tiny grad moves 2*lr
+
+
+def test_graph_replay_equals_eager(pkg):
+    from tt_splat_b200 import camera, model, train
+    sc = _setup(pkg, seed=1)
+    cams = [camera.Camera.from_dict(c) for c in sc["cams"]]
+    tg = [torch.from_numpy(t) for t in sc["targets"]]
+    m1 = model.GaussianModel.from_arrays(sc["params"], device=DEV)
+    m2 = model.GaussianModel.from_arrays(sc["params"], device=DEV)
+    kw = dict(sh_degree=3, noise_lr=5e5, relocate_every=2, dead_thr=0.005, offset=0.005, lambda_o=0.01, lambda_s=0.01,
+              seed=3)
+    a = train.TrainStep(m1, cams, tg, use_graph=True, **kw)
+    b = train.TrainStep(m2, cams, tg, use_graph=False, **kw)
+    for _ in range(5):
+        la, lb = a.step(), b.step()
+        assert torch.equal(la, lb)
+    assert torch.equal(m1.flat, m2.flat)
+    assert len(a.graphs) == 2
+
+
+def test_training_reduces_loss(pkg):
+    from tt_splat_b200 import camera, mcmc, model
+    sc = _setup(pkg, seed=2, G=2000, res=48, views=3)
+    target_model = model.GaussianModel.from_arrays(sc["params"], device=DEV)
+    cams = [camera.Camera.from_dict(c) for c in sc["cams"]]
+    from tt_splat_b200 import render
+    with torch.no_grad():
+        gts = [render.render(target_model, c, sh_degree=3).detach() for c in cams]
+    fresh = pkg.synthetic.config2(seed=9, G=2000, H=48, W=80, n_views=1)["params"]
+    m = model.GaussianModel.from_arrays(fresh, device=DEV)
+    hist, moved = mcmc.train_mcmc(m, cams, gts, iters=120, relocate_every=40, noise_lr=50.0, sh_degree=3)
+    assert hist[-1] < 0.7 * hist[0], (hist[0], hist[-1])
+    assert moved >= 0

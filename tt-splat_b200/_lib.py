@@ -1,0 +1,95 @@
+"""ctypes binding of the C ABI in ``include/ttsplat_b200.h`` (``libttsplat_b200.so``).
+
+The library is loaded on first use from this package directory (it is built in-tree by
+``build.py``).  There is no fallback: a missing library, a missing CUDA device or a non-CUDA
+tensor raises.  Every call passes the current torch CUDA stream, so the ops order with torch
+work and can be captured in CUDA graphs.
+"""
+import ctypes as C
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libttsplat_b200.so")
+
+P = C.c_void_p
+I = C.c_int
+F = C.c_float
+D = C.c_double
+SZ = C.c_size_t
+U64 = C.c_uint64
+
+SIGNATURES = {
+    "tts_version": (I, []),
+    "tts_last_error": (C.c_char_p, []),
+    "tts_read_status": (I, [P]),
+    "tts_project": (I, [P, I, I, P, I, I, I, F, F, P, P, P, P, P, P]),
+    "tts_bin_workspace_bytes": (SZ, [I, I, I, I]),
+    "tts_bin_from_mu2d": (I, [P, P, I, I, I, I, I, I, P, P, P, P, P, SZ, P]),
+    "tts_bin_pack": (I, [P, P, P, P, P, I, I, I, I, I, I, F, P, P, P, P, P, P, SZ, P]),
+    "tts_pack_operands": (I, [P, P, P, I, I, P, P]),
+    "tts_unpack_slot_grads": (I, [P, I, I, P, P, P, P]),
+    "tts_render_fwd": (I, [P, I, P, I, I, I, I, P, I, P, P, P, P]),
+    "tts_render_bwd": (I, [P, P, I, I, I, I, P, P, P, P, P, P, P]),
+    "tts_loss_workspace_bytes": (SZ, [I, I, I]),
+    "tts_loss_l1_ssim": (I, [P, P, I, I, I, F, F, P, P, P, SZ, P]),
+    "tts_backward_params": (I, [P, I, I, P, I, I, I, I, I, F, F, F, P, P, P, F, F, P, P]),
+    "tts_adam_sgld": (I, [P, P, P, P, I, I, P, P, D, D, D, F, P, U64, P]),
+    "tts_step_begin": (I, [P, P]),
+    "tts_sgld": (I, [P, I, D, F, P, P, U64, P]),
+    "tts_relocate_workspace_bytes": (SZ, [I]),
+    "tts_relocate": (I, [P, P, P, I, F, F, F, P, P, P, U64, P, P, P, SZ, P]),
+    "tts_wsr_dense_fwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P]),
+    "tts_wsr_dense_bwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P, P, P, P, P, P]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load (once) and return the CUDA library; raises when it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with __graft_entry__.build() "
+                               "(there is no CPU fallback)")
+        h = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+class TTSError(RuntimeError):
+    pass
+
+
+def call(name, *args):
+    """Call an entry point; raise ValueError (bad argument) or RuntimeError (CUDA/capacity)."""
+    rc = getattr(lib(), name)(*args)
+    if rc != 0:
+        msg = lib().tts_last_error().decode()
+        if rc == 1:
+            raise ValueError(f"{name}: {msg}")
+        raise TTSError(f"{name}: {msg} (code {rc})")
+
+
+def ptr(t):
+    """Device pointer of a CUDA tensor (None -> NULL)."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("tt-splat B200 ops need CUDA tensors (no CPU fallback)")
+    return C.c_void_p(t.data_ptr())
+
+
+def stream(device=None):
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda():
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA is not available: tt-splat B200 has no CPU fallback")

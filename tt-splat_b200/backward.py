@@ -1,0 +1,47 @@
+"""The hand-derived WSR + poly-splat backward as an autograd Function (mirrors
+spike/backward.py:11-63) on the dense CUDA kernels.
+
+``wsr_polysplat(theta_u[G,6], o[G], color[G,3], w_b, Phi[P,6], c_b[3], keep[G]) -> C[P,3]``,
+differentiable in theta_u, o, color and w_b like ``WSRPolySplatHot``.
+"""
+import torch
+
+from . import ops
+
+
+def wsr_polysplat_ref(theta_u, o, color, w_b, Phi, c_b, keep=None):
+    """spike/backward.py:11-20 written with torch ops (autograd reference, any device)."""
+    u = Phi @ theta_u.t()
+    w_geo = u.clamp(min=0.0) ** 2
+    if keep is not None:
+        w_geo = w_geo * keep[None, :]
+    w = o[None, :] * w_geo
+    num = w @ color + w_b * c_b[None, :]
+    den = w.sum(1, keepdim=True) + w_b
+    return num / den
+
+
+class WSRPolySplatHot(torch.autograd.Function):
+    """Manual forward + backward on the CUDA kernels (spike/backward.py:23-58)."""
+
+    @staticmethod
+    def forward(ctx, theta_u, o, color, w_b, Phi, c_b, keep):
+        f = lambda t: None if t is None else t.detach().float().contiguous()  # noqa: E731
+        th, oo, col, Ph, cb, kp = f(theta_u), f(o), f(color), f(Phi), f(c_b), f(keep)
+        wb = torch.as_tensor(w_b, dtype=torch.float32, device=th.device).detach().reshape(1).contiguous()
+        C, den = ops.wsr_dense_fwd(th, oo, col, wb, Ph, cb, kp)
+        ctx.save_for_backward(th, oo, col, wb, Ph, cb, C, den)
+        ctx.keep = kp
+        ctx.wb_shape = torch.as_tensor(w_b).shape
+        return C
+
+    @staticmethod
+    def backward(ctx, gC):
+        th, oo, col, wb, Ph, cb, C, den = ctx.saved_tensors
+        gth, go, gcol, gwb = ops.wsr_dense_bwd(th, oo, col, wb, Ph, cb, ctx.keep, C, den, gC.float().contiguous())
+        return gth, go, gcol, gwb.reshape(ctx.wb_shape), None, None, None
+
+
+def wsr_polysplat(theta_u, o, color, w_b, Phi, c_b, keep=None):
+    """spike/backward.py:61-63."""
+    return WSRPolySplatHot.apply(theta_u, o, color, w_b, Phi, c_b, keep)

@@ -1,0 +1,141 @@
+"""The binned render operator pair of tools/m4_train_binned.py on the B200 kernels.
+
+- ``TileMap`` (:60-72), ``assign_bins`` (:75-127, canonical stable order, bit-exact),
+  ``theta_u_gathered`` (:130-143, torch expression);
+- ``_operands(model, cam, tmap, R, K)`` (:189-212): geometry, activations, binning and the
+  per-tile operand gather, differentiable in the model parameters;
+- ``_DevRenderBinned.apply(theta_u, color_o, o_col, w_b, Phi, gidx, c_b, H, W)`` (:154-186):
+  the per-tile WSR forward and backward on operands in the reference's layout.
+"""
+import torch
+
+from . import forward, ops
+from .camera import as_camera, pack_cameras
+from .model import flat_of
+
+K_POLY = 4.0
+
+
+class TileMap:
+    """tools/m4_train_binned.py:60-72."""
+
+    def __init__(self, H, W, device="cuda"):
+        assert H % 16 == 0 and W % 16 == 0
+        self.H, self.W, self.nty, self.ntx = H, W, H // 16, W // 16
+        self.T = self.nty * self.ntx
+        p = torch.arange(256)
+        self.Phi = forward.phi((p % 16).float() + 0.5, (p // 16).float() + 0.5).to(device)
+        t = torch.arange(self.T)
+        ty, tx = t // self.ntx, t % self.ntx
+        self.origins = torch.stack([(tx * 16).float(), (ty * 16).float()], dim=1).to(device)
+        gr = ty[:, None] * 16 + (p // 16)[None, :]
+        gc = tx[:, None] * 16 + (p % 16)[None, :]
+        self.gidx = (gr * W + gc).reshape(-1).long().to(device)
+
+
+def bin_tables(mu2d, keep, tmap, R=1, K=128):
+    """Device binning tables for mu2d[G,2] (or [V,G,2]): idx (int32, -1 unused), count, cand,
+    and the stencil-indexed inverse table."""
+    idx, count, cand, inv = ops.bin_from_mu2d(mu2d, keep, tmap.H, tmap.W, R, K)
+    return dict(idx=idx, count=count, cand=cand, inv=inv)
+
+
+@torch.no_grad()
+def assign_bins(mu2d, keep, tmap, R, K):
+    """tools/m4_train_binned.py:75-127 -> idx[T,K] long (0 in invalid slots), valid[T,K] bool."""
+    idx, _, _, _ = ops.bin_from_mu2d(mu2d.detach(), keep.detach(), tmap.H, tmap.W, R, K, with_inv=False)
+    idx = idx[0]
+    valid = idx >= 0
+    return torch.where(valid, idx, torch.zeros_like(idx)).long(), valid
+
+
+def theta_u_gathered(conic_t, mu_t, origins, k):
+    """tools/m4_train_binned.py:130-143 (torch expression, reference op order)."""
+    mu = mu_t - origins[:, None, :]
+    a, b, c = conic_t[..., 0], conic_t[..., 1], conic_t[..., 2]
+    mux, muy = mu[..., 0], mu[..., 1]
+    ik = 1.0 / k
+    Q = a * mux * mux + 2.0 * b * mux * muy + c * muy * muy
+    return torch.stack([-a * ik, -c * ik, -2.0 * b * ik, 2.0 * (a * mux + b * muy) * ik,
+                        2.0 * (b * mux + c * muy) * ik, 1.0 - Q * ik], dim=-1).transpose(1, 2).contiguous()
+
+
+class _Operands(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, flat, cams_t, cfg):
+        G, sh_degree, H, W, R, K, k, blur, near = cfg
+        flat_d = flat.detach().contiguous()
+        pj = ops.project(flat_d, G, sh_degree, cams_t, H, W, blur, near)
+        bp = ops.bin_pack(pj, G, H, W, R, K, k)
+        s = bp["slots"][0]                                           # [T,K,12]
+        theta_u = s[..., 0:6].transpose(1, 2).contiguous()
+        color_o = s[..., 6:9].contiguous()
+        o_col = s[..., 9:10].contiguous()
+        w_b = torch.nn.functional.softplus(flat_d[59 * G])
+        idx = bp["idx"][0]
+        valid = idx >= 0
+        ctx.save_for_backward(flat_d, cams_t, bp["inv"])
+        ctx.cfg = cfg
+        ctx.mark_non_differentiable(idx, valid)
+        return theta_u, color_o, o_col, w_b, torch.where(valid, idx, torch.zeros_like(idx)).long(), valid
+
+    @staticmethod
+    def backward(ctx, gth, gcol, goc, gwb, _gi, _gv):
+        flat, cams_t, inv = ctx.saved_tensors
+        G, sh_degree, H, W, R, K, k, blur, near = ctx.cfg
+        T = (H // 16) * (W // 16)
+        dev = flat.device
+        z = lambda t, shp: torch.zeros(shp, device=dev) if t is None else t.float()  # noqa: E731
+        gth, gcol, goc = z(gth, (T, 6, K)), z(gcol, (T, K, 3)), z(goc, (T, K, 1))
+        sg = torch.cat([gth.transpose(1, 2), gcol, goc], -1).contiguous()[None]     # [1,T,K,10]
+        part = torch.zeros(1, T, device=dev)
+        if gwb is not None:
+            part[0, 0] = gwb
+        grads = ops.backward_params(flat, G, sh_degree, cams_t, H, W, R, K, inv, sg, part, k, blur, near)
+        return grads, None, None
+
+
+def _operands(model, cam, tmap, R, K, cached_bins=None, sh_degree=0, blur=0.3, near=0.2):
+    """tools/m4_train_binned.py:189-212 -> (theta_u[T,6,K], color_o_t[T,K,3], o_col_t[T,K,1], w_b,
+    (idx, valid)).  The colour is the SH colour of degree ``sh_degree`` (0 = the reference's DC)."""
+    if cached_bins is not None:
+        raise NotImplementedError("cached_bins: the device path re-bins every call")
+    cam = as_camera(cam)
+    flat = flat_of(model)
+    G = model.means3d.shape[0]
+    cfg = (G, int(sh_degree), cam.H, cam.W, int(R), int(K), K_POLY, float(blur), float(near))
+    th, col, oc, w_b, idx, valid = _Operands.apply(flat, pack_cameras([cam], flat.device), cfg)
+    return th, col, oc, w_b, (idx, valid)
+
+
+class _DevRenderBinned(torch.autograd.Function):
+    """tools/m4_train_binned.py:154-186: render from per-tile operands; grads for the first four."""
+
+    @staticmethod
+    def forward(ctx, theta_u, color_o, o_col, w_b, Phi, gidx, c_b, H, W):
+        T, K = theta_u.shape[0], theta_u.shape[2]
+        assert Phi.shape == (256, 6) and gidx.numel() == T * 256, "standard 16x16 TileMap operands expected"
+        slots = ops.pack_operands(theta_u.detach().float().contiguous(), color_o.detach().float().contiguous(),
+                                  o_col.detach().float().contiguous())[None]
+        count = torch.full((1, T), K, dtype=torch.int32, device=theta_u.device)
+        wb = torch.as_tensor(w_b, dtype=torch.float32, device=theta_u.device).detach().reshape(1).contiguous()
+        cb = c_b.detach().float().contiguous().to(theta_u.device)
+        rf = ops.render_fwd(slots, count, H, W, wb, cb, w_b_is_raw=False)
+        ctx.save_for_backward(slots, count, cb, rf["img"], rf["den"])
+        ctx.shape = (H, W, torch.as_tensor(w_b).shape)
+        return rf["img"][0]
+
+    @staticmethod
+    def backward(ctx, gimg):
+        slots, count, cb, img, den = ctx.saved_tensors
+        H, W, wshape = ctx.shape
+        rb = ops.render_bwd(slots, count, H, W, cb, img, den, gimg.float().contiguous()[None])
+        gth, gcol, goc = ops.unpack_slot_grads(rb["slot_grads"][0])
+        return gth, gcol, goc, rb["gwb"].sum().reshape(wshape), None, None, None, None, None
+
+
+def render_binned_device(model, cam, tmap, R=1, K=128, sh_degree=0):
+    """tools/m4_train_binned.py:215-219."""
+    thU, col, oc, w_b, _ = _operands(model, cam, tmap, R, K, sh_degree=sh_degree)
+    c_b = getattr(model, "c_b", torch.ones(3, device=thU.device))
+    return _DevRenderBinned.apply(thU, col, oc, w_b, tmap.Phi, tmap.gidx, c_b, tmap.H, tmap.W)

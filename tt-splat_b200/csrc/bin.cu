@@ -1,0 +1,388 @@
+// Spatial-hash binning (replaces assign_bins, tools/m4_train_binned.py:75-127).
+//
+// Each kept gaussian scatters to one home cell (cell size = tile size = 16 px); each 16x16
+// tile gathers the candidates of its (2R+1)^2 neighbour cells, keys them exactly as the
+// reference (tile-local key q = clamp(long(dist2), 0, 2047) with dist2 in fp32, no FMA
+// contraction), and keeps the K smallest of (q, stencil offset j, gaussian id) in ascending
+// order — the stable order of the reference's packed sort key.  Per tile, candidates up to
+// BS_CAP are sorted in shared memory; larger candidate sets first run an MSB radix select over
+// the 51-bit key (digits q | j | g) until at most BS_CAP keys remain below the threshold.
+// The epilogue writes idx/count/cand, the stencil-indexed inverse table used by the
+// deterministic slot->gaussian reduction, and (optionally) the packed slot rows
+// theta_u[6] | color_o[3] | o_col of _operands (:207-211, theta_u_gathered :130-143).
+#include "common.cuh"
+
+namespace tts {
+
+constexpr int BS_THREADS = 256;
+constexpr int BS_CAP = 4096;
+constexpr int BS_MAXS = 49;  // (2R+1)^2 for R <= 3
+typedef unsigned long long u64;
+
+// Home cell coordinate: clamp(long(floor(m/16)), 0, n-1) with torch's conversion of
+// non-finite / out-of-range values to INT64_MIN (which then clamps to 0).
+__device__ __forceinline__ int cell_coord(float m, int n) {
+  const float v = floorf(__fdiv_rn(m, 16.0f));
+  if (!(v >= 0.0f && v < 9.223372036854775808e18f)) return 0;
+  return v >= (float)(n - 1) ? n - 1 : (int)v;
+}
+
+// Warp-aggregated atomic increment of per-cell counters; returns this lane's rank in its cell.
+__device__ __forceinline__ void count_cell(int cell, int* counters, int2* out) {
+  const unsigned mask = __ballot_sync(0xffffffffu, cell >= 0);
+  if (cell < 0) return;
+  const unsigned peers = __match_any_sync(mask, cell);
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(peers) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(counters + cell, __popc(peers));
+  base = __shfl_sync(peers, base, leader);
+  *out = make_int2(cell, base + __popc(peers & ((1u << lane) - 1u)));
+}
+
+__global__ void k_cell_count(const float2* __restrict__ mu2d, const uint8_t* __restrict__ keep, int G,
+                             int ntx, int nty, int* __restrict__ cell_count, int2* __restrict__ cell_rank) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int v = blockIdx.y;
+  const int T = ntx * nty;
+  int cell = -1;
+  if (g < G) {
+    const long long o = (long long)v * G + g;
+    if (keep[o]) {
+      const float2 m = mu2d[o];
+      cell = cell_coord(m.y, nty) * ntx + cell_coord(m.x, ntx);
+    } else {
+      cell_rank[o] = make_int2(-1, 0);
+    }
+  }
+  int2 cr;
+  count_cell(cell, cell_count + (long long)v * T, &cr);
+  if (cell >= 0) cell_rank[(long long)v * G + g] = cr;
+}
+
+// Exclusive scan of the per-cell counts of one view: start[0..T], start[T] = total.
+__global__ void __launch_bounds__(1024) k_cell_scan(const int* __restrict__ cnt, int* __restrict__ start, int T) {
+  __shared__ int warp_sums[32];
+  const int v = blockIdx.x;
+  const int* c = cnt + (long long)v * T;
+  int* s = start + (long long)v * (T + 1);
+  const int per = (T + blockDim.x - 1) / blockDim.x;
+  const int beg = min(T, (int)threadIdx.x * per), end = min(T, beg + per);
+  int local = 0;
+  for (int i = beg; i < end; ++i) local += c[i];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int incl = local;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) warp_sums[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x >> 5;
+    int ws = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, ws, d);
+      if (lane >= d) ws += y;
+    }
+    if (lane < nw) warp_sums[lane] = ws;
+  }
+  __syncthreads();
+  int run = incl - local + (wid > 0 ? warp_sums[wid - 1] : 0);
+  for (int i = beg; i < end; ++i) {
+    s[i] = run;
+    run += c[i];
+  }
+  if (threadIdx.x == blockDim.x - 1) s[T] = run;
+}
+
+__global__ void k_cell_scatter(const float2* __restrict__ mu2d, const int2* __restrict__ cell_rank,
+                               const int* __restrict__ start, int G, int T, float4* __restrict__ rec) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int v = blockIdx.y;
+  if (g >= G) return;
+  const long long o = (long long)v * G + g;
+  const int2 cr = cell_rank[o];
+  if (cr.x < 0) return;
+  const float2 m = mu2d[o];
+  rec[(long long)v * G + start[(long long)v * (T + 1) + cr.x] + cr.y] = make_float4(__int_as_float(g), m.x, m.y, 0.f);
+}
+
+__device__ __forceinline__ void bitonic_sort(u64* s, int P) {
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < (P >> 1); i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool asc = (lo & size) == 0;
+        const u64 a = s[lo], b = s[hi];
+        if ((a > b) == asc) {
+          s[lo] = b;
+          s[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Quantised distance of the reference: clamp(long(dist2), 0, 2047), torch's INT64_MIN for
+// non-finite or >= 2^63 values clamping to 0.
+__device__ __forceinline__ u64 make_key(int j, float4 r, float ctx, float cty) {
+  const float dx = __fsub_rn(r.y, ctx);
+  const float dy = __fsub_rn(r.z, cty);
+  const float d2 = __fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy));
+  unsigned q = 0;
+  if (d2 >= 0.0f && d2 < 9.223372036854775808e18f) q = d2 >= 2047.0f ? 2047u : (unsigned)d2;
+  return ((u64)q << 40) | ((u64)(unsigned)j << 32) | (u64)(unsigned)__float_as_int(r.x);
+}
+
+template <bool PACK>
+__global__ void __launch_bounds__(BS_THREADS)
+    k_bin_select(const int* __restrict__ cell_start, const float4* __restrict__ rec, int G, int ntx, int nty,
+                 int R, int K, const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
+                 int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv,
+                 float* __restrict__ slots) {
+  __shared__ u64 skeys[BS_CAP];
+  __shared__ int shist[2048];
+  __shared__ int s_beg[BS_MAXS], s_len[BS_MAXS], s_off[BS_MAXS + 1];
+  __shared__ u64 s_pval, s_pmask;
+  __shared__ int s_below, s_le, s_cnt;
+
+  const int t = blockIdx.x, v = blockIdx.y, T = ntx * nty;
+  const int tx = t % ntx, ty = t / ntx;
+  const int D = 2 * R + 1, S = D * D;
+  const int tid = threadIdx.x;
+  const int* cs = cell_start + (long long)v * (T + 1);
+  const float4* rv = rec + (long long)v * G;
+
+  if (tid < S) {
+    // stencil offset j = (dy+R)*D + (dx+R) as seen from the gaussian: tile = home cell + (dy, dx)
+    const int dy = tid / D - R, dx = tid % D - R;
+    const int cy = ty - dy, cx = tx - dx;
+    int beg = 0, len = 0;
+    if (cy >= 0 && cy < nty && cx >= 0 && cx < ntx) {
+      const int c = cy * ntx + cx;
+      beg = cs[c];
+      len = cs[c + 1] - beg;
+    }
+    s_beg[tid] = beg;
+    s_len[tid] = len;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int o = 0;
+    for (int j = 0; j < S; ++j) {
+      s_off[j] = o;
+      o += s_len[j];
+    }
+    s_off[S] = o;
+  }
+  __syncthreads();
+  const int n = s_off[S];
+  const float ctx = __fmul_rn(__fadd_rn((float)tx, 0.5f), 16.0f);
+  const float cty = __fmul_rn(__fadd_rn((float)ty, 0.5f), 16.0f);
+
+  int nsel;
+  if (n <= BS_CAP) {
+    for (int j = 0; j < S; ++j) {
+      const int len = s_len[j], beg = s_beg[j], off = s_off[j];
+      for (int i = tid; i < len; i += BS_THREADS) skeys[off + i] = make_key(j, rv[beg + i], ctx, cty);
+    }
+    nsel = n;
+  } else {
+    // MSB radix select of the K-th smallest key; stop as soon as the keys at or below the
+    // current bucket fit in shared memory, then collect them.
+    const int shifts[5] = {40, 32, 21, 10, 0};
+    const int bits[5] = {11, 8, 11, 11, 10};
+    if (tid == 0) {
+      s_pval = 0ull;
+      s_pmask = 0ull;
+      s_below = 0;
+    }
+    __syncthreads();
+    nsel = 0;
+    for (int d = 0; d < 5; ++d) {
+      const int shift = shifts[d], nb = 1 << bits[d];
+      for (int i = tid; i < nb; i += BS_THREADS) shist[i] = 0;
+      __syncthreads();
+      const u64 pval = s_pval, pmask = s_pmask;
+      for (int j = 0; j < S; ++j) {
+        const int len = s_len[j], beg = s_beg[j];
+        for (int i = tid; i < len; i += BS_THREADS) {
+          const u64 key = make_key(j, rv[beg + i], ctx, cty);
+          if ((key & pmask) == pval) atomicAdd(&shist[(int)((key >> shift) & (u64)(nb - 1))], 1);
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        const int need = K - s_below;
+        int c = 0, b = 0;
+        for (; b < nb - 1; ++b) {
+          if (c + shist[b] >= need) break;
+          c += shist[b];
+        }
+        s_below += c;
+        s_pval = pval | ((u64)b << shift);
+        s_pmask = pmask | ((u64)(nb - 1) << shift);
+        s_le = s_below + shist[b];
+        s_cnt = 0;
+      }
+      __syncthreads();
+      if (s_le <= BS_CAP) {
+        const u64 upper = s_pval | ((1ull << shift) - 1ull);
+        for (int j = 0; j < S; ++j) {
+          const int len = s_len[j], beg = s_beg[j];
+          for (int i = tid; i < len; i += BS_THREADS) {
+            const u64 key = make_key(j, rv[beg + i], ctx, cty);
+            if (key <= upper) skeys[atomicAdd(&s_cnt, 1)] = key;
+          }
+        }
+        __syncthreads();
+        nsel = s_cnt;
+        break;
+      }
+    }
+  }
+  int P = 1;
+  while (P < nsel) P <<= 1;
+  for (int i = nsel + tid; i < P; i += BS_THREADS) skeys[i] = ~0ull;
+  __syncthreads();
+  bitonic_sort(skeys, P);
+
+  const int cnt = min(n, K);
+  const float ox = (float)(tx * 16), oy = (float)(ty * 16);
+  for (int k = tid; k < K; k += BS_THREADS) {
+    const long long o = ((long long)v * T + t) * K + k;
+    if (k < cnt) {
+      const u64 key = skeys[k];
+      const int g = (int)(unsigned)(key & 0xffffffffull);
+      const int j = (int)((key >> 32) & 0xffull);
+      idx[o] = g;
+      if (inv) inv[((long long)v * G + g) * S + j] = t * K + k;
+      if (PACK) {
+        // theta_u_gathered (tools/m4_train_binned.py:130-143) in the reference's fp32 op order
+        const float4* p = reinterpret_cast<const float4*>(proj + ((long long)v * G + g) * TTS_PROJ_FLOATS);
+        const float4 p0 = p[0], p1 = p[1], p2 = p[2];
+        const float mux = __fsub_rn(p0.x, ox), muy = __fsub_rn(p0.y, oy);
+        const float a = p0.z, b = p0.w, c = p1.x;
+        const float Q = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(a, mux), mux),
+                                            __fmul_rn(__fmul_rn(__fmul_rn(2.0f, b), mux), muy)),
+                                  __fmul_rn(__fmul_rn(c, muy), muy));
+        float4* dst = reinterpret_cast<float4*>(slots + o * TTS_SLOT_FLOATS);
+        dst[0] = make_float4(__fmul_rn(-a, inv_k), __fmul_rn(-c, inv_k), __fmul_rn(__fmul_rn(-2.0f, b), inv_k),
+                             __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(a, mux), __fmul_rn(b, muy))), inv_k));
+        dst[1] = make_float4(__fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(b, mux), __fmul_rn(c, muy))), inv_k),
+                             __fsub_rn(1.0f, __fmul_rn(Q, inv_k)), p1.y, p1.z);
+        dst[2] = make_float4(p1.w, p2.x, 0.f, 0.f);
+      }
+    } else {
+      idx[o] = -1;
+    }
+  }
+  if (tid == 0) {
+    count[(long long)v * T + t] = cnt;
+    cand[(long long)v * T + t] = n;
+  }
+}
+
+// ---- host launchers --------------------------------------------------------------------------
+struct BinWorkspace {
+  int* cell_count;   // [V][T]
+  int* cell_start;   // [V][T+1]
+  int2* cell_rank;   // [V][G]
+  float4* rec;       // [V][G]
+};
+
+static size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t bin_workspace_bytes(int G, int V, int T) {
+  return align_up((size_t)V * T * 4) + align_up((size_t)V * (T + 1) * 4) + align_up((size_t)V * G * 8) +
+         align_up((size_t)V * G * 16);
+}
+
+static BinWorkspace carve(void* ws, int G, int V, int T) {
+  char* p = static_cast<char*>(ws);
+  BinWorkspace w;
+  w.cell_count = reinterpret_cast<int*>(p);
+  p += align_up((size_t)V * T * 4);
+  w.cell_start = reinterpret_cast<int*>(p);
+  p += align_up((size_t)V * (T + 1) * 4);
+  w.cell_rank = reinterpret_cast<int2*>(p);
+  p += align_up((size_t)V * G * 8);
+  w.rec = reinterpret_cast<float4*>(p);
+  return w;
+}
+
+static int bin_core(const float* mu2d, const int* cell_count, const int2* cell_rank, int G, int V, int ntx,
+                    int nty, int R, int K, const float* proj, float inv_k, int* idx, int* count, int* cand,
+                    int* inv, float* slots, BinWorkspace w, cudaStream_t st) {
+  const int T = ntx * nty;
+  const int S = (2 * R + 1) * (2 * R + 1);
+  if (inv) {
+    if (cudaMemsetAsync(inv, 0xff, (size_t)V * G * S * 4, st) != cudaSuccess) return check_launch("memset inv");
+  }
+  k_cell_scan<<<V, 1024, 0, st>>>(cell_count, w.cell_start, T);
+  dim3 gg((G + 255) / 256, V);
+  if (G > 0) k_cell_scatter<<<gg, 256, 0, st>>>(reinterpret_cast<const float2*>(mu2d), cell_rank, w.cell_start, G, T, w.rec);
+  dim3 gt(T, V);
+  if (proj && slots)
+    k_bin_select<true><<<gt, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, proj, inv_k, idx, count, cand,
+                                                  inv, slots);
+  else
+    k_bin_select<false><<<gt, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, nullptr, inv_k, idx, count,
+                                                   cand, inv, nullptr);
+  return check_launch("binning");
+}
+
+static int validate(int G, int V, int H, int W, int R, int K) {
+  TTS_REQUIRE(G >= 0 && V >= 1, "G must be >= 0 and V >= 1");
+  TTS_REQUIRE(H > 0 && W > 0 && H % 16 == 0 && W % 16 == 0, "H and W must be positive multiples of 16");
+  TTS_REQUIRE(R >= 0 && R <= 3, "R must be in [0, 3]");
+  TTS_REQUIRE(K >= 1 && K <= 256, "K must be in [1, 256]");
+  return TTS_OK;
+}
+
+}  // namespace tts
+
+using namespace tts;
+
+extern "C" size_t tts_bin_workspace_bytes(int G, int V, int H, int W) {
+  return bin_workspace_bytes(G, V, (H / 16) * (W / 16));
+}
+
+extern "C" int tts_bin_from_mu2d(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W, int R, int K,
+                                 int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (int rc = validate(G, V, H, W, R, K)) return rc;
+  const int ntx = W / 16, nty = H / 16, T = ntx * nty;
+  if (workspace_bytes < bin_workspace_bytes(G, V, T)) return fail(TTS_ERR_CAPACITY, "binning workspace too small");
+  TTS_REQUIRE(idx && count && cand && workspace, "null output or workspace pointer");
+  TTS_REQUIRE(G == 0 || (mu2d && keep), "null mu2d/keep");
+  cudaStream_t st = as_stream(stream);
+  BinWorkspace w = carve(workspace, G, V, T);
+  if (cudaMemsetAsync(w.cell_count, 0, (size_t)V * T * 4, st) != cudaSuccess) return check_launch("memset counts");
+  if (G > 0)
+    k_cell_count<<<dim3((G + 255) / 256, V), 256, 0, st>>>(reinterpret_cast<const float2*>(mu2d), keep, G, ntx, nty,
+                                                            w.cell_count, w.cell_rank);
+  return bin_core(mu2d, w.cell_count, w.cell_rank, G, V, ntx, nty, R, K, nullptr, 0.f, idx, count, cand, inv, nullptr,
+                  w, st);
+}
+
+extern "C" int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float* proj, const int32_t* cell_count,
+                            const int32_t* cell_rank, int G, int V, int H, int W, int R, int K, float k_poly,
+                            int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv, float* slots, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  (void)keep;
+  if (int rc = validate(G, V, H, W, R, K)) return rc;
+  const int ntx = W / 16, nty = H / 16, T = ntx * nty;
+  if (workspace_bytes < bin_workspace_bytes(G, V, T)) return fail(TTS_ERR_CAPACITY, "binning workspace too small");
+  TTS_REQUIRE(idx && count && cand && inv && slots && proj && cell_count && cell_rank, "null pointer");
+  TTS_REQUIRE(aligned16(proj) && aligned16(slots), "proj and slots must be 16-byte aligned");
+  TTS_REQUIRE(k_poly > 0.f, "k must be positive");
+  BinWorkspace w = carve(workspace, G, V, T);
+  return bin_core(mu2d, cell_count, reinterpret_cast<const int2*>(cell_rank), G, V, ntx, nty, R, K, proj,
+                  (float)(1.0 / (double)k_poly), idx, count, cand, inv, slots, w, as_stream(stream));
+}

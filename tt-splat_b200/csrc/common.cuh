@@ -1,0 +1,142 @@
+// Shared device helpers for the tt-splat B200 kernels (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <string>
+
+#include "../../include/ttsplat_b200.h"
+
+namespace tts {
+
+// ---- host-side error plumbing ------------------------------------------------------------
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int check_launch(const char* what);
+
+#define TTS_REQUIRE(cond, msg)                                   \
+  do {                                                           \
+    if (!(cond)) return ::tts::fail(TTS_ERR_INVALID, (msg));     \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Device status word (bounded waits that gave up record here instead of trapping).
+extern __device__ int g_status;
+constexpr int STATUS_MBAR_TIMEOUT = 1;
+
+// ---- flat parameter layout (spike/model.py:28-47) ------------------------------------------
+struct ParamLayout {
+  int G;
+  __host__ __device__ int means() const { return 0; }
+  __host__ __device__ int log_scales() const { return 3 * G; }
+  __host__ __device__ int quats() const { return 6 * G; }
+  __host__ __device__ int opacity() const { return 10 * G; }
+  __host__ __device__ int color_dc() const { return 11 * G; }
+  __host__ __device__ int color_rest() const { return 14 * G; }
+  __host__ __device__ int w_b_raw() const { return 59 * G; }
+  __host__ __device__ long long total() const { return 59LL * G + 1; }
+};
+
+struct Cam {
+  float R[9], t[3], fx, fy, cx, cy, c[3];
+};
+
+__device__ __forceinline__ Cam load_cam(const float* cams, int v) {
+  Cam c;
+  const float* p = cams + v * TTS_CAM_FLOATS;
+#pragma unroll
+  for (int i = 0; i < 9; i++) c.R[i] = __ldg(p + i);
+#pragma unroll
+  for (int i = 0; i < 3; i++) c.t[i] = __ldg(p + 9 + i);
+  c.fx = __ldg(p + 12); c.fy = __ldg(p + 13); c.cx = __ldg(p + 14); c.cy = __ldg(p + 15);
+#pragma unroll
+  for (int i = 0; i < 3; i++) c.c[i] = __ldg(p + 16 + i);
+  return c;
+}
+
+// torch.nn.functional.softplus(beta=1, threshold=20) and its derivative.
+__device__ __forceinline__ float softplusf(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float softplus_grad(float x) {
+  if (x > 20.f) return 1.f;
+  float z = expf(x);
+  return z / (z + 1.f);
+}
+__device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x)); }
+
+// ---- bounded mbarrier + bulk copy (1-D TMA, no multicast) ----------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for phase `parity` with an iteration limit; on timeout record the status and report
+// false.  try_wait itself suspends for a hardware-defined interval, so the limit is ~seconds.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (int it = 0; it < (1 << 22); ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicOr(&g_status, STATUS_MBAR_TIMEOUT);
+  return false;
+}
+
+// ---- Philox4x32-10 (Salmon et al., SC'11 "Parallel random numbers: as easy as 1, 2, 3") ----
+struct U4 {
+  uint32_t x, y, z, w;
+};
+__device__ __forceinline__ U4 philox4x32_10(U4 ctr, uint32_t k0, uint32_t k1) {
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    uint32_t hi0 = __umulhi(M0, ctr.x), lo0 = M0 * ctr.x;
+    uint32_t hi1 = __umulhi(M1, ctr.z), lo1 = M1 * ctr.z;
+    U4 n;
+    n.x = hi1 ^ ctr.y ^ k0;
+    n.y = lo1;
+    n.z = hi0 ^ ctr.w ^ k1;
+    n.w = lo0;
+    ctr = n;
+    k0 += W0;
+    k1 += W1;
+  }
+  return ctr;
+}
+// Uniform in (0, 1] from 32 random bits (never 0, so log() is finite).
+__device__ __forceinline__ float u01(uint32_t b) { return (float)(b >> 8) * (1.0f / 16777216.0f) + (0.5f / 16777216.0f); }
+// Uniform in [0, 1).
+__device__ __forceinline__ float u01_open(uint32_t b) { return (float)(b >> 8) * (1.0f / 16777216.0f); }
+// Box-Muller: two standard normals from two uniforms.
+__device__ __forceinline__ void box_muller(uint32_t a, uint32_t b, float& n0, float& n1) {
+  float r = sqrtf(-2.0f * logf(u01(a)));
+  float s, c;
+  sincospif(2.0f * u01_open(b), &s, &c);
+  n0 = r * c;
+  n1 = r * s;
+}
+
+}  // namespace tts

@@ -1,0 +1,236 @@
+"""Functional wrappers over the C ABI: allocate outputs with torch, call on the current stream.
+
+Shapes follow ``include/ttsplat_b200.h``.  Every function validates that its tensors are CUDA
+and contiguous and raises otherwise (no CPU fallback).
+"""
+import numpy as np
+import torch
+
+from ._lib import call, lib, ptr, stream
+
+SLOT_FLOATS = 12
+SLOT_GRAD_FLOATS = 10
+PROJ_FLOATS = 12
+
+
+def _dev(*ts):
+    for t in ts:
+        if t is not None:
+            if not t.is_cuda:
+                raise RuntimeError("tt-splat B200 ops need CUDA tensors (no CPU fallback)")
+            if not t.is_contiguous():
+                raise ValueError("tensors must be contiguous")
+
+
+def tiles(H, W):
+    if H % 16 or W % 16:
+        raise AssertionError("H and W must be multiples of 16 (TileMap, tools/m4_train_binned.py:62)")
+    return W // 16, H // 16, (W // 16) * (H // 16)
+
+
+class Workspace:
+    """A grow-only device scratch buffer."""
+
+    def __init__(self, device):
+        self.device = device
+        self.buf = torch.empty(0, dtype=torch.uint8, device=device)
+
+    def get(self, nbytes):
+        if self.buf.numel() < nbytes:
+            self.buf = torch.empty(int(nbytes), dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+def project(flat, G, sh_degree, cams, H, W, blur=0.3, near=0.2, out=None):
+    """Geometry + SH + activations for V = cams.shape[0] views (also counts home cells)."""
+    _dev(flat, cams)
+    V = cams.shape[0]
+    _, _, T = tiles(H, W)
+    dev = flat.device
+    if out is None:
+        out = dict(proj=torch.empty(V, G, PROJ_FLOATS, device=dev), mu2d=torch.empty(V, G, 2, device=dev),
+                   keep=torch.empty(V, G, dtype=torch.uint8, device=dev),
+                   cell_count=torch.zeros(V, T, dtype=torch.int32, device=dev),
+                   cell_rank=torch.empty(V, G, 2, dtype=torch.int32, device=dev))
+    else:
+        out["cell_count"].zero_()
+    call("tts_project", ptr(flat), G, sh_degree, ptr(cams), V, H, W, float(blur), float(near), ptr(out["proj"]),
+         ptr(out["mu2d"]), ptr(out["keep"]), ptr(out["cell_count"]), ptr(out["cell_rank"]), stream())
+    return out
+
+
+def bin_from_mu2d(mu2d, keep, H, W, R, K, ws=None, with_inv=True):
+    """assign_bins on given mu2d[V,G,2] / keep[V,G] (uint8 or bool)."""
+    if mu2d.dim() == 2:
+        mu2d, keep = mu2d[None], keep[None]
+    keep = keep.to(torch.uint8).contiguous()
+    mu2d = mu2d.float().contiguous()
+    _dev(mu2d, keep)
+    V, G = mu2d.shape[0], mu2d.shape[1]
+    _, _, T = tiles(H, W)
+    dev = mu2d.device
+    S = (2 * R + 1) ** 2
+    idx = torch.empty(V, T, K, dtype=torch.int32, device=dev)
+    count = torch.empty(V, T, dtype=torch.int32, device=dev)
+    cand = torch.empty(V, T, dtype=torch.int32, device=dev)
+    inv = torch.empty(V, G, S, dtype=torch.int32, device=dev) if with_inv else None
+    nbytes = lib().tts_bin_workspace_bytes(G, V, H, W)
+    ws = ws or Workspace(dev)
+    buf = ws.get(nbytes)
+    call("tts_bin_from_mu2d", ptr(mu2d), ptr(keep), G, V, H, W, R, K, ptr(idx), ptr(count), ptr(cand), ptr(inv),
+         ptr(buf), nbytes, stream())
+    return idx, count, cand, inv
+
+
+def bin_pack(pj, G, H, W, R, K, k=4.0, ws=None, out=None):
+    """Binning + slot-row pack on the output of ``project``."""
+    V = pj["proj"].shape[0]
+    _, _, T = tiles(H, W)
+    dev = pj["proj"].device
+    S = (2 * R + 1) ** 2
+    if out is None:
+        out = dict(idx=torch.empty(V, T, K, dtype=torch.int32, device=dev),
+                   count=torch.empty(V, T, dtype=torch.int32, device=dev),
+                   cand=torch.empty(V, T, dtype=torch.int32, device=dev),
+                   inv=torch.empty(V, G, S, dtype=torch.int32, device=dev),
+                   slots=torch.empty(V, T, K, SLOT_FLOATS, device=dev))
+    nbytes = lib().tts_bin_workspace_bytes(G, V, H, W)
+    ws = ws or Workspace(dev)
+    buf = ws.get(nbytes)
+    call("tts_bin_pack", ptr(pj["mu2d"]), ptr(pj["keep"]), ptr(pj["proj"]), ptr(pj["cell_count"]), ptr(pj["cell_rank"]),
+         G, V, H, W, R, K, float(k), ptr(out["idx"]), ptr(out["count"]), ptr(out["cand"]), ptr(out["inv"]),
+         ptr(out["slots"]), ptr(buf), nbytes, stream())
+    return out
+
+
+def render_fwd(slots, count, H, W, w_b, c_b, bf16=False, out=None, w_b_is_raw=True):
+    """Per-tile forward; ``w_b`` is a 1-element device tensor: the model's w_b_raw (softplus
+    applied on the device) or, with ``w_b_is_raw=False``, the activated background weight."""
+    _dev(slots, count, w_b, c_b)
+    V, T, K = slots.shape[0], slots.shape[1], slots.shape[2]
+    dev = slots.device
+    if out is None:
+        out = dict(img=torch.empty(V, H, W, 3, device=dev), den=torch.empty(V, H, W, device=dev))
+    call("tts_render_fwd", ptr(slots), int(bool(bf16)), ptr(count), V, H, W, K, ptr(w_b), int(bool(w_b_is_raw)), ptr(c_b),
+         ptr(out["img"]), ptr(out["den"]), stream())
+    return out
+
+
+def render_bwd(slots, count, H, W, c_b, img, den, gimg, out=None):
+    _dev(slots, count, c_b, img, den, gimg)
+    V, T, K = slots.shape[0], slots.shape[1], slots.shape[2]
+    dev = slots.device
+    if out is None:
+        out = dict(slot_grads=torch.empty(V, T, K, SLOT_GRAD_FLOATS, device=dev), gwb=torch.empty(V, T, device=dev))
+    call("tts_render_bwd", ptr(slots), ptr(count), V, H, W, K, ptr(c_b), ptr(img), ptr(den), ptr(gimg),
+         ptr(out["slot_grads"]), ptr(out["gwb"]), stream())
+    return out
+
+
+def loss_l1_ssim(img, target, lam=0.2, grad_scale=1.0, ws=None, out=None):
+    _dev(img, target)
+    if img.dim() == 3:
+        img, target = img[None], target[None]
+    V, H, W = img.shape[0], img.shape[1], img.shape[2]
+    dev = img.device
+    if out is None:
+        out = dict(gimg=torch.empty_like(img), loss=torch.empty(V, device=dev))
+    nbytes = lib().tts_loss_workspace_bytes(V, H, W)
+    ws = ws or Workspace(dev)
+    buf = ws.get(nbytes)
+    call("tts_loss_l1_ssim", ptr(img), ptr(target), V, H, W, float(lam), float(grad_scale), ptr(out["gimg"]),
+         ptr(out["loss"]), ptr(buf), nbytes, stream())
+    return out
+
+
+def backward_params(flat, G, sh_degree, cams, H, W, R, K, inv, slot_grads, gwb, k=4.0, blur=0.3, near=0.2,
+                    lambda_o=0.0, lambda_s=0.0, out=None):
+    _dev(flat, cams, inv, slot_grads, gwb)
+    V = cams.shape[0]
+    grads = out if out is not None else torch.empty_like(flat)
+    call("tts_backward_params", ptr(flat), G, sh_degree, ptr(cams), V, H, W, R, K, float(k), float(blur), float(near),
+         ptr(inv), ptr(slot_grads), ptr(gwb), float(lambda_o), float(lambda_s), ptr(grads), stream())
+    return grads
+
+
+def sgld(flat, G, step, lr_means, noise_lr, eps_noise=None, seed=0):
+    _dev(flat, step, eps_noise)
+    call("tts_sgld", ptr(flat), G, float(lr_means), float(noise_lr), ptr(eps_noise), ptr(step),
+         int(seed) & (2 ** 64 - 1), stream())
+
+
+def step_begin(step):
+    call("tts_step_begin", ptr(step), stream())
+
+
+def adam_sgld(flat, grads, m, v, G, sh_degree, step, lr7, betas=(0.9, 0.999), eps=1e-8, noise_lr=0.0,
+              eps_noise=None, seed=0):
+    _dev(flat, grads, m, v, step, lr7)
+    call("tts_adam_sgld", ptr(flat), ptr(grads), ptr(m), ptr(v), G, sh_degree, ptr(step), ptr(lr7), float(betas[0]),
+         float(betas[1]), float(eps), float(noise_lr), ptr(eps_noise), int(seed) & (2 ** 64 - 1), stream())
+
+
+def relocate(flat, m, v, G, step, dead_thr=0.005, dead_frac=0.0, offset=0.0, targets_in=None, noise_in=None, seed=0,
+             ws=None, out=None):
+    _dev(flat, m, v, step)
+    dev = flat.device
+    if out is None:
+        out = dict(n_dead=torch.zeros(1, dtype=torch.int32, device=dev),
+                   targets=torch.empty(G, dtype=torch.int32, device=dev))
+    nbytes = lib().tts_relocate_workspace_bytes(G)
+    ws = ws or Workspace(dev)
+    buf = ws.get(nbytes)
+    call("tts_relocate", ptr(flat), ptr(m), ptr(v), G, float(dead_thr), float(dead_frac), float(offset), ptr(targets_in),
+         ptr(noise_in), ptr(step), int(seed) & (2 ** 64 - 1), ptr(out["n_dead"]), ptr(out["targets"]), ptr(buf), nbytes,
+         stream())
+    return out
+
+
+def pack_operands(theta_u, color_o, o_col):
+    _dev(theta_u, color_o, o_col)
+    VT, K = theta_u.shape[0], theta_u.shape[2]
+    slots = torch.empty(VT, K, SLOT_FLOATS, device=theta_u.device)
+    call("tts_pack_operands", ptr(theta_u), ptr(color_o), ptr(o_col), VT, K, ptr(slots), stream())
+    return slots
+
+
+def unpack_slot_grads(slot_grads):
+    _dev(slot_grads)
+    VT, K = slot_grads.shape[0], slot_grads.shape[1]
+    dev = slot_grads.device
+    gth = torch.empty(VT, 6, K, device=dev)
+    gcol = torch.empty(VT, K, 3, device=dev)
+    goc = torch.empty(VT, K, 1, device=dev)
+    call("tts_unpack_slot_grads", ptr(slot_grads), VT, K, ptr(gth), ptr(gcol), ptr(goc), stream())
+    return gth, gcol, goc
+
+
+def wsr_dense_fwd(theta_u, o, color, w_b, Phi, c_b, keep=None):
+    _dev(theta_u, o, color, w_b, Phi, c_b, keep)
+    P, G = Phi.shape[0], theta_u.shape[0]
+    C = torch.empty(P, 3, device=Phi.device)
+    den = torch.empty(P, device=Phi.device)
+    call("tts_wsr_dense_fwd", ptr(theta_u), ptr(o), ptr(color), ptr(w_b), ptr(Phi), ptr(c_b), ptr(keep), P, G, ptr(C),
+         ptr(den), stream())
+    return C, den
+
+
+def wsr_dense_bwd(theta_u, o, color, w_b, Phi, c_b, keep, C, den, gC):
+    _dev(theta_u, o, color, w_b, Phi, c_b, keep, C, den, gC)
+    P, G = Phi.shape[0], theta_u.shape[0]
+    dev = Phi.device
+    gth = torch.empty(G, 6, device=dev)
+    go = torch.empty(G, device=dev)
+    gcol = torch.empty(G, 3, device=dev)
+    gwb = torch.empty(1, device=dev)
+    call("tts_wsr_dense_bwd", ptr(theta_u), ptr(o), ptr(color), ptr(w_b), ptr(Phi), ptr(c_b), ptr(keep), P, G, ptr(C),
+         ptr(den), ptr(gC), ptr(gth), ptr(go), ptr(gcol), ptr(gwb), stream())
+    return gth, go, gcol, gwb
+
+
+def read_status():
+    """Read and clear the device status word (bounded waits that gave up); synchronous."""
+    import ctypes
+    s = np.zeros(1, np.int32)
+    call("tts_read_status", ctypes.c_void_p(s.ctypes.data))
+    return int(s[0])

@@ -1,0 +1,68 @@
+"""End-to-end binned render: gaussian model + camera(s) -> image(s) (mirrors spike/render.py:14-49).
+
+``render(model, cam, arm="A", k, blur_eps, near, sh_degree)`` keeps the reference signature and
+runs the B200 path: the fused projection kernel (geometry + SH colour + activations), the
+bit-exact binning with its slot-row pack, and the fused per-tile forward.  It is differentiable:
+the backward runs the fused per-tile backward and the parameter backward kernel, returning the
+gradient of every model parameter.  Rendering is binned (16x16 tiles, radius-R neighbour cells,
+K gaussians per tile, the reference's ``tools/m4_train_binned.py`` operator), which equals the
+dense ``spike.render`` whenever no tile overflows K and no gaussian reaches past its stencil.
+Only arm A (plain weighted-sum rendering) is on this path.
+"""
+import torch
+
+from . import ops
+from ._lib import require_cuda
+from .camera import as_camera, pack_cameras
+from .model import flat_of
+
+ARMS = ("A", "B", "C0", "C", "SZ", "RV", "D")
+
+
+class _BinnedRender(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, flat, cams_t, c_b, cfg):
+        G, sh_degree, H, W, R, K, k, blur, near, bf16 = cfg
+        flat_d = flat.detach().contiguous()
+        pj = ops.project(flat_d, G, sh_degree, cams_t, H, W, blur, near)
+        bp = ops.bin_pack(pj, G, H, W, R, K, k)
+        slots = bp["slots"].to(torch.bfloat16).contiguous() if bf16 else bp["slots"]
+        rf = ops.render_fwd(slots, bp["count"], H, W, flat_d[59 * G:], c_b, bf16=bf16)
+        ctx.save_for_backward(flat_d, cams_t, c_b, bp["slots"], bp["count"], bp["inv"], rf["img"], rf["den"])
+        ctx.cfg = cfg
+        ctx.bins = bp
+        return rf["img"]
+
+    @staticmethod
+    def backward(ctx, gimg):
+        flat, cams_t, c_b, slots, count, inv, img, den = ctx.saved_tensors
+        G, sh_degree, H, W, R, K, k, blur, near, _ = ctx.cfg
+        rb = ops.render_bwd(slots, count, H, W, c_b, img, den, gimg.contiguous())
+        grads = ops.backward_params(flat, G, sh_degree, cams_t, H, W, R, K, inv, rb["slot_grads"], rb["gwb"], k, blur, near)
+        return grads, None, None, None
+
+
+def render_views(model, cams, k=4.0, blur_eps=0.3, near=0.2, sh_degree=0, R=1, K=128, bf16=False):
+    """Render V views in one batched launch per stage -> [V, H, W, 3]."""
+    require_cuda()
+    cams = [as_camera(c) for c in cams]
+    flat = flat_of(model)
+    if not flat.is_cuda:
+        raise RuntimeError("the model must live on a CUDA device (no CPU fallback)")
+    G = model.means3d.shape[0]
+    H, W = cams[0].H, cams[0].W
+    ops.tiles(H, W)
+    cams_t = pack_cameras(cams, flat.device)
+    c_b = getattr(model, "c_b", None)
+    c_b = torch.ones(3, device=flat.device) if c_b is None else c_b.to(flat.device).float().contiguous()
+    cfg = (G, int(sh_degree), H, W, int(R), int(K), float(k), float(blur_eps), float(near), bool(bf16))
+    return _BinnedRender.apply(flat, cams_t, c_b, cfg)
+
+
+def render(model, cam, arm="A", k=4.0, blur_eps=0.3, near=0.2, sh_degree=0, R=1, K=128, bf16=False):
+    """spike/render.py:14-49 on the B200 path -> [H, W, 3]."""
+    if arm not in ARMS:
+        raise ValueError(f"unknown arm {arm!r}")
+    if arm != "A":
+        raise NotImplementedError(f"arm {arm!r} is not on the B200 hot path (only arm A, plain WSR)")
+    return render_views(model, [cam], k, blur_eps, near, sh_degree, R, K, bf16)[0]

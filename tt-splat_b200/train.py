@@ -1,0 +1,203 @@
+"""Device-resident, CUDA-graph-captured train step (mirrors spike/train.py:9-41 and the step of
+tools/resident_traced.py:667-757).
+
+One ``TrainStep`` owns every buffer of the step for a fixed set of views, so a step allocates
+nothing and synchronises nothing with the host:
+
+    step_begin -> project (V views) -> bin + pack -> render forward -> loss forward+gradient
+    -> render backward -> slot->gaussian reduction + parameter backward
+    [-> NCCL all-reduce of the gradient across ranks] -> Adam (+ SGLD) [-> relocation]
+
+The first step runs eagerly (it also loads the kernels); later steps replay CUDA graphs
+captured from the same launches (one graph per step variant: with or without relocation;
+with a process group, one graph before and one after the all-reduce).  ``step()`` returns the
+device tensor holding the step's mean loss; reading it is the only synchronisation.
+"""
+import numpy as np
+import torch
+
+from . import ops
+from ._lib import require_cuda
+from .camera import as_camera, pack_cameras
+from .model import GaussianModel, flat_of, lr_vector, view
+
+DEFAULT_LR = {"means": 5e-3, "scales": 5e-3, "quats": 1e-3, "opacity": 5e-2, "opacity_sh": 5e-2, "color": 1e-2,
+              "wb": 1e-2, "depth": 1e-2}   # spike/train.py:9-12
+
+
+class TrainStep:
+    def __init__(self, model, cameras, gt_images, sh_degree=0, lambda_ssim=0.2, lr=None, K=128, R=1, k=4.0,
+                 blur=0.3, near=0.2, noise_lr=0.0, relocate_every=0, dead_thr=0.005, dead_frac=0.0, offset=0.0,
+                 lambda_o=0.0, lambda_s=0.0, seed=0, n_views_total=None, process_group=None, use_graph=True):
+        require_cuda()
+        if not isinstance(model, GaussianModel):
+            raise TypeError("TrainStep trains a tt_splat_b200.model.GaussianModel (flat device buffer)")
+        self.model = model
+        self.flat = model.flat.data
+        dev = self.flat.device
+        self.dev = dev
+        self.G = model.G
+        cams = [as_camera(c) for c in cameras]
+        self.V = len(cams)
+        self.H, self.W = cams[0].H, cams[0].W
+        ops.tiles(self.H, self.W)
+        self.cams_t = pack_cameras(cams, dev)
+        self.targets = torch.stack([torch.as_tensor(g, dtype=torch.float32).to(dev) for g in gt_images]).contiguous()
+        if self.targets.shape != (self.V, self.H, self.W, 3):
+            raise ValueError(f"gt images must be [H,W,3] = {(self.H, self.W, 3)} each")
+        self.sh_degree, self.lam, self.K, self.R, self.k = int(sh_degree), float(lambda_ssim), int(K), int(R), float(k)
+        self.blur, self.near = float(blur), float(near)
+        self.noise_lr, self.relocate_every = float(noise_lr), int(relocate_every)
+        self.dead_thr, self.dead_frac, self.offset = float(dead_thr), float(dead_frac), float(offset)
+        self.lambda_o, self.lambda_s, self.seed = float(lambda_o), float(lambda_s), int(seed)
+        self.pg = process_group
+        self.n_views_total = int(n_views_total or self.V)
+        self.grad_scale = 1.0 / self.n_views_total
+        self.lr = {**DEFAULT_LR, **(lr or {})}
+        self.lr7 = lr_vector(self.lr, dev)
+        self.use_graph = use_graph
+        G, V, H, W, K = self.G, self.V, self.H, self.W, self.K
+        T = (H // 16) * (W // 16)
+        S = (2 * self.R + 1) ** 2
+        e = lambda *s, dt=torch.float32: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
+        self.pj = dict(proj=e(V, G, ops.PROJ_FLOATS), mu2d=e(V, G, 2), keep=e(V, G, dt=torch.uint8),
+                       cell_count=torch.zeros(V, T, dtype=torch.int32, device=dev), cell_rank=e(V, G, 2, dt=torch.int32))
+        self.bp = dict(idx=e(V, T, K, dt=torch.int32), count=e(V, T, dt=torch.int32), cand=e(V, T, dt=torch.int32),
+                       inv=e(V, G, S, dt=torch.int32), slots=e(V, T, K, ops.SLOT_FLOATS))
+        self.rf = dict(img=e(V, H, W, 3), den=e(V, H, W))
+        self.lo = dict(gimg=e(V, H, W, 3), loss=e(V))
+        self.rb = dict(slot_grads=e(V, T, K, ops.SLOT_GRAD_FLOATS), gwb=e(V, T))
+        self.grads = torch.zeros_like(self.flat)
+        self.m = torch.zeros_like(self.flat)
+        self.v = torch.zeros_like(self.flat)
+        self.step_t = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.reloc = dict(n_dead=torch.zeros(1, dtype=torch.int32, device=dev), targets=e(G, dt=torch.int32))
+        self.ws_bin, self.ws_loss, self.ws_reloc = ops.Workspace(dev), ops.Workspace(dev), ops.Workspace(dev)
+        self.ws_bin.get(ops.lib().tts_bin_workspace_bytes(G, V, H, W))
+        self.ws_loss.get(ops.lib().tts_loss_workspace_bytes(V, H, W))
+        self.ws_reloc.get(ops.lib().tts_relocate_workspace_bytes(G) if G >= 2 else 0)
+        self.loss_mean = e(1)
+        self.n_moved = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.it = 0
+        self.graphs = {}
+        self.kernels_per_step = None
+
+    # ---- the launches of one step --------------------------------------------------------
+    def _fwd_bwd(self):
+        G, H, W, R, K = self.G, self.H, self.W, self.R, self.K
+        ops.step_begin(self.step_t)
+        ops.project(self.flat, G, self.sh_degree, self.cams_t, H, W, self.blur, self.near, out=self.pj)
+        ops.bin_pack(self.pj, G, H, W, R, K, self.k, ws=self.ws_bin, out=self.bp)
+        ops.render_fwd(self.bp["slots"], self.bp["count"], H, W, self.flat[59 * G:], self.model.c_b, out=self.rf)
+        ops.loss_l1_ssim(self.rf["img"], self.targets, self.lam, self.grad_scale, ws=self.ws_loss, out=self.lo)
+        ops.render_bwd(self.bp["slots"], self.bp["count"], H, W, self.model.c_b, self.rf["img"], self.rf["den"],
+                       self.lo["gimg"], out=self.rb)
+        ops.backward_params(self.flat, G, self.sh_degree, self.cams_t, H, W, R, K, self.bp["inv"],
+                            self.rb["slot_grads"], self.rb["gwb"], self.k, self.blur, self.near, self.lambda_o,
+                            self.lambda_s, out=self.grads)
+        torch.sum(self.lo["loss"], dim=0, keepdim=True, out=self.loss_mean)
+
+    def _update(self, relocate):
+        ops.adam_sgld(self.flat, self.grads, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
+                      noise_lr=self.noise_lr, seed=self.seed)
+        if relocate:
+            ops.relocate(self.flat, self.m, self.v, self.G, self.step_t, self.dead_thr, self.dead_frac, self.offset,
+                         seed=self.seed, ws=self.ws_reloc, out=self.reloc)
+            self.n_moved.add_(self.reloc["n_dead"])
+
+    def _allreduce(self):
+        import torch.distributed as dist
+        dist.all_reduce(self.grads, group=self.pg)
+        dist.all_reduce(self.loss_mean, group=self.pg)
+
+    def _run(self, relocate):
+        if self.pg is None:
+            self._fwd_bwd()
+            self._update(relocate)
+        else:
+            self._fwd_bwd()
+            self._allreduce()
+            self._update(relocate)
+
+    def _graph_run(self, relocate):
+        if self.pg is None:
+            key = ("all", relocate)
+            if key not in self.graphs:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._fwd_bwd()
+                    self._update(relocate)
+                self.graphs[key] = g
+            self.graphs[key].replay()
+        else:
+            if "fb" not in self.graphs:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._fwd_bwd()
+                self.graphs["fb"] = g
+            key = ("up", relocate)
+            if key not in self.graphs:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._update(relocate)
+                self.graphs[key] = g
+            self.graphs["fb"].replay()
+            self._allreduce()
+            self.graphs[key].replay()
+
+    def launches(self, relocate):
+        """Kernels of this library launched by one step (memsets and torch ops excluded)."""
+        n = 12 + 1                                        # forward/backward chain + Adam/SGLD
+        if relocate:
+            n += 7 + (7 if self.dead_frac > 0 else 0)     # relocation (+ quantile select)
+        return n
+
+    def step(self):
+        """One training iteration (spike/mcmc.py:97-111 order); returns the device loss tensor."""
+        it = self.it
+        relocate = bool(self.relocate_every) and it > 0 and it % self.relocate_every == 0 and self.G >= 2
+        self.kernels_per_step = self.launches(relocate)
+        if self.use_graph and it > 0:
+            self._graph_run(relocate)
+        else:
+            self._run(relocate)
+        self.it += 1
+        return self.loss_mean.view(())
+
+    def mean_loss_value(self):
+        """Mean photometric loss of the last step (+ the MCMC regulariser when enabled); syncs."""
+        total = float(self.loss_mean.item()) / self.n_views_total
+        if self.lambda_o or self.lambda_s:
+            o = torch.sigmoid(view(self.flat, self.G, "opacity_raw"))
+            s = torch.exp(view(self.flat, self.G, "log_scales"))
+            total += self.lambda_o * float(o.mean()) + self.lambda_s * float(s.mean())
+        return total
+
+    def release(self):
+        """Drop the captured graphs (call before destroying a process group)."""
+        self.graphs.clear()
+
+
+def fit(model, cameras, gt_images, arm="A", iters=800, lambda_ssim=0.2, lr=None, k=4.0, blur_eps=0.3, near=0.2,
+        log_every=0, sh_degree=0, K=128, R=1):
+    """spike/train.py:15-33 on the B200 path: returns the per-iteration mean loss history."""
+    if arm != "A":
+        raise NotImplementedError("only arm A is on the B200 hot path")
+    st = TrainStep(model, cameras, gt_images, sh_degree=sh_degree, lambda_ssim=lambda_ssim, lr=lr, K=K, R=R, k=k,
+                   blur=blur_eps, near=near)
+    hist = []
+    for it in range(iters):
+        hist.append(st.step().clone())
+        if log_every and (it % log_every == 0 or it == iters - 1):
+            print(f"    iter {it:4d}  loss {float(hist[-1]) / st.V:.5f}")
+    return (torch.stack(hist) / st.V).cpu().tolist() if hist else []
+
+
+@torch.no_grad()
+def eval_psnr(model, cameras, gt_images, arm="A", **kw):
+    """spike/train.py:36-41."""
+    from .metrics import psnr
+    from .render import render
+    vals = [float(psnr(render(model, cam, arm, **kw), torch.as_tensor(gt).to(model.flat.device)))
+            for cam, gt in zip(cameras, gt_images)]
+    return sum(vals) / len(vals)
