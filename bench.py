@@ -184,7 +184,7 @@ def run_ours(args, rank, world, local_rank):
     from tt_splat_b200 import camera, model, ops, train
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    sc = pkg.synthetic.config2()
+    sc = pkg.synthetic.config2(G=CONFIG["G"], n_views=max(CONFIG["views"], 1))
     V = CONFIG["views"]
     per = V // world
     mine = list(range(rank * per, (rank + 1) * per)) if world <= V else [rank % V]
@@ -229,6 +229,12 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- end to end through the public API: pinned H2D of the step's targets, D2H of the loss
     h2d = targets_host.numel() * 4
+    if args.skip_e2e:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": steps_per_s, "unit": "steps/s", "config": CONFIG,
+                              "stage_ms": stages}), flush=True)
+        st.release()
+        return
     barrier()
     torch.cuda.synchronize()
     e0.record()
@@ -328,7 +334,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--views", type=int, default=CONFIG["views"], help="reduced batch for profiling captures")
+    ap.add_argument("--gaussians", type=int, default=CONFIG["G"], help="reduced G for profiling captures")
+    ap.add_argument("--skip-e2e", action="store_true", help="skip the end-to-end and render legs (profiling)")
     args = ap.parse_args()
+    if args.views != CONFIG["views"] or args.gaussians != CONFIG["G"]:
+        CONFIG.update(views=args.views, G=args.gaussians,
+                      workload=f"reduced profiling case: G={args.gaussians}, {args.views} views 1264x832")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

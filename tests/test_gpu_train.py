@@ -26,7 +26,7 @@ def test_one_step_vs_oracle(pkg):
                          lambda_o=0.01, lambda_s=0.01, use_graph=False)
     st.step()
     total, losses, grads = pipeline.loss_and_grads(p, sc["cams"], sc["targets"], 3, lambda_o=0.01, lambda_s=0.01)
-    assert abs(st.mean_loss_value() - total) < 1e-5
+    assert abs(st.mean_loss_value() - total) < 1e-4 * total
     G = p["means3d"].shape[0]
     for n in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc", "color_rest"):
         assert rel_l2(model.view(st.grads, G, n).cpu().numpy(), grads[n]) < 1e-3, n

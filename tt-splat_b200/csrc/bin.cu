@@ -110,6 +110,23 @@ __global__ void k_cell_scatter(const float2* __restrict__ mu2d, const int2* __re
   rec[(long long)v * G + start[(long long)v * (T + 1) + cr.x] + cr.y] = make_float4(__int_as_float(g), m.x, m.y, 0.f);
 }
 
+// Exclusive prefix sum over the block (BS_THREADS threads); ends with a barrier.
+__device__ __forceinline__ int block_excl_scan(int x, int* s_scan) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int incl = x;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) s_scan[wid] = incl;
+  __syncthreads();
+  int base = 0;
+  for (int w = 0; w < wid; ++w) base += s_scan[w];
+  __syncthreads();
+  return base + incl - x;
+}
+
 __device__ __forceinline__ void bitonic_sort(u64* s, int P) {
   for (int size = 2; size <= P; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
@@ -150,6 +167,7 @@ __global__ void __launch_bounds__(BS_THREADS)
   __shared__ int s_beg[BS_MAXS], s_len[BS_MAXS], s_off[BS_MAXS + 1];
   __shared__ u64 s_pval, s_pmask;
   __shared__ int s_below, s_le, s_cnt;
+  __shared__ int s_scan[BS_THREADS / 32];
 
   const int t = blockIdx.x, v = blockIdx.y, T = ntx * nty;
   const int tx = t % ntx, ty = t / ntx;
@@ -192,6 +210,46 @@ __global__ void __launch_bounds__(BS_THREADS)
       for (int i = tid; i < len; i += BS_THREADS) skeys[off + i] = make_key(j, rv[beg + i], ctx, cty);
     }
     nsel = n;
+    if (n > K) {
+      // select before sorting: q* = the quantised distance of the K-th smallest key; only keys
+      // with q <= q* can be kept, so only those are sorted
+      for (int i = tid; i < 2048; i += BS_THREADS) shist[i] = 0;
+      __syncthreads();
+      for (int i = tid; i < n; i += BS_THREADS) atomicAdd(&shist[(int)(skeys[i] >> 40)], 1);
+      __syncthreads();
+      int loc = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) loc += shist[tid * 8 + b];
+      const int excl = block_excl_scan(loc, s_scan);
+      if (excl < K && K <= excl + loc) {
+        int c = excl, b = 0;
+        for (; b < 7; ++b) {
+          if (c + shist[tid * 8 + b] >= K) break;
+          c += shist[tid * 8 + b];
+        }
+        s_le = c + shist[tid * 8 + b];      // keys with q <= q*
+        s_pval = (u64)(tid * 8 + b);        // q*
+      }
+      __syncthreads();
+      const unsigned qstar = (unsigned)s_pval;
+      // compact the selected keys to the front: each thread stages its contiguous chunk
+      const int per = (n + BS_THREADS - 1) / BS_THREADS;   // <= BS_CAP / BS_THREADS = 16
+      u64 mine[BS_CAP / BS_THREADS];
+      int cnt = 0;
+#pragma unroll
+      for (int j = 0; j < BS_CAP / BS_THREADS; ++j) {
+        const int i = tid * per + j;
+        mine[j] = (j < per && i < n) ? skeys[i] : ~0ull;
+        cnt += (j < per && i < n && (unsigned)(mine[j] >> 40) <= qstar) ? 1 : 0;
+      }
+      const int off = block_excl_scan(cnt, s_scan);
+#pragma unroll
+      for (int j = 0, w = off; j < BS_CAP / BS_THREADS; ++j) {
+        if (j < per && tid * per + j < n && (unsigned)(mine[j] >> 40) <= qstar) skeys[w++] = mine[j];
+      }
+      __syncthreads();
+      nsel = s_le;
+    }
   } else {
     // MSB radix select of the K-th smallest key; stop as soon as the keys at or below the
     // current bucket fit in shared memory, then collect them.

@@ -3,21 +3,21 @@
 //
 // SSIM uses the valid separable Gaussian window (tools/loss_manual.py:28-55; pytorch_msssim
 // convention) on inputs clamped to [0,1] (spike/metrics.py:6-7).  Two tiled kernels per
-// (view, channel):
-//   k_ssim_fwd : output tile 32x16 of the SSIM map.  Loads the (32+win-1)x(16+win-1) input
-//                halo into shared memory, filters the five maps x, y, x^2, y^2, xy along the
-//                rows then the columns, and writes dS/dmu_x, dS/d(x^2 filtered),
-//                dS/d(xy filtered) plus a per-block partial of sum(S).
-//   k_ssim_bwd : input tile 32x16.  Applies the transposed filter to the three dS maps
-//                (zero outside the valid region), combines them with x and y into the SSIM
-//                gradient, adds the L1 gradient, and writes a per-block partial of sum|x-y|.
-// A final one-block-per-view kernel reduces the partials in a fixed order (deterministic).
+// (view, channel), each a separable filter with register blocking so that every shared-memory
+// load feeds several FMAs (a thread slides an RB-long window along a row, then along a column):
+//   k_ssim_fwd : output tile 64x32 of the SSIM map.  Loads the (64+win-1)x(32+win-1) input
+//                halo, filters the five maps x, y, x^2, y^2, xy along rows then columns, and
+//                writes dS/dmu_x, dS/d(filtered x^2), dS/d(filtered xy) plus a per-block
+//                partial of sum(S).
+//   k_ssim_bwd : input tile 64x32.  Applies the transposed filter to the three dS maps (zero
+//                outside the valid region), combines them with x and y into the SSIM gradient,
+//                adds the L1 gradient, and writes a per-block partial of sum|x - y|.
+// A one-block-per-view kernel reduces the partials in a fixed order (deterministic).
 #include "common.cuh"
 
 namespace tts {
 
-constexpr int LT_W = 32, LT_H = 16, LWIN_MAX = 11;
-constexpr int LI_W = LT_W + LWIN_MAX - 1, LI_H = LT_H + LWIN_MAX - 1;
+constexpr int LT_W = 64, LT_H = 32, LWIN_MAX = 11, RB = 8;
 constexpr float SSIM_C1 = 0.01f * 0.01f, SSIM_C2 = 0.03f * 0.03f;
 
 struct Window {
@@ -25,70 +25,123 @@ struct Window {
   int win;
 };
 
+// shared-memory geometry for a window WIN: input rows/cols with odd strides (bank-conflict free
+// when lanes walk down rows)
+template <int WIN>
+struct LGeom {
+  static constexpr int IH = LT_H + WIN - 1, IW = LT_W + WIN - 1;
+  static constexpr int XS = IW | 1;        // odd row stride of the input tiles
+  static constexpr int HS = LT_W + 1;      // odd row stride of the row-filtered maps
+};
+
+template <int WIN>
 __global__ void __launch_bounds__(256)
-    k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, Window wd,
+    k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
                float* __restrict__ maps, float* __restrict__ part) {
-  __shared__ float sx[LI_H][LI_W + 1], sy[LI_H][LI_W + 1];
-  __shared__ float h[5][LI_H][LT_W + 1];
+  using LG = LGeom<WIN>;
+  extern __shared__ float smem[];
+  float* sx = smem;                            // [IH][XS]
+  float* sy = sx + LG::IH * LG::XS;            // [IH][XS]
+  float* h = sy + LG::IH * LG::XS;             // [5][IH][HS]
   __shared__ float red[8];
-  const int win = wd.win;
-  const int Ho = H - win + 1, Wo = W - win + 1;
-  const int vc = blockIdx.z, v = vc / 3, ch = vc % 3;
-  const int ox0 = blockIdx.x * LT_W, oy0 = blockIdx.y * LT_H;
-  const int tid = threadIdx.y * blockDim.x + threadIdx.x;
-  const int IW = LT_W + win - 1, IH = LT_H + win - 1;
-  for (int i = tid; i < IH * IW; i += 256) {
-    const int r = i / IW, c = i % IW;
-    const int gy = oy0 + r, gx = ox0 + c;
+  const int Ho = H - WIN + 1, Wo = W - WIN + 1;
+  int b = blockIdx.x;
+  const int ch = b % 3; b /= 3;
+  const int bx = b % gx; b /= gx;
+  const int by = b % gy;
+  const int v = b / gy;
+  const int vc = v * 3 + ch;
+  const int ox0 = bx * LT_W, oy0 = by * LT_H;
+  const int tid = threadIdx.x;
+  float g[WIN];
+#pragma unroll
+  for (int k = 0; k < WIN; k++) g[k] = wd.g[k];
+  for (int i = tid; i < LG::IH * LG::IW; i += 256) {
+    const int r = i / LG::IW, c = i % LG::IW;
+    const int yy = oy0 + r, xx = ox0 + c;
     float x = 0.f, y = 0.f;
-    if (gy < H && gx < W) {
-      const long long q = (((long long)v * H + gy) * W + gx) * 3 + ch;
+    if (yy < H && xx < W) {
+      const long long q = (((long long)v * H + yy) * W + xx) * 3 + ch;
       x = fminf(fmaxf(img[q], 0.f), 1.f);
       y = fminf(fmaxf(tgt[q], 0.f), 1.f);
     }
-    sx[r][c] = x;
-    sy[r][c] = y;
+    sx[r * LG::XS + c] = x;
+    sy[r * LG::XS + c] = y;
   }
   __syncthreads();
-  for (int i = tid; i < IH * LT_W; i += 256) {
-    const int r = i / LT_W, c = i % LT_W;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
-    for (int k = 0; k < win; ++k) {
-      const float x = sx[r][c + k], y = sy[r][c + k], gk = wd.g[k];
-      a0 = fmaf(gk, x, a0);
-      a1 = fmaf(gk, y, a1);
-      a2 = fmaf(gk, x * x, a2);
-      a3 = fmaf(gk, y * y, a3);
-      a4 = fmaf(gk, x * y, a4);
+  // rows: item = (row r, segment of RB outputs); lanes walk down rows (odd stride: no conflicts)
+  for (int it = tid; it < LG::IH * (LT_W / RB); it += 256) {
+    const int r = it % LG::IH, c0 = (it / LG::IH) * RB;
+    float a[5][RB];
+#pragma unroll
+    for (int m = 0; m < 5; m++)
+#pragma unroll
+      for (int o = 0; o < RB; o++) a[m][o] = 0.f;
+#pragma unroll
+    for (int i = 0; i < RB + WIN - 1; i++) {
+      const float x = sx[r * LG::XS + c0 + i], y = sy[r * LG::XS + c0 + i];
+      const float xx = x * x, yy = y * y, xy = x * y;
+#pragma unroll
+      for (int o = 0; o < RB; o++) {
+        const int k = i - o;
+        if (k >= 0 && k < WIN) {
+          a[0][o] = fmaf(g[k], x, a[0][o]);
+          a[1][o] = fmaf(g[k], y, a[1][o]);
+          a[2][o] = fmaf(g[k], xx, a[2][o]);
+          a[3][o] = fmaf(g[k], yy, a[3][o]);
+          a[4][o] = fmaf(g[k], xy, a[4][o]);
+        }
+      }
     }
-    h[0][r][c] = a0; h[1][r][c] = a1; h[2][r][c] = a2; h[3][r][c] = a3; h[4][r][c] = a4;
+#pragma unroll
+    for (int m = 0; m < 5; m++)
+#pragma unroll
+      for (int o = 0; o < RB; o++) h[(m * LG::IH + r) * LG::HS + c0 + o] = a[m][o];
   }
   __syncthreads();
+  // columns: item = (column c, segment of RB output rows); lanes walk along columns
   float ssum = 0.f;
   const long long plane = (long long)Ho * Wo;
   float* mbase = maps + (long long)vc * 3 * plane;
-  for (int i = tid; i < LT_H * LT_W; i += 256) {
-    const int r = i / LT_W, c = i % LT_W;
-    const int oy = oy0 + r, ox = ox0 + c;
-    if (oy >= Ho || ox >= Wo) continue;
-    float f[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < win; ++k) {
-      const float gk = wd.g[k];
+  for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
+    const int c = it % LT_W, r0 = (it / LT_W) * RB;
+    float f[5][RB];
 #pragma unroll
-      for (int m = 0; m < 5; m++) f[m] = fmaf(gk, h[m][r + k][c], f[m]);
+    for (int m = 0; m < 5; m++)
+#pragma unroll
+      for (int o = 0; o < RB; o++) f[m][o] = 0.f;
+#pragma unroll
+    for (int i = 0; i < RB + WIN - 1; i++) {
+      float hv[5];
+#pragma unroll
+      for (int m = 0; m < 5; m++) hv[m] = h[(m * LG::IH + r0 + i) * LG::HS + c];
+#pragma unroll
+      for (int o = 0; o < RB; o++) {
+        const int k = i - o;
+        if (k >= 0 && k < WIN) {
+#pragma unroll
+          for (int m = 0; m < 5; m++) f[m][o] = fmaf(g[k], hv[m], f[m][o]);
+        }
+      }
     }
-    const float mux = f[0], muy = f[1];
-    const float mux2 = mux * mux, muy2 = muy * muy;
-    const float sxx = f[2] - mux2, syy = f[3] - muy2, sxy = f[4] - mux * muy;
-    const float A1 = 2.f * mux * muy + SSIM_C1, A2 = 2.f * sxy + SSIM_C2;
-    const float B1 = mux2 + muy2 + SSIM_C1, B2 = sxx + syy + SSIM_C2;
-    const float D = B1 * B2;
-    const float S = (A1 * A2) / D;
-    ssum += S;
-    const long long q = (long long)oy * Wo + ox;
-    mbase[q] = (2.f / D) * (muy * (A2 - A1) - S * mux * (B2 - B1));   // dS/dmu_x
-    mbase[plane + q] = -S / B2;                                       // dS/d filt(x^2)
-    mbase[2 * plane + q] = 2.f * A1 / D;                              // dS/d filt(xy)
+    const int ox = ox0 + c;
+#pragma unroll
+    for (int o = 0; o < RB; o++) {
+      const int oy = oy0 + r0 + o;
+      if (oy >= Ho || ox >= Wo) continue;
+      const float mux = f[0][o], muy = f[1][o];
+      const float mux2 = mux * mux, muy2 = muy * muy;
+      const float sxx = f[2][o] - mux2, syy = f[3][o] - muy2, sxy = f[4][o] - mux * muy;
+      const float A1 = 2.f * mux * muy + SSIM_C1, A2 = 2.f * sxy + SSIM_C2;
+      const float B1 = mux2 + muy2 + SSIM_C1, B2 = sxx + syy + SSIM_C2;
+      const float D = B1 * B2;
+      const float S = (A1 * A2) / D;
+      ssum += S;
+      const long long q = (long long)oy * Wo + ox;
+      mbase[q] = (2.f / D) * (muy * (A2 - A1) - S * mux * (B2 - B1));   // dS/dmu_x
+      mbase[plane + q] = -S / B2;                                       // dS/d filt(x^2)
+      mbase[2 * plane + q] = 2.f * A1 / D;                              // dS/d filt(xy)
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
@@ -97,77 +150,117 @@ __global__ void __launch_bounds__(256)
   if (tid == 0) {
     float s = 0.f;
     for (int i = 0; i < 8; ++i) s += red[i];
-    part[(long long)vc * gridDim.x * gridDim.y + blockIdx.y * gridDim.x + blockIdx.x] = s;
+    part[(long long)vc * gx * gy + by * gx + bx] = s;
   }
 }
 
+template <int WIN>
 __global__ void __launch_bounds__(256)
-    k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, Window wd, float lambda,
-               float grad_scale, const float* __restrict__ maps, float* __restrict__ gimg, float* __restrict__ part) {
-  __shared__ float sm[3][LI_H][LI_W + 1];
-  __shared__ float h[3][LI_H][LT_W + 1];
+    k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
+               float lambda, float grad_scale, const float* __restrict__ maps, float* __restrict__ gimg,
+               float* __restrict__ part) {
+  using LG = LGeom<WIN>;
+  extern __shared__ float smem[];
+  float* sm = smem;                            // [3][IH][XS]
+  float* h = sm + 3 * LG::IH * LG::XS;         // [3][IH][HS]
   __shared__ float red[8];
-  const int win = wd.win;
-  const int Ho = H - win + 1, Wo = W - win + 1;
-  const int vc = blockIdx.z, v = vc / 3, ch = vc % 3;
-  const int x0 = blockIdx.x * LT_W, y0 = blockIdx.y * LT_H;
-  const int tid = threadIdx.y * blockDim.x + threadIdx.x;
-  const int IW = LT_W + win - 1, IH = LT_H + win - 1;
+  const int Ho = H - WIN + 1, Wo = W - WIN + 1;
+  int b = blockIdx.x;
+  const int ch = b % 3; b /= 3;
+  const int bx = b % gx; b /= gx;
+  const int by = b % gy;
+  const int v = b / gy;
+  const int vc = v * 3 + ch;
+  const int x0 = bx * LT_W, y0 = by * LT_H;
+  const int tid = threadIdx.x;
+  float g[WIN];
+#pragma unroll
+  for (int k = 0; k < WIN; k++) g[k] = wd.g[k];
   const long long plane = (long long)Ho * Wo;
   const float* mbase = maps + (long long)vc * 3 * plane;
-  // map rows [y0-win+1, y0+LT_H), cols [x0-win+1, x0+LT_W); zero outside the valid region
-  for (int i = tid; i < IH * IW; i += 256) {
-    const int r = i / IW, c = i % IW;
-    const int my = y0 - (win - 1) + r, mx = x0 - (win - 1) + c;
-    float a = 0.f, b = 0.f, d = 0.f;
+  // map rows [y0-WIN+1, y0+LT_H), cols [x0-WIN+1, x0+LT_W); zero outside the valid region
+  for (int i = tid; i < LG::IH * LG::IW; i += 256) {
+    const int r = i / LG::IW, c = i % LG::IW;
+    const int my = y0 - (WIN - 1) + r, mx = x0 - (WIN - 1) + c;
+    float a = 0.f, bb = 0.f, d = 0.f;
     if (my >= 0 && my < Ho && mx >= 0 && mx < Wo) {
       const long long q = (long long)my * Wo + mx;
       a = mbase[q];
-      b = mbase[plane + q];
+      bb = mbase[plane + q];
       d = mbase[2 * plane + q];
     }
-    sm[0][r][c] = a;
-    sm[1][r][c] = b;
-    sm[2][r][c] = d;
+    sm[(0 * LG::IH + r) * LG::XS + c] = a;
+    sm[(1 * LG::IH + r) * LG::XS + c] = bb;
+    sm[(2 * LG::IH + r) * LG::XS + c] = d;
   }
   __syncthreads();
-  for (int i = tid; i < IH * LT_W; i += 256) {
-    const int r = i / LT_W, c = i % LT_W;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
-    for (int k = 0; k < win; ++k) {
-      const float gk = wd.g[k];
-      const int cc = c + (win - 1) - k;
-      a0 = fmaf(gk, sm[0][r][cc], a0);
-      a1 = fmaf(gk, sm[1][r][cc], a1);
-      a2 = fmaf(gk, sm[2][r][cc], a2);
+  // transposed row filter: t[r][c] = sum_k g[k] m[r][c + WIN-1 - k]
+  for (int it = tid; it < LG::IH * (LT_W / RB); it += 256) {
+    const int r = it % LG::IH, c0 = (it / LG::IH) * RB;
+    float a[3][RB];
+#pragma unroll
+    for (int m = 0; m < 3; m++)
+#pragma unroll
+      for (int o = 0; o < RB; o++) a[m][o] = 0.f;
+#pragma unroll
+    for (int i = 0; i < RB + WIN - 1; i++) {
+      float mv[3];
+#pragma unroll
+      for (int m = 0; m < 3; m++) mv[m] = sm[(m * LG::IH + r) * LG::XS + c0 + i];
+#pragma unroll
+      for (int o = 0; o < RB; o++) {
+        const int k = (WIN - 1) - (i - o);
+        if (k >= 0 && k < WIN) {
+#pragma unroll
+          for (int m = 0; m < 3; m++) a[m][o] = fmaf(g[k], mv[m], a[m][o]);
+        }
+      }
     }
-    h[0][r][c] = a0; h[1][r][c] = a1; h[2][r][c] = a2;
+#pragma unroll
+    for (int m = 0; m < 3; m++)
+#pragma unroll
+      for (int o = 0; o < RB; o++) h[(m * LG::IH + r) * LG::HS + c0 + o] = a[m][o];
   }
   __syncthreads();
   const float Ns = (float)(3.0 * (double)Ho * (double)Wo);
   const float N = (float)(3.0 * (double)H * (double)W);
   float l1 = 0.f;
-  for (int i = tid; i < LT_H * LT_W; i += 256) {
-    const int r = i / LT_W, c = i % LT_W;
-    const int gy = y0 + r, gx = x0 + c;
-    if (gy >= H || gx >= W) continue;
-    float t0 = 0.f, t1 = 0.f, t2 = 0.f;
-    for (int k = 0; k < win; ++k) {
-      const float gk = wd.g[k];
-      const int rr = r + (win - 1) - k;
-      t0 = fmaf(gk, h[0][rr][c], t0);
-      t1 = fmaf(gk, h[1][rr][c], t1);
-      t2 = fmaf(gk, h[2][rr][c], t2);
+  for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
+    const int c = it % LT_W, r0 = (it / LT_W) * RB;
+    float t[3][RB];
+#pragma unroll
+    for (int m = 0; m < 3; m++)
+#pragma unroll
+      for (int o = 0; o < RB; o++) t[m][o] = 0.f;
+#pragma unroll
+    for (int i = 0; i < RB + WIN - 1; i++) {
+      float hv[3];
+#pragma unroll
+      for (int m = 0; m < 3; m++) hv[m] = h[(m * LG::IH + r0 + i) * LG::HS + c];
+#pragma unroll
+      for (int o = 0; o < RB; o++) {
+        const int k = (WIN - 1) - (i - o);
+        if (k >= 0 && k < WIN) {
+#pragma unroll
+          for (int m = 0; m < 3; m++) t[m][o] = fmaf(g[k], hv[m], t[m][o]);
+        }
+      }
     }
-    const long long q = (((long long)v * H + gy) * W + gx) * 3 + ch;
-    const float xr = img[q], yr = tgt[q];
-    const float x = fminf(fmaxf(xr, 0.f), 1.f), y = fminf(fmaxf(yr, 0.f), 1.f);
-    const float mask = (xr >= 0.f && xr <= 1.f) ? 1.f : 0.f;
-    const float dmean = (t0 + 2.f * x * t1 + y * t2) / Ns;
-    const float diff = xr - yr;
-    const float sgn = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
-    l1 += fabsf(diff);
-    gimg[q] = grad_scale * ((1.f - lambda) * sgn / N + lambda * (-dmean) * mask);
+    const int xx = x0 + c;
+#pragma unroll
+    for (int o = 0; o < RB; o++) {
+      const int yy = y0 + r0 + o;
+      if (yy >= H || xx >= W) continue;
+      const long long q = (((long long)v * H + yy) * W + xx) * 3 + ch;
+      const float xr = img[q], yr = tgt[q];
+      const float x = fminf(fmaxf(xr, 0.f), 1.f), y = fminf(fmaxf(yr, 0.f), 1.f);
+      const float mask = (xr >= 0.f && xr <= 1.f) ? 1.f : 0.f;
+      const float dmean = (t[0][o] + 2.f * x * t[1][o] + y * t[2][o]) / Ns;
+      const float diff = xr - yr;
+      const float sgn = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
+      l1 += fabsf(diff);
+      gimg[q] = grad_scale * ((1.f - lambda) * sgn / N + lambda * (-dmean) * mask);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
@@ -176,7 +269,7 @@ __global__ void __launch_bounds__(256)
   if (tid == 0) {
     float s = 0.f;
     for (int i = 0; i < 8; ++i) s += red[i];
-    part[(long long)vc * gridDim.x * gridDim.y + blockIdx.y * gridDim.x + blockIdx.x] = s;
+    part[(long long)vc * gx * gy + by * gx + bx] = s;
   }
 }
 
@@ -239,6 +332,27 @@ static LossGeom loss_geom(int H, int W) {
   return lg;
 }
 
+template <int WIN>
+static int launch_loss(const float* img, const float* target, int V, int H, int W, float lambda, float grad_scale,
+                       const Window& wd, const LossGeom& lg, float* maps, float* spart, float* lpart, float* gimg,
+                       cudaStream_t st) {
+  using LG = LGeom<WIN>;
+  const size_t fsm = (size_t)(2 * LG::IH * LG::XS + 5 * LG::IH * LG::HS) * 4;
+  const size_t bsm = (size_t)(3 * LG::IH * LG::XS + 3 * LG::IH * LG::HS) * 4;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_ssim_fwd<WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
+    cudaFuncSetAttribute(k_ssim_bwd<WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
+    attr_set = true;
+  }
+  k_ssim_fwd<WIN><<<(unsigned)(V * 3 * lg.fbx * lg.fby), 256, fsm, st>>>(img, target, H, W, lg.fbx, lg.fby, wd, maps,
+                                                                        spart);
+  if (int rc = check_launch("ssim_fwd")) return rc;
+  k_ssim_bwd<WIN><<<(unsigned)(V * 3 * lg.bbx * lg.bby), 256, bsm, st>>>(img, target, H, W, lg.bbx, lg.bby, wd, lambda,
+                                                                        grad_scale, maps, gimg, lpart);
+  return check_launch("ssim_bwd");
+}
+
 }  // namespace tts
 
 using namespace tts;
@@ -266,11 +380,15 @@ extern "C" int tts_loss_l1_ssim(const float* img, const float* target, int V, in
   p += a256((size_t)V * 3 * lg.fbx * lg.fby * 4);
   float* lpart = reinterpret_cast<float*>(p);
   cudaStream_t st = as_stream(stream);
-  k_ssim_fwd<<<dim3(lg.fbx, lg.fby, V * 3), dim3(32, 8), 0, st>>>(img, target, H, W, wd, maps, spart);
-  if (int rc = check_launch("ssim_fwd")) return rc;
-  k_ssim_bwd<<<dim3(lg.bbx, lg.bby, V * 3), dim3(32, 8), 0, st>>>(img, target, H, W, wd, lambda, grad_scale, maps,
-                                                                   gimg, lpart);
-  if (int rc = check_launch("ssim_bwd")) return rc;
+  int rc;
+  switch (wd.win) {
+    case 3: rc = launch_loss<3>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
+    case 5: rc = launch_loss<5>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
+    case 7: rc = launch_loss<7>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
+    case 9: rc = launch_loss<9>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
+    default: rc = launch_loss<11>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
+  }
+  if (rc) return rc;
   k_loss_reduce<<<V, 256, 0, st>>>(spart, lg.fbx * lg.fby, lpart, lg.bbx * lg.bby, H, W, lg.win, lambda, loss);
   return check_launch("loss_reduce");
 }

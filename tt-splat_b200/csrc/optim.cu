@@ -63,13 +63,17 @@ __device__ __forceinline__ void sgld_one(float* __restrict__ params, const Param
   }
 }
 
+// Element-parallel Adam over [0, n) of the flat buffer: each thread updates four consecutive
+// elements (one 16-byte vector of p, g, m, v when aligned); the group learning rate of an
+// element follows from its index (segment boundaries at 3G, 6G, 10G, 11G, 14G).
+__device__ __forceinline__ float lr_of(long long i, long long G, const float nss[6]) {
+  return i < 3 * G ? nss[0] : i < 6 * G ? nss[1] : i < 10 * G ? nss[2] : i < 11 * G ? nss[3] : i < 14 * G ? nss[4] : nss[5];
+}
+
 __global__ void __launch_bounds__(256)
-    k_adam_sgld(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ m,
-                float* __restrict__ v, int G, int sh_degree, const int* __restrict__ step_ptr,
-                const double* __restrict__ lr7, double beta1, double beta2, double eps, float noise_lr,
-                const float* __restrict__ eps_noise, unsigned long long seed) {
-  const int g = blockIdx.x * blockDim.x + threadIdx.x;
-  const ParamLayout L{G};
+    k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ m,
+           float* __restrict__ v, int G, long long n, const int* __restrict__ step_ptr,
+           const double* __restrict__ lr7, double beta1, double beta2, double eps) {
   const int step = *step_ptr;
   // scalars in double like the Python-side arithmetic of torch's Adam, cast to fp32 at use
   const double bc1 = 1.0 - pow(beta1, (double)step);
@@ -80,33 +84,48 @@ __global__ void __launch_bounds__(256)
   a.w2 = (float)(1.0 - beta2);
   a.bc2_sqrt = (float)sqrt(bc2);
   a.eps = (float)eps;
-  if (g == 0) adam_elem(params, grads, m, v, L.w_b_raw(), a, (float)(-lr7[6] / bc1));
-  if (g >= G) return;
-  const float nss[6] = {(float)(-lr7[0] / bc1), (float)(-lr7[1] / bc1), (float)(-lr7[2] / bc1),
-                        (float)(-lr7[3] / bc1), (float)(-lr7[4] / bc1), (float)(-lr7[5] / bc1)};
+  float nss[6];
 #pragma unroll
-  for (int c = 0; c < 3; c++) adam_elem(params, grads, m, v, L.means() + 3LL * g + c, a, nss[0]);
+  for (int k = 0; k < 6; k++) nss[k] = (float)(-lr7[k] / bc1);
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (tid == 0) adam_elem(params, grads, m, v, 59LL * G, a, (float)(-lr7[6] / bc1));   // w_b_raw
+  const long long e0 = tid * 4;
+  if (e0 >= n) return;
+  if (e0 + 4 <= n) {
+    float4 p4 = *reinterpret_cast<const float4*>(params + e0);
+    const float4 g4 = *reinterpret_cast<const float4*>(grads + e0);
+    float4 m4 = *reinterpret_cast<const float4*>(m + e0);
+    float4 v4 = *reinterpret_cast<const float4*>(v + e0);
+    float* pp = &p4.x;
+    const float* gg = &g4.x;
+    float* mm = &m4.x;
+    float* vv = &v4.x;
 #pragma unroll
-  for (int c = 0; c < 3; c++) adam_elem(params, grads, m, v, L.log_scales() + 3LL * g + c, a, nss[1]);
-#pragma unroll
-  for (int c = 0; c < 4; c++) adam_elem(params, grads, m, v, L.quats() + 4LL * g + c, a, nss[2]);
-  adam_elem(params, grads, m, v, L.opacity() + (long long)g, a, nss[3]);
-#pragma unroll
-  for (int c = 0; c < 3; c++) adam_elem(params, grads, m, v, L.color_dc() + 3LL * g + c, a, nss[4]);
-  if (sh_degree > 0) {
-    // torch skips parameters without a gradient: colour rest only trains when SH is on
-    for (int c = 0; c < 45; c++) adam_elem(params, grads, m, v, L.color_rest() + 45LL * g + c, a, nss[5]);
+    for (int j = 0; j < 4; j++) {
+      const float gr = gg[j];
+      float mj = __fadd_rn(mm[j], __fmul_rn(a.w1, __fsub_rn(gr, mm[j])));
+      float vj = __fadd_rn(__fmul_rn(vv[j], a.b2), __fmul_rn(__fmul_rn(a.w2, gr), gr));
+      const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vj), a.bc2_sqrt), a.eps);
+      pp[j] = __fadd_rn(pp[j], __fdiv_rn(__fmul_rn(lr_of(e0 + j, G, nss), mj), denom));
+      mm[j] = mj;
+      vv[j] = vj;
+    }
+    *reinterpret_cast<float4*>(params + e0) = p4;
+    *reinterpret_cast<float4*>(m + e0) = m4;
+    *reinterpret_cast<float4*>(v + e0) = v4;
+  } else {
+    for (long long e = e0; e < n; ++e) adam_elem(params, grads, m, v, e, a, lr_of(e, G, nss));
   }
-  if (noise_lr <= 0.f) return;
-  sgld_one(params, L, g, lr7[0], noise_lr, eps_noise, step, seed);
 }
 
-__global__ void __launch_bounds__(256) k_sgld(float* __restrict__ params, int G, double lr_means, float noise_lr,
-                                              const float* __restrict__ eps_noise, const int* __restrict__ step_ptr,
-                                              unsigned long long seed) {
+// SGLD for every gaussian; the means learning rate is read from the device (lr_ptr[0], the
+// optimizer's lr vector) or, when lr_ptr is null, given by value.
+__global__ void __launch_bounds__(256) k_sgld(float* __restrict__ params, int G, const double* __restrict__ lr_ptr,
+                                              double lr_means, float noise_lr, const float* __restrict__ eps_noise,
+                                              const int* __restrict__ step_ptr, unsigned long long seed) {
   const int g = blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= G) return;
-  sgld_one(params, ParamLayout{G}, g, lr_means, noise_lr, eps_noise, *step_ptr, seed);
+  sgld_one(params, ParamLayout{G}, g, lr_ptr ? lr_ptr[0] : lr_means, noise_lr, eps_noise, *step_ptr, seed);
 }
 
 __global__ void k_step_begin(int* step) { *step += 1; }
@@ -126,16 +145,24 @@ extern "C" int tts_adam_sgld(float* params, const float* grads, float* m, float*
                              const float* eps_noise, uint64_t seed, void* stream) {
   TTS_REQUIRE(G >= 0 && params && grads && m && v && step && lr7, "null pointer or negative G");
   TTS_REQUIRE(beta1 >= 0.0 && beta1 < 1.0 && beta2 >= 0.0 && beta2 < 1.0, "betas must be in [0, 1)");
-  const int blocks = G > 0 ? (G + 255) / 256 : 1;
-  k_adam_sgld<<<blocks, 256, 0, as_stream(stream)>>>(params, grads, m, v, G, sh_degree, step, lr7, beta1, beta2, eps,
-                                                      noise_lr, eps_noise, seed);
-  return check_launch("adam_sgld");
+  TTS_REQUIRE(aligned16(params) && aligned16(grads) && aligned16(m) && aligned16(v), "buffers must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  // torch skips parameters without a gradient: the colour rest trains only with SH on
+  const long long n = sh_degree > 0 ? 59LL * G : 14LL * G;
+  const long long blocks = (n + 4 * 256 - 1) / (4 * 256);
+  k_adam<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, st>>>(params, grads, m, v, G, n, step, lr7, beta1, beta2, eps);
+  if (int rc = check_launch("adam")) return rc;
+  if (noise_lr > 0.f && G > 0) {
+    k_sgld<<<(G + 255) / 256, 256, 0, st>>>(params, G, lr7, 0.0, noise_lr, eps_noise, step, seed);
+    return check_launch("sgld");
+  }
+  return TTS_OK;
 }
 
 extern "C" int tts_sgld(float* params, int G, double lr_means, float noise_lr, const float* eps_noise,
                         const int32_t* step, uint64_t seed, void* stream) {
   TTS_REQUIRE(G >= 0 && params && step, "null pointer or negative G");
   if (G == 0) return TTS_OK;
-  k_sgld<<<(G + 255) / 256, 256, 0, as_stream(stream)>>>(params, G, lr_means, noise_lr, eps_noise, step, seed);
+  k_sgld<<<(G + 255) / 256, 256, 0, as_stream(stream)>>>(params, G, nullptr, lr_means, noise_lr, eps_noise, step, seed);
   return check_launch("sgld");
 }

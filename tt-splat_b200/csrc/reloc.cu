@@ -70,21 +70,40 @@ __global__ void __launch_bounds__(256) k_rl_hist(const float* __restrict__ param
   }
 }
 
-__global__ void k_rl_pick(RelocState* st, int* hist, int shift, int bits) {
+// Pick the bucket holding the needed rank for both selections: 256 threads scan 8 bins each.
+__global__ void __launch_bounds__(256) k_rl_pick(RelocState* st, int* hist, int shift, int bits) {
+  __shared__ int s_scan[8];
   const int nb = 1 << bits;
-  if (threadIdx.x < 2) {
-    const int w = threadIdx.x;
-    int c = 0, b = 0;
-    for (; b < nb - 1; ++b) {
-      if (c + hist[w * nb + b] >= st->need[w]) break;
-      c += hist[w * nb + b];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int per = nb / 256;      // 8 or 4 bins per thread
+  for (int w = 0; w < 2; ++w) {
+    const int need = st->need[w];   // read by every thread before the barrier below
+    int loc = 0;
+    for (int b = 0; b < per; ++b) loc += hist[w * nb + tid * per + b];
+    int incl = loc;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
     }
-    st->need[w] -= c;
-    st->pval[w] |= (unsigned)b << shift;
-    st->pmask[w] |= (unsigned)(nb - 1) << shift;
+    if (lane == 31) s_scan[wid] = incl;
+    __syncthreads();
+    int base = 0;
+    for (int i = 0; i < wid; ++i) base += s_scan[i];
+    const int excl = base + incl - loc;
+    if (excl < need && need <= excl + loc) {
+      int c = excl, b = 0;
+      for (; b < per - 1; ++b) {
+        if (c + hist[w * nb + tid * per + b] >= need) break;
+        c += hist[w * nb + tid * per + b];
+      }
+      st->need[w] = need - c;
+      st->pval[w] |= (unsigned)(tid * per + b) << shift;
+      st->pmask[w] |= (unsigned)(nb - 1) << shift;
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 2 * 2048; i += blockDim.x) hist[i] = 0;
+  for (int i = tid; i < 2 * 2048; i += blockDim.x) hist[i] = 0;
 }
 
 __global__ void k_rl_thr(RelocState* st) {
