@@ -163,7 +163,7 @@ def stage_times(st, torch, reps=3):
                        st.lo["gimg"], out=st.rb)
         ev[5].record()
         ops.backward_params(st.flat, G, st.sh_degree, st.cams_t, H, W, R, K, st.bp["inv"], st.rb["slot_grads"],
-                            st.rb["gwb"], st.k, st.blur, st.near, st.lambda_o, st.lambda_s, out=st.grads)
+                            st.rb["gwb"], st.k, st.blur, st.near, st.lambda_o, st.lambda_s, out=st.grads, ws=st.ws_bwd)
         ev[6].record()
         ops.adam_sgld(st.flat, st.grads, st.m, st.v, G, st.sh_degree, st.step_t, st.lr7, noise_lr=st.noise_lr,
                       seed=st.seed)

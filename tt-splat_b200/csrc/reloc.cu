@@ -150,23 +150,61 @@ __global__ void __launch_bounds__(RL_BLOCK) k_rl_count(const float* __restrict__
   }
 }
 
-__global__ void k_rl_scan(int nblk, int G, int* bcnt, double* bsum, RelocState* st, int* n_dead_out) {
-  if (threadIdx.x != 0) return;
+// Exclusive scan of the per-block dead counts and alive sums (one block; blocks of the
+// opacity array are split into contiguous runs per thread, so the order of the sums is fixed).
+__global__ void __launch_bounds__(1024) k_rl_scan(int nblk, int G, int* bcnt, double* bsum, RelocState* st,
+                                                  int* n_dead_out) {
+  __shared__ int sc[32];
+  __shared__ double ss[32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int per = (nblk + 1023) / 1024;
+  const int beg = min(nblk, tid * per), end = min(nblk, beg + per);
   int c = 0;
   double s = 0.0;
-  for (int b = 0; b < nblk; ++b) {
-    const int cb = bcnt[b];
-    const double sb = bsum[b];
-    bcnt[b] = c;
-    bsum[b] = s;
-    c += cb;
-    s += sb;
+  for (int b = beg; b < end; ++b) {
+    c += bcnt[b];
+    s += bsum[b];
   }
-  const int n_alive = G - c;
-  st->n_dead = (c == 0 || n_alive == 0) ? 0 : c;   // the reference moves nothing then
-  st->n_alive = n_alive;
-  st->total = s;
-  *n_dead_out = st->n_dead;
+  int ci = c;
+  double si = s;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int yc = __shfl_up_sync(0xffffffffu, ci, d);
+    const double ys = __shfl_up_sync(0xffffffffu, si, d);
+    if (lane >= d) {
+      ci += yc;
+      si += ys;
+    }
+  }
+  if (lane == 31) {
+    sc[wid] = ci;
+    ss[wid] = si;
+  }
+  __syncthreads();
+  int cb = 0;
+  double sb = 0.0;
+  for (int w = 0; w < wid; ++w) {
+    cb += sc[w];
+    sb += ss[w];
+  }
+  int runc = cb + ci - c;
+  double runs = sb + si - s;
+  for (int b = beg; b < end; ++b) {
+    const int x = bcnt[b];
+    const double y = bsum[b];
+    bcnt[b] = runc;
+    bsum[b] = runs;
+    runc += x;
+    runs += y;
+  }
+  if (tid == 1023) {
+    const int n_dead = runc;
+    const int n_alive = G - n_dead;
+    st->n_dead = (n_dead == 0 || n_alive == 0) ? 0 : n_dead;   // the reference moves nothing then
+    st->n_alive = n_alive;
+    st->total = runs;
+    *n_dead_out = st->n_dead;
+  }
 }
 
 __global__ void __launch_bounds__(RL_BLOCK) k_rl_lists(const float* __restrict__ params, int G,
@@ -265,36 +303,48 @@ __device__ __forceinline__ void zero_moments(float* m, float* v, const ParamLayo
   for (int c = 0; c < 45; c++) { m[L.color_rest() + 45 * g + c] = 0.f; v[L.color_rest() + 45 * g + c] = 0.f; }
 }
 
-__global__ void k_rl_apply_dead(float* __restrict__ params, float* __restrict__ m, float* __restrict__ v, int G,
-                                const RelocState* __restrict__ st, const int* __restrict__ dead_list,
-                                const int* __restrict__ targets, const int* __restrict__ nat, float offset,
-                                const float* __restrict__ noise_in, const int* __restrict__ step_ptr,
-                                unsigned long long seed) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+// One warp per dead slot: lanes copy the 59 parameters of the target and zero the moments.
+__global__ void __launch_bounds__(256)
+    k_rl_apply_dead(float* __restrict__ params, float* __restrict__ m, float* __restrict__ v, int G,
+                    const RelocState* __restrict__ st, const int* __restrict__ dead_list,
+                    const int* __restrict__ targets, const int* __restrict__ nat, float offset,
+                    const float* __restrict__ noise_in, const int* __restrict__ step_ptr, unsigned long long seed) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (i >= st->n_dead) return;
   const ParamLayout L{G};
   const int d = dead_list[i], t = targets[i];
-  float e[3];
-  if (noise_in) {
-#pragma unroll
-    for (int c = 0; c < 3; c++) e[c] = noise_in[3 * i + c];
-  } else {
-    const U4 r = philox4x32_10(U4{(uint32_t)i, 2u, (uint32_t)*step_ptr, 0x4f46u}, (uint32_t)seed, (uint32_t)(seed >> 32));
-    float n3;
-    box_muller(r.x, r.y, e[0], e[1]);
-    box_muller(r.z, r.w, e[2], n3);
+  // field f of the 59 per-gaussian parameters -> flat index for gaussian x
+  auto at = [&](int f, int x) -> long long {
+    return f < 3 ? L.means() + 3LL * x + f
+         : f < 6 ? L.log_scales() + 3LL * x + (f - 3)
+         : f < 10 ? L.quats() + 4LL * x + (f - 6)
+         : f < 11 ? L.opacity() + (long long)x
+         : f < 14 ? L.color_dc() + 3LL * x + (f - 11)
+         : L.color_rest() + 45LL * x + (f - 14);
+  };
+  float e[3] = {0.f, 0.f, 0.f};
+  if (lane < 3) {
+    if (noise_in) {
+      e[0] = noise_in[3 * i + lane];
+    } else {
+      const U4 r = philox4x32_10(U4{(uint32_t)i, 2u, (uint32_t)*step_ptr, 0x4f46u}, (uint32_t)seed, (uint32_t)(seed >> 32));
+      float n3;
+      box_muller(r.x, r.y, e[0], e[1]);
+      box_muller(r.z, r.w, e[2], n3);
+      e[0] = e[lane];
+    }
   }
-#pragma unroll
-  for (int c = 0; c < 3; c++) {
-    params[L.means() + 3 * d + c] = params[L.means() + 3 * t + c] + offset * e[c];
-    params[L.log_scales() + 3 * d + c] = params[L.log_scales() + 3 * t + c];
-    params[L.color_dc() + 3 * d + c] = params[L.color_dc() + 3 * t + c];
+  for (int f = lane; f < 59; f += 32) {
+    const long long src = at(f, t), dst = at(f, d);
+    float val;
+    if (f < 3) val = params[src] + offset * e[0];
+    else if (f == 10) val = split_logit(opacity_of(params, L, t), nat[t] + 1);
+    else val = params[src];
+    params[dst] = val;
+    m[dst] = 0.f;
+    v[dst] = 0.f;
   }
-#pragma unroll
-  for (int c = 0; c < 4; c++) params[L.quats() + 4 * d + c] = params[L.quats() + 4 * t + c];
-  for (int c = 0; c < 45; c++) params[L.color_rest() + 45 * d + c] = params[L.color_rest() + 45 * t + c];
-  params[L.opacity() + d] = split_logit(opacity_of(params, L, t), nat[t] + 1);
-  zero_moments(m, v, L, d);
 }
 
 __global__ void k_rl_apply_targets(float* __restrict__ params, float* __restrict__ m, float* __restrict__ v, int G,
@@ -378,10 +428,10 @@ extern "C" int tts_relocate(float* params, float* m, float* v, int G, float dead
     k_rl_thr<<<1, 1, 0, st>>>(w.st);
   }
   k_rl_count<<<nblk, RL_BLOCK, 0, st>>>(params, G, w.st, w.bcnt, w.bsum);
-  k_rl_scan<<<1, 32, 0, st>>>(nblk, G, w.bcnt, w.bsum, w.st, n_dead_out);
+  k_rl_scan<<<1, 1024, 0, st>>>(nblk, G, w.bcnt, w.bsum, w.st, n_dead_out);
   k_rl_lists<<<nblk, RL_BLOCK, 0, st>>>(params, G, w.st, w.bcnt, w.bsum, w.dead_list, w.cdf);
   k_rl_sample<<<(G + 255) / 256, 256, 0, st>>>(w.st, w.cdf, G, targets_in, step, seed, targets_out, w.nat);
-  k_rl_apply_dead<<<(G + 255) / 256, 256, 0, st>>>(params, m, v, G, w.st, w.dead_list, targets_out, w.nat, offset,
+  k_rl_apply_dead<<<(unsigned)(((long long)G * 32 + 255) / 256), 256, 0, st>>>(params, m, v, G, w.st, w.dead_list, targets_out, w.nat, offset,
                                                     offset_noise_in, step, seed);
   k_rl_apply_targets<<<(G + 255) / 256, 256, 0, st>>>(params, m, v, G, w.nat);
   return check_launch("relocate");

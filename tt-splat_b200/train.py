@@ -73,6 +73,8 @@ class TrainStep:
         self.step_t = torch.zeros(1, dtype=torch.int32, device=dev)
         self.reloc = dict(n_dead=torch.zeros(1, dtype=torch.int32, device=dev), targets=e(G, dt=torch.int32))
         self.ws_bin, self.ws_loss, self.ws_reloc = ops.Workspace(dev), ops.Workspace(dev), ops.Workspace(dev)
+        self.ws_bwd = ops.Workspace(dev)
+        self.ws_bwd.get(ops.lib().tts_backward_workspace_bytes(G, V))
         self.ws_bin.get(ops.lib().tts_bin_workspace_bytes(G, V, H, W))
         self.ws_loss.get(ops.lib().tts_loss_workspace_bytes(V, H, W))
         self.ws_reloc.get(ops.lib().tts_relocate_workspace_bytes(G) if G >= 2 else 0)
@@ -94,7 +96,7 @@ class TrainStep:
                        self.lo["gimg"], out=self.rb)
         ops.backward_params(self.flat, G, self.sh_degree, self.cams_t, H, W, R, K, self.bp["inv"],
                             self.rb["slot_grads"], self.rb["gwb"], self.k, self.blur, self.near, self.lambda_o,
-                            self.lambda_s, out=self.grads)
+                            self.lambda_s, out=self.grads, ws=self.ws_bwd)
         torch.sum(self.lo["loss"], dim=0, keepdim=True, out=self.loss_mean)
 
     def _update(self, relocate):
@@ -147,7 +149,7 @@ class TrainStep:
 
     def launches(self, relocate):
         """Kernels of this library launched by one step (memsets and torch ops excluded)."""
-        n = 12 + 1                                        # forward/backward chain + Adam/SGLD
+        n = 13 + 1 + (1 if self.noise_lr > 0 else 0)      # forward/backward chain + Adam (+ SGLD)
         if relocate:
             n += 7 + (7 if self.dead_frac > 0 else 0)     # relocation (+ quantile select)
         return n
