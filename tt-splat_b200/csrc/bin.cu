@@ -156,12 +156,205 @@ __device__ __forceinline__ u64 make_key(int j, float4 r, float ctx, float cty) {
   return ((u64)q << 40) | ((u64)(unsigned)j << 32) | (u64)(unsigned)__float_as_int(r.x);
 }
 
+// Writes the outputs of one tile from its sorted keys (threads first, first+step, ... of the
+// caller's group): idx/count/cand, the stencil-indexed inverse table and, with PACK, the slot
+// rows theta_u (tools/m4_train_binned.py:130-143, the reference's fp32 op order) | color_o | keo.
+template <bool PACK>
+__device__ __forceinline__ void emit_tile(const u64* keys, int n, int v, int t, int ntx, int T, int G, int S, int K,
+                                          const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
+                                          int* __restrict__ inv, float* __restrict__ slots, int first, int step) {
+  const int cnt = min(n, K);
+  const int tx = t % ntx, ty = t / ntx;
+  const float ox = (float)(tx * 16), oy = (float)(ty * 16);
+  for (int k = first; k < K; k += step) {
+    const long long o = ((long long)v * T + t) * K + k;
+    if (k < cnt) {
+      const u64 key = keys[k];
+      const int g = (int)(unsigned)(key & 0xffffffffull);
+      const int j = (int)((key >> 32) & 0xffull);
+      idx[o] = g;
+      if (inv) inv[((long long)v * G + g) * S + j] = t * K + k;
+      if (PACK) {
+        const float4* p = reinterpret_cast<const float4*>(proj + ((long long)v * G + g) * TTS_PROJ_FLOATS);
+        const float4 p0 = p[0], p1 = p[1], p2 = p[2];
+        const float mux = __fsub_rn(p0.x, ox), muy = __fsub_rn(p0.y, oy);
+        const float a = p0.z, b = p0.w, c = p1.x;
+        const float Q = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(a, mux), mux),
+                                            __fmul_rn(__fmul_rn(__fmul_rn(2.0f, b), mux), muy)),
+                                  __fmul_rn(__fmul_rn(c, muy), muy));
+        float4* dst = reinterpret_cast<float4*>(slots + o * TTS_SLOT_FLOATS);
+        dst[0] = make_float4(__fmul_rn(-a, inv_k), __fmul_rn(-c, inv_k), __fmul_rn(__fmul_rn(-2.0f, b), inv_k),
+                             __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(a, mux), __fmul_rn(b, muy))), inv_k));
+        dst[1] = make_float4(__fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(b, mux), __fmul_rn(c, muy))), inv_k),
+                             __fsub_rn(1.0f, __fmul_rn(Q, inv_k)), p1.y, p1.z);
+        dst[2] = make_float4(p1.w, p2.x, 0.f, 0.f);
+      }
+    } else {
+      idx[o] = -1;
+    }
+  }
+}
+
+// Cell ranges of the tile's stencil: entry j = (dy+R)*D + (dx+R) holds the home cell of the
+// gaussians that see this tile at offset (dy, dx), i.e. cell = tile - (dy, dx).
+__device__ __forceinline__ void stencil_range(int j, int R, int tx, int ty, int ntx, int nty, const int* cs, int& beg,
+                                              int& len) {
+  const int D = 2 * R + 1;
+  const int dy = j / D - R, dx = j % D - R;
+  const int cy = ty - dy, cx = tx - dx;
+  beg = 0;
+  len = 0;
+  if (cy >= 0 && cy < nty && cx >= 0 && cx < ntx) {
+    const int c = cy * ntx + cx;
+    beg = cs[c];
+    len = cs[c + 1] - beg;
+  }
+}
+
+constexpr int WB_WARPS = 4;
+constexpr int WCAP = 1024;
+
+// One warp per tile for tiles with at most WCAP candidates (tiles with more are appended to the
+// overflow list for the block kernel).  Keys in per-warp shared memory; when n > K a two-level
+// histogram of q (64 then 32 bins) finds q*, the keys with q <= q* are compacted in place and
+// only those are sorted (warp-synchronous bitonic sort, no block barriers).
+template <bool PACK>
+__global__ void __launch_bounds__(WB_WARPS * 32)
+    k_bin_warp(const int* __restrict__ cell_start, const float4* __restrict__ rec, int G, int ntx, int nty, int R,
+               int K, int V, const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
+               int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv, float* __restrict__ slots,
+               int* __restrict__ ovf_list, int* __restrict__ ovf_count) {
+  extern __shared__ u64 wsm[];
+  __shared__ int whist[WB_WARPS][64];
+  __shared__ int wbeg[WB_WARPS][BS_MAXS], wlen[WB_WARPS][BS_MAXS], woff[WB_WARPS][BS_MAXS + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = ntx * nty;
+  const long long gt = (long long)blockIdx.x * WB_WARPS + warp;
+  if (gt >= (long long)V * T) return;
+  const int v = (int)(gt / T), t = (int)(gt % T);
+  const int tx = t % ntx, ty = t / ntx;
+  const int D = 2 * R + 1, S = D * D;
+  u64* buf = wsm + (size_t)warp * WCAP;
+  int* hist = whist[warp];
+  const int* cs = cell_start + (long long)v * (T + 1);
+  const float4* rv = rec + (long long)v * G;
+  for (int j = lane; j < S; j += 32) {
+    int b, l;
+    stencil_range(j, R, tx, ty, ntx, nty, cs, b, l);
+    wbeg[warp][j] = b;
+    wlen[warp][j] = l;
+  }
+  __syncwarp();
+  if (lane == 0) {
+    int o = 0;
+    for (int j = 0; j < S; ++j) {
+      woff[warp][j] = o;
+      o += wlen[warp][j];
+    }
+    woff[warp][S] = o;
+  }
+  __syncwarp();
+  const int n = woff[warp][S];
+  if (n > WCAP) {
+    if (lane == 0) ovf_list[atomicAdd(ovf_count, 1)] = (int)gt;
+    return;
+  }
+  const float ctx = __fmul_rn(__fadd_rn((float)tx, 0.5f), 16.0f);
+  const float cty = __fmul_rn(__fadd_rn((float)ty, 0.5f), 16.0f);
+  for (int j = 0; j < S; ++j) {
+    const int l = wlen[warp][j], b = wbeg[warp][j], off = woff[warp][j];
+    for (int i = lane; i < l; i += 32) buf[off + i] = make_key(j, rv[b + i], ctx, cty);
+  }
+  __syncwarp();
+  int m = n;
+  if (n > K) {
+    // level 1: the top 6 of the 11 bits of q
+    hist[lane] = 0;
+    hist[lane + 32] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) atomicAdd(&hist[(int)((buf[i] >> 45) & 63ull)], 1);
+    __syncwarp();
+    const int h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
+    int incl = h0 + h1;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
+    }
+    const int excl = incl - h0 - h1;
+    const bool hit1 = excl < K && K <= incl;
+    const int src1 = __ffs(__ballot_sync(0xffffffffu, hit1)) - 1;
+    const int b1_l = (excl + h0 >= K) ? 2 * lane : 2 * lane + 1;
+    const int below_l = (excl + h0 >= K) ? excl : excl + h0;
+    const int b1 = __shfl_sync(0xffffffffu, b1_l, src1);
+    const int below1 = __shfl_sync(0xffffffffu, below_l, src1);
+    __syncwarp();
+    // level 2: the low 5 bits of q among keys in bucket b1
+    hist[lane] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const unsigned q = (unsigned)(buf[i] >> 40);
+      if ((int)(q >> 5) == b1) atomicAdd(&hist[q & 31u], 1);
+    }
+    __syncwarp();
+    const int hv = hist[lane];
+    int incl2 = hv;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl2, d);
+      if (lane >= d) incl2 += y;
+    }
+    const int need = K - below1;
+    const bool hit2 = (incl2 - hv) < need && need <= incl2;
+    const int src2 = __ffs(__ballot_sync(0xffffffffu, hit2)) - 1;
+    const unsigned qstar = (unsigned)(b1 * 32 + src2);
+    m = below1 + __shfl_sync(0xffffffffu, incl2, src2);
+    // compact the keys with q <= q* to the front (writes never pass the chunk being read)
+    int w = 0;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int base = 0; base < n; base += 32) {
+      const int i = base + lane;
+      const u64 key = i < n ? buf[i] : ~0ull;
+      const bool sel = i < n && (unsigned)(key >> 40) <= qstar;
+      const unsigned bal = __ballot_sync(0xffffffffu, sel);
+      __syncwarp();
+      if (sel) buf[w + __popc(bal & lt)] = key;
+      w += __popc(bal);
+      __syncwarp();
+    }
+  }
+  int P = 1;
+  while (P < m) P <<= 1;
+  for (int i = m + lane; i < P; i += 32) buf[i] = ~0ull;
+  __syncwarp();
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = lane; i < (P >> 1); i += 32) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool asc = (lo & size) == 0;
+        const u64 a = buf[lo], b = buf[hi];
+        if ((a > b) == asc) {
+          buf[lo] = b;
+          buf[hi] = a;
+        }
+      }
+      __syncwarp();
+    }
+  }
+  emit_tile<PACK>(buf, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
+  if (lane == 0) {
+    count[(long long)v * T + t] = min(n, K);
+    cand[(long long)v * T + t] = n;
+  }
+}
+
 template <bool PACK>
 __global__ void __launch_bounds__(BS_THREADS)
     k_bin_select(const int* __restrict__ cell_start, const float4* __restrict__ rec, int G, int ntx, int nty,
                  int R, int K, const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
                  int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv,
-                 float* __restrict__ slots) {
+                 float* __restrict__ slots, const int* __restrict__ list, const int* __restrict__ list_count) {
   __shared__ u64 skeys[BS_CAP];
   __shared__ int shist[2048];
   __shared__ int s_beg[BS_MAXS], s_len[BS_MAXS], s_off[BS_MAXS + 1];
@@ -169,23 +362,21 @@ __global__ void __launch_bounds__(BS_THREADS)
   __shared__ int s_below, s_le, s_cnt;
   __shared__ int s_scan[BS_THREADS / 32];
 
-  const int t = blockIdx.x, v = blockIdx.y, T = ntx * nty;
-  const int tx = t % ntx, ty = t / ntx;
+  const int T = ntx * nty;
   const int D = 2 * R + 1, S = D * D;
   const int tid = threadIdx.x;
+  const int n_list = *list_count;
+  for (int li = blockIdx.x; li < n_list; li += gridDim.x) {
+  const int gt = list[li];
+  const int v = gt / T, t = gt % T;
+  const int tx = t % ntx, ty = t / ntx;
   const int* cs = cell_start + (long long)v * (T + 1);
   const float4* rv = rec + (long long)v * G;
+  __syncthreads();   // the previous tile's shared state is no longer read
 
   if (tid < S) {
-    // stencil offset j = (dy+R)*D + (dx+R) as seen from the gaussian: tile = home cell + (dy, dx)
-    const int dy = tid / D - R, dx = tid % D - R;
-    const int cy = ty - dy, cx = tx - dx;
-    int beg = 0, len = 0;
-    if (cy >= 0 && cy < nty && cx >= 0 && cx < ntx) {
-      const int c = cy * ntx + cx;
-      beg = cs[c];
-      len = cs[c + 1] - beg;
-    }
+    int beg, len;
+    stencil_range(tid, R, tx, ty, ntx, nty, cs, beg, len);
     s_beg[tid] = beg;
     s_len[tid] = len;
   }
@@ -310,39 +501,11 @@ __global__ void __launch_bounds__(BS_THREADS)
   __syncthreads();
   bitonic_sort(skeys, P);
 
-  const int cnt = min(n, K);
-  const float ox = (float)(tx * 16), oy = (float)(ty * 16);
-  for (int k = tid; k < K; k += BS_THREADS) {
-    const long long o = ((long long)v * T + t) * K + k;
-    if (k < cnt) {
-      const u64 key = skeys[k];
-      const int g = (int)(unsigned)(key & 0xffffffffull);
-      const int j = (int)((key >> 32) & 0xffull);
-      idx[o] = g;
-      if (inv) inv[((long long)v * G + g) * S + j] = t * K + k;
-      if (PACK) {
-        // theta_u_gathered (tools/m4_train_binned.py:130-143) in the reference's fp32 op order
-        const float4* p = reinterpret_cast<const float4*>(proj + ((long long)v * G + g) * TTS_PROJ_FLOATS);
-        const float4 p0 = p[0], p1 = p[1], p2 = p[2];
-        const float mux = __fsub_rn(p0.x, ox), muy = __fsub_rn(p0.y, oy);
-        const float a = p0.z, b = p0.w, c = p1.x;
-        const float Q = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(a, mux), mux),
-                                            __fmul_rn(__fmul_rn(__fmul_rn(2.0f, b), mux), muy)),
-                                  __fmul_rn(__fmul_rn(c, muy), muy));
-        float4* dst = reinterpret_cast<float4*>(slots + o * TTS_SLOT_FLOATS);
-        dst[0] = make_float4(__fmul_rn(-a, inv_k), __fmul_rn(-c, inv_k), __fmul_rn(__fmul_rn(-2.0f, b), inv_k),
-                             __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(a, mux), __fmul_rn(b, muy))), inv_k));
-        dst[1] = make_float4(__fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(b, mux), __fmul_rn(c, muy))), inv_k),
-                             __fsub_rn(1.0f, __fmul_rn(Q, inv_k)), p1.y, p1.z);
-        dst[2] = make_float4(p1.w, p2.x, 0.f, 0.f);
-      }
-    } else {
-      idx[o] = -1;
-    }
-  }
+  emit_tile<PACK>(skeys, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, tid, BS_THREADS);
   if (tid == 0) {
-    count[(long long)v * T + t] = cnt;
+    count[(long long)v * T + t] = min(n, K);
     cand[(long long)v * T + t] = n;
+  }
   }
 }
 
@@ -352,13 +515,14 @@ struct BinWorkspace {
   int* cell_start;   // [V][T+1]
   int2* cell_rank;   // [V][G]
   float4* rec;       // [V][G]
+  int* ovf;          // [1 + V*T]: count, then the tiles left to the block kernel
 };
 
 static size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
 size_t bin_workspace_bytes(int G, int V, int T) {
   return align_up((size_t)V * T * 4) + align_up((size_t)V * (T + 1) * 4) + align_up((size_t)V * G * 8) +
-         align_up((size_t)V * G * 16);
+         align_up((size_t)V * G * 16) + align_up((size_t)(V * T + 1) * 4);
 }
 
 static BinWorkspace carve(void* ws, int G, int V, int T) {
@@ -371,6 +535,8 @@ static BinWorkspace carve(void* ws, int G, int V, int T) {
   w.cell_rank = reinterpret_cast<int2*>(p);
   p += align_up((size_t)V * G * 8);
   w.rec = reinterpret_cast<float4*>(p);
+  p += align_up((size_t)V * G * 16);
+  w.ovf = reinterpret_cast<int*>(p);
   return w;
 }
 
@@ -385,13 +551,28 @@ static int bin_core(const float* mu2d, const int* cell_count, const int2* cell_r
   k_cell_scan<<<V, 1024, 0, st>>>(cell_count, w.cell_start, T);
   dim3 gg((G + 255) / 256, V);
   if (G > 0) k_cell_scatter<<<gg, 256, 0, st>>>(reinterpret_cast<const float2*>(mu2d), cell_rank, w.cell_start, G, T, w.rec);
-  dim3 gt(T, V);
-  if (proj && slots)
-    k_bin_select<true><<<gt, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, proj, inv_k, idx, count, cand,
-                                                  inv, slots);
-  else
-    k_bin_select<false><<<gt, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, nullptr, inv_k, idx, count,
-                                                   cand, inv, nullptr);
+  if (cudaMemsetAsync(w.ovf, 0, 4, st) != cudaSuccess) return check_launch("memset overflow count");
+  const long long tiles = (long long)V * T;
+  const unsigned wblocks = (unsigned)((tiles + WB_WARPS - 1) / WB_WARPS);
+  const size_t wsmem = (size_t)WB_WARPS * WCAP * sizeof(u64);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_bin_warp<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    cudaFuncSetAttribute(k_bin_warp<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    attr = true;
+  }
+  const unsigned bblocks = (unsigned)(tiles < 296 ? tiles : 296);   // two blocks per SM loop over the list
+  if (proj && slots) {
+    k_bin_warp<true><<<wblocks, WB_WARPS * 32, wsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, proj, inv_k,
+                                                            idx, count, cand, inv, slots, w.ovf + 1, w.ovf);
+    k_bin_select<true><<<bblocks, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, proj, inv_k, idx, count,
+                                                       cand, inv, slots, w.ovf + 1, w.ovf);
+  } else {
+    k_bin_warp<false><<<wblocks, WB_WARPS * 32, wsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, nullptr, inv_k,
+                                                             idx, count, cand, inv, nullptr, w.ovf + 1, w.ovf);
+    k_bin_select<false><<<bblocks, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, nullptr, inv_k, idx,
+                                                        count, cand, inv, nullptr, w.ovf + 1, w.ovf);
+  }
   return check_launch("binning");
 }
 
