@@ -139,4 +139,40 @@ __device__ __forceinline__ void box_muller(uint32_t a, uint32_t b, float& n0, fl
   n1 = r * s;
 }
 
+// ---- packed FP32 pairs (sm_100a .f32x2 arithmetic: two IEEE fp32 lanes per instruction) ----
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 mk2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void split2(f32x2 a, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(a));
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f32x2 relu2(f32x2 a) {
+  float lo, hi;
+  split2(a, lo, hi);
+  return mk2(fmaxf(lo, 0.f), fmaxf(hi, 0.f));
+}
+__device__ __forceinline__ float hsum2(f32x2 a) {
+  float lo, hi;
+  split2(a, lo, hi);
+  return lo + hi;
+}
+
 }  // namespace tts

@@ -56,17 +56,33 @@ __global__ void __launch_bounds__(256)
   float g[WIN];
 #pragma unroll
   for (int k = 0; k < WIN; k++) g[k] = wd.g[k];
-  for (int i = tid; i < LG::IH * LG::IW; i += 256) {
-    const int r = i / LG::IW, c = i % LG::IW;
-    const int yy = oy0 + r, xx = ox0 + c;
-    float x = 0.f, y = 0.f;
-    if (yy < H && xx < W) {
-      const long long q = (((long long)v * H + yy) * W + xx) * 3 + ch;
-      x = fminf(fmaxf(img[q], 0.f), 1.f);
-      y = fminf(fmaxf(tgt[q], 0.f), 1.f);
+  {
+    // issue every load of the halo tile before the first shared-memory store (memory-level
+    // parallelism: the trip count is a compile-time constant)
+    constexpr int NL = (LG::IH * LG::IW + 255) / 256;
+    float xv[NL], yv[NL];
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = tid + 256 * u;
+      const int r = i / LG::IW, c = i % LG::IW;
+      const int yy = oy0 + r, xx = ox0 + c;
+      xv[u] = 0.f;
+      yv[u] = 0.f;
+      if (i < LG::IH * LG::IW && yy < H && xx < W) {
+        const long long q = (((long long)v * H + yy) * W + xx) * 3 + ch;
+        xv[u] = __ldg(img + q);
+        yv[u] = __ldg(tgt + q);
+      }
     }
-    sx[r * LG::XS + c] = x;
-    sy[r * LG::XS + c] = y;
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = tid + 256 * u;
+      if (i < LG::IH * LG::IW) {
+        const int r = i / LG::IW, c = i % LG::IW;
+        sx[r * LG::XS + c] = fminf(fmaxf(xv[u], 0.f), 1.f);
+        sy[r * LG::XS + c] = fminf(fmaxf(yv[u], 0.f), 1.f);
+      }
+    }
   }
   __syncthreads();
   // rows: item = (row r, segment of RB outputs); lanes walk down rows (odd stride: no conflicts)
@@ -179,19 +195,34 @@ __global__ void __launch_bounds__(256)
   const long long plane = (long long)Ho * Wo;
   const float* mbase = maps + (long long)vc * 3 * plane;
   // map rows [y0-WIN+1, y0+LT_H), cols [x0-WIN+1, x0+LT_W); zero outside the valid region
-  for (int i = tid; i < LG::IH * LG::IW; i += 256) {
-    const int r = i / LG::IW, c = i % LG::IW;
-    const int my = y0 - (WIN - 1) + r, mx = x0 - (WIN - 1) + c;
-    float a = 0.f, bb = 0.f, d = 0.f;
-    if (my >= 0 && my < Ho && mx >= 0 && mx < Wo) {
-      const long long q = (long long)my * Wo + mx;
-      a = mbase[q];
-      bb = mbase[plane + q];
-      d = mbase[2 * plane + q];
+  {
+    constexpr int NL = (LG::IH * LG::IW + 255) / 256;
+    float av[NL], bv[NL], dv[NL];
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = tid + 256 * u;
+      const int r = i / LG::IW, c = i % LG::IW;
+      const int my = y0 - (WIN - 1) + r, mx = x0 - (WIN - 1) + c;
+      av[u] = 0.f;
+      bv[u] = 0.f;
+      dv[u] = 0.f;
+      if (i < LG::IH * LG::IW && my >= 0 && my < Ho && mx >= 0 && mx < Wo) {
+        const long long q = (long long)my * Wo + mx;
+        av[u] = __ldg(mbase + q);
+        bv[u] = __ldg(mbase + plane + q);
+        dv[u] = __ldg(mbase + 2 * plane + q);
+      }
     }
-    sm[(0 * LG::IH + r) * LG::XS + c] = a;
-    sm[(1 * LG::IH + r) * LG::XS + c] = bb;
-    sm[(2 * LG::IH + r) * LG::XS + c] = d;
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = tid + 256 * u;
+      if (i < LG::IH * LG::IW) {
+        const int r = i / LG::IW, c = i % LG::IW;
+        sm[(0 * LG::IH + r) * LG::XS + c] = av[u];
+        sm[(1 * LG::IH + r) * LG::XS + c] = bv[u];
+        sm[(2 * LG::IH + r) * LG::XS + c] = dv[u];
+      }
+    }
   }
   __syncthreads();
   // transposed row filter: t[r][c] = sum_k g[k] m[r][c + WIN-1 - k]

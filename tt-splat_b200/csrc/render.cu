@@ -2,8 +2,9 @@
 //
 // Forward (replaces _DevRenderBinned.forward, tools/m4_train_binned.py:156-166): the tile's
 // slot rows (theta_u[6] | color_o[3] | o_col) are staged in shared memory by one bulk copy
-// (cp.async.bulk, completion on an mbarrier); each thread owns RENDER_PPT pixels of one tile
-// row and loops over the slots with the rows broadcast from shared memory:
+// (cp.async.bulk, completion on an mbarrier); each thread owns two adjacent pixel pairs of one
+// tile row, evaluated with sm_100a packed .f32x2 arithmetic, and loops over the slots with the
+// rows broadcast from shared memory:
 //   u = theta . Phi(px, py) = (t0 px + (t2 py + t3)) px + ((t1 py + t4) py + t5)
 //   w = max(u, 0)^2;  num += w color_o;  den += w o_col
 // then C = (num + w_b c_b) / (den + w_b).  The [256 x K] weight matrix never leaves registers.
@@ -13,17 +14,16 @@
 // (gnum = gC/den, gden = -(gC.C)/den) are broadcast from shared memory; every per-slot sum
 // (gcolor_o = w^T gnum, go_col = w^T gden, gtheta = Phi^T (2 relu(u) gw)) stays in the
 // thread's registers, so no cross-thread reduction is needed.  gtheta is accumulated per row
-// through the moments sum(gu), sum(gu px), sum(gu px^2).
+// through the moments sum(gu), sum(gu px), sum(gu px^2); adjacent pixels run as .f32x2 pairs.
 #include "common.cuh"
 
 namespace tts {
 
-constexpr int RENDER_PPT = 2;                       // pixels per thread (same row, 8 apart)
-constexpr int RENDER_THREADS = 256 / RENDER_PPT;    // 128
+constexpr int FWD_THREADS = 64;   // 4 pixels per thread: two adjacent pairs of one row
 constexpr int KMAX = 256;
 
 template <bool BF16>
-__global__ void __launch_bounds__(RENDER_THREADS)
+__global__ void __launch_bounds__(FWD_THREADS)
     k_render_fwd(const void* __restrict__ slots_, const int* __restrict__ count, int ntx, int T, int H, int W, int K,
                  const float* __restrict__ w_b_ptr, int w_b_is_raw, const float* __restrict__ c_b,
                  float* __restrict__ img, float* __restrict__ den_out) {
@@ -35,9 +35,7 @@ __global__ void __launch_bounds__(RENDER_THREADS)
   bool ok = true;
   if (!BF16) {
     const float* src = static_cast<const float*>(slots_) + row0 * TTS_SLOT_FLOATS;
-    if (tid == 0) {
-      mbar_init(&bar, 1);
-    }
+    if (tid == 0) mbar_init(&bar, 1);
     __syncthreads();
     if (n > 0) {
       if (tid == 0) {
@@ -49,23 +47,19 @@ __global__ void __launch_bounds__(RENDER_THREADS)
     }
   } else {
     const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(slots_) + row0 * TTS_SLOT_FLOATS;
-    for (int i = tid; i < n * TTS_SLOT_FLOATS; i += RENDER_THREADS) s_rows[i] = __bfloat162float(src[i]);
+    for (int i = tid; i < n * TTS_SLOT_FLOATS; i += FWD_THREADS) s_rows[i] = __bfloat162float(src[i]);
     __syncthreads();
   }
   if (!ok) return;   // status recorded; nothing of the tile is written
 
   const float wb = w_b_is_raw ? softplusf(*w_b_ptr) : *w_b_ptr;
-  const float cb0 = c_b[0], cb1 = c_b[1], cb2 = c_b[2];
-  const int ly = tid / (16 / RENDER_PPT);
-  const int lx0 = tid % (16 / RENDER_PPT);
+  const int ly = tid >> 2;
+  const int lxa = 2 * (tid & 3), lxb = lxa + 8;       // pixels lxa, lxa+1, lxb, lxb+1 of row ly
   const float py = (float)ly + 0.5f;
-  float px[RENDER_PPT];
-  float acc[RENDER_PPT][4];
-#pragma unroll
-  for (int i = 0; i < RENDER_PPT; i++) {
-    px[i] = (float)(lx0 + i * (16 / RENDER_PPT)) + 0.5f;
-    acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  }
+  const f32x2 pxa = mk2((float)lxa + 0.5f, (float)lxa + 1.5f);
+  const f32x2 pxb = mk2((float)lxb + 0.5f, (float)lxb + 1.5f);
+  const f32x2 z = mk2(0.f, 0.f);
+  f32x2 a0 = z, a1 = z, a2 = z, a3 = z, b0 = z, b1 = z, b2 = z, b3 = z;
   const float4* rows = reinterpret_cast<const float4*>(s_rows);
 #pragma unroll 2
   for (int s = 0; s < n; ++s) {
@@ -74,27 +68,30 @@ __global__ void __launch_bounds__(RENDER_THREADS)
     const float4 C = rows[3 * s + 2];   // cb oc 0 0
     const float srow = fmaf(A.z, py, A.w);
     const float rrow = fmaf(fmaf(A.y, py, B.x), py, B.y);
-#pragma unroll
-    for (int i = 0; i < RENDER_PPT; i++) {
-      const float u = fmaf(fmaf(A.x, px[i], srow), px[i], rrow);
-      const float r = fmaxf(u, 0.f);
-      const float w = r * r;
-      acc[i][0] = fmaf(w, B.z, acc[i][0]);
-      acc[i][1] = fmaf(w, B.w, acc[i][1]);
-      acc[i][2] = fmaf(w, C.x, acc[i][2]);
-      acc[i][3] = fmaf(w, C.y, acc[i][3]);
-    }
+    const f32x2 t0 = mk2(A.x, A.x), s2 = mk2(srow, srow), r2 = mk2(rrow, rrow);
+    const f32x2 cr = mk2(B.z, B.z), cg = mk2(B.w, B.w), cb = mk2(C.x, C.x), oc = mk2(C.y, C.y);
+    const f32x2 ra = relu2(fma2(fma2(t0, pxa, s2), pxa, r2));
+    const f32x2 rb = relu2(fma2(fma2(t0, pxb, s2), pxb, r2));
+    const f32x2 wa = mul2(ra, ra), wbv = mul2(rb, rb);
+    a0 = fma2(wa, cr, a0); a1 = fma2(wa, cg, a1); a2 = fma2(wa, cb, a2); a3 = fma2(wa, oc, a3);
+    b0 = fma2(wbv, cr, b0); b1 = fma2(wbv, cg, b1); b2 = fma2(wbv, cb, b2); b3 = fma2(wbv, oc, b3);
   }
   const int tx = t % ntx, ty = t / ntx;
   const int gy = ty * 16 + ly;
+  const float cb0 = c_b[0], cb1 = c_b[1], cb2 = c_b[2];
+  float n0[4], n1[4], n2[4], dd[4];
+  split2(a0, n0[0], n0[1]); split2(b0, n0[2], n0[3]);
+  split2(a1, n1[0], n1[1]); split2(b1, n1[2], n1[3]);
+  split2(a2, n2[0], n2[1]); split2(b2, n2[2], n2[3]);
+  split2(a3, dd[0], dd[1]); split2(b3, dd[2], dd[3]);
+  const int lx[4] = {lxa, lxa + 1, lxb, lxb + 1};
 #pragma unroll
-  for (int i = 0; i < RENDER_PPT; i++) {
-    const int gx = tx * 16 + lx0 + i * (16 / RENDER_PPT);
-    const long long p = ((long long)v * H + gy) * W + gx;
-    const float d = acc[i][3] + wb;
-    img[3 * p + 0] = (acc[i][0] + wb * cb0) / d;
-    img[3 * p + 1] = (acc[i][1] + wb * cb1) / d;
-    img[3 * p + 2] = (acc[i][2] + wb * cb2) / d;
+  for (int i = 0; i < 4; i++) {
+    const long long p = ((long long)v * H + gy) * W + tx * 16 + lx[i];
+    const float d = dd[i] + wb;
+    img[3 * p + 0] = (n0[i] + wb * cb0) / d;
+    img[3 * p + 1] = (n1[i] + wb * cb1) / d;
+    img[3 * p + 2] = (n2[i] + wb * cb2) / d;
     den_out[p] = d;
   }
 }
@@ -103,13 +100,14 @@ __global__ void __launch_bounds__(256)
     k_render_bwd(const float* __restrict__ slots, const int* __restrict__ count, int ntx, int T, int H, int W, int K,
                  const float* __restrict__ c_b, const float* __restrict__ img, const float* __restrict__ den,
                  const float* __restrict__ gimg, float* __restrict__ slot_grads, float* __restrict__ gwb_partial) {
-  __shared__ __align__(16) float4 s_pix[256];
+  // per-pixel upstream terms, one array per component so that two adjacent pixels load as a pair
+  __shared__ __align__(16) float s_g0[256], s_g1[256], s_g2[256], s_gd[256];
   __shared__ float s_red[32];
   const int t = blockIdx.x, v = blockIdx.y, tid = threadIdx.x;
   const int tx = t % ntx, ty = t / ntx;
   const int n = count[(long long)v * T + t];
   const float cb0 = c_b[0], cb1 = c_b[1], cb2 = c_b[2];
-  // per-pixel upstream terms (tools/m4_train_binned.py:178-179, spike/backward.py:46-48)
+  // gnum = gC/den, gden = -(gC.C)/den (tools/m4_train_binned.py:178-179, spike/backward.py:46-48)
   float wbp = 0.f;
   for (int p = tid; p < 256; p += blockDim.x) {
     const long long q = ((long long)v * H + ty * 16 + (p >> 4)) * W + tx * 16 + (p & 15);
@@ -118,7 +116,10 @@ __global__ void __launch_bounds__(256)
     const float d = den[q];
     const float gn0 = g0 / d, gn1 = g1 / d, gn2 = g2 / d;
     const float gd = -(g0 * c0 + g1 * c1 + g2 * c2) / d;
-    s_pix[p] = make_float4(gn0, gn1, gn2, gd);
+    s_g0[p] = gn0;
+    s_g1[p] = gn1;
+    s_g2[p] = gn2;
+    s_gd[p] = gd;
     wbp += gn0 * cb0 + gn1 * cb1 + gn2 * cb2 + gd;
   }
   // deterministic block reduction of the w_b partial
@@ -136,47 +137,54 @@ __global__ void __launch_bounds__(256)
   const long long o = ((long long)v * T + t) * K + k;
   const float4* row = reinterpret_cast<const float4*>(slots + o * TTS_SLOT_FLOATS);
   const float4 A = row[0], B = row[1], C = row[2];
-  const float t0 = A.x, t1 = A.y, t2 = A.z, t3 = A.w, t4 = B.x, t5 = B.y;
-  const float cr = B.z, cg = B.w, cbb = C.x, oc = C.y;
-  float gc0 = 0.f, gc1 = 0.f, gc2 = 0.f, goc = 0.f;
+  const f32x2 t0 = mk2(A.x, A.x);
+  const float t1 = A.y, t2 = A.z, t3 = A.w, t4 = B.x, t5 = B.y;
+  const f32x2 cr = mk2(B.z, B.z), cg = mk2(B.w, B.w), cbb = mk2(C.x, C.x), oc = mk2(C.y, C.y);
+  const f32x2 z = mk2(0.f, 0.f);
+  f32x2 gc0 = z, gc1 = z, gc2 = z, goc = z;
   float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f, g4 = 0.f, g5 = 0.f;
   for (int ly = 0; ly < 16; ++ly) {
     const float py = (float)ly + 0.5f;
     const float srow = fmaf(t2, py, t3);
     const float rrow = fmaf(fmaf(t1, py, t4), py, t5);
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+    const f32x2 s2 = mk2(srow, srow), r2 = mk2(rrow, rrow);
+    f32x2 a0 = z, a1 = z, a2 = z;
 #pragma unroll
-    for (int lx = 0; lx < 16; ++lx) {
-      const float px = (float)lx + 0.5f;
-      const float4 P = s_pix[ly * 16 + lx];
-      const float u = fmaf(fmaf(t0, px, srow), px, rrow);
-      const float r = fmaxf(u, 0.f);
-      const float w = r * r;
-      gc0 = fmaf(w, P.x, gc0);
-      gc1 = fmaf(w, P.y, gc1);
-      gc2 = fmaf(w, P.z, gc2);
-      goc = fmaf(w, P.w, goc);
-      const float gw = fmaf(P.x, cr, fmaf(P.y, cg, fmaf(P.z, cbb, P.w * oc)));
-      const float gu = r * gw;
-      a0 += gu;
-      const float tpx = gu * px;
-      a1 += tpx;
-      a2 = fmaf(tpx, px, a2);
+    for (int lp = 0; lp < 8; ++lp) {
+      const f32x2 px = mk2((float)(2 * lp) + 0.5f, (float)(2 * lp) + 1.5f);
+      const int pi = ly * 16 + 2 * lp;
+      const f32x2 P0 = *reinterpret_cast<const f32x2*>(&s_g0[pi]);
+      const f32x2 P1 = *reinterpret_cast<const f32x2*>(&s_g1[pi]);
+      const f32x2 P2 = *reinterpret_cast<const f32x2*>(&s_g2[pi]);
+      const f32x2 P3 = *reinterpret_cast<const f32x2*>(&s_gd[pi]);
+      const f32x2 r = relu2(fma2(fma2(t0, px, s2), px, r2));
+      const f32x2 w = mul2(r, r);
+      gc0 = fma2(w, P0, gc0);
+      gc1 = fma2(w, P1, gc1);
+      gc2 = fma2(w, P2, gc2);
+      goc = fma2(w, P3, goc);
+      const f32x2 gw = fma2(P0, cr, fma2(P1, cg, fma2(P2, cbb, mul2(P3, oc))));
+      const f32x2 gu = mul2(r, gw);
+      a0 = add2(a0, gu);
+      const f32x2 tpx = mul2(gu, px);
+      a1 = add2(a1, tpx);
+      a2 = fma2(tpx, px, a2);
     }
-    g0 += a2;
-    g1 = fmaf(py * py, a0, g1);
-    g2 = fmaf(py, a1, g2);
-    g3 += a1;
-    g4 = fmaf(py, a0, g4);
-    g5 += a0;
+    const float s0 = hsum2(a0), s1 = hsum2(a1), s2s = hsum2(a2);
+    g0 += s2s;
+    g1 = fmaf(py * py, s0, g1);
+    g2 = fmaf(py, s1, g2);
+    g3 += s1;
+    g4 = fmaf(py, s0, g4);
+    g5 += s0;
   }
   // rows are 40 B: 8-byte aligned, so store as float2
   float2* out = reinterpret_cast<float2*>(slot_grads + o * TTS_SLOT_GRAD_FLOATS);
   out[0] = make_float2(2.f * g0, 2.f * g1);
   out[1] = make_float2(2.f * g2, 2.f * g3);
   out[2] = make_float2(2.f * g4, 2.f * g5);
-  out[3] = make_float2(gc0, gc1);
-  out[4] = make_float2(gc2, goc);
+  out[3] = make_float2(hsum2(gc0), hsum2(gc1));
+  out[4] = make_float2(hsum2(gc2), hsum2(goc));
 }
 
 // theta_u[VT,6,K], color_o[VT,K,3], o_col[VT,K,1] -> slot rows
@@ -225,9 +233,9 @@ extern "C" int tts_render_fwd(const void* slots, int slots_bf16, const int32_t* 
   dim3 grid(T, V);
   cudaStream_t st = as_stream(stream);
   if (slots_bf16)
-    k_render_fwd<true><<<grid, RENDER_THREADS, 0, st>>>(slots, count, ntx, T, H, W, K, w_b, w_b_is_raw, c_b, img, den);
+    k_render_fwd<true><<<grid, FWD_THREADS, 0, st>>>(slots, count, ntx, T, H, W, K, w_b, w_b_is_raw, c_b, img, den);
   else
-    k_render_fwd<false><<<grid, RENDER_THREADS, 0, st>>>(slots, count, ntx, T, H, W, K, w_b, w_b_is_raw, c_b, img, den);
+    k_render_fwd<false><<<grid, FWD_THREADS, 0, st>>>(slots, count, ntx, T, H, W, K, w_b, w_b_is_raw, c_b, img, den);
   return check_launch("render_fwd");
 }
 
