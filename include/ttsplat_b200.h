@@ -69,6 +69,15 @@ size_t tts_bin_workspace_bytes(int G, int V, int H, int W);
 int tts_bin_from_mu2d(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W, int R,
                       int K, int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv,
                       void* workspace, size_t workspace_bytes, void* stream);
+/* Allocation-free variant of tts_bin_from_mu2d (no counterpart in the reference): for callers
+ * that cannot allocate device memory when they bin (inside CUDA-graph stream capture, or embedded
+ * in a host runtime that owns the allocator).  Scratch comes from a 16 MiB static device array per
+ * GPU, held until exit; problems whose tts_bin_workspace_bytes exceeds 16 MiB are rejected with
+ * TTS_ERR_CAPACITY.  The first call on a device looks up that array's address (set-up), so make
+ * it before any stream capture.  All calls share the array: calls that overlap on the GPU race. */
+int tts_bin_from_mu2d_noalloc(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W,
+                              int R, int K, int32_t* idx, int32_t* count, int32_t* cand,
+                              int32_t* inv, void* stream);
 int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float* proj,
                  const int32_t* cell_count, const int32_t* cell_rank, int G, int V, int H, int W,
                  int R, int K, float k_poly, int32_t* idx, int32_t* count, int32_t* cand,

@@ -10,6 +10,9 @@
 // The epilogue writes idx/count/cand, the stencil-indexed inverse table used by the
 // deterministic slot->gaussian reduction, and (optionally) the packed slot rows
 // theta_u[6] | color_o[3] | o_col of _operands (:207-211, theta_u_gathered :130-143).
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 
 namespace tts {
@@ -624,4 +627,57 @@ extern "C" int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float*
   BinWorkspace w = carve(workspace, G, V, T);
   return bin_core(mu2d, cell_count, reinterpret_cast<const int2*>(cell_rank), G, V, ntx, nty, R, K, proj,
                   (float)(1.0 / (double)k_poly), idx, count, cand, inv, slots, w, as_stream(stream));
+}
+
+// ---- allocation-free binning -------------------------------------------------------------------
+// Some callers cannot allocate device memory at the point where they bin: code that records the
+// binning into a CUDA graph while stream capture is active (cudaMalloc is not allowed there),
+// renderers embedded in another runtime that owns the device allocator and hands this library only
+// its input and output buffers, and real-time loops that forbid allocation (and the device-wide
+// synchronisation cudaMalloc/cudaFree can cause) after start-up.  For them, tts_bin_from_mu2d_noalloc
+// runs the same binning with its scratch in a fixed static device array instead of a caller
+// workspace.  The array is NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library
+// until the process exits; problems whose workspace (tts_bin_workspace_bytes) exceeds it are
+// rejected.  All calls share the array, so calls that overlap on the GPU (different streams, or
+// different host threads on one device without ordering) race on it and must be serialised.
+namespace {
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(16) << 20;   // 16 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+// The host-side name g_noalloc_scratch is only a stand-in for the symbol: its device address is
+// looked up once per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(TTS_ERR_INVALID, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(TTS_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TTS_OK;
+}
+}  // namespace
+
+extern "C" int tts_bin_from_mu2d_noalloc(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W, int R,
+                                         int K, int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv,
+                                         void* stream) {
+  if (int rc = validate(G, V, H, W, R, K)) return rc;
+  const size_t need = bin_workspace_bytes(G, V, (H / 16) * (W / 16));
+  if (need > NOALLOC_SCRATCH_BYTES)
+    return fail(TTS_ERR_CAPACITY, "binning needs " + std::to_string(need) + " bytes of scratch, more than the " +
+                                      std::to_string(NOALLOC_SCRATCH_BYTES) +
+                                      "-byte static buffer of the allocation-free entry point");
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // same launches as tts_bin_from_mu2d; the counters it needs at zero are cleared there
+  return tts_bin_from_mu2d(mu2d, keep, G, V, H, W, R, K, idx, count, cand, inv, scratch, NOALLOC_SCRATCH_BYTES,
+                           stream);
 }
