@@ -186,8 +186,9 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     sc = pkg.synthetic.config2(G=CONFIG["G"], n_views=max(CONFIG["views"], 1))
     V = CONFIG["views"]
-    per = V // world
-    mine = list(range(rank * per, (rank + 1) * per)) if world <= V else [rank % V]
+    mine = train.partition_views(V, world, rank)
+    if not mine:
+        raise SystemExit(f"rank {rank}: more ranks than views ({V})")
     cams = [camera.Camera.from_dict(sc["cams"][i]) for i in mine]
     targets_host = torch.from_numpy(np.stack([sc["targets"][i] for i in mine])).pin_memory()
     m = model.GaussianModel.from_arrays(sc["params"], device=dev)

@@ -25,6 +25,23 @@ DEFAULT_LR = {"means": 5e-3, "scales": 5e-3, "quats": 1e-3, "opacity": 5e-2, "op
               "wb": 1e-2, "depth": 1e-2}   # spike/train.py:9-12
 
 
+def partition_views(n_views, world, rank):
+    """The views rank ``rank`` of ``world`` renders: contiguous, as even as possible (ranks beyond
+    the number of views get none).  Every rank's gradient carries the 1/n_views scale of the
+    reference's mean over cameras (spike/train.py:27), so the sum over ranks is the mean."""
+    base, extra = divmod(n_views, world)
+    start = rank * base + min(rank, extra)
+    return list(range(start, start + base + (1 if rank < extra else 0)))
+
+
+def reduce_across_ranks(grads, loss_sum, group=None):
+    """Sum the flat gradient and the per-rank loss sums over the process group (one all-reduce
+    each, every rank in the same order)."""
+    import torch.distributed as dist
+    dist.all_reduce(grads, group=group)
+    dist.all_reduce(loss_sum, group=group)
+
+
 class TrainStep:
     def __init__(self, model, cameras, gt_images, sh_degree=0, lambda_ssim=0.2, lr=None, K=128, R=1, k=4.0,
                  blur=0.3, near=0.2, noise_lr=0.0, relocate_every=0, dead_thr=0.005, dead_frac=0.0, offset=0.0,
@@ -108,9 +125,7 @@ class TrainStep:
             self.n_moved.add_(self.reloc["n_dead"])
 
     def _allreduce(self):
-        import torch.distributed as dist
-        dist.all_reduce(self.grads, group=self.pg)
-        dist.all_reduce(self.loss_mean, group=self.pg)
+        reduce_across_ranks(self.grads, self.loss_mean, self.pg)
 
     def _run(self, relocate):
         if self.pg is None:
