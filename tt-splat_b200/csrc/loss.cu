@@ -4,9 +4,8 @@
 // SSIM uses the valid separable Gaussian window (tools/loss_manual.py:28-55; pytorch_msssim
 // convention) on inputs clamped to [0,1] (spike/metrics.py:6-7).  Two tiled kernels, each a
 // separable filter with register blocking so that every shared-memory load feeds several FMAs
-// (a thread slides an RB-long window along a row, then along a column).  Both run as persistent
-// blocks over (view, channel, tile) with the next tile's halo streaming into a second shared
-// buffer by cp.async while the current one is filtered:
+// (a thread slides an RB-long window along a row, then along a column), with the maps paired in
+// sm_100a .f32x2 FMAs:
 //   k_ssim_fwd : output tile 64x32 of the SSIM map.  Loads the (64+win-1)x(32+win-1) input
 //                halo, filters the five maps x, y, x^2, y^2, xy along rows then columns, and
 //                writes dS/dmu_x, dS/d(filtered x^2), dS/d(filtered xy) plus a per-block
@@ -36,14 +35,6 @@ struct LGeom {
   static constexpr int HS = LT_W + 1;      // odd row stride of the row-filtered maps
 };
 
-// 4-byte asynchronous global->shared copy; src_bytes = 0 writes a zero (halo outside the image).
-__device__ __forceinline__ void cp_async4(float* dst, const float* src, int src_bytes) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-
 struct TileId {
   int v, ch, bx, by;
 };
@@ -60,262 +51,298 @@ __device__ __forceinline__ TileId decode_tile(int tile, int gx, int gy) {
   return t;
 }
 
-// Persistent blocks walk the tiles with stride gridDim.x; the halo of the next tile streams into
-// the second buffer (cp.async) while the current one is filtered.
+// Packed f32x2 arithmetic on (x, y) and (x^2, y^2): the five filtered maps cost two .f32x2 FMAs
+// and one scalar FMA per tap instead of five FMAs.
 template <int WIN>
 __global__ void __launch_bounds__(256)
-    k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, int ntiles,
-               Window wd, float* __restrict__ maps, float* __restrict__ part) {
+    k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
+               float* __restrict__ maps, float* __restrict__ part) {
   using LG = LGeom<WIN>;
-  constexpr int BUF = LG::IH * LG::XS;
   extern __shared__ float smem[];
-  float* sx = smem;                            // [2][IH][XS]
-  float* sy = sx + 2 * BUF;                    // [2][IH][XS]
-  float* h = sy + 2 * BUF;                     // [5][IH][HS]
+  f32x2* sxy = reinterpret_cast<f32x2*>(smem);                    // [IH][XS] (x, y) clamped
+  f32x2* hxy = sxy + LG::IH * LG::XS;                             // [IH][HS] row-filtered (x, y)
+  f32x2* hqq = hxy + LG::IH * LG::HS;                             // [IH][HS] row-filtered (x^2, y^2)
+  float* hxy1 = reinterpret_cast<float*>(hqq + LG::IH * LG::HS);  // [IH][HS] row-filtered x*y
   __shared__ float red[8];
   const int Ho = H - WIN + 1, Wo = W - WIN + 1;
+  const TileId id = decode_tile(blockIdx.x, gx, gy);
+  const int vc = id.v * 3 + id.ch;
+  const int ox0 = id.bx * LT_W, oy0 = id.by * LT_H;
   const int tid = threadIdx.x;
   float g[WIN];
+  f32x2 g2[WIN];
 #pragma unroll
-  for (int k = 0; k < WIN; k++) g[k] = wd.g[k];
-  auto issue = [&](int tile, int b) {
-    const TileId id = decode_tile(tile, gx, gy);
-    const int ox0 = id.bx * LT_W, oy0 = id.by * LT_H;
-    for (int i = tid; i < LG::IH * LG::IW; i += 256) {
+  for (int k = 0; k < WIN; k++) {
+    g[k] = wd.g[k];
+    g2[k] = mk2(g[k], g[k]);
+  }
+  {
+    // issue every load of the halo tile before the first shared-memory store
+    constexpr int NL = (LG::IH * LG::IW + 255) / 256;
+    float xv[NL], yv[NL];
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = tid + 256 * u;
       const int r = i / LG::IW, c = i % LG::IW;
       const int yy = oy0 + r, xx = ox0 + c;
-      const bool in = yy < H && xx < W;
-      const long long q = in ? (((long long)id.v * H + yy) * W + xx) * 3 + id.ch : 0;
-      cp_async4(sx + b * BUF + r * LG::XS + c, img + q, in ? 4 : 0);
-      cp_async4(sy + b * BUF + r * LG::XS + c, tgt + q, in ? 4 : 0);
+      xv[u] = 0.f;
+      yv[u] = 0.f;
+      if (i < LG::IH * LG::IW && yy < H && xx < W) {
+        const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
+        xv[u] = __ldg(img + q);
+        yv[u] = __ldg(tgt + q);
+      }
     }
-    cp_async_commit();
-  };
-  int buf = 0;
-  if ((int)blockIdx.x < ntiles) issue(blockIdx.x, 0);
-  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int next = tile + gridDim.x;
-    if (next < ntiles) issue(next, buf ^ 1);
-    else cp_async_commit();
-    cp_async_wait_1();
-    __syncthreads();
-    const TileId id = decode_tile(tile, gx, gy);
-    const int vc = id.v * 3 + id.ch;
-    const int ox0 = id.bx * LT_W, oy0 = id.by * LT_H;
-    const float* bx_ = sx + buf * BUF;
-    const float* by_ = sy + buf * BUF;
-    // rows: item = (row r, segment of RB outputs); lanes walk down rows (odd stride)
-    for (int it = tid; it < LG::IH * (LT_W / RB); it += 256) {
-      const int r = it % LG::IH, c0 = (it / LG::IH) * RB;
-      float a[5][RB];
 #pragma unroll
-      for (int m = 0; m < 5; m++)
-#pragma unroll
-        for (int o = 0; o < RB; o++) a[m][o] = 0.f;
-#pragma unroll
-      for (int i = 0; i < RB + WIN - 1; i++) {
+    for (int u = 0; u < NL; ++u) {
+      const int i = tid + 256 * u;
+      if (i < LG::IH * LG::IW) {
+        const int r = i / LG::IW, c = i % LG::IW;
         // SSIM sees the inputs clamped to [0, 1] (spike/metrics.py:6-7)
-        const float x = fminf(fmaxf(bx_[r * LG::XS + c0 + i], 0.f), 1.f);
-        const float y = fminf(fmaxf(by_[r * LG::XS + c0 + i], 0.f), 1.f);
-        const float xx = x * x, yy = y * y, xy = x * y;
-#pragma unroll
-        for (int o = 0; o < RB; o++) {
-          const int k = i - o;
-          if (k >= 0 && k < WIN) {
-            a[0][o] = fmaf(g[k], x, a[0][o]);
-            a[1][o] = fmaf(g[k], y, a[1][o]);
-            a[2][o] = fmaf(g[k], xx, a[2][o]);
-            a[3][o] = fmaf(g[k], yy, a[3][o]);
-            a[4][o] = fmaf(g[k], xy, a[4][o]);
-          }
-        }
+        sxy[r * LG::XS + c] = mk2(fminf(fmaxf(xv[u], 0.f), 1.f), fminf(fmaxf(yv[u], 0.f), 1.f));
       }
-#pragma unroll
-      for (int m = 0; m < 5; m++)
-#pragma unroll
-        for (int o = 0; o < RB; o++) h[(m * LG::IH + r) * LG::HS + c0 + o] = a[m][o];
     }
-    __syncthreads();
-    float ssum = 0.f;
-    const long long plane = (long long)Ho * Wo;
-    float* mbase = maps + (long long)vc * 3 * plane;
-    for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
-      const int c = it % LT_W, r0 = (it / LT_W) * RB;
-      float f[5][RB];
+  }
+  __syncthreads();
+  // rows: item = (row r, segment of RB outputs); lanes walk down rows (odd stride)
+  for (int it = tid; it < LG::IH * (LT_W / RB); it += 256) {
+    const int r = it % LG::IH, c0 = (it / LG::IH) * RB;
+    const f32x2 z = mk2(0.f, 0.f);
+    f32x2 axy[RB], aqq[RB];
+    float a1[RB];
 #pragma unroll
-      for (int m = 0; m < 5; m++)
+    for (int o = 0; o < RB; o++) {
+      axy[o] = z;
+      aqq[o] = z;
+      a1[o] = 0.f;
+    }
 #pragma unroll
-        for (int o = 0; o < RB; o++) f[m][o] = 0.f;
-#pragma unroll
-      for (int i = 0; i < RB + WIN - 1; i++) {
-        float hv[5];
-#pragma unroll
-        for (int m = 0; m < 5; m++) hv[m] = h[(m * LG::IH + r0 + i) * LG::HS + c];
-#pragma unroll
-        for (int o = 0; o < RB; o++) {
-          const int k = i - o;
-          if (k >= 0 && k < WIN) {
-#pragma unroll
-            for (int m = 0; m < 5; m++) f[m][o] = fmaf(g[k], hv[m], f[m][o]);
-          }
-        }
-      }
-      const int ox = ox0 + c;
+    for (int i = 0; i < RB + WIN - 1; i++) {
+      const f32x2 XY = sxy[r * LG::XS + c0 + i];
+      const f32x2 QQ = mul2(XY, XY);
+      float x, y;
+      split2(XY, x, y);
+      const float xy = x * y;
 #pragma unroll
       for (int o = 0; o < RB; o++) {
-        const int oy = oy0 + r0 + o;
-        if (oy >= Ho || ox >= Wo) continue;
-        const float mux = f[0][o], muy = f[1][o];
-        const float mux2 = mux * mux, muy2 = muy * muy;
-        const float sxx = f[2][o] - mux2, syy = f[3][o] - muy2, sxy = f[4][o] - mux * muy;
-        const float A1 = 2.f * mux * muy + SSIM_C1, A2 = 2.f * sxy + SSIM_C2;
-        const float B1 = mux2 + muy2 + SSIM_C1, B2 = sxx + syy + SSIM_C2;
-        const float iD = 1.f / (B1 * B2), iB2 = 1.f / B2;
-        const float S = (A1 * A2) * iD;
-        ssum += S;
-        const long long q = (long long)oy * Wo + ox;
-        mbase[q] = 2.f * iD * (muy * (A2 - A1) - S * mux * (B2 - B1));   // dS/dmu_x
-        mbase[plane + q] = -S * iB2;                                     // dS/d filt(x^2)
-        mbase[2 * plane + q] = 2.f * A1 * iD;                            // dS/d filt(xy)
+        const int k = i - o;
+        if (k >= 0 && k < WIN) {
+          axy[o] = fma2(g2[k], XY, axy[o]);
+          aqq[o] = fma2(g2[k], QQ, aqq[o]);
+          a1[o] = fmaf(g[k], xy, a1[o]);
+        }
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-    if ((tid & 31) == 0) red[tid >> 5] = ssum;
-    __syncthreads();
-    if (tid == 0) {
-      float s = 0.f;
-      for (int i = 0; i < 8; ++i) s += red[i];
-      part[(long long)vc * gx * gy + id.by * gx + id.bx] = s;
+    for (int o = 0; o < RB; o++) {
+      hxy[r * LG::HS + c0 + o] = axy[o];
+      hqq[r * LG::HS + c0 + o] = aqq[o];
+      hxy1[r * LG::HS + c0 + o] = a1[o];
     }
-    buf ^= 1;
+  }
+  __syncthreads();
+  // columns: item = (column c, segment of RB output rows); lanes walk along columns
+  float ssum = 0.f;
+  const long long plane = (long long)Ho * Wo;
+  float* mbase = maps + (long long)vc * 3 * plane;
+  for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
+    const int c = it % LT_W, r0 = (it / LT_W) * RB;
+    const f32x2 z = mk2(0.f, 0.f);
+    f32x2 fxy[RB], fqq[RB];
+    float f1[RB];
+#pragma unroll
+    for (int o = 0; o < RB; o++) {
+      fxy[o] = z;
+      fqq[o] = z;
+      f1[o] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < RB + WIN - 1; i++) {
+      const f32x2 XY = hxy[(r0 + i) * LG::HS + c];
+      const f32x2 QQ = hqq[(r0 + i) * LG::HS + c];
+      const float P = hxy1[(r0 + i) * LG::HS + c];
+#pragma unroll
+      for (int o = 0; o < RB; o++) {
+        const int k = i - o;
+        if (k >= 0 && k < WIN) {
+          fxy[o] = fma2(g2[k], XY, fxy[o]);
+          fqq[o] = fma2(g2[k], QQ, fqq[o]);
+          f1[o] = fmaf(g[k], P, f1[o]);
+        }
+      }
+    }
+    const int ox = ox0 + c;
+#pragma unroll
+    for (int o = 0; o < RB; o++) {
+      const int oy = oy0 + r0 + o;
+      if (oy >= Ho || ox >= Wo) continue;
+      float mux, muy, fx2, fy2;
+      split2(fxy[o], mux, muy);
+      split2(fqq[o], fx2, fy2);
+      const float mux2 = mux * mux, muy2 = muy * muy;
+      const float sxx = fx2 - mux2, syy = fy2 - muy2, sxy_ = f1[o] - mux * muy;
+      const float A1 = 2.f * mux * muy + SSIM_C1, A2 = 2.f * sxy_ + SSIM_C2;
+      const float B1 = mux2 + muy2 + SSIM_C1, B2 = sxx + syy + SSIM_C2;
+      const float iD = 1.f / (B1 * B2), iB2 = 1.f / B2;
+      const float S = (A1 * A2) * iD;
+      ssum += S;
+      const long long q = (long long)oy * Wo + ox;
+      mbase[q] = 2.f * iD * (muy * (A2 - A1) - S * mux * (B2 - B1));   // dS/dmu_x
+      mbase[plane + q] = -S * iB2;                                     // dS/d filt(x^2)
+      mbase[2 * plane + q] = 2.f * A1 * iD;                            // dS/d filt(xy)
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ssum;
+  __syncthreads();
+  if (tid == 0) {
+    float s = 0.f;
+    for (int i = 0; i < 8; ++i) s += red[i];
+    part[(long long)vc * gx * gy + id.by * gx + id.bx] = s;
   }
 }
 
+// Transposed filter of (dS/dmu_x, dS/d filt(x^2)) as one .f32x2 pair and dS/d filt(xy) alone.
 template <int WIN>
 __global__ void __launch_bounds__(256)
-    k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, int ntiles,
-               Window wd, float lambda, float grad_scale, const float* __restrict__ maps, float* __restrict__ gimg,
+    k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
+               float lambda, float grad_scale, const float* __restrict__ maps, float* __restrict__ gimg,
                float* __restrict__ part) {
   using LG = LGeom<WIN>;
-  constexpr int BUF = 3 * LG::IH * LG::XS;
   extern __shared__ float smem[];
-  float* sm = smem;                            // [2][3][IH][XS]
-  float* h = sm + 2 * BUF;                     // [3][IH][HS]
+  f32x2* s01 = reinterpret_cast<f32x2*>(smem);                    // [IH][XS] (m0, m1)
+  float* s2 = reinterpret_cast<float*>(s01 + LG::IH * LG::XS);    // [IH][XS] m2
+  f32x2* h01 = reinterpret_cast<f32x2*>(smem + 3 * LG::IH * LG::XS + (LG::IH * LG::XS & 1));
+  float* h2 = reinterpret_cast<float*>(h01 + LG::IH * LG::HS);
   __shared__ float red[8];
   const int Ho = H - WIN + 1, Wo = W - WIN + 1;
+  const TileId id = decode_tile(blockIdx.x, gx, gy);
+  const int vc = id.v * 3 + id.ch;
+  const int x0 = id.bx * LT_W, y0 = id.by * LT_H;
   const int tid = threadIdx.x;
   float g[WIN];
+  f32x2 g2[WIN];
 #pragma unroll
-  for (int k = 0; k < WIN; k++) g[k] = wd.g[k];
+  for (int k = 0; k < WIN; k++) {
+    g[k] = wd.g[k];
+    g2[k] = mk2(g[k], g[k]);
+  }
   const long long plane = (long long)Ho * Wo;
-  // map rows [y0-WIN+1, y0+LT_H), cols [x0-WIN+1, x0+LT_W); zero outside the valid region
-  auto issue = [&](int tile, int b) {
-    const TileId id = decode_tile(tile, gx, gy);
-    const int x0 = id.bx * LT_W, y0 = id.by * LT_H;
-    const float* mbase = maps + (long long)(id.v * 3 + id.ch) * 3 * plane;
-    for (int i = tid; i < LG::IH * LG::IW; i += 256) {
+  const float* mbase = maps + (long long)vc * 3 * plane;
+  {
+    // map rows [y0-WIN+1, y0+LT_H), cols [x0-WIN+1, x0+LT_W); zero outside the valid region
+    constexpr int NL = (LG::IH * LG::IW + 255) / 256;
+    float av[NL], bv[NL], dv[NL];
+#pragma unroll
+    for (int u = 0; u < NL; ++u) {
+      const int i = tid + 256 * u;
       const int r = i / LG::IW, c = i % LG::IW;
       const int my = y0 - (WIN - 1) + r, mx = x0 - (WIN - 1) + c;
-      const bool in = my >= 0 && my < Ho && mx >= 0 && mx < Wo;
-      const long long q = in ? (long long)my * Wo + mx : 0;
-      float* d = sm + b * BUF + r * LG::XS + c;
-      cp_async4(d, mbase + q, in ? 4 : 0);
-      cp_async4(d + LG::IH * LG::XS, mbase + plane + q, in ? 4 : 0);
-      cp_async4(d + 2 * LG::IH * LG::XS, mbase + 2 * plane + q, in ? 4 : 0);
-    }
-    cp_async_commit();
-  };
-  const float Ns = (float)(3.0 * (double)Ho * (double)Wo);
-  const float N = (float)(3.0 * (double)H * (double)W);
-  int buf = 0;
-  if ((int)blockIdx.x < ntiles) issue(blockIdx.x, 0);
-  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int next = tile + gridDim.x;
-    if (next < ntiles) issue(next, buf ^ 1);
-    else cp_async_commit();
-    cp_async_wait_1();
-    __syncthreads();
-    const TileId id = decode_tile(tile, gx, gy);
-    const int vc = id.v * 3 + id.ch;
-    const int x0 = id.bx * LT_W, y0 = id.by * LT_H;
-    const float* smb = sm + buf * BUF;
-    // transposed row filter: t[r][c] = sum_k g[k] m[r][c + WIN-1 - k]
-    for (int it = tid; it < LG::IH * (LT_W / RB); it += 256) {
-      const int r = it % LG::IH, c0 = (it / LG::IH) * RB;
-      float a[3][RB];
-#pragma unroll
-      for (int m = 0; m < 3; m++)
-#pragma unroll
-        for (int o = 0; o < RB; o++) a[m][o] = 0.f;
-#pragma unroll
-      for (int i = 0; i < RB + WIN - 1; i++) {
-        float mv[3];
-#pragma unroll
-        for (int m = 0; m < 3; m++) mv[m] = smb[(m * LG::IH + r) * LG::XS + c0 + i];
-#pragma unroll
-        for (int o = 0; o < RB; o++) {
-          const int k = (WIN - 1) - (i - o);
-          if (k >= 0 && k < WIN) {
-#pragma unroll
-            for (int m = 0; m < 3; m++) a[m][o] = fmaf(g[k], mv[m], a[m][o]);
-          }
-        }
+      av[u] = 0.f;
+      bv[u] = 0.f;
+      dv[u] = 0.f;
+      if (i < LG::IH * LG::IW && my >= 0 && my < Ho && mx >= 0 && mx < Wo) {
+        const long long q = (long long)my * Wo + mx;
+        av[u] = __ldg(mbase + q);
+        bv[u] = __ldg(mbase + plane + q);
+        dv[u] = __ldg(mbase + 2 * plane + q);
       }
-#pragma unroll
-      for (int m = 0; m < 3; m++)
-#pragma unroll
-        for (int o = 0; o < RB; o++) h[(m * LG::IH + r) * LG::HS + c0 + o] = a[m][o];
     }
-    __syncthreads();
-    float l1 = 0.f;
-    for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
-      const int c = it % LT_W, r0 = (it / LT_W) * RB;
-      float t[3][RB];
 #pragma unroll
-      for (int m = 0; m < 3; m++)
-#pragma unroll
-        for (int o = 0; o < RB; o++) t[m][o] = 0.f;
-#pragma unroll
-      for (int i = 0; i < RB + WIN - 1; i++) {
-        float hv[3];
-#pragma unroll
-        for (int m = 0; m < 3; m++) hv[m] = h[(m * LG::IH + r0 + i) * LG::HS + c];
-#pragma unroll
-        for (int o = 0; o < RB; o++) {
-          const int k = (WIN - 1) - (i - o);
-          if (k >= 0 && k < WIN) {
-#pragma unroll
-            for (int m = 0; m < 3; m++) t[m][o] = fmaf(g[k], hv[m], t[m][o]);
-          }
-        }
+    for (int u = 0; u < NL; ++u) {
+      const int i = tid + 256 * u;
+      if (i < LG::IH * LG::IW) {
+        const int r = i / LG::IW, c = i % LG::IW;
+        s01[r * LG::XS + c] = mk2(av[u], bv[u]);
+        s2[r * LG::XS + c] = dv[u];
       }
-      const int xx = x0 + c;
+    }
+  }
+  __syncthreads();
+  // transposed row filter: t[r][c] = sum_k g[k] m[r][c + WIN-1 - k]
+  for (int it = tid; it < LG::IH * (LT_W / RB); it += 256) {
+    const int r = it % LG::IH, c0 = (it / LG::IH) * RB;
+    const f32x2 z = mk2(0.f, 0.f);
+    f32x2 a01[RB];
+    float a2[RB];
+#pragma unroll
+    for (int o = 0; o < RB; o++) {
+      a01[o] = z;
+      a2[o] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < RB + WIN - 1; i++) {
+      const f32x2 M01 = s01[r * LG::XS + c0 + i];
+      const float M2 = s2[r * LG::XS + c0 + i];
 #pragma unroll
       for (int o = 0; o < RB; o++) {
-        const int yy = y0 + r0 + o;
-        if (yy >= H || xx >= W) continue;
-        const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
-        const float xr = img[q], yr = tgt[q];
-        const float x = fminf(fmaxf(xr, 0.f), 1.f), y = fminf(fmaxf(yr, 0.f), 1.f);
-        const float mask = (xr >= 0.f && xr <= 1.f) ? 1.f : 0.f;
-        const float dmean = (t[0][o] + 2.f * x * t[1][o] + y * t[2][o]) / Ns;
-        const float diff = xr - yr;
-        const float sgn = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
-        l1 += fabsf(diff);
-        gimg[q] = grad_scale * ((1.f - lambda) * sgn / N + lambda * (-dmean) * mask);
+        const int k = (WIN - 1) - (i - o);
+        if (k >= 0 && k < WIN) {
+          a01[o] = fma2(g2[k], M01, a01[o]);
+          a2[o] = fmaf(g[k], M2, a2[o]);
+        }
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
-    if ((tid & 31) == 0) red[tid >> 5] = l1;
-    __syncthreads();
-    if (tid == 0) {
-      float s = 0.f;
-      for (int i = 0; i < 8; ++i) s += red[i];
-      part[(long long)vc * gx * gy + id.by * gx + id.bx] = s;
+    for (int o = 0; o < RB; o++) {
+      h01[r * LG::HS + c0 + o] = a01[o];
+      h2[r * LG::HS + c0 + o] = a2[o];
     }
-    buf ^= 1;
+  }
+  __syncthreads();
+  const float Ns = (float)(3.0 * (double)Ho * (double)Wo);
+  const float N = (float)(3.0 * (double)H * (double)W);
+  float l1 = 0.f;
+  for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
+    const int c = it % LT_W, r0 = (it / LT_W) * RB;
+    const f32x2 z = mk2(0.f, 0.f);
+    f32x2 t01[RB];
+    float t2[RB];
+#pragma unroll
+    for (int o = 0; o < RB; o++) {
+      t01[o] = z;
+      t2[o] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < RB + WIN - 1; i++) {
+      const f32x2 H01 = h01[(r0 + i) * LG::HS + c];
+      const float H2 = h2[(r0 + i) * LG::HS + c];
+#pragma unroll
+      for (int o = 0; o < RB; o++) {
+        const int k = (WIN - 1) - (i - o);
+        if (k >= 0 && k < WIN) {
+          t01[o] = fma2(g2[k], H01, t01[o]);
+          t2[o] = fmaf(g[k], H2, t2[o]);
+        }
+      }
+    }
+    const int xx = x0 + c;
+#pragma unroll
+    for (int o = 0; o < RB; o++) {
+      const int yy = y0 + r0 + o;
+      if (yy >= H || xx >= W) continue;
+      const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
+      const float xr = img[q], yr = tgt[q];
+      const float x = fminf(fmaxf(xr, 0.f), 1.f), y = fminf(fmaxf(yr, 0.f), 1.f);
+      const float mask = (xr >= 0.f && xr <= 1.f) ? 1.f : 0.f;
+      float t0, t1;
+      split2(t01[o], t0, t1);
+      const float dmean = (t0 + 2.f * x * t1 + y * t2[o]) / Ns;
+      const float diff = xr - yr;
+      const float sgn = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
+      l1 += fabsf(diff);
+      gimg[q] = grad_scale * ((1.f - lambda) * sgn / N + lambda * (-dmean) * mask);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  if ((tid & 31) == 0) red[tid >> 5] = l1;
+  __syncthreads();
+  if (tid == 0) {
+    float s = 0.f;
+    for (int i = 0; i < 8; ++i) s += red[i];
+    part[(long long)vc * gx * gy + id.by * gx + id.bx] = s;
   }
 }
 
@@ -383,21 +410,19 @@ static int launch_loss(const float* img, const float* target, int V, int H, int 
                        const Window& wd, const LossGeom& lg, float* maps, float* spart, float* lpart, float* gimg,
                        cudaStream_t st) {
   using LG = LGeom<WIN>;
-  const size_t fsm = (size_t)(4 * LG::IH * LG::XS + 5 * LG::IH * LG::HS) * 4;
-  const size_t bsm = (size_t)(6 * LG::IH * LG::XS + 3 * LG::IH * LG::HS) * 4;
+  const size_t fsm = (size_t)(LG::IH * LG::XS * 2 + LG::IH * LG::HS * 5) * 4;
+  const size_t bsm = (size_t)(LG::IH * LG::XS * 3 + (LG::IH * LG::XS & 1) + LG::IH * LG::HS * 3) * 4;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(k_ssim_fwd<WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
     cudaFuncSetAttribute(k_ssim_bwd<WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
     attr_set = true;
   }
-  const int nf = V * 3 * lg.fbx * lg.fby, nb = V * 3 * lg.bbx * lg.bby;
-  const int resident = 148 * 2;     // two blocks per SM fit the double-buffered tiles
-  k_ssim_fwd<WIN><<<(unsigned)(nf < resident ? nf : resident), 256, fsm, st>>>(img, target, H, W, lg.fbx, lg.fby, nf, wd,
-                                                                                maps, spart);
+  k_ssim_fwd<WIN><<<(unsigned)(V * 3 * lg.fbx * lg.fby), 256, fsm, st>>>(img, target, H, W, lg.fbx, lg.fby, wd, maps,
+                                                                        spart);
   if (int rc = check_launch("ssim_fwd")) return rc;
-  k_ssim_bwd<WIN><<<(unsigned)(nb < resident ? nb : resident), 256, bsm, st>>>(img, target, H, W, lg.bbx, lg.bby, nb, wd,
-                                                                                lambda, grad_scale, maps, gimg, lpart);
+  k_ssim_bwd<WIN><<<(unsigned)(V * 3 * lg.bbx * lg.bby), 256, bsm, st>>>(img, target, H, W, lg.bbx, lg.bby, wd, lambda,
+                                                                        grad_scale, maps, gimg, lpart);
   return check_launch("ssim_bwd");
 }
 
