@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(256)
       const float sxx = fx2 - mux2, syy = fy2 - muy2, sxy_ = f1[o] - mux * muy;
       const float A1 = 2.f * mux * muy + SSIM_C1, A2 = 2.f * sxy_ + SSIM_C2;
       const float B1 = mux2 + muy2 + SSIM_C1, B2 = sxx + syy + SSIM_C2;
-      const float iD = 1.f / (B1 * B2), iB2 = 1.f / B2;
+      const float iD = __frcp_rn(B1 * B2), iB2 = __frcp_rn(B2);
       const float S = (A1 * A2) * iD;
       ssum += S;
       const long long q = (long long)oy * Wo + ox;
@@ -230,6 +230,22 @@ __global__ void __launch_bounds__(256)
   }
   const long long plane = (long long)Ho * Wo;
   const float* mbase = maps + (long long)vc * 3 * plane;
+  // the image/target values of this thread's epilogue (one column item per thread: LT_W x LT_H/RB
+  // = 256 items) are fetched up front, together with the map halo
+  static_assert(LT_W * (LT_H / RB) == 256, "one column item per thread");
+  const int ec = tid % LT_W, er0 = (tid / LT_W) * RB;
+  float ximg[RB], xtgt[RB];
+#pragma unroll
+  for (int o = 0; o < RB; o++) {
+    const int yy = y0 + er0 + o, xx = x0 + ec;
+    ximg[o] = 0.f;
+    xtgt[o] = 0.f;
+    if (yy < H && xx < W) {
+      const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
+      ximg[o] = __ldg(img + q);
+      xtgt[o] = __ldg(tgt + q);
+    }
+  }
   {
     // map rows [y0-WIN+1, y0+LT_H), cols [x0-WIN+1, x0+LT_W); zero outside the valid region
     constexpr int NL = (LG::IH * LG::IW + 255) / 256;
@@ -291,11 +307,11 @@ __global__ void __launch_bounds__(256)
     }
   }
   __syncthreads();
-  const float Ns = (float)(3.0 * (double)Ho * (double)Wo);
-  const float N = (float)(3.0 * (double)H * (double)W);
+  const float inv_Ns = (float)(1.0 / (3.0 * (double)Ho * (double)Wo));
+  const float l1w = (float)((1.0 - (double)lambda) / (3.0 * (double)H * (double)W));
   float l1 = 0.f;
-  for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
-    const int c = it % LT_W, r0 = (it / LT_W) * RB;
+  {
+    const int c = ec, r0 = er0;
     const f32x2 z = mk2(0.f, 0.f);
     f32x2 t01[RB];
     float t2[RB];
@@ -323,16 +339,16 @@ __global__ void __launch_bounds__(256)
       const int yy = y0 + r0 + o;
       if (yy >= H || xx >= W) continue;
       const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
-      const float xr = img[q], yr = tgt[q];
+      const float xr = ximg[o], yr = xtgt[o];
       const float x = fminf(fmaxf(xr, 0.f), 1.f), y = fminf(fmaxf(yr, 0.f), 1.f);
       const float mask = (xr >= 0.f && xr <= 1.f) ? 1.f : 0.f;
       float t0, t1;
       split2(t01[o], t0, t1);
-      const float dmean = (t0 + 2.f * x * t1 + y * t2[o]) / Ns;
+      const float dmean = (t0 + 2.f * x * t1 + y * t2[o]) * inv_Ns;
       const float diff = xr - yr;
       const float sgn = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
       l1 += fabsf(diff);
-      gimg[q] = grad_scale * ((1.f - lambda) * sgn / N + lambda * (-dmean) * mask);
+      gimg[q] = grad_scale * (l1w * sgn + lambda * (-dmean) * mask);
     }
   }
 #pragma unroll
