@@ -1,6 +1,6 @@
 """Benchmark of the headline workload: the device-resident, graph-captured 3DGS train step.
 
-Workload: G = 100,000 gaussians, SH degree 3, a batch of 8 cameras on a
+Workload (benchmark config 2): G = 100,000 gaussians, SH degree 3, a batch of 8 cameras on a
 radius-4 ring (1264x832, 16x16 tiles, K = 128, R = 1), 0.8*L1 + 0.2*(1-SSIM) loss with the
 11x11 window, fused Adam (lr 1.6e-4 on means, beta 0.9/0.999), MCMC SGLD noise (noise_lr 5e5)
 and relocation of the 1% lowest-opacity gaussians every step, plus the MCMC regulariser.
@@ -333,6 +333,96 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def run_config(args, rank, world, local_rank, cid):
+    """Benchmark configs 3 and 4 (extra lines; the headline is config 2).
+
+    config 3: G = 1M clustered, 1920x1072 (1080 cropped to whole tiles), K = 256, fp32; each rank
+              renders one view forward + backward (weak scaling); reports candidate overflow.
+    config 4: G = 3M, 64 views 1264x832 on a seeded spiral, K = 128, forward only; views
+              partitioned over the ranks with no collective (strong scaling); frames/s, MPix/s.
+    """
+    import torch
+    import torch.distributed as dist
+    pkg = __graft_entry__.load_package()
+    from tt_splat_b200 import camera, ops, train
+    from tt_splat_b200.model import pack_arrays
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if cid == 3:
+        sc = pkg.synthetic.config3(n_views=max(world, 1))
+        mine = [rank]
+    else:
+        sc = pkg.synthetic.config4()
+        mine = train.partition_views(len(sc["cams"]), world, rank)
+    p = sc["params"]
+    G, K, sh = p["means3d"].shape[0], sc["K"], sc["sh_degree"]
+    H, W = sc["cams"][0]["H"], sc["cams"][0]["W"]
+    flat = pack_arrays(p).to(dev)
+    c_b = torch.ones(3, device=dev)
+    chunk = 8                                   # views per launch (bounds the per-view buffers)
+    groups = [mine[i:i + chunk] for i in range(0, len(mine), chunk)]
+    cams_t = [camera.pack_cameras([camera.Camera.from_dict(sc["cams"][i]) for i in gv], dev) for gv in groups]
+    ws = ops.Workspace(dev)
+    state = {}
+
+    def once():
+        for ct in cams_t:
+            pj = ops.project(flat, G, sh, ct, H, W, out=state.get("pj"))
+            state["pj"] = pj
+            bp = ops.bin_pack(pj, G, H, W, 1, K, ws=ws, out=state.get("bp"), with_inv=(cid == 3))
+            state["bp"] = bp
+            rf = ops.render_fwd(bp["slots"], bp["count"], H, W, flat[59 * G:], c_b, out=state.get("rf"))
+            state["rf"] = rf
+            if cid == 3:
+                tg = state.setdefault("tg", torch.rand(rf["img"].shape, device=dev, generator=torch.Generator(dev).manual_seed(5)))
+                lo = ops.loss_l1_ssim(rf["img"], tg, 0.2, 1.0, ws=state.setdefault("wsl", ops.Workspace(dev)),
+                                      out=state.get("lo"))
+                state["lo"] = lo
+                rb = ops.render_bwd(bp["slots"], bp["count"], H, W, c_b, rf["img"], rf["den"], lo["gimg"],
+                                    out=state.get("rb"))
+                state["rb"] = rb
+                state["grads"] = ops.backward_params(flat, G, sh, ct, H, W, 1, K, bp["inv"], rb["slot_grads"],
+                                                     rb["gwb"], out=state.get("grads"),
+                                                     ws=state.setdefault("wsb", ops.Workspace(dev)))
+
+    for _ in range(max(args.warmup, 3)):
+        once()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, min(args.steps, 50 if cid == 3 else 10))
+    e0.record()
+    for _ in range(steps):
+        once()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    if cid == 3:
+        cand = state["bp"]["cand"].reshape(-1).long()
+        over = torch.clamp(cand - K, min=0)
+        extra = {"overflow_tiles": int((over > 0).sum()), "overflow_total": int(over.sum()),
+                 "max_candidates": int(cand.max())}
+    else:
+        extra = {}
+    n_views_job = world if cid == 3 else len(sc["cams"])
+    if rank == 0:
+        line = {"metric": ("fwd+bwd views/s (config 3)" if cid == 3 else "render frames/s (config 4)"),
+                "value": (world if cid == 3 else len(sc["cams"])) / (ms / 1e3), "unit": "views/s" if cid == 3 else "frames/s",
+                "n_gpus": world, "steps": steps, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak" if cid == 3 else "strong", "dtype": "f32", "data": "synthetic (seeded)",
+                "mpix_s": n_views_job * H * W / 1e6 / (ms / 1e3),
+                "config": {"workload": f"config{cid}", "G": G, "H": H, "W": W, "K": K, "sh_degree": sh,
+                           "views_per_rank": len(mine)}, **extra}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def cpu_baseline_sample():
     """The oracle port timed on a bounded sample of the workload (one view + optimizer)."""
     import time as _t
@@ -364,6 +454,8 @@ def main():
     ap.add_argument("--views", type=int, default=CONFIG["views"], help="reduced batch for profiling captures")
     ap.add_argument("--gaussians", type=int, default=CONFIG["G"], help="reduced G for profiling captures")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the end-to-end and render legs (profiling)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+                    help="2: the headline train step; 3 / 4: the extra benchmark render configs")
     args = ap.parse_args()
     if args.views != CONFIG["views"] or args.gaussians != CONFIG["G"]:
         CONFIG.update(views=args.views, G=args.gaussians,
@@ -382,7 +474,10 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
-    run_ours(args, rank, world, local_rank)
+    if args.config == 2:
+        run_ours(args, rank, world, local_rank)
+    else:
+        run_config(args, rank, world, local_rank, args.config)
 
 
 if __name__ == "__main__":

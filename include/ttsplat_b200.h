@@ -64,7 +64,7 @@ int tts_project(const float* params, int G, int sh_degree, const float* cams, in
  * tile*2048 + clamp(long(dist2),0,2047), ties by stencil offset j then gaussian id), plus the
  * inverse table of tools/m9_scatter_oracle.py:20-35 (indexed by stencil offset) and, when
  * proj/slots are given, the operand gather of _operands :207-211 with theta_u_gathered
- * :130-143.  G < 2^31, K <= 256, R <= 3. */
+ * :130-143.  G < 2^31, K <= 256, R <= 3.  inv may be NULL (forward-only rendering). */
 size_t tts_bin_workspace_bytes(int G, int V, int H, int W);
 int tts_bin_from_mu2d(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W, int R,
                       int K, int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv,

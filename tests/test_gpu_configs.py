@@ -1,0 +1,81 @@
+"""The two larger benchmark scenes at full size: config 3 (1M clustered gaussians, 1920x1072,
+K=256) and config 4 (3M gaussians, SH degree 3, 1264x832, forward-only novel views).
+
+The device projection feeds both the device binning and the oracle binning, so the tables must
+agree bit for bit (tools/m4_train_binned.py:75-127 restated in oracle/binning.py); the images
+are checked against the oracle's binned forward on the same tables (1e-3 max abs, fp32)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import binning, render as orender
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _project_and_bin(pkg, sc, views, with_inv):
+    from tt_splat_b200 import camera, ops
+    from tt_splat_b200.model import pack_arrays
+    p = sc["params"]
+    G, K = p["means3d"].shape[0], sc["K"]
+    H, W = sc["cams"][0]["H"], sc["cams"][0]["W"]
+    flat = pack_arrays(p).to(DEV)
+    cams = camera.pack_cameras([camera.Camera.from_dict(sc["cams"][v]) for v in views], DEV)
+    pj = ops.project(flat, G, sc["sh_degree"], cams, H, W)
+    bp = ops.bin_pack(pj, G, H, W, 1, K, with_inv=with_inv)
+    return flat, pj, bp, G, K, H, W
+
+
+def _oracle_tiles(rows, valid, w_b, tm, sel):
+    """The binned forward (tools/m4_train_binned.py:226-230) for the tiles ``sel`` only."""
+    r = np.where(valid[sel][..., None], rows[sel], np.float32(0))      # rows past count are unused
+    theta = np.transpose(r[..., :6], (0, 2, 1))
+    col, oc = r[..., 6:9], r[..., 9:10]
+    u = np.maximum(np.matmul(tm.Phi[None], theta), np.float32(0))
+    w = u * u
+    num = np.matmul(w, col) + w_b * np.ones(3, np.float32)
+    den = np.matmul(w, oc) + w_b
+    return num / den                                          # [len(sel), 256, 3]
+
+
+def _check_view(pj, bp, v, H, W, K, flat, G):
+    from tt_splat_b200 import ops
+    mu = pj["mu2d"][v].cpu().numpy()
+    keep = pj["keep"][v].cpu().numpy().astype(bool)
+    tm = binning.tile_map(H, W)
+    b = binning.assign_bins(mu, keep, tm, 1, K)
+    idx = bp["idx"][v].cpu().numpy()
+    cand = bp["cand"][v].cpu().numpy()
+    assert np.array_equal(idx, np.where(b.valid, b.idx, -1))
+    assert np.array_equal(bp["count"][v].cpu().numpy(), b.valid.sum(1))
+    assert np.array_equal(cand, b.cand)
+    # forward on the device's own slot rows vs the oracle's binned forward on the same rows, on
+    # the 64 fullest tiles and 64 seeded random ones
+    c_b = torch.ones(3, device=DEV)
+    rf = ops.render_fwd(bp["slots"][v:v + 1].contiguous(), bp["count"][v:v + 1].contiguous(), H, W,
+                        flat[59 * G:], c_b)
+    rows = bp["slots"][v].cpu().numpy()
+    sel = np.unique(np.concatenate([np.argsort(-cand, kind="stable")[:64],
+                                    np.random.default_rng(v).integers(0, tm.T, 64)]))
+    w_b = np.float32(orender.softplus(np.float32(flat[59 * G].item())))
+    ref = _oracle_tiles(rows, idx >= 0, w_b, tm, sel)
+    got = rf["img"][0].cpu().numpy().reshape(-1, 3)[tm.gidx.reshape(tm.T, -1)[sel]]
+    assert np.abs(got - ref).max() < 1e-3
+    return cand
+
+
+def test_config3_full_scene_bins_and_image(pkg):
+    sc = pkg.synthetic.config3(n_views=1)
+    flat, pj, bp, G, K, H, W = _project_and_bin(pkg, sc, [0], with_inv=True)
+    cand = _check_view(pj, bp, 0, H, W, K, flat, G)
+    assert int((cand > K).sum()) > 0                   # the clustered scene overflows K=256
+
+
+def test_config4_full_scene_forward_only(pkg):
+    sc = pkg.synthetic.config4()
+    views = [0, 37]
+    flat, pj, bp, G, K, H, W = _project_and_bin(pkg, sc, views, with_inv=False)
+    assert bp["inv"] is None
+    for v in range(len(views)):
+        _check_view(pj, bp, v, H, W, K, flat, G)

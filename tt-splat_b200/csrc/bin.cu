@@ -621,7 +621,7 @@ extern "C" int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float*
   if (int rc = validate(G, V, H, W, R, K)) return rc;
   const int ntx = W / 16, nty = H / 16, T = ntx * nty;
   if (workspace_bytes < bin_workspace_bytes(G, V, T)) return fail(TTS_ERR_CAPACITY, "binning workspace too small");
-  TTS_REQUIRE(idx && count && cand && inv && slots && proj && cell_count && cell_rank, "null pointer");
+  TTS_REQUIRE(idx && count && cand && slots && proj && cell_count && cell_rank, "null pointer");
   TTS_REQUIRE(aligned16(proj) && aligned16(slots), "proj and slots must be 16-byte aligned");
   TTS_REQUIRE(k_poly > 0.f, "k must be positive");
   BinWorkspace w = carve(workspace, G, V, T);

@@ -82,8 +82,9 @@ def bin_from_mu2d(mu2d, keep, H, W, R, K, ws=None, with_inv=True):
     return idx, count, cand, inv
 
 
-def bin_pack(pj, G, H, W, R, K, k=4.0, ws=None, out=None):
-    """Binning + slot-row pack on the output of ``project``."""
+def bin_pack(pj, G, H, W, R, K, k=4.0, ws=None, out=None, with_inv=True):
+    """Binning + slot-row pack on the output of ``project`` (``with_inv=False``: no inverse table,
+    for forward-only rendering)."""
     V = pj["proj"].shape[0]
     _, _, T = tiles(H, W)
     dev = pj["proj"].device
@@ -92,7 +93,7 @@ def bin_pack(pj, G, H, W, R, K, k=4.0, ws=None, out=None):
         out = dict(idx=torch.empty(V, T, K, dtype=torch.int32, device=dev),
                    count=torch.empty(V, T, dtype=torch.int32, device=dev),
                    cand=torch.empty(V, T, dtype=torch.int32, device=dev),
-                   inv=torch.empty(V, G, S, dtype=torch.int32, device=dev),
+                   inv=torch.empty(V, G, S, dtype=torch.int32, device=dev) if with_inv else None,
                    slots=torch.empty(V, T, K, SLOT_FLOATS, device=dev))
     nbytes = lib().tts_bin_workspace_bytes(G, V, H, W)
     ws = ws or Workspace(dev)

@@ -24,8 +24,9 @@ class _BinnedRender(torch.autograd.Function):
     def forward(ctx, flat, cams_t, c_b, cfg):
         G, sh_degree, H, W, R, K, k, blur, near, bf16 = cfg
         flat_d = flat.detach().contiguous()
+        need_grad = ctx.needs_input_grad[0]
         pj = ops.project(flat_d, G, sh_degree, cams_t, H, W, blur, near)
-        bp = ops.bin_pack(pj, G, H, W, R, K, k)
+        bp = ops.bin_pack(pj, G, H, W, R, K, k, with_inv=need_grad)
         slots = bp["slots"].to(torch.bfloat16).contiguous() if bf16 else bp["slots"]
         rf = ops.render_fwd(slots, bp["count"], H, W, flat_d[59 * G:], c_b, bf16=bf16)
         ctx.save_for_backward(flat_d, cams_t, c_b, bp["slots"], bp["count"], bp["inv"], rf["img"], rf["den"])
