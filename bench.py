@@ -273,6 +273,11 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_e2e = float(t.item())
+    # the replicated update must leave every rank with the same parameter bits (outside timing)
+    replicas_ok = True
+    if world > 1:
+        from tt_splat_b200.train import replicas_agree
+        replicas_ok = replicas_agree(st.flat, pg)
 
     # ---- render MPix/s: forward of the 8-view batch (project + bin + render), device-timed ----
     rend_ms = None
@@ -318,7 +323,7 @@ def run_ours(args, rank, world, local_rank):
             "roofline_hbm": {"bound": "hbm", "kernel": "adam", "achieved": adam_gbs, "peak": peaks.get("hbm_gbs"),
                              "unit": "GB/s", "frac": adam_gbs / peaks.get("hbm_gbs", 6538.0), "traffic": None,
                              "work": f"28 B x {59 * st.G + 1} parameter elements per launch (read p,g,m,v; write p,m,v)"},
-            "stage_ms": stages, "clocks": clk_s,
+            "stage_ms": stages, "clocks": clk_s, "replicas_agree": replicas_ok,
             "e2e": {"value": args.steps / (ms_e2e / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": launches * args.steps,

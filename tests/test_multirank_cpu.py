@@ -78,3 +78,28 @@ def test_two_gloo_ranks_reduce_to_the_single_process_gradient():
         assert np.abs(g - full_g).max() <= 1e-9 * max(1.0, np.abs(full_g).max())
         assert abs(l - full_l) < 1e-9
     assert np.array_equal(out[0][0], out[1][0])      # replicas see the same bits
+
+
+def _replica_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import __graft_entry__
+        __graft_entry__.load_package()
+        from tt_splat_b200.train import replicas_agree
+        flat = torch.from_numpy(np.random.default_rng(3).standard_normal(59 * 300 + 1).astype(np.float32))
+        same = replicas_agree(flat)
+        if rank == 1:                                    # a planted one-ulp divergence on one rank
+            flat[1234] = float(np.nextafter(flat[1234].numpy(), np.float32(np.inf)))
+        out[rank] = (same, replicas_agree(flat))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_replica_check_detects_a_one_ulp_divergence():
+    world = 2
+    port = _free_port()
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_replica_worker, args=(world, port, out), nprocs=world, start_method="spawn", join=True)
+    assert [out[r] for r in range(world)] == [(True, False), (True, False)]

@@ -42,6 +42,24 @@ def reduce_across_ranks(grads, loss_sum, group=None):
     dist.all_reduce(loss_sum, group=group)
 
 
+def replica_checksum(flat):
+    """Order-independent 64-bit checksum of a parameter buffer's bits (sum of its 32-bit words,
+    in int64 so that no addition overflows for buffers below 2^31 words)."""
+    return flat.detach().contiguous().view(torch.int32).to(torch.int64).sum().reshape(1)
+
+
+def replicas_agree(flat, group=None):
+    """Whether every rank of ``group`` holds bit-identical parameters: the checksum's min and
+    max over the ranks (two all-reduces, every rank in the same order) must coincide.  The
+    replicated update keeps replicas equal; this is the periodic check that they are."""
+    import torch.distributed as dist
+    c = replica_checksum(flat)
+    lo, hi = c.clone(), c.clone()
+    dist.all_reduce(lo, op=dist.ReduceOp.MIN, group=group)
+    dist.all_reduce(hi, op=dist.ReduceOp.MAX, group=group)
+    return bool(lo.item() == hi.item())
+
+
 class TrainStep:
     def __init__(self, model, cameras, gt_images, sh_degree=0, lambda_ssim=0.2, lr=None, K=128, R=1, k=4.0,
                  blur=0.3, near=0.2, noise_lr=0.0, relocate_every=0, dead_thr=0.005, dead_frac=0.0, offset=0.0,
@@ -189,6 +207,13 @@ class TrainStep:
             s = torch.exp(view(self.flat, self.G, "log_scales"))
             total += self.lambda_o * float(o.mean()) + self.lambda_s * float(s.mean())
         return total
+
+    def check_replicas(self):
+        """Raise if the ranks' parameter replicas have diverged (a no-op without a process group)."""
+        if self.pg is None:
+            return
+        if not replicas_agree(self.flat, self.pg):
+            raise RuntimeError(f"parameter replicas differ across ranks after step {self.it}")
 
     def release(self):
         """Drop the captured graphs (call before destroying a process group)."""
