@@ -142,13 +142,17 @@ def run_reference(args, rank, world):
 
 # ----------------------------------------------------------------------------------------------
 def stage_times(st, torch, reps=3):
-    """Per-stage device times of one eager step (CUDA events on the launching stream)."""
+    """Per-stage device times of one eager step (CUDA events on the launching stream, the stages
+    queued behind a device-side spin so that host launch latency is excluded)."""
     from tt_splat_b200 import ops
     names = ["project", "bin_pack", "render_fwd", "loss", "render_bwd", "backward_params", "adam", "sgld", "relocate"]
     acc = {n: [] for n in names}
     G, H, W, R, K = st.G, st.H, st.W, st.R, st.K
     for _ in range(reps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        # a device-side spin ahead of the stages lets the host enqueue them all before the GPU
+        # reaches them, so the event deltas are device time, not host launch latency
+        torch.cuda._sleep(4_000_000)
         ev[0].record()
         ops.step_begin(st.step_t)
         ops.project(st.flat, G, st.sh_degree, st.cams_t, H, W, st.blur, st.near, out=st.pj)
@@ -163,7 +167,8 @@ def stage_times(st, torch, reps=3):
                        st.lo["gimg"], out=st.rb)
         ev[5].record()
         ops.backward_params(st.flat, G, st.sh_degree, st.cams_t, H, W, R, K, st.bp["inv"], st.rb["slot_grads"],
-                            st.rb["gwb"], st.k, st.blur, st.near, st.lambda_o, st.lambda_s, out=st.grads, ws=st.ws_bwd)
+                            st.rb["gwb"], st.k, st.blur, st.near, st.lambda_o, st.lambda_s, out=st.grads, ws=st.ws_bwd,
+                            proj=st.pj["proj"])
         ev[6].record()
         ops.adam_sgld(st.flat, st.grads, st.m, st.v, G, st.sh_degree, st.step_t, st.lr7, noise_lr=0.0)
         ev[7].record()
@@ -388,7 +393,8 @@ def run_config(args, rank, world, local_rank, cid):
                 state["rb"] = rb
                 state["grads"] = ops.backward_params(flat, G, sh, ct, H, W, 1, K, bp["inv"], rb["slot_grads"],
                                                      rb["gwb"], out=state.get("grads"),
-                                                     ws=state.setdefault("wsb", ops.Workspace(dev)))
+                                                     ws=state.setdefault("wsb", ops.Workspace(dev)),
+                                                     proj=pj["proj"])
 
     for _ in range(max(args.warmup, 3)):
         once()

@@ -126,11 +126,14 @@ int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W,
  * activation grads of operands_manual.bwd_manual :103-110 and the SH colour backward; sums
  * over the V views in view order; adds the reg_loss gradient (spike/mcmc.py:18-22) and the
  * w_b_raw gradient from the per-tile partials.  grads has the params layout (overwritten).
- * The per-(view, gaussian) records go through the workspace (tts_backward_workspace_bytes). */
+ * proj is the tts_project output for the same params and cameras (its 2-D means and conics
+ * feed the theta-build backward).  The per-(view, gaussian) gathered records go through the
+ * workspace (tts_backward_workspace_bytes). */
 size_t tts_backward_workspace_bytes(int G, int V);
 int tts_backward_params(const float* params, int G, int sh_degree, const float* cams, int V,
                         int H, int W, int R, int K, float k_poly, float blur, float near_plane,
-                        const int32_t* inv, const float* slot_grads, const float* gwb_partial,
+                        const float* proj, const int32_t* inv, const float* slot_grads,
+                        const float* gwb_partial,
                         float lambda_o, float lambda_s, float* grads, void* workspace,
                         size_t workspace_bytes, void* stream);
 

@@ -216,6 +216,31 @@ __device__ __forceinline__ void stencil_range(int j, int R, int tx, int ty, int 
 
 constexpr int WB_WARPS = 4;
 constexpr int WCAP = 1024;
+constexpr int WTIES = 64;   // ties at the selection boundary resolved by rank (more: sorted with the rest)
+
+// Warp-synchronous bitonic sort of keys[0, m) in place (padded with ~0 up to the next power of
+// two, which must fit the buffer).
+__device__ __forceinline__ void sort_front(u64* keys, int m, int lane) {
+  int P = 1;
+  while (P < m) P <<= 1;
+  for (int i = m + lane; i < P; i += 32) keys[i] = ~0ull;
+  __syncwarp();
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = lane; i < (P >> 1); i += 32) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool asc = (lo & size) == 0;
+        const u64 a = keys[lo], b = keys[hi];
+        if ((a > b) == asc) {
+          keys[lo] = b;
+          keys[hi] = a;
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
 
 // One warp per tile for tiles with at most WCAP candidates (tiles with more are appended to the
 // overflow list for the block kernel).  Keys in per-warp shared memory; when n > K a two-level
@@ -229,6 +254,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
                int* __restrict__ ovf_list, int* __restrict__ ovf_count) {
   extern __shared__ u64 wsm[];
   __shared__ int whist[WB_WARPS][64];
+  __shared__ u64 wties[WB_WARPS][WTIES];
   __shared__ int wbeg[WB_WARPS][BS_MAXS], wlen[WB_WARPS][BS_MAXS], woff[WB_WARPS][BS_MAXS + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T = ntx * nty;
@@ -312,39 +338,55 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
     const int src2 = __ffs(__ballot_sync(0xffffffffu, hit2)) - 1;
     const unsigned qstar = (unsigned)(b1 * 32 + src2);
     m = below1 + __shfl_sync(0xffffffffu, incl2, src2);
-    // compact the keys with q <= q* to the front (writes never pass the chunk being read)
-    int w = 0;
+    const int hq = __shfl_sync(0xffffffffu, hv, src2);    // keys with q == q*
+    const int c_lt = m - hq;                                 // keys with q < q* (all kept)
     const unsigned lt = (1u << lane) - 1u;
-    for (int base = 0; base < n; base += 32) {
-      const int i = base + lane;
-      const u64 key = i < n ? buf[i] : ~0ull;
-      const bool sel = i < n && (unsigned)(key >> 40) <= qstar;
-      const unsigned bal = __ballot_sync(0xffffffffu, sel);
-      __syncwarp();
-      if (sel) buf[w + __popc(bal & lt)] = key;
-      w += __popc(bal);
-      __syncwarp();
-    }
-  }
-  int P = 1;
-  while (P < m) P <<= 1;
-  for (int i = m + lane; i < P; i += 32) buf[i] = ~0ull;
-  __syncwarp();
-  for (int size = 2; size <= P; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = lane; i < (P >> 1); i += 32) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool asc = (lo & size) == 0;
-        const u64 a = buf[lo], b = buf[hi];
-        if ((a > b) == asc) {
-          buf[lo] = b;
-          buf[hi] = a;
-        }
+    if (m > K && hq <= WTIES) {
+      // Ties at q* straddle the K boundary: the keys with q < q* go to the front, the ties to a
+      // side list; each tie's rank among the ties (by stencil offset, then id: unique per tile)
+      // places the K - c_lt smallest directly behind the sorted front, so only c_lt < K keys
+      // need sorting.
+      u64* ties = wties[warp];
+      int w = 0, tw = 0;
+      for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        const u64 key = i < n ? buf[i] : ~0ull;
+        const unsigned q = (unsigned)(key >> 40);
+        const bool lo = i < n && q < qstar, eq = i < n && q == qstar;
+        const unsigned bl = __ballot_sync(0xffffffffu, lo), be = __ballot_sync(0xffffffffu, eq);
+        __syncwarp();
+        if (lo) buf[w + __popc(bl & lt)] = key;
+        if (eq) ties[tw + __popc(be & lt)] = key;
+        w += __popc(bl);
+        tw += __popc(be);
+        __syncwarp();
+      }
+      sort_front(buf, c_lt, lane);
+      const int need = K - c_lt;
+      for (int i = lane; i < hq; i += 32) {
+        const u64 key = ties[i];
+        int rank = 0;
+        for (int t2 = 0; t2 < hq; ++t2) rank += ties[t2] < key;
+        if (rank < need) buf[c_lt + rank] = key;
       }
       __syncwarp();
+      m = -1;    // sorted
+    } else {
+      // compact the keys with q <= q* to the front (writes never pass the chunk being read)
+      int w = 0;
+      for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        const u64 key = i < n ? buf[i] : ~0ull;
+        const bool sel = i < n && (unsigned)(key >> 40) <= qstar;
+        const unsigned bal = __ballot_sync(0xffffffffu, sel);
+        __syncwarp();
+        if (sel) buf[w + __popc(bal & lt)] = key;
+        w += __popc(bal);
+        __syncwarp();
+      }
     }
   }
+  if (m >= 0) sort_front(buf, m, lane);
   emit_tile<PACK>(buf, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
   if (lane == 0) {
     count[(long long)v * T + t] = min(n, K);

@@ -15,23 +15,48 @@ struct Loaded {
   float m[3], q[4], ls[3], op, dc[3];
 };
 
-__device__ __forceinline__ void load_params(const float* __restrict__ p, const ParamLayout& L, int g, Loaded& x) {
+// ---- lanes-per-gaussian layout ---------------------------------------------------------------
+// A block of 128 threads covers GPB = 128 / LPG gaussians with LPG consecutive lanes each; lane
+// vl of a gaussian handles the views vl, vl + LPG, ...  The block's parameters (59 floats per
+// gaussian) are staged once in shared memory with coalesced loads, so a gaussian's parameters
+// are read from memory once for all views.
+constexpr int GB_THREADS = 128;
+constexpr int PSTRIDE = 59;   // odd row stride: lanes of different gaussians hit different banks
+
+template <int GPB>
+__device__ __forceinline__ void stage_params(const float* __restrict__ params, int G, int g0, float* s_p) {
+  const ParamLayout L{G};
+  const int ng = min(GPB, G - g0);
+  const int offs[6] = {L.means(), L.log_scales(), L.quats(), L.opacity(), L.color_dc(), L.color_rest()};
+  const int width[6] = {3, 3, 4, 1, 3, 45};
+  const int col[6] = {0, 3, 6, 10, 11, 14};
+#pragma unroll
+  for (int f = 0; f < 6; ++f) {
+    const int w = width[f], n = ng * w;
+    const float* src = params + offs[f] + (long long)g0 * w;
+    for (int i = threadIdx.x; i < n; i += GB_THREADS) {
+      const int gg = i / w, c = i - gg * w;
+      s_p[gg * PSTRIDE + col[f] + c] = __ldg(src + i);
+    }
+  }
+}
+
+__device__ __forceinline__ void load_staged(const float* s, Loaded& x) {
 #pragma unroll
   for (int i = 0; i < 3; i++) {
-    x.m[i] = p[L.means() + 3 * g + i];
-    x.ls[i] = p[L.log_scales() + 3 * g + i];
-    x.dc[i] = p[L.color_dc() + 3 * g + i];
+    x.m[i] = s[i];
+    x.ls[i] = s[3 + i];
+    x.dc[i] = s[11 + i];
   }
 #pragma unroll
-  for (int i = 0; i < 4; i++) x.q[i] = p[L.quats() + 4 * g + i];
-  x.op = p[L.opacity() + g];
+  for (int i = 0; i < 4; i++) x.q[i] = s[6 + i];
+  x.op = s[10];
 }
 
 // SH colour pre-clamp value r + 0.5 per channel (spike/sh.py:55-72) or the DC colour
-// 0.5 + C0*dc (spike/forward.py:69-71).
+// 0.5 + C0*dc (spike/forward.py:69-71); rest coefficients from the staged row.
 template <int DEG>
-__device__ __forceinline__ void colour_pre(const float* __restrict__ p, const ParamLayout& L, int g, const Loaded& x,
-                                           const float d[3], float pre[3]) {
+__device__ __forceinline__ void colour_pre(const float* s, const Loaded& x, const float d[3], float pre[3]) {
   if (DEG == 0) {
 #pragma unroll
     for (int c = 0; c < 3; c++) pre[c] = 0.5f + SH_C0 * x.dc[c];
@@ -44,210 +69,264 @@ __device__ __forceinline__ void colour_pre(const float* __restrict__ p, const Pa
   for (int c = 0; c < 3; c++) {
     float r = b[0] * x.dc[c];
 #pragma unroll
-    for (int k = 1; k < NB; k++) r += b[k] * p[L.color_rest() + 45 * g + 3 * (k - 1) + c];
+    for (int k = 1; k < NB; k++) r += b[k] * s[14 + 3 * (k - 1) + c];
     pre[c] = r + 0.5f;
   }
 }
 
-template <int DEG>
-__global__ void __launch_bounds__(128)
-    k_project(const float* __restrict__ params, int G, const float* __restrict__ cams, int ntx, int nty, float blur,
-              float near_plane, float* __restrict__ proj, float* __restrict__ mu2d, uint8_t* __restrict__ keep,
-              int* __restrict__ cell_count, int2* __restrict__ cell_rank) {
-  const int g = blockIdx.x * blockDim.x + threadIdx.x;
-  const int v = blockIdx.y;
+template <int DEG, int LPG>
+__global__ void __launch_bounds__(GB_THREADS)
+    k_project(const float* __restrict__ params, int G, const float* __restrict__ cams, int V, int ntx, int nty,
+              float blur, float near_plane, float* __restrict__ proj, float* __restrict__ mu2d,
+              uint8_t* __restrict__ keep, int* __restrict__ cell_count, int2* __restrict__ cell_rank) {
+  constexpr int GPB = GB_THREADS / LPG;
+  __shared__ float s_p[GPB * PSTRIDE];
+  const int g0 = blockIdx.x * GPB;
+  stage_params<GPB>(params, G, g0, s_p);
+  __syncthreads();
+  const int gl = threadIdx.x / LPG, vl = threadIdx.x % LPG;
+  const int g = g0 + gl;
   const int T = ntx * nty;
-  const ParamLayout L{G};
-  int cell = -1;
-  if (g < G) {
-    const Cam cam = load_cam(cams, v);
-    Loaded x;
-    load_params(params, L, g, x);
-    GeomFwd f;
-    geom_forward(x.m, x.q, x.ls, cam, blur, near_plane, f);
-    float d[3] = {0.f, 0.f, 0.f}, nrm;
-    if (DEG > 0) view_dir(x.m, cam, d, nrm);
-    float pre[3];
-    colour_pre<DEG>(params, L, g, x, d, pre);
-    const float o = sigmoidf(x.op);
-    const float keo = f.keep ? o : 0.f;
-    const long long o_ = (long long)v * G + g;
-    float4* pr = reinterpret_cast<float4*>(proj + o_ * TTS_PROJ_FLOATS);
-    pr[0] = make_float4(f.mux, f.muy, f.a, f.b);
-    pr[1] = make_float4(f.c, keo * fmaxf(pre[0], 0.f), keo * fmaxf(pre[1], 0.f), keo * fmaxf(pre[2], 0.f));
-    pr[2] = make_float4(keo, f.mcz, 0.f, 0.f);
-    reinterpret_cast<float2*>(mu2d)[o_] = make_float2(f.mux, f.muy);
-    keep[o_] = f.keep ? 1 : 0;
-    if (f.keep) cell = cell_coord_g(f.muy, nty) * ntx + cell_coord_g(f.mux, ntx);
-    else cell_rank[o_] = make_int2(-1, 0);
-  }
-  // warp-aggregated home-cell count (one atomic per distinct cell per warp)
-  const unsigned mask = __ballot_sync(0xffffffffu, cell >= 0);
-  if (cell >= 0) {
-    const unsigned peers = __match_any_sync(mask, cell);
-    const int lane = threadIdx.x & 31;
-    const int leader = __ffs(peers) - 1;
-    int base = 0;
-    if (lane == leader) base = atomicAdd(cell_count + (long long)v * T + cell, __popc(peers));
-    base = __shfl_sync(peers, base, leader);
-    cell_rank[(long long)v * G + g] = make_int2(cell, base + __popc(peers & ((1u << lane) - 1u)));
+  const float* sp = s_p + gl * PSTRIDE;
+  Loaded x;
+  if (g < G) load_staged(sp, x);
+  const float o = g < G ? sigmoidf(x.op) : 0.f;
+  const int nit = (V + LPG - 1) / LPG;     // uniform trip count: the warp-wide cell count below
+  for (int it = 0; it < nit; ++it) {
+    const int v = vl + it * LPG;
+    int key = -1;                          // v * T + home cell of a kept (gaussian, view)
+    if (g < G && v < V) {
+      const Cam cam = load_cam(cams, v);
+      GeomFwd f;
+      geom_forward(x.m, x.q, x.ls, cam, blur, near_plane, f);
+      float d[3] = {0.f, 0.f, 0.f}, nrm;
+      if (DEG > 0) view_dir(x.m, cam, d, nrm);
+      float pre[3];
+      colour_pre<DEG>(sp, x, d, pre);
+      const float keo = f.keep ? o : 0.f;
+      const long long o_ = (long long)v * G + g;
+      float4* pr = reinterpret_cast<float4*>(proj + o_ * TTS_PROJ_FLOATS);
+      pr[0] = make_float4(f.mux, f.muy, f.a, f.b);
+      pr[1] = make_float4(f.c, keo * fmaxf(pre[0], 0.f), keo * fmaxf(pre[1], 0.f), keo * fmaxf(pre[2], 0.f));
+      pr[2] = make_float4(keo, f.mcz, 0.f, 0.f);
+      reinterpret_cast<float2*>(mu2d)[o_] = make_float2(f.mux, f.muy);
+      keep[o_] = f.keep ? 1 : 0;
+      if (f.keep) key = v * T + cell_coord_g(f.muy, nty) * ntx + cell_coord_g(f.mux, ntx);
+      else cell_rank[o_] = make_int2(-1, 0);
+    }
+    // warp-aggregated home-cell count (one atomic per distinct (view, cell) per warp)
+    const unsigned mask = __ballot_sync(0xffffffffu, key >= 0);
+    if (key >= 0) {
+      const unsigned peers = __match_any_sync(mask, key);
+      const int lane = threadIdx.x & 31;
+      const int leader = __ffs(peers) - 1;
+      int base = 0;
+      if (lane == leader) base = atomicAdd(cell_count + key, __popc(peers));
+      base = __shfl_sync(peers, base, leader);
+      cell_rank[(long long)v * G + g] = make_int2(key - v * T, base + __popc(peers & ((1u << lane) - 1u)));
+    }
   }
 }
 
-// Per (gaussian, view): slot->gaussian gather over the stencil slots (ascending j,
-// deterministic) with the theta-build backward (tools/operands_manual.py:65-80), geometry
-// backward (tools/geom_bwd.py:67-152), activation backward (tools/operands_manual.py:103-110)
-// and the view-direction part of the SH backward.  Writes 16 floats per (view, gaussian):
-// gmeans[3], gquat[4], gscale[3], gopacity_raw, gcolour_pre[3] (the gradient reaching the
-// SH sum, masked by the clamp), 0, 0.  The SH coefficient gradients need only gcolour_pre and
-// the direction, so the per-view record stays small and the reduction recomputes the basis.
-template <int DEG>
-__global__ void __launch_bounds__(128)
-    k_backward_view(const float* __restrict__ params, int G, const float* __restrict__ cams, int ntx, int nty, int S,
-                    int K, float inv_k, float blur, float near_plane, const int* __restrict__ inv,
-                    const float* __restrict__ slot_grads, float4* __restrict__ scratch) {
-  const int g = blockIdx.x * blockDim.x + threadIdx.x;
-  const int v = blockIdx.y;
-  if (g >= G) return;
-  const ParamLayout L{G};
-  const int T = ntx * nty;
-  float4* out = scratch + ((long long)v * G + g) * 4;
-  const int* iv = inv + ((long long)v * G + g) * S;
+// Address of entry e (0..58) of gaussian g's parameter row in the flat buffer.
+__device__ __forceinline__ long long field_addr(int e, int g, const ParamLayout& L) {
+  if (e < 3) return L.means() + 3LL * g + e;
+  if (e < 6) return L.log_scales() + 3LL * g + (e - 3);
+  if (e < 10) return L.quats() + 4LL * g + (e - 6);
+  if (e < 11) return L.opacity() + (long long)g;
+  if (e < 14) return L.color_dc() + 3LL * g + (e - 11);
+  return L.color_rest() + 45LL * g + (e - 14);
+}
+
+// Sum over the LPG lanes of one gaussian (xor butterfly: every lane ends with the same bits).
+template <int LPG>
+__device__ __forceinline__ float lane_sum(float a) {
+#pragma unroll
+  for (int o = 1; o < LPG; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+  return a;
+}
+
+// Slot->gaussian gather, one thread per (view, gaussian): the gaussian's (<= (2R+1)^2) slot
+// gradients are summed in ascending stencil order (deterministic; build_inv/gather_reduce of
+// tools/m9_scatter_oracle.py:20-42) through the theta-build backward (_theta_bwd,
+// tools/operands_manual.py:65-80) into a 12-float record (ga, gb, gc, gmx | gmy, gcolour_o[3] |
+// go_col, valid, 0, 0).  A slim kernel: many warps in flight to cover the random row reads.
+__global__ void __launch_bounds__(256)
+    k_slot_gather(const float* __restrict__ proj, int G, int V, int ntx, int T, int S, int K, float inv_k,
+                  const int* __restrict__ inv, const float* __restrict__ slot_grads, float4* __restrict__ rec) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)V * G) return;
+  const int v = (int)(i / G);
+  const int* iv = inv + i * S;
+  // the first nine stencil slots (all of them for R <= 1) are fetched together
+  int sl[9];
   bool any = false;
-  for (int j = 0; j < S; ++j) any |= iv[j] >= 0;
+#pragma unroll
+  for (int j = 0; j < 9; ++j) {
+    sl[j] = j < S ? __ldg(iv + j) : -1;
+    any |= sl[j] >= 0;
+  }
+  if (S > 9)
+    for (int j = 9; j < S; ++j) any |= __ldg(iv + j) >= 0;
+  float4* out = rec + i * 3;
   if (!any) {
     const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-    out[0] = z; out[1] = z; out[2] = z; out[3] = z;
+    out[0] = z; out[1] = z; out[2] = z;
     return;
   }
-  Loaded x;
-  load_params(params, L, g, x);
-  const float o = sigmoidf(x.op);
-  const Cam cam = load_cam(cams, v);
-  GeomFwd f;
-  geom_forward(x.m, x.q, x.ls, cam, blur, near_plane, f);
-  float ga = 0.f, gb = 0.f, gc = 0.f, gmx = 0.f, gmy = 0.f, gcol[3] = {0.f, 0.f, 0.f}, goc = 0.f;
-  for (int j = 0; j < S; ++j) {
-    const int s = iv[j];
-    if (s < 0) continue;
+  const float4 p0 = __ldg(reinterpret_cast<const float4*>(proj + i * TTS_PROJ_FLOATS));
+  const float pc = __ldg(proj + i * TTS_PROJ_FLOATS + 4);
+  const float fmux = p0.x, fmuy = p0.y, fa = p0.z, fb = p0.w, fc = pc;
+  float ga = 0.f, gb = 0.f, gc = 0.f, gmx = 0.f, gmy = 0.f, gcol0 = 0.f, gcol1 = 0.f, gcol2 = 0.f, goc = 0.f;
+  const float* vsg = slot_grads + (long long)v * T * K * TTS_SLOT_GRAD_FLOATS;
+  auto gather = [&](int s) {
     const int t = s / K;
-    const float mux = f.mux - (float)((t % ntx) * 16);
-    const float muy = f.muy - (float)((t / ntx) * 16);
+    const float mux = fmux - (float)((t % ntx) * 16);
+    const float muy = fmuy - (float)((t / ntx) * 16);
     // 40-byte rows are 8-byte aligned: read them as five float2
-    const float2* sg = reinterpret_cast<const float2*>(slot_grads + ((long long)v * T * K + s) * TTS_SLOT_GRAD_FLOATS);
-    const float2 a01 = sg[0], a23 = sg[1], a45 = sg[2], c01 = sg[3], c2o = sg[4];
+    const float2* sg = reinterpret_cast<const float2*>(vsg + (long long)s * TTS_SLOT_GRAD_FLOATS);
+    const float2 a01 = __ldg(sg), a23 = __ldg(sg + 1), a45 = __ldg(sg + 2), c01 = __ldg(sg + 3), c2o = __ldg(sg + 4);
     const float g0 = -a01.x * inv_k, g1 = -a01.y * inv_k, g2 = -a23.x * inv_k;
     const float g3 = -a23.y * inv_k, g4 = -a45.x * inv_k, g5 = -a45.y * inv_k;
     ga += g0 + g3 * (-2.f * mux) + g5 * mux * mux;
     gb += 2.f * g2 + g3 * (-2.f * muy) + g4 * (-2.f * mux) + g5 * (2.f * mux * muy);
     gc += g1 + g4 * (-2.f * muy) + g5 * muy * muy;
-    gmx += g3 * (-2.f * f.a) + g4 * (-2.f * f.b) + g5 * (2.f * f.a * mux + 2.f * f.b * muy);
-    gmy += g3 * (-2.f * f.b) + g4 * (-2.f * f.c) + g5 * (2.f * f.b * mux + 2.f * f.c * muy);
-    gcol[0] += c01.x;
-    gcol[1] += c01.y;
-    gcol[2] += c2o.x;
+    gmx += g3 * (-2.f * fa) + g4 * (-2.f * fb) + g5 * (2.f * fa * mux + 2.f * fb * muy);
+    gmy += g3 * (-2.f * fb) + g4 * (-2.f * fc) + g5 * (2.f * fb * mux + 2.f * fc * muy);
+    gcol0 += c01.x;
+    gcol1 += c01.y;
+    gcol2 += c2o.x;
     goc += c2o.y;
+  };
+#pragma unroll
+  for (int j = 0; j < 9; ++j)
+    if (sl[j] >= 0) gather(sl[j]);
+  for (int j = 9; j < S; ++j) {
+    const int s = __ldg(iv + j);
+    if (s >= 0) gather(s);
   }
-  float gm[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f}, gs[3] = {0.f, 0.f, 0.f};
-  geom_backward(f, cam, ga, gb, gc, gmx, gmy, gm, gq, gs);
-  float d[3] = {0.f, 0.f, 0.f}, nrm = 1.f;
-  if (DEG > 0) view_dir(x.m, cam, d, nrm);
-  float pre[3];
-  colour_pre<DEG>(params, L, g, x, d, pre);
-  const float keepf = f.keep ? 1.f : 0.f;
-  const float keo = keepf * o;
-  const float gkeo = gcol[0] * fmaxf(pre[0], 0.f) + gcol[1] * fmaxf(pre[1], 0.f) + gcol[2] * fmaxf(pre[2], 0.f) + goc;
-  const float gop = gkeo * keepf * o * (1.f - o);
-  float gr[3];
-#pragma unroll
-  for (int c = 0; c < 3; c++) gr[c] = pre[c] >= 0.f ? gcol[c] * keo : 0.f;   // torch clamp passes at 0
-  if (DEG > 0) {
-    // direction gradient through the normalisation d = dirs / max(|dirs|, 1e-12)
-    constexpr int NB = (DEG + 1) * (DEG + 1);
-    float gd[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-    for (int k = 1; k < NB; k++) {
-      float dx, dy, dz;
-      sh_basis_grad(k, d[0], d[1], d[2], dx, dy, dz);
-      float w = 0.f;
-#pragma unroll
-      for (int c = 0; c < 3; c++) w += params[L.color_rest() + 45 * g + 3 * (k - 1) + c] * gr[c];
-      gd[0] += w * dx;
-      gd[1] += w * dy;
-      gd[2] += w * dz;
-    }
-    if (nrm > 1e-12f) {
-      const float dd = d[0] * gd[0] + d[1] * gd[1] + d[2] * gd[2];
-#pragma unroll
-      for (int i = 0; i < 3; i++) gm[i] += (gd[i] - d[i] * dd) / nrm;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 3; i++) gm[i] += gd[i] / 1e-12f;
-    }
-  }
-  out[0] = make_float4(gm[0], gm[1], gm[2], gq[0]);
-  out[1] = make_float4(gq[1], gq[2], gq[3], gs[0]);
-  out[2] = make_float4(gs[1], gs[2], gop, gr[0]);
-  out[3] = make_float4(gr[1], gr[2], 0.f, 0.f);
+  out[0] = make_float4(ga, gb, gc, gmx);
+  out[1] = make_float4(gmy, gcol0, gcol1, gcol2);
+  out[2] = make_float4(goc, 1.f, 0.f, 0.f);
 }
 
-// Per gaussian: sum the per-view records in view order (deterministic), form the SH coefficient
-// gradients basis_k(d_v) * gcolour_pre_v, add the reg_loss gradient (spike/mcmc.py:18-22) and
-// write the parameter gradient.
-template <int DEG>
-__global__ void __launch_bounds__(128)
-    k_backward_reduce(const float* __restrict__ params, int G, const float* __restrict__ cams, int V,
-                      const float4* __restrict__ scratch, float lambda_o, float lambda_s, float* __restrict__ grads) {
-  const int g = blockIdx.x * blockDim.x + threadIdx.x;
-  if (g >= G) return;
-  const ParamLayout L{G};
+// Parameter backward, one gaussian per LPG lanes, each lane over its views: from the gathered
+// record, the geometry backward (tools/geom_bwd.py:67-152), activation backward
+// (tools/operands_manual.py:103-110) and SH backward (coefficients and viewing direction); the
+// lanes' partial sums are combined by a butterfly, then the reg_loss gradient
+// (spike/mcmc.py:18-22) is added and the gaussian's 59 gradients are written.
+template <int DEG, int LPG>
+__global__ void __launch_bounds__(GB_THREADS, 3)
+    k_backward(const float* __restrict__ params, int G, const float* __restrict__ cams, int V, float blur,
+               float near_plane, const float4* __restrict__ rec, float lambda_o, float lambda_s,
+               float* __restrict__ grads) {
+  constexpr int GPB = GB_THREADS / LPG;
   constexpr int NB = (DEG + 1) * (DEG + 1);
+  __shared__ float s_p[GPB * PSTRIDE];
+  const int g0 = blockIdx.x * GPB;
+  stage_params<GPB>(params, G, g0, s_p);
+  __syncthreads();
+  const int gl = threadIdx.x / LPG, vl = threadIdx.x % LPG;
+  const int g = g0 + gl;
+  const ParamLayout L{G};
+  const float* sp = s_p + gl * PSTRIDE;
   Loaded x;
-  load_params(params, L, g, x);
+  if (g < G) load_staged(sp, x);
+  const float o = g < G ? sigmoidf(x.op) : 0.f;
   float gm[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f}, gs[3] = {0.f, 0.f, 0.f}, gop = 0.f;
   float gco[NB][3];
 #pragma unroll
   for (int k = 0; k < NB; k++)
 #pragma unroll
     for (int c = 0; c < 3; c++) gco[k][c] = 0.f;
-  for (int v = 0; v < V; ++v) {
-    const float4* r = scratch + ((long long)v * G + g) * 4;
-    const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
-    gm[0] += r0.x; gm[1] += r0.y; gm[2] += r0.z;
-    gq[0] += r0.w; gq[1] += r1.x; gq[2] += r1.y; gq[3] += r1.z;
-    gs[0] += r1.w; gs[1] += r2.x; gs[2] += r2.y;
-    gop += r2.z;
-    const float gr[3] = {r2.w, r3.x, r3.y};
-    if (gr[0] == 0.f && gr[1] == 0.f && gr[2] == 0.f) continue;
-    float d[3] = {0.f, 0.f, 0.f}, nrm;
-    if (DEG > 0) {
+  if (g < G) {
+    for (int v = vl; v < V; v += LPG) {
+      const float4* r = rec + ((long long)v * G + g) * 3;
+      const float4 r0 = __ldg(r), r1 = __ldg(r + 1), r2 = __ldg(r + 2);
+      if (r2.y == 0.f) continue;       // no valid slot in this view
+      const float ga = r0.x, gb = r0.y, gc = r0.z, gmx = r0.w, gmy = r1.x;
+      const float gcol[3] = {r1.y, r1.z, r1.w};
+      const float goc = r2.x;
       const Cam cam = load_cam(cams, v);
-      view_dir(x.m, cam, d, nrm);
+      GeomFwd f;
+      geom_forward(x.m, x.q, x.ls, cam, blur, near_plane, f);
+      geom_backward(f, cam, ga, gb, gc, gmx, gmy, gm, gq, gs);
+      float d[3] = {0.f, 0.f, 0.f}, nrm = 1.f;
+      if (DEG > 0) view_dir(x.m, cam, d, nrm);
+      float pre[3];
+      colour_pre<DEG>(sp, x, d, pre);
+      const float keepf = f.keep ? 1.f : 0.f;
+      const float keo = keepf * o;
+      const float gkeo =
+          gcol[0] * fmaxf(pre[0], 0.f) + gcol[1] * fmaxf(pre[1], 0.f) + gcol[2] * fmaxf(pre[2], 0.f) + goc;
+      gop += gkeo * keepf * o * (1.f - o);
+      float gr[3];
+#pragma unroll
+      for (int c = 0; c < 3; c++) gr[c] = pre[c] >= 0.f ? gcol[c] * keo : 0.f;   // torch clamp passes at 0
+      float b[16];
+      sh_basis(DEG, d[0], d[1], d[2], b);
+#pragma unroll
+      for (int k = 0; k < NB; k++)
+#pragma unroll
+        for (int c = 0; c < 3; c++) gco[k][c] += b[k] * gr[c];
+      if (DEG > 0) {
+        // direction gradient through the normalisation d = dirs / max(|dirs|, 1e-12)
+        float gd[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 1; k < NB; k++) {
+          float dx, dy, dz;
+          sh_basis_grad(k, d[0], d[1], d[2], dx, dy, dz);
+          float w = 0.f;
+#pragma unroll
+          for (int c = 0; c < 3; c++) w += sp[14 + 3 * (k - 1) + c] * gr[c];
+          gd[0] += w * dx;
+          gd[1] += w * dy;
+          gd[2] += w * dz;
+        }
+        if (nrm > 1e-12f) {
+          const float dd = d[0] * gd[0] + d[1] * gd[1] + d[2] * gd[2];
+#pragma unroll
+          for (int i = 0; i < 3; i++) gm[i] += (gd[i] - d[i] * dd) / nrm;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 3; i++) gm[i] += gd[i] / 1e-12f;
+        }
+      }
     }
-    float b[16];
-    sh_basis(DEG, d[0], d[1], d[2], b);
-#pragma unroll
-    for (int k = 0; k < NB; k++)
-#pragma unroll
-      for (int c = 0; c < 3; c++) gco[k][c] += b[k] * gr[c];
   }
-  const float o = sigmoidf(x.op);
-  gop += lambda_o / (float)G * o * (1.f - o);
+  // combine the lanes (all lanes of the warp take part: the shuffles are warp-wide)
+#pragma unroll
+  for (int i = 0; i < 3; i++) {
+    gm[i] = lane_sum<LPG>(gm[i]);
+    gs[i] = lane_sum<LPG>(gs[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) gq[i] = lane_sum<LPG>(gq[i]);
+  gop = lane_sum<LPG>(gop);
+#pragma unroll
+  for (int k = 0; k < NB; k++)
+#pragma unroll
+    for (int c = 0; c < 3; c++) gco[k][c] = lane_sum<LPG>(gco[k][c]);
+  if (g >= G) return;
+  // the lanes share the writes: lane vl writes the entries e (0..58 of the gaussian's
+  // parameter row) with e % LPG == vl
+  auto put = [&](int e, float val) {
+    if (e % LPG == vl) grads[field_addr(e, g, L)] = val;
+  };
 #pragma unroll
   for (int i = 0; i < 3; i++) {
     const float s = expf(x.ls[i]);
-    grads[L.means() + 3 * g + i] = gm[i];
-    grads[L.log_scales() + 3 * g + i] = gs[i] * s + lambda_s / (3.f * (float)G) * s;
-    grads[L.color_dc() + 3 * g + i] = gco[0][i];
+    put(i, gm[i]);
+    put(3 + i, gs[i] * s + lambda_s / (3.f * (float)G) * s);
+    put(11 + i, gco[0][i]);
   }
 #pragma unroll
-  for (int i = 0; i < 4; i++) grads[L.quats() + 4 * g + i] = gq[i];
-  grads[L.opacity() + g] = gop;
-  float* gr_rest = grads + L.color_rest() + 45 * g;
+  for (int i = 0; i < 4; i++) put(6 + i, gq[i]);
+  put(10, gop + lambda_o / (float)G * o * (1.f - o));
 #pragma unroll
   for (int k = 1; k < 16; k++)
 #pragma unroll
-    for (int c = 0; c < 3; c++) gr_rest[3 * (k - 1) + c] = k < NB ? gco[k < NB ? k : 0][c] : 0.f;
+    for (int c = 0; c < 3; c++) put(14 + 3 * (k - 1) + c, k < NB ? gco[k < NB ? k : 0][c] : 0.f);
 }
 
 // Deterministic sum of the per-tile w_b partials; grads[59G] = sum * softplus'(w_b_raw).
@@ -275,6 +354,28 @@ __global__ void __launch_bounds__(1024) k_wb_reduce(const float* __restrict__ pa
   }
 }
 
+
+static int lanes_for(int V) { return V >= 8 ? 8 : V >= 4 ? 4 : V >= 2 ? 2 : 1; }
+
+template <int DEG, int LPG>
+static void launch_project(const float* params, int G, const float* cams, int V, int ntx, int nty, float blur,
+                           float near_plane, float* proj, float* mu2d, uint8_t* keep, int* cc, int2* cr, cudaStream_t st) {
+  constexpr int GPB = GB_THREADS / LPG;
+  k_project<DEG, LPG><<<(G + GPB - 1) / GPB, GB_THREADS, 0, st>>>(params, G, cams, V, ntx, nty, blur, near_plane, proj,
+                                                                   mu2d, keep, cc, cr);
+}
+
+template <int DEG>
+static void project_deg(int lpg, const float* params, int G, const float* cams, int V, int ntx, int nty, float blur,
+                        float near_plane, float* proj, float* mu2d, uint8_t* keep, int* cc, int2* cr, cudaStream_t st) {
+  switch (lpg) {
+    case 1: launch_project<DEG, 1>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, st); break;
+    case 2: launch_project<DEG, 2>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, st); break;
+    case 4: launch_project<DEG, 4>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, st); break;
+    default: launch_project<DEG, 8>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, st); break;
+  }
+}
+
 }  // namespace tts
 
 using namespace tts;
@@ -286,50 +387,64 @@ extern "C" int tts_project(const float* params, int G, int sh_degree, const floa
   TTS_REQUIRE(sh_degree >= 0 && sh_degree <= 3, "sh_degree must be in [0, 3]");
   TTS_REQUIRE(H > 0 && W > 0 && H % 16 == 0 && W % 16 == 0, "H and W must be positive multiples of 16");
   TTS_REQUIRE(aligned16(proj), "proj must be 16-byte aligned");
+  TTS_REQUIRE((long long)V * (H / 16) * (W / 16) < (1LL << 31), "V * tiles must fit in 31 bits");
   if (G == 0) return TTS_OK;
-  dim3 grid((G + 127) / 128, V);
   cudaStream_t st = as_stream(stream);
-  const int ntx = W / 16, nty = H / 16;
+  const int ntx = W / 16, nty = H / 16, lpg = lanes_for(V);
   int2* cr = reinterpret_cast<int2*>(cell_rank);
   switch (sh_degree) {
-    case 0: k_project<0><<<grid, 128, 0, st>>>(params, G, cams, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr); break;
-    case 1: k_project<1><<<grid, 128, 0, st>>>(params, G, cams, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr); break;
-    case 2: k_project<2><<<grid, 128, 0, st>>>(params, G, cams, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr); break;
-    default: k_project<3><<<grid, 128, 0, st>>>(params, G, cams, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr); break;
+    case 0: project_deg<0>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, st); break;
+    case 1: project_deg<1>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, st); break;
+    case 2: project_deg<2>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, st); break;
+    default: project_deg<3>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, st); break;
   }
   return check_launch("project");
 }
 
 extern "C" size_t tts_backward_workspace_bytes(int G, int V) {
-  return (G > 0 && V > 0) ? (size_t)V * G * 64 : 0;
+  return (G > 0 && V > 0) ? (size_t)V * G * 48 : 0;   // one gathered 12-float record per (view, gaussian)
 }
 
 extern "C" int tts_backward_params(const float* params, int G, int sh_degree, const float* cams, int V, int H, int W,
-                                   int R, int K, float k_poly, float blur, float near_plane, const int32_t* inv,
-                                   const float* slot_grads, const float* gwb_partial, float lambda_o, float lambda_s,
-                                   float* grads, void* workspace, size_t workspace_bytes, void* stream) {
+                                   int R, int K, float k_poly, float blur, float near_plane, const float* proj,
+                                   const int32_t* inv, const float* slot_grads, const float* gwb_partial,
+                                   float lambda_o, float lambda_s, float* grads, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
   TTS_REQUIRE(G >= 1 && V >= 1, "G and V must be >= 1");
   TTS_REQUIRE(sh_degree >= 0 && sh_degree <= 3, "sh_degree must be in [0, 3]");
   TTS_REQUIRE(H > 0 && W > 0 && H % 16 == 0 && W % 16 == 0, "H and W must be positive multiples of 16");
   TTS_REQUIRE(R >= 0 && R <= 3 && K >= 1 && K <= 256, "R in [0,3] and K in [1,256]");
+  TTS_REQUIRE(params && cams && proj && inv && slot_grads && gwb_partial && grads, "null pointer");
   TTS_REQUIRE(((uintptr_t)slot_grads & 7u) == 0, "slot_grads must be 8-byte aligned");
+  TTS_REQUIRE(aligned16(proj), "proj must be 16-byte aligned");
   TTS_REQUIRE(workspace && aligned16(workspace), "workspace must be a 16-byte aligned device buffer");
   if (workspace_bytes < tts_backward_workspace_bytes(G, V)) return fail(TTS_ERR_CAPACITY, "backward workspace too small");
   const int ntx = W / 16, nty = H / 16, S = (2 * R + 1) * (2 * R + 1);
   const float inv_k = (float)(1.0 / (double)k_poly);
   cudaStream_t st = as_stream(stream);
-  float4* scr = static_cast<float4*>(workspace);
-  dim3 gv((G + 127) / 128, V), g1((G + 127) / 128);
-#define TTS_BWD(D)                                                                                               \
-  k_backward_view<D><<<gv, 128, 0, st>>>(params, G, cams, ntx, nty, S, K, inv_k, blur, near_plane, inv, slot_grads, \
-                                         scr);                                                                    \
-  k_backward_reduce<D><<<g1, 128, 0, st>>>(params, G, cams, V, scr, lambda_o, lambda_s, grads);
-  switch (sh_degree) {
-    case 0: TTS_BWD(0) break;
-    case 1: TTS_BWD(1) break;
-    case 2: TTS_BWD(2) break;
-    default: TTS_BWD(3) break;
+  const int lpg = lanes_for(V);
+  float4* rec = static_cast<float4*>(workspace);
+  const long long nvg = (long long)V * G;
+  k_slot_gather<<<(unsigned)((nvg + 255) / 256), 256, 0, st>>>(proj, G, V, ntx, ntx * nty, S, K, inv_k, inv,
+                                                              slot_grads, rec);
+  if (int rc = check_launch("slot_gather")) return rc;
+#define TTS_BWD(D, P)                                                                                              \
+  k_backward<D, P><<<(G + GB_THREADS / P - 1) / (GB_THREADS / P), GB_THREADS, 0, st>>>(                           \
+      params, G, cams, V, blur, near_plane, rec, lambda_o, lambda_s, grads);
+#define TTS_BWD_DEG(D)            \
+  switch (lpg) {                  \
+    case 1: TTS_BWD(D, 1) break;  \
+    case 2: TTS_BWD(D, 2) break;  \
+    case 4: TTS_BWD(D, 4) break;  \
+    default: TTS_BWD(D, 8) break; \
   }
+  switch (sh_degree) {
+    case 0: TTS_BWD_DEG(0) break;
+    case 1: TTS_BWD_DEG(1) break;
+    case 2: TTS_BWD_DEG(2) break;
+    default: TTS_BWD_DEG(3) break;
+  }
+#undef TTS_BWD_DEG
 #undef TTS_BWD
   if (int rc = check_launch("backward_params")) return rc;
   k_wb_reduce<<<1, 1024, 0, st>>>(gwb_partial, V * ntx * nty, params, G, grads);

@@ -74,21 +74,28 @@ __global__ void __launch_bounds__(256)
     k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ m,
            float* __restrict__ v, int G, long long n, const int* __restrict__ step_ptr,
            const double* __restrict__ lr7, double beta1, double beta2, double eps) {
-  const int step = *step_ptr;
-  // scalars in double like the Python-side arithmetic of torch's Adam, cast to fp32 at use
-  const double bc1 = 1.0 - pow(beta1, (double)step);
-  const double bc2 = 1.0 - pow(beta2, (double)step);
-  AdamScalars a;
-  a.w1 = (float)(1.0 - beta1);
-  a.b2 = (float)beta2;
-  a.w2 = (float)(1.0 - beta2);
-  a.bc2_sqrt = (float)sqrt(bc2);
-  a.eps = (float)eps;
+  // scalars in double like the Python-side arithmetic of torch's Adam, cast to fp32 at use;
+  // computed once per block (the double pow is far costlier than the per-element update)
+  __shared__ AdamScalars s_a;
+  __shared__ float s_nss[7];
+  if (threadIdx.x == 0) {
+    const int step = *step_ptr;
+    const double bc1 = 1.0 - pow(beta1, (double)step);
+    const double bc2 = 1.0 - pow(beta2, (double)step);
+    s_a.w1 = (float)(1.0 - beta1);
+    s_a.b2 = (float)beta2;
+    s_a.w2 = (float)(1.0 - beta2);
+    s_a.bc2_sqrt = (float)sqrt(bc2);
+    s_a.eps = (float)eps;
+    for (int k = 0; k < 7; k++) s_nss[k] = (float)(-lr7[k] / bc1);
+  }
+  __syncthreads();
+  const AdamScalars a = s_a;
   float nss[6];
 #pragma unroll
-  for (int k = 0; k < 6; k++) nss[k] = (float)(-lr7[k] / bc1);
+  for (int k = 0; k < 6; k++) nss[k] = s_nss[k];
   const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (tid == 0) adam_elem(params, grads, m, v, 59LL * G, a, (float)(-lr7[6] / bc1));   // w_b_raw
+  if (tid == 0) adam_elem(params, grads, m, v, 59LL * G, a, s_nss[6]);   // w_b_raw
   const long long e0 = tid * 4;
   if (e0 >= n) return;
   if (e0 + 4 <= n) {

@@ -145,15 +145,19 @@ def loss_l1_ssim(img, target, lam=0.2, grad_scale=1.0, ws=None, out=None):
 
 
 def backward_params(flat, G, sh_degree, cams, H, W, R, K, inv, slot_grads, gwb, k=4.0, blur=0.3, near=0.2,
-                    lambda_o=0.0, lambda_s=0.0, out=None, ws=None):
+                    lambda_o=0.0, lambda_s=0.0, out=None, ws=None, proj=None):
+    """Parameter gradient from the per-slot gradients; ``proj`` is the projection of the same
+    parameters and cameras (recomputed when not given)."""
     _dev(flat, cams, inv, slot_grads, gwb)
     V = cams.shape[0]
+    if proj is None:
+        proj = project(flat, G, sh_degree, cams, H, W, blur, near)["proj"]
     grads = out if out is not None else torch.empty_like(flat)
     nbytes = lib().tts_backward_workspace_bytes(G, V)
     ws = ws or Workspace(flat.device)
     buf = ws.get(nbytes)
     call("tts_backward_params", ptr(flat), G, sh_degree, ptr(cams), V, H, W, R, K, float(k), float(blur), float(near),
-         ptr(inv), ptr(slot_grads), ptr(gwb), float(lambda_o), float(lambda_s), ptr(grads), ptr(buf), nbytes, stream())
+         ptr(proj), ptr(inv), ptr(slot_grads), ptr(gwb), float(lambda_o), float(lambda_s), ptr(grads), ptr(buf), nbytes, stream())
     return grads
 
 

@@ -29,17 +29,19 @@ class _BinnedRender(torch.autograd.Function):
         bp = ops.bin_pack(pj, G, H, W, R, K, k, with_inv=need_grad)
         slots = bp["slots"].to(torch.bfloat16).contiguous() if bf16 else bp["slots"]
         rf = ops.render_fwd(slots, bp["count"], H, W, flat_d[59 * G:], c_b, bf16=bf16)
-        ctx.save_for_backward(flat_d, cams_t, c_b, bp["slots"], bp["count"], bp["inv"], rf["img"], rf["den"])
+        ctx.save_for_backward(flat_d, cams_t, c_b, bp["slots"], bp["count"], bp["inv"], rf["img"], rf["den"],
+                              pj["proj"])
         ctx.cfg = cfg
         ctx.bins = bp
         return rf["img"]
 
     @staticmethod
     def backward(ctx, gimg):
-        flat, cams_t, c_b, slots, count, inv, img, den = ctx.saved_tensors
+        flat, cams_t, c_b, slots, count, inv, img, den, proj = ctx.saved_tensors
         G, sh_degree, H, W, R, K, k, blur, near, _ = ctx.cfg
         rb = ops.render_bwd(slots, count, H, W, c_b, img, den, gimg.contiguous())
-        grads = ops.backward_params(flat, G, sh_degree, cams_t, H, W, R, K, inv, rb["slot_grads"], rb["gwb"], k, blur, near)
+        grads = ops.backward_params(flat, G, sh_degree, cams_t, H, W, R, K, inv, rb["slot_grads"], rb["gwb"], k, blur, near,
+                                    proj=proj)
         return grads, None, None, None
 
 

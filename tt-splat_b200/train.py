@@ -131,7 +131,7 @@ class TrainStep:
                        self.lo["gimg"], out=self.rb)
         ops.backward_params(self.flat, G, self.sh_degree, self.cams_t, H, W, R, K, self.bp["inv"],
                             self.rb["slot_grads"], self.rb["gwb"], self.k, self.blur, self.near, self.lambda_o,
-                            self.lambda_s, out=self.grads, ws=self.ws_bwd)
+                            self.lambda_s, out=self.grads, ws=self.ws_bwd, proj=self.pj["proj"])
         torch.sum(self.lo["loss"], dim=0, keepdim=True, out=self.loss_mean)
 
     def _update(self, relocate):
