@@ -96,13 +96,9 @@ __global__ void __launch_bounds__(256)
   for (int k = 0; k < 6; k++) nss[k] = s_nss[k];
   const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (tid == 0) adam_elem(params, grads, m, v, 59LL * G, a, s_nss[6]);   // w_b_raw
-  const long long e0 = tid * 4;
-  if (e0 >= n) return;
-  if (e0 + 4 <= n) {
-    float4 p4 = *reinterpret_cast<const float4*>(params + e0);
-    const float4 g4 = *reinterpret_cast<const float4*>(grads + e0);
-    float4 m4 = *reinterpret_cast<const float4*>(m + e0);
-    float4 v4 = *reinterpret_cast<const float4*>(v + e0);
+  // grid-stride over 16-byte vectors, two vectors of each array in flight per thread
+  const long long nv = n / 4, stride = (long long)gridDim.x * blockDim.x;
+  auto update4 = [&](long long e0, float4& p4, const float4& g4, float4& m4, float4& v4) {
     float* pp = &p4.x;
     const float* gg = &g4.x;
     float* mm = &m4.x;
@@ -110,19 +106,42 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const float gr = gg[j];
-      float mj = __fadd_rn(mm[j], __fmul_rn(a.w1, __fsub_rn(gr, mm[j])));
-      float vj = __fadd_rn(__fmul_rn(vv[j], a.b2), __fmul_rn(__fmul_rn(a.w2, gr), gr));
+      const float mj = __fadd_rn(mm[j], __fmul_rn(a.w1, __fsub_rn(gr, mm[j])));
+      const float vj = __fadd_rn(__fmul_rn(vv[j], a.b2), __fmul_rn(__fmul_rn(a.w2, gr), gr));
       const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vj), a.bc2_sqrt), a.eps);
       pp[j] = __fadd_rn(pp[j], __fdiv_rn(__fmul_rn(lr_of(e0 + j, G, nss), mj), denom));
       mm[j] = mj;
       vv[j] = vj;
     }
-    *reinterpret_cast<float4*>(params + e0) = p4;
-    *reinterpret_cast<float4*>(m + e0) = m4;
-    *reinterpret_cast<float4*>(v + e0) = v4;
-  } else {
-    for (long long e = e0; e < n; ++e) adam_elem(params, grads, m, v, e, a, lr_of(e, G, nss));
+  };
+  float4* P = reinterpret_cast<float4*>(params);
+  const float4* Gr = reinterpret_cast<const float4*>(grads);
+  float4* M = reinterpret_cast<float4*>(m);
+  float4* Vv = reinterpret_cast<float4*>(v);
+  for (long long i = tid; i < nv; i += 2 * stride) {
+    const long long j = i + stride;
+    const bool two = j < nv;
+    float4 pa = P[i], ma = M[i], va = Vv[i];
+    const float4 ga = Gr[i];
+    float4 pb, mb, vb, gb;
+    if (two) {
+      pb = P[j];
+      mb = M[j];
+      vb = Vv[j];
+      gb = Gr[j];
+    }
+    update4(4 * i, pa, ga, ma, va);
+    P[i] = pa;
+    M[i] = ma;
+    Vv[i] = va;
+    if (two) {
+      update4(4 * j, pb, gb, mb, vb);
+      P[j] = pb;
+      M[j] = mb;
+      Vv[j] = vb;
+    }
   }
+  for (long long e = 4 * nv + tid; e < n; e += stride) adam_elem(params, grads, m, v, e, a, lr_of(e, G, nss));
 }
 
 // SGLD for every gaussian; the means learning rate is read from the device (lr_ptr[0], the
@@ -156,7 +175,9 @@ extern "C" int tts_adam_sgld(float* params, const float* grads, float* m, float*
   cudaStream_t st = as_stream(stream);
   // torch skips parameters without a gradient: the colour rest trains only with SH on
   const long long n = sh_degree > 0 ? 59LL * G : 14LL * G;
-  const long long blocks = (n + 4 * 256 - 1) / (4 * 256);
+  // two 16-byte vectors per thread per pass; at most 8 blocks of 256 per SM (148 SMs), looping
+  long long blocks = (n + 8 * 256 - 1) / (8 * 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
   k_adam<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, st>>>(params, grads, m, v, G, n, step, lr7, beta1, beta2, eps);
   if (int rc = check_launch("adam")) return rc;
   if (noise_lr > 0.f && G > 0) {

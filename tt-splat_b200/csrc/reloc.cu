@@ -1,172 +1,79 @@
 // 3DGS-MCMC relocation on the device (replaces relocate + reset_adam_state, spike/mcmc.py:41-87).
 //
+// One cooperative kernel (all blocks co-resident; phases separated by a grid barrier whose
+// wait is bounded) over contiguous per-block ranges of the gaussians:
 //   1. threshold: dead_thr, or the torch.quantile of the opacities at dead_frac, found by an
 //      exact MSB radix select (11/11/10-bit digits of the fp32 bit pattern, order-preserving
-//      for the non-negative opacities) of the two bracketing order statistics;
-//   2. per-block dead counts and alive opacity sums, one scan block, then the ascending dead
-//      list and the inclusive opacity CDF over the alive set (float64);
+//      for the non-negative opacities) of the two bracketing order statistics; every block
+//      reads the merged digit histogram and picks the same bucket;
+//   2. per-block dead counts and alive opacity sums; each block sums its predecessors in block
+//      order and writes its part of the ascending dead list and of the inclusive opacity CDF
+//      over the alive set (float64, one fixed summation order);
 //   3. one target per dead slot, drawn with replacement proportional to opacity (binary search
 //      of a Philox uniform in the CDF) or injected; per-target occurrence counts n;
 //   4. dead slots take the target's parameters (+ offset * N(0,1) on the means) and the split
-//      opacity logit(o_t / (n_t + 1)); targets get the same split; Adam moments of every
-//      touched gaussian are zeroed.  Steps run as separate stream-ordered kernels, so targets
-//      are read before their opacity is rewritten.
+//      opacity logit(o_t / (n_t + 1)); then targets get the same split (after a barrier, so the
+//      dead slots read the targets' old opacity); Adam moments of every touched gaussian are
+//      zeroed.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace tts {
 
-constexpr int RL_BLOCK = 1024;
+constexpr int RK_THREADS = 512;
+constexpr int STATUS_GRID_TIMEOUT = 2;
 
-struct RelocState {
-  unsigned pval[2], pmask[2];
-  int need[2];           // remaining rank (1-based) inside the current prefix
-  float thr;
-  int n_dead, n_alive;
-  double total;
-  int lo, hi;
-  float weight;
+struct GridBar {
+  unsigned count, gen;
 };
 
 __device__ __forceinline__ float opacity_of(const float* params, const ParamLayout& L, int g) {
   return sigmoidf(params[L.opacity() + g]);
 }
 
-__global__ void k_rl_init(RelocState* st, int G, float dead_thr, float dead_frac) {
-  st->pval[0] = st->pval[1] = 0u;
-  st->pmask[0] = st->pmask[1] = 0u;
-  if (dead_frac > 0.f) {
-    // torch.quantile: ranks = q * (n - 1) in the input dtype; below = long(ranks); above = ceil
-    const float ranks = dead_frac * (float)(G - 1);
-    st->lo = (int)ranks;
-    st->hi = (int)ceilf(ranks);
-    st->weight = ranks - (float)st->lo;
-  } else {
-    st->lo = st->hi = 0;
-    st->weight = 0.f;
-  }
-  st->need[0] = st->lo + 1;
-  st->need[1] = st->hi + 1;
-  st->thr = dead_thr;
-}
-
-__global__ void __launch_bounds__(256) k_rl_hist(const float* __restrict__ params, int G, int shift, int bits,
-                                                 const RelocState* __restrict__ st, int* __restrict__ hist) {
-  __shared__ int sh[2][2048];
-  const int nb = 1 << bits;
-  for (int i = threadIdx.x; i < 2 * nb; i += blockDim.x) sh[i / nb][i % nb] = 0;
-  __syncthreads();
-  const ParamLayout L{G};
-  const unsigned pv0 = st->pval[0], pm0 = st->pmask[0], pv1 = st->pval[1], pm1 = st->pmask[1];
-  for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < G; g += gridDim.x * blockDim.x) {
-    const unsigned b = __float_as_uint(opacity_of(params, L, g));
-    const unsigned d = (b >> shift) & (unsigned)(nb - 1);
-    if ((b & pm0) == pv0) atomicAdd(&sh[0][d], 1);
-    if ((b & pm1) == pv1) atomicAdd(&sh[1][d], 1);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 2 * nb; i += blockDim.x) {
-    const int c = sh[i / nb][i % nb];
-    if (c) atomicAdd(hist + i, c);
-  }
-}
-
-// Pick the bucket holding the needed rank for both selections: 256 threads scan 8 bins each.
-__global__ void __launch_bounds__(256) k_rl_pick(RelocState* st, int* hist, int shift, int bits) {
-  __shared__ int s_scan[8];
-  const int nb = 1 << bits;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const int per = nb / 256;      // 8 or 4 bins per thread
-  for (int w = 0; w < 2; ++w) {
-    const int need = st->need[w];   // read by every thread before the barrier below
-    int loc = 0;
-    for (int b = 0; b < per; ++b) loc += hist[w * nb + tid * per + b];
-    int incl = loc;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += y;
-    }
-    if (lane == 31) s_scan[wid] = incl;
-    __syncthreads();
-    int base = 0;
-    for (int i = 0; i < wid; ++i) base += s_scan[i];
-    const int excl = base + incl - loc;
-    if (excl < need && need <= excl + loc) {
-      int c = excl, b = 0;
-      for (; b < per - 1; ++b) {
-        if (c + hist[w * nb + tid * per + b] >= need) break;
-        c += hist[w * nb + tid * per + b];
-      }
-      st->need[w] = need - c;
-      st->pval[w] |= (unsigned)(tid * per + b) << shift;
-      st->pmask[w] |= (unsigned)(nb - 1) << shift;
-    }
-    __syncthreads();
-  }
-  for (int i = tid; i < 2 * 2048; i += blockDim.x) hist[i] = 0;
-}
-
-__global__ void k_rl_thr(RelocState* st) {
-  const float lo = __uint_as_float(st->pval[0]), hi = __uint_as_float(st->pval[1]);
-  const float w = st->weight;
-  // torch lerp: weight < 0.5 ? a + w (b - a) : b - (b - a)(1 - w)
-  st->thr = w < 0.5f ? lo + w * (hi - lo) : hi - (hi - lo) * (1.f - w);
-}
-
-// Block-level dead count and alive opacity sum (double), in a fixed reduction order.
-__global__ void __launch_bounds__(RL_BLOCK) k_rl_count(const float* __restrict__ params, int G,
-                                                       const RelocState* __restrict__ st, int* __restrict__ bcnt,
-                                                       double* __restrict__ bsum) {
-  __shared__ int sc[RL_BLOCK / 32];
-  __shared__ double ss[RL_BLOCK / 32];
-  const ParamLayout L{G};
-  const int g = blockIdx.x * RL_BLOCK + threadIdx.x;
-  int dead = 0;
-  double alive = 0.0;
-  if (g < G) {
-    const float o = opacity_of(params, L, g);
-    if (o < st->thr) dead = 1;
-    else alive = (double)o;
-  }
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) {
-    dead += __shfl_xor_sync(0xffffffffu, dead, d);
-    alive += __shfl_xor_sync(0xffffffffu, alive, d);
-  }
-  if ((threadIdx.x & 31) == 0) {
-    sc[threadIdx.x >> 5] = dead;
-    ss[threadIdx.x >> 5] = alive;
-  }
+// Grid-wide barrier for a cooperative launch: the last block to arrive resets the count and
+// bumps the generation; the others wait for the new generation with an iteration limit (on
+// timeout the status word records it and the kernel unwinds: every later barrier also gives up).
+__device__ __forceinline__ bool grid_sync(GridBar* bar, unsigned nblocks, int* s_flag) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    int c = 0;
-    double s = 0.0;
-    for (int i = 0; i < RL_BLOCK / 32; ++i) {
-      c += sc[i];
-      s += ss[i];
+    volatile unsigned* vgen = &bar->gen;
+    const unsigned gen = *vgen;
+    __threadfence();
+    const unsigned arrived = atomicAdd(&bar->count, 1u);
+    int ok = 1;
+    if (arrived == nblocks - 1) {
+      bar->count = 0u;
+      __threadfence();
+      atomicAdd(&bar->gen, 1u);
+    } else {
+      int it = 0;
+      while (*vgen == gen) {
+        if (++it > (1 << 24)) {
+          ok = 0;
+          atomicOr(&g_status, STATUS_GRID_TIMEOUT);
+          break;
+        }
+        __nanosleep(64);
+      }
     }
-    bcnt[blockIdx.x] = c;
-    bsum[blockIdx.x] = s;
+    __threadfence();
+    *s_flag = ok;
   }
+  __syncthreads();
+  return *s_flag != 0;
 }
 
-// Exclusive scan of the per-block dead counts and alive sums (one block; blocks of the
-// opacity array are split into contiguous runs per thread, so the order of the sums is fixed).
-__global__ void __launch_bounds__(1024) k_rl_scan(int nblk, int G, int* bcnt, double* bsum, RelocState* st,
-                                                  int* n_dead_out) {
-  __shared__ int sc[32];
-  __shared__ double ss[32];
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const int per = (nblk + 1023) / 1024;
-  const int beg = min(nblk, tid * per), end = min(nblk, beg + per);
-  int c = 0;
-  double s = 0.0;
-  for (int b = beg; b < end; ++b) {
-    c += bcnt[b];
-    s += bsum[b];
-  }
-  int ci = c;
-  double si = s;
+// Block-wide inclusive scan of (int, double) pairs in thread order; returns the block totals.
+struct ScanPair {
+  int c;
+  double s;
+};
+__device__ __forceinline__ ScanPair block_incl_scan(int c, double x, int& ci, double& si, ScanPair* s_w) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  ci = c;
+  si = x;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
     const int yc = __shfl_up_sync(0xffffffffu, ci, d);
@@ -176,111 +83,53 @@ __global__ void __launch_bounds__(1024) k_rl_scan(int nblk, int G, int* bcnt, do
       si += ys;
     }
   }
-  if (lane == 31) {
-    sc[wid] = ci;
-    ss[wid] = si;
-  }
+  if (lane == 31) s_w[wid] = ScanPair{ci, si};
   __syncthreads();
   int cb = 0;
   double sb = 0.0;
   for (int w = 0; w < wid; ++w) {
-    cb += sc[w];
-    sb += ss[w];
+    cb += s_w[w].c;
+    sb += s_w[w].s;
   }
-  int runc = cb + ci - c;
-  double runs = sb + si - s;
-  for (int b = beg; b < end; ++b) {
-    const int x = bcnt[b];
-    const double y = bsum[b];
-    bcnt[b] = runc;
-    bsum[b] = runs;
-    runc += x;
-    runs += y;
-  }
-  if (tid == 1023) {
-    const int n_dead = runc;
-    const int n_alive = G - n_dead;
-    st->n_dead = (n_dead == 0 || n_alive == 0) ? 0 : n_dead;   // the reference moves nothing then
-    st->n_alive = n_alive;
-    st->total = runs;
-    *n_dead_out = st->n_dead;
-  }
-}
-
-__global__ void __launch_bounds__(RL_BLOCK) k_rl_lists(const float* __restrict__ params, int G,
-                                                       const RelocState* __restrict__ st, const int* __restrict__ bcnt,
-                                                       const double* __restrict__ bsum, int* __restrict__ dead_list,
-                                                       double* __restrict__ cdf) {
-  __shared__ int sc[RL_BLOCK / 32];
-  __shared__ double ss[RL_BLOCK / 32];
-  const ParamLayout L{G};
-  const int g = blockIdx.x * RL_BLOCK + threadIdx.x;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  int dead = 0;
-  double alive = 0.0;
-  if (g < G) {
-    const float o = opacity_of(params, L, g);
-    if (o < st->thr) dead = 1;
-    else alive = (double)o;
-  }
-  int ci = dead;
-  double si = alive;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int yc = __shfl_up_sync(0xffffffffu, ci, d);
-    const double ys = __shfl_up_sync(0xffffffffu, si, d);
-    if (lane >= d) {
-      ci += yc;
-      si += ys;
-    }
-  }
-  if (lane == 31) {
-    sc[wid] = ci;
-    ss[wid] = si;
+  ci += cb;
+  si += sb;
+  ScanPair tot{0, 0.0};
+  for (int w = 0; w < RK_THREADS / 32; ++w) {
+    tot.c += s_w[w].c;
+    tot.s += s_w[w].s;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int c = 0;
-    double s = 0.0;
-    for (int i = 0; i < RL_BLOCK / 32; ++i) {
-      const int tc = sc[i];
-      const double ts = ss[i];
-      sc[i] = c;
-      ss[i] = s;
-      c += tc;
-      s += ts;
-    }
-  }
-  __syncthreads();
-  if (g >= G) return;
-  const int rank = bcnt[blockIdx.x] + sc[wid] + ci - dead;
-  const double incl = bsum[blockIdx.x] + ss[wid] + si;
-  if (dead) dead_list[rank] = g;
-  cdf[g] = incl;
+  return tot;
 }
 
-__global__ void k_rl_sample(const RelocState* __restrict__ st, const double* __restrict__ cdf, int G,
-                            const int* __restrict__ targets_in, const int* __restrict__ step_ptr,
-                            unsigned long long seed, int* __restrict__ targets, int* __restrict__ nat) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= st->n_dead) return;
-  int t;
-  if (targets_in) {
-    t = targets_in[i];
-  } else {
-    const U4 r = philox4x32_10(U4{(uint32_t)i, 1u, (uint32_t)*step_ptr, 0x524cu}, (uint32_t)seed, (uint32_t)(seed >> 32));
-    const double u = ((double)(r.x >> 5) * 67108864.0 + (double)(r.y >> 6)) * (1.0 / 9007199254740992.0);
-    const double x = u * st->total;
-    int lo = 0, hi = G - 1;   // first g with cdf[g] > x (always an alive gaussian)
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (cdf[mid] > x) hi = mid;
-      else lo = mid + 1;
-    }
-    t = lo;
-  }
-  targets[i] = t;
-  atomicAdd(nat + t, 1);
+struct RelocArgs {
+  float* params;
+  float* m;
+  float* v;
+  int G;
+  float dead_thr, dead_frac, offset;
+  const int* targets_in;
+  const float* noise_in;
+  const int* step_ptr;
+  unsigned long long seed;
+  int* n_dead_out;
+  int* targets;
+  GridBar* bar;
+  int* hist;        // [3 passes][2 selections][2048]
+  int* bcnt;        // [nblocks]
+  double* bsum;     // [nblocks]
+  int* dead_list;   // [G]
+  double* cdf;      // [G]
+  int* nat;         // [G], zeroed before the launch
+};
+
+__device__ __forceinline__ long long field_index(const ParamLayout& L, int f, int x) {
+  return f < 3 ? L.means() + 3LL * x + f
+       : f < 6 ? L.log_scales() + 3LL * x + (f - 3)
+       : f < 10 ? L.quats() + 4LL * x + (f - 6)
+       : f < 11 ? L.opacity() + (long long)x
+       : f < 14 ? L.color_dc() + 3LL * x + (f - 11)
+       : L.color_rest() + 45LL * x + (f - 14);
 }
 
 __device__ __forceinline__ float split_logit(float o, int n) {
@@ -303,90 +152,270 @@ __device__ __forceinline__ void zero_moments(float* m, float* v, const ParamLayo
   for (int c = 0; c < 45; c++) { m[L.color_rest() + 45 * g + c] = 0.f; v[L.color_rest() + 45 * g + c] = 0.f; }
 }
 
-// One warp per dead slot: lanes copy the 59 parameters of the target and zero the moments.
-__global__ void __launch_bounds__(256)
-    k_rl_apply_dead(float* __restrict__ params, float* __restrict__ m, float* __restrict__ v, int G,
-                    const RelocState* __restrict__ st, const int* __restrict__ dead_list,
-                    const int* __restrict__ targets, const int* __restrict__ nat, float offset,
-                    const float* __restrict__ noise_in, const int* __restrict__ step_ptr, unsigned long long seed) {
-  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (i >= st->n_dead) return;
-  const ParamLayout L{G};
-  const int d = dead_list[i], t = targets[i];
-  // field f of the 59 per-gaussian parameters -> flat index for gaussian x
-  auto at = [&](int f, int x) -> long long {
-    return f < 3 ? L.means() + 3LL * x + f
-         : f < 6 ? L.log_scales() + 3LL * x + (f - 3)
-         : f < 10 ? L.quats() + 4LL * x + (f - 6)
-         : f < 11 ? L.opacity() + (long long)x
-         : f < 14 ? L.color_dc() + 3LL * x + (f - 11)
-         : L.color_rest() + 45LL * x + (f - 14);
-  };
-  float e[3] = {0.f, 0.f, 0.f};
-  if (lane < 3) {
-    if (noise_in) {
-      e[0] = noise_in[3 * i + lane];
+__global__ void __launch_bounds__(RK_THREADS) k_relocate(RelocArgs a) {
+  __shared__ __align__(16) int sh[2][2048];
+  __shared__ ScanPair s_w[RK_THREADS / 32];
+  __shared__ int s_flag;
+  __shared__ unsigned s_pval[2], s_pmask[2];
+  __shared__ int s_need[2];
+  __shared__ int s_pick[2][2];     // (bucket, rank consumed before it) per selection
+  const ParamLayout L{a.G};
+  const int G = a.G, tid = threadIdx.x;
+  const unsigned nb = gridDim.x;
+  const int chunk = (G + (int)nb - 1) / (int)nb;
+  const int beg = min(G, (int)blockIdx.x * chunk), end = min(G, beg + chunk);
+  // ---- 1. threshold ----------------------------------------------------------------------------
+  float thr = a.dead_thr;
+  if (a.dead_frac > 0.f) {
+    // torch.quantile: ranks = q * (n - 1) in the input dtype; below = long(ranks); above = ceil
+    const float ranks = a.dead_frac * (float)(G - 1);
+    const int lo = (int)ranks, hi = (int)ceilf(ranks);
+    const float weight = ranks - (float)lo;
+    if (tid < 2) {
+      s_pval[tid] = 0u;
+      s_pmask[tid] = 0u;
+      s_need[tid] = (tid == 0 ? lo : hi) + 1;
+    }
+    const int shifts[3] = {21, 10, 0}, bits[3] = {11, 11, 10};
+    for (int d = 0; d < 3; ++d) {
+      const int nbins = 1 << bits[d];
+      for (int i = tid; i < 2 * 2048; i += RK_THREADS) sh[i >> 11][i & 2047] = 0;
+      __syncthreads();
+      const unsigned pv0 = s_pval[0], pm0 = s_pmask[0], pv1 = s_pval[1], pm1 = s_pmask[1];
+      for (int g = beg + tid; g < end; g += RK_THREADS) {
+        const unsigned b = __float_as_uint(opacity_of(a.params, L, g));
+        const unsigned dg = (b >> shifts[d]) & (unsigned)(nbins - 1);
+        if ((b & pm0) == pv0) atomicAdd(&sh[0][dg], 1);
+        if ((b & pm1) == pv1) atomicAdd(&sh[1][dg], 1);
+      }
+      __syncthreads();
+      int* gh = a.hist + d * 2 * 2048;
+      for (int i = tid; i < 2 * nbins; i += RK_THREADS) {
+        const int w = i / nbins, bin = i - w * nbins;
+        const int c = sh[w][bin];
+        if (c) atomicAdd(gh + w * 2048 + bin, c);
+      }
+      if (!grid_sync(a.bar, nb, &s_flag)) return;
+      // every block picks the same buckets from the merged histogram
+      for (int w = 0; w < 2; ++w) {
+        const int need = s_need[w];
+        const int per = nbins / RK_THREADS;        // 4 or 2 bins per thread
+        int loc = 0;
+        for (int q = 0; q < per; ++q) loc += __ldcg(gh + w * 2048 + tid * per + q);
+        int ci;
+        double si;
+        block_incl_scan(loc, 0.0, ci, si, s_w);
+        const int excl = ci - loc;
+        if (excl < need && need <= ci) {
+          int c = excl, q = 0;
+          for (; q < per - 1; ++q) {
+            const int h = __ldcg(gh + w * 2048 + tid * per + q);
+            if (c + h >= need) break;
+            c += h;
+          }
+          s_pick[w][0] = tid * per + q;
+          s_pick[w][1] = c;
+        }
+        __syncthreads();
+        if (tid == 0) {
+          s_need[w] = need - s_pick[w][1];
+          s_pval[w] |= (unsigned)s_pick[w][0] << shifts[d];
+          s_pmask[w] |= (unsigned)(nbins - 1) << shifts[d];
+        }
+        __syncthreads();
+      }
+    }
+    const float olo = __uint_as_float(s_pval[0]), ohi = __uint_as_float(s_pval[1]);
+    // torch lerp: weight < 0.5 ? a + w (b - a) : b - (b - a)(1 - w)
+    thr = weight < 0.5f ? olo + weight * (ohi - olo) : ohi - (ohi - olo) * (1.f - weight);
+  }
+  // ---- 2. counts, dead list, CDF ----------------------------------------------------------------
+  // block totals: tiles of RK_THREADS in ascending order, each by the same block scan that the
+  // list pass repeats (so a block's last CDF entry equals its total bit for bit)
+  int bc = 0;
+  double bs = 0.0;
+  for (int base = beg; base < end; base += RK_THREADS) {
+    const int g = base + tid;
+    int dead = 0;
+    double alive = 0.0;
+    if (g < end) {
+      const float o = opacity_of(a.params, L, g);
+      if (o < thr) dead = 1;
+      else alive = (double)o;
+    }
+    int ci;
+    double si;
+    const ScanPair t = block_incl_scan(dead, alive, ci, si, s_w);
+    bc += t.c;
+    bs += t.s;
+  }
+  if (tid == 0) {
+    a.bcnt[blockIdx.x] = bc;
+    a.bsum[blockIdx.x] = bs;
+  }
+  if (!grid_sync(a.bar, nb, &s_flag)) return;
+  // predecessors (in block order) and the totals, summed identically by every block: the
+  // per-block values are fetched in parallel, then added in block order by one thread
+  int* s_bc = &sh[0][0];
+  double* s_bs = reinterpret_cast<double*>(&sh[1][0]);       // nb <= 1024 doubles fit in sh[1]
+  for (unsigned b = tid; b < nb; b += RK_THREADS) {
+    s_bc[b] = __ldcg(a.bcnt + b);
+    s_bs[b] = __ldcg(a.bsum + b);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int c = 0, cpre = 0;
+    double s = 0.0, spre = 0.0;
+    for (unsigned b = 0; b < nb; ++b) {
+      if (b == blockIdx.x) {
+        cpre = c;
+        spre = s;
+      }
+      c += s_bc[b];
+      s += s_bs[b];
+    }
+    s_w[0] = ScanPair{cpre, spre};
+    s_w[1] = ScanPair{c, s};
+  }
+  __syncthreads();
+  int runc = s_w[0].c;
+  const double spre = s_w[0].s;
+  double runs = 0.0;     // in-block running sum, associated like the block total above
+  const int n_dead_all = s_w[1].c;
+  const double total = s_w[1].s;
+  __syncthreads();
+  const int n_alive = G - n_dead_all;
+  const int n_dead = (n_dead_all == 0 || n_alive == 0) ? 0 : n_dead_all;   // the reference moves nothing then
+  if (blockIdx.x == 0 && tid == 0) *a.n_dead_out = n_dead;
+  if (n_dead == 0) return;            // uniform across the grid
+  for (int base = beg; base < end; base += RK_THREADS) {
+    const int g = base + tid;
+    int dead = 0;
+    double alive = 0.0;
+    if (g < end) {
+      const float o = opacity_of(a.params, L, g);
+      if (o < thr) dead = 1;
+      else alive = (double)o;
+    }
+    int ci;
+    double si;
+    const ScanPair t = block_incl_scan(dead, alive, ci, si, s_w);
+    if (g < end) {
+      if (dead) a.dead_list[runc + ci - 1] = g;
+      // spre + (in-block inclusive sum): the block's last entry is spre + its total, the next
+      // block's prefix exactly, and the grid's last entry equals the total
+      a.cdf[g] = spre + (runs + si);
+    }
+    runc += t.c;
+    runs += t.s;
+  }
+  if (!grid_sync(a.bar, nb, &s_flag)) return;
+  // ---- 3. targets: one warp per dead slot; the CDF search splits the range 33 ways per round
+  // (32 pivots loaded at once), so a search takes ~log33(G) dependent loads instead of log2(G)
+  const int step = *a.step_ptr;
+  const int lane = tid & 31;
+  const int nwarps = (int)nb * (RK_THREADS / 32);
+  for (int i = blockIdx.x * (RK_THREADS / 32) + (tid >> 5); i < n_dead; i += nwarps) {
+    int t;
+    if (a.targets_in) {
+      t = a.targets_in[i];
     } else {
-      const U4 r = philox4x32_10(U4{(uint32_t)i, 2u, (uint32_t)*step_ptr, 0x4f46u}, (uint32_t)seed, (uint32_t)(seed >> 32));
-      float n3;
-      box_muller(r.x, r.y, e[0], e[1]);
-      box_muller(r.z, r.w, e[2], n3);
-      e[0] = e[lane];
+      const U4 r = philox4x32_10(U4{(uint32_t)i, 1u, (uint32_t)step, 0x524cu}, (uint32_t)a.seed,
+                                 (uint32_t)(a.seed >> 32));
+      const double u = ((double)(r.x >> 5) * 67108864.0 + (double)(r.y >> 6)) * (1.0 / 9007199254740992.0);
+      double x = u * total;
+      if (x >= total) x = nextafter(total, 0.0);   // u < 1, but the product can round up
+      // first g with cdf[g] > x (always an alive gaussian): the answer lies in [lo, hi)
+      int lo = 0, hi = G;
+      while (hi - lo > 32) {
+        const long long span = hi - lo;
+        const int piv = lo + (int)(span * (lane + 1) / 33);
+        const unsigned bal = __ballot_sync(0xffffffffu, __ldcg(a.cdf + piv) > x);
+        const int f = bal ? __ffs(bal) - 1 : 32;
+        const int nlo = f > 0 ? lo + (int)(span * f / 33) + 1 : lo;
+        const int nhi = f < 32 ? lo + (int)(span * (f + 1) / 33) + 1 : hi;
+        lo = nlo;
+        hi = nhi;
+      }
+      const int gq = lo + lane;
+      const unsigned bal = __ballot_sync(0xffffffffu, gq < hi && __ldcg(a.cdf + gq) > x);
+      t = bal ? lo + __ffs(bal) - 1 : hi - 1;
+    }
+    if (lane == 0) {
+      a.targets[i] = t;
+      atomicAdd(a.nat + t, 1);
     }
   }
-  for (int f = lane; f < 59; f += 32) {
-    const long long src = at(f, t), dst = at(f, d);
-    float val;
-    if (f < 3) val = params[src] + offset * e[0];
-    else if (f == 10) val = split_logit(opacity_of(params, L, t), nat[t] + 1);
-    else val = params[src];
-    params[dst] = val;
-    m[dst] = 0.f;
-    v[dst] = 0.f;
+  if (!grid_sync(a.bar, nb, &s_flag)) return;
+  // ---- 4a. dead slots: one warp per slot copies the target's 59 parameters --------------------
+  for (int i = blockIdx.x * (RK_THREADS / 32) + (tid >> 5); i < n_dead; i += nwarps) {
+    const int d = __ldcg(a.dead_list + i), t = __ldcg(a.targets + i);
+    float e = 0.f;
+    if (lane < 3) {
+      if (a.noise_in) {
+        e = a.noise_in[3 * i + lane];
+      } else {
+        const U4 r = philox4x32_10(U4{(uint32_t)i, 2u, (uint32_t)step, 0x4f46u}, (uint32_t)a.seed,
+                                   (uint32_t)(a.seed >> 32));
+        float n0, n1, n2, n3;
+        box_muller(r.x, r.y, n0, n1);
+        box_muller(r.z, r.w, n2, n3);
+        e = lane == 0 ? n0 : lane == 1 ? n1 : n2;
+      }
+    }
+    const int nt = __ldcg(a.nat + t);
+    for (int f = lane; f < 59; f += 32) {
+      const long long src = field_index(L, f, t), dst = field_index(L, f, d);
+      float val;
+      if (f < 3) val = a.params[src] + a.offset * e;
+      else if (f == 10) val = split_logit(opacity_of(a.params, L, t), nt + 1);
+      else val = a.params[src];
+      a.params[dst] = val;
+      a.m[dst] = 0.f;
+      a.v[dst] = 0.f;
+    }
   }
-}
-
-__global__ void k_rl_apply_targets(float* __restrict__ params, float* __restrict__ m, float* __restrict__ v, int G,
-                                   const int* __restrict__ nat) {
-  const int g = blockIdx.x * blockDim.x + threadIdx.x;
-  if (g >= G) return;
-  const int n = nat[g];
-  if (n == 0) return;
-  const ParamLayout L{G};
-  params[L.opacity() + g] = split_logit(opacity_of(params, L, g), n + 1);
-  zero_moments(m, v, L, g);
+  if (!grid_sync(a.bar, nb, &s_flag)) return;
+  // ---- 4b. targets: split opacity, zero moments ------------------------------------------------
+  for (int g = beg + tid; g < end; g += RK_THREADS) {
+    const int n = __ldcg(a.nat + g);
+    if (n == 0) continue;
+    a.params[L.opacity() + g] = split_logit(opacity_of(a.params, L, g), n + 1);
+    zero_moments(a.m, a.v, L, g);
+  }
 }
 
 static size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
-struct RelocWs {
-  RelocState* st;
-  int* hist;
-  int* bcnt;
-  double* bsum;
-  int* dead_list;
-  double* cdf;
-  int* nat;
-};
+static int reloc_grid() {
+  int dev = 0, sms = 0, per = 0;
+  cudaGetDevice(&dev);
+  static int cached[64] = {0};
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_relocate, RK_THREADS, 0);
+  int n = sms * (per > 2 ? 2 : per);      // co-resident by construction; two blocks per SM at most
+  if (n < 1) n = 1;
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  return n;
+}
 
-static size_t reloc_bytes(int G, RelocWs* w, char* base) {
-  const int nblk = (G + RL_BLOCK - 1) / RL_BLOCK;
+static size_t reloc_bytes(int G, int nblk, RelocArgs* w, char* base) {
   size_t off = 0;
   auto take = [&](size_t n) {
     char* p = base ? base + off : nullptr;
     off += a256(n);
     return p;
   };
-  char* p0 = take(sizeof(RelocState));
-  char* p1 = take(2 * 2048 * 4);
+  char* p0 = take(sizeof(GridBar));
+  char* p1 = take(3 * 2 * 2048 * 4);
   char* p2 = take((size_t)nblk * 4);
   char* p3 = take((size_t)nblk * 8);
   char* p4 = take((size_t)G * 4);
   char* p5 = take((size_t)G * 8);
   char* p6 = take((size_t)G * 4);
   if (w) {
-    w->st = reinterpret_cast<RelocState*>(p0);
+    w->bar = reinterpret_cast<GridBar*>(p0);
     w->hist = reinterpret_cast<int*>(p1);
     w->bcnt = reinterpret_cast<int*>(p2);
     w->bsum = reinterpret_cast<double*>(p3);
@@ -401,7 +430,8 @@ static size_t reloc_bytes(int G, RelocWs* w, char* base) {
 
 using namespace tts;
 
-extern "C" size_t tts_relocate_workspace_bytes(int G) { return G > 0 ? reloc_bytes(G, nullptr, nullptr) : 0; }
+// Sized for up to 1024 blocks, more than any grid reloc_grid() returns.
+extern "C" size_t tts_relocate_workspace_bytes(int G) { return G > 0 ? reloc_bytes(G, 1024, nullptr, nullptr) : 0; }
 
 extern "C" int tts_relocate(float* params, float* m, float* v, int G, float dead_thr, float dead_frac, float offset,
                             const int32_t* targets_in, const float* offset_noise_in, const int32_t* step, uint64_t seed,
@@ -411,28 +441,37 @@ extern "C" int tts_relocate(float* params, float* m, float* v, int G, float dead
   TTS_REQUIRE(params && m && v && step && n_dead_out && targets_out && workspace, "null pointer");
   TTS_REQUIRE(dead_frac < 1.f, "dead_frac must be < 1");
   if (workspace_bytes < tts_relocate_workspace_bytes(G)) return fail(TTS_ERR_CAPACITY, "relocation workspace too small");
-  RelocWs w;
-  reloc_bytes(G, &w, static_cast<char*>(workspace));
+  RelocArgs a;
+  const int nblk = std::min(reloc_grid(), 1024);
+  reloc_bytes(G, 1024, &a, static_cast<char*>(workspace));
+  a.params = params;
+  a.m = m;
+  a.v = v;
+  a.G = G;
+  a.dead_thr = dead_thr;
+  a.dead_frac = dead_frac;
+  a.offset = offset;
+  a.targets_in = targets_in;
+  a.noise_in = offset_noise_in;
+  a.step_ptr = step;
+  a.seed = seed;
+  a.n_dead_out = n_dead_out;
+  a.targets = targets_out;
   cudaStream_t st = as_stream(stream);
-  const int nblk = (G + RL_BLOCK - 1) / RL_BLOCK;
-  if (cudaMemsetAsync(w.hist, 0, 2 * 2048 * 4, st) != cudaSuccess) return check_launch("memset hist");
-  if (cudaMemsetAsync(w.nat, 0, (size_t)G * 4, st) != cudaSuccess) return check_launch("memset nat");
-  k_rl_init<<<1, 1, 0, st>>>(w.st, G, dead_thr, dead_frac);
-  if (dead_frac > 0.f) {
-    const int shifts[3] = {21, 10, 0}, bits[3] = {11, 11, 10};
-    const int hb = min(148 * 4, (G + 255) / 256);
-    for (int d = 0; d < 3; ++d) {
-      k_rl_hist<<<hb, 256, 0, st>>>(params, G, shifts[d], bits[d], w.st, w.hist);
-      k_rl_pick<<<1, 256, 0, st>>>(w.st, w.hist, shifts[d], bits[d]);
-    }
-    k_rl_thr<<<1, 1, 0, st>>>(w.st);
-  }
-  k_rl_count<<<nblk, RL_BLOCK, 0, st>>>(params, G, w.st, w.bcnt, w.bsum);
-  k_rl_scan<<<1, 1024, 0, st>>>(nblk, G, w.bcnt, w.bsum, w.st, n_dead_out);
-  k_rl_lists<<<nblk, RL_BLOCK, 0, st>>>(params, G, w.st, w.bcnt, w.bsum, w.dead_list, w.cdf);
-  k_rl_sample<<<(G + 255) / 256, 256, 0, st>>>(w.st, w.cdf, G, targets_in, step, seed, targets_out, w.nat);
-  k_rl_apply_dead<<<(unsigned)(((long long)G * 32 + 255) / 256), 256, 0, st>>>(params, m, v, G, w.st, w.dead_list, targets_out, w.nat, offset,
-                                                    offset_noise_in, step, seed);
-  k_rl_apply_targets<<<(G + 255) / 256, 256, 0, st>>>(params, m, v, G, w.nat);
+  // the barrier word, the digit histograms and the per-target counts start at zero
+  const size_t head = reinterpret_cast<char*>(a.bcnt) - static_cast<char*>(workspace);
+  if (cudaMemsetAsync(workspace, 0, head, st) != cudaSuccess) return check_launch("memset relocation state");
+  if (cudaMemsetAsync(a.nat, 0, (size_t)G * 4, st) != cudaSuccess) return check_launch("memset nat");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)nblk);
+  cfg.blockDim = dim3(RK_THREADS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, k_relocate, a) != cudaSuccess) return check_launch("relocate (cooperative launch)");
   return check_launch("relocate");
 }
