@@ -218,6 +218,51 @@ constexpr int WB_WARPS = 4;
 constexpr int WCAP = 1024;
 constexpr int WTIES = 64;   // ties at the selection boundary resolved by rank (more: sorted with the rest)
 
+// Warp bucket sort of keys[0, m) (m <= WCAP/2; the upper half of the warp's buffer is the
+// scratch): keys are distributed into 64 buckets by the top 6 bits of their 11-bit distance
+// (exclusive offsets from a histogram), then each key's position inside its bucket is its rank
+// among the bucket's keys (keys are unique: one stencil offset per gaussian and tile).  Buckets
+// beyond 64 keys would make the ranking quadratic: the caller then falls back to the bitonic
+// sort.  Returns false (keys untouched) in that case.
+__device__ __forceinline__ bool bucket_sort(u64* keys, int m, int lane, int* hist, int* start) {
+  u64* tmp = keys + WCAP / 2;
+  hist[lane] = 0;
+  hist[lane + 32] = 0;
+  __syncwarp();
+  for (int i = lane; i < m; i += 32) atomicAdd(&hist[(int)((keys[i] >> 45) & 63ull)], 1);
+  __syncwarp();
+  const int h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
+  if (__any_sync(0xffffffffu, h0 > 64 || h1 > 64)) return false;
+  int incl = h0 + h1;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  const int excl = incl - h0 - h1;
+  start[2 * lane] = excl;
+  start[2 * lane + 1] = excl + h0;
+  hist[2 * lane] = excl;            // hist becomes the scatter cursor
+  hist[2 * lane + 1] = excl + h0;
+  if (lane == 31) start[64] = incl;
+  __syncwarp();
+  for (int i = lane; i < m; i += 32) {
+    const u64 k = keys[i];
+    tmp[atomicAdd(&hist[(int)((k >> 45) & 63ull)], 1)] = k;
+  }
+  __syncwarp();
+  for (int i = lane; i < m; i += 32) {
+    const u64 k = tmp[i];
+    const int b = (int)((k >> 45) & 63ull);
+    const int s = start[b], e = start[b + 1];
+    int r = 0;
+    for (int t = s; t < e; ++t) r += tmp[t] < k;
+    keys[s + r] = k;
+  }
+  __syncwarp();
+  return true;
+}
+
 // Warp-synchronous bitonic sort of keys[0, m) in place (padded with ~0 up to the next power of
 // two, which must fit the buffer).
 __device__ __forceinline__ void sort_front(u64* keys, int m, int lane) {
@@ -254,6 +299,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
                int* __restrict__ ovf_list, int* __restrict__ ovf_count) {
   extern __shared__ u64 wsm[];
   __shared__ int whist[WB_WARPS][64];
+  __shared__ int wstart[WB_WARPS][65];
   __shared__ u64 wties[WB_WARPS][WTIES];
   __shared__ int wbeg[WB_WARPS][BS_MAXS], wlen[WB_WARPS][BS_MAXS], woff[WB_WARPS][BS_MAXS + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -361,7 +407,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
         tw += __popc(be);
         __syncwarp();
       }
-      sort_front(buf, c_lt, lane);
+      if (c_lt > WCAP / 2 || !bucket_sort(buf, c_lt, lane, hist, wstart[warp])) sort_front(buf, c_lt, lane);
       const int need = K - c_lt;
       for (int i = lane; i < hq; i += 32) {
         const u64 key = ties[i];
@@ -386,7 +432,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
       }
     }
   }
-  if (m >= 0) sort_front(buf, m, lane);
+  if (m >= 0 && (m > WCAP / 2 || !bucket_sort(buf, m, lane, hist, wstart[warp]))) sort_front(buf, m, lane);
   emit_tile<PACK>(buf, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
   if (lane == 0) {
     count[(long long)v * T + t] = min(n, K);
