@@ -211,9 +211,17 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(max(args.warmup, 3)):
         st.step()
     torch.cuda.synchronize()
-    stages = stage_times(st, torch) if rank == 0 else None
-    # the per-stage pass ran one more step's update; keep the step counter consistent
+    # per-stage device times on rank 0; its parameters, moments and step counter are restored
+    # afterwards so that the ranks stay in lockstep (same step, bitwise-equal replicas)
+    stages = None
+    if rank == 0:
+        snap = [t.clone() for t in (st.flat, st.m, st.v, st.step_t)]
+        stages = stage_times(st, torch)
+        for t, c in zip((st.flat, st.m, st.v, st.step_t), snap):
+            t.copy_(c)
+        del snap
     torch.cuda.synchronize()
+    ops.read_status()          # clear the device status word before the timed region
     barrier()
 
     # ---- device-timed region: graph replays, inputs resident ---------------------------------
@@ -278,6 +286,11 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_e2e = float(t.item())
+    # bounded device waits that gave up during the timed steps (0 = none), max over ranks
+    status = torch.tensor([ops.read_status()], device=dev)
+    if world > 1:
+        dist.all_reduce(status, op=dist.ReduceOp.MAX)
+    status = int(status.item())
     # the replicated update must leave every rank with the same parameter bits (outside timing)
     replicas_ok = True
     if world > 1:
@@ -318,7 +331,8 @@ def run_ours(args, rank, world, local_rank):
             "metric": METRIC, "value": steps_per_s, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 2 shapes; random-init model)",
-            "config": {**CONFIG, "views_per_rank": len(mine), "parallelism": f"view-split x{world} + NCCL allreduce",
+            "config": {**CONFIG, "views_per_rank": len(mine), "parallelism": (f"view-split x{world} + NVLink peer optimizer step" if st.regions is not None
+                                                     else f"view-split x{world}" + (" + NCCL allreduce" if world > 1 else "")),
                        "l2": "per-step working set > 126 MB L2 (targets, images, slot rows, SSIM maps)"},
             "render_mpix_s": (V * CONFIG["H"] * CONFIG["W"] / 1e6) / (rend_ms / 1e3) if rend_ms and world == 1 else None,
             "roofline": {"bound": "fp32", "kernel": "render_bwd", "achieved": achieved, "peak": fp32_peak,
@@ -328,7 +342,7 @@ def run_ours(args, rank, world, local_rank):
             "roofline_hbm": {"bound": "hbm", "kernel": "adam", "achieved": adam_gbs, "peak": peaks.get("hbm_gbs"),
                              "unit": "GB/s", "frac": adam_gbs / peaks.get("hbm_gbs", 6538.0), "traffic": None,
                              "work": f"28 B x {59 * st.G + 1} parameter elements per launch (read p,g,m,v; write p,m,v)"},
-            "stage_ms": stages, "clocks": clk_s, "replicas_agree": replicas_ok,
+            "stage_ms": stages, "clocks": clk_s, "replicas_agree": replicas_ok, "device_status": status,
             "e2e": {"value": args.steps / (ms_e2e / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": launches * args.steps,

@@ -3,7 +3,8 @@
  *
  * Every entry point takes plain device pointers, sizes and a CUDA stream (as void*, NULL = the
  * legacy default stream), launches asynchronously on that stream, performs no host<->device
- * synchronisation and no allocation, and returns a status code (TTS_OK = 0).  On failure,
+ * synchronisation and no allocation (the setup calls tts_peer_alloc / tts_ipc_* excepted), and
+ * returns a status code (TTS_OK = 0).  On failure,
  * tts_last_error() describes the problem (thread-local).  Scratch memory is passed in by the
  * caller; each *_workspace_bytes() function gives the size an entry point needs.
  *
@@ -46,7 +47,8 @@ extern "C" {
 int tts_version(void);
 const char* tts_last_error(void);
 
-/* Device status word written by kernels instead of trapping (bounded waits that gave up). */
+/* Device status word written by kernels instead of trapping (bounded waits that gave up):
+ * 1 = a bulk-copy wait of the forward, 2 = a relocation grid barrier, 4 = a peer barrier. */
 int tts_read_status(int* status_host);      /* synchronous read + clear; diagnostic only */
 
 /* ---- geometry + SH colour + activations --------------------------------------------------
@@ -163,6 +165,33 @@ int tts_relocate(float* params, float* m, float* v, int G, float dead_thr, float
                  float offset, const int32_t* targets_in, const float* offset_noise_in,
                  const int32_t* step, uint64_t seed, int32_t* n_dead_out, int32_t* targets_out,
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- multi-GPU optimizer step over NVLink peer memory -------------------------------------
+ * Replaces the gradient all-reduce + replicated torch.optim.Adam of a view-split batch
+ * (spike/train.py:27-29 with the views spread over N ranks).  Buffers shared between the
+ * ranks of one node are allocated here (tts_peer_alloc: cudaMalloc, zero-filled) and
+ * exchanged with CUDA IPC handles (tts_ipc_handle_bytes bytes each; the host moves them).
+ * Per step: tts_peer_barrier(phase 0) once every rank's gradient and loss are written;
+ * tts_adam_peer: rank `rank` sums the N gradients of its 1/N shard in rank order, updates
+ * the shard (and, on rank N-1, w_b_raw) with its moments m, v, and stores the new values into
+ * all N parameter buffers; loss_total = sum of the N losses; tts_peer_barrier(phase 1) before
+ * the parameters are read again.  params/grads/loss/flags are host arrays of N device
+ * pointers (index = rank; this rank's own buffers included); flags point at 2*8 int32 per
+ * rank, zero at start; epoch is a device int that grows every step (the step counter).  A
+ * barrier that waits too long ORs 4 into the status word (tts_read_status) and returns.
+ * N <= 8. */
+size_t tts_ipc_handle_bytes(void);
+int tts_peer_alloc(size_t bytes, void** ptr);
+int tts_peer_free(void* ptr);
+int tts_ipc_export(void* ptr, void* handle_out);
+int tts_ipc_open(const void* handle, void** ptr_out);
+int tts_ipc_close(void* ptr);
+int tts_peer_barrier(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch,
+                     void* stream);
+int tts_adam_peer(float* const* params, const float* const* grads, float* m, float* v, int G,
+                  int sh_degree, int rank, int N, const int32_t* step, const double* lr7,
+                  double beta1, double beta2, double eps, const float* const* loss,
+                  float* loss_total, void* stream);
 
 /* ---- dense WSR (spike/backward.py:61-63, wsr_polysplat) -----------------------------------
  * C[P,3] from theta_u[G,6], o[G], color[G,3], w_b (device scalar), Phi[P,6], c_b[3], keep[G]

@@ -35,7 +35,7 @@ def test_binding_matches_header(pkg):
     assert sorted(_lib.SIGNATURES) == declared()
     txt = open(HDR).read().replace("\n", " ")
     for name, (_, args) in _lib.SIGNATURES.items():
-        m = re.search(rf"\b{name}\(([^)]*)\)", txt)
+        m = re.search(rf"(?:int|size_t|char\*|void)\s+\**{name}\(([^)]*)\);", txt)
         params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(args), name
 

@@ -42,6 +42,14 @@ SIGNATURES = {
     "tts_sgld": (I, [P, I, D, F, P, P, U64, P]),
     "tts_relocate_workspace_bytes": (SZ, [I]),
     "tts_relocate": (I, [P, P, P, I, F, F, F, P, P, P, U64, P, P, P, SZ, P]),
+    "tts_ipc_handle_bytes": (SZ, []),
+    "tts_peer_alloc": (I, [SZ, C.POINTER(P)]),
+    "tts_peer_free": (I, [P]),
+    "tts_ipc_export": (I, [P, P]),
+    "tts_ipc_open": (I, [P, C.POINTER(P)]),
+    "tts_ipc_close": (I, [P]),
+    "tts_peer_barrier": (I, [P, I, I, I, P, P]),
+    "tts_adam_peer": (I, [P, P, P, P, I, I, I, I, P, P, D, D, D, P, P, P]),
     "tts_wsr_dense_fwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P]),
     "tts_wsr_dense_bwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P, P, P, P, P, P]),
 }

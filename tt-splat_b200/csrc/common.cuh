@@ -65,7 +65,7 @@ __device__ __forceinline__ float softplus_grad(float x) {
 }
 __device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x)); }
 
-// ---- bounded mbarrier + bulk copy (1-D TMA, no multicast) ----------------------------------
+// ---- bounded mbarrier + bulk copy (1-D TMA, one destination CTA) -------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

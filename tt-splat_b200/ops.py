@@ -242,3 +242,18 @@ def read_status():
     s = np.zeros(1, np.int32)
     call("tts_read_status", ctypes.c_void_p(s.ctypes.data))
     return int(s[0])
+
+
+def peer_barrier(regions, phase, epoch):
+    """tts_peer_barrier over the ranks of a PeerRegions (phase 0 or 1; epoch = device step)."""
+    _dev(epoch)
+    call("tts_peer_barrier", regions.t_flags, regions.rank, regions.world, int(phase), ptr(epoch), stream())
+
+
+def adam_peer(regions, m, v, G, sh_degree, step, lr7, loss_total, betas=(0.9, 0.999), eps=1e-8):
+    """tts_adam_peer: this rank's shard of the summed gradient through Adam, broadcast to all."""
+    _dev(m, v, step, lr7, loss_total)
+    call("tts_adam_peer", regions.t_params, regions.t_grads, ptr(m), ptr(v), G, sh_degree, regions.rank,
+         regions.world, ptr(step), ptr(lr7), float(betas[0]), float(betas[1]), float(eps), regions.t_loss,
+         ptr(loss_total), stream())
+

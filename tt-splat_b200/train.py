@@ -63,7 +63,8 @@ def replicas_agree(flat, group=None):
 class TrainStep:
     def __init__(self, model, cameras, gt_images, sh_degree=0, lambda_ssim=0.2, lr=None, K=128, R=1, k=4.0,
                  blur=0.3, near=0.2, noise_lr=0.0, relocate_every=0, dead_thr=0.005, dead_frac=0.0, offset=0.0,
-                 lambda_o=0.0, lambda_s=0.0, seed=0, n_views_total=None, process_group=None, use_graph=True):
+                 lambda_o=0.0, lambda_s=0.0, seed=0, n_views_total=None, process_group=None, use_graph=True,
+                 exchange="peer"):
         require_cuda()
         if not isinstance(model, GaussianModel):
             raise TypeError("TrainStep trains a tt_splat_b200.model.GaussianModel (flat device buffer)")
@@ -86,6 +87,18 @@ class TrainStep:
         self.dead_thr, self.dead_frac, self.offset = float(dead_thr), float(dead_frac), float(offset)
         self.lambda_o, self.lambda_s, self.seed = float(lambda_o), float(lambda_s), int(seed)
         self.pg = process_group
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange must be 'peer' (NVLink peer-memory optimizer step) or 'nccl'")
+        self.regions = None
+        if self.pg is not None:
+            import torch.distributed as dist
+            if exchange == "peer" and dist.get_world_size(self.pg) > 1:
+                from .peer import PeerRegions
+                # parameters and gradients live in the region the peers write into / read from
+                self.regions = PeerRegions(self.flat.numel(), dev, self.pg)
+                self.regions.params.copy_(self.flat)
+                model.flat.data = self.regions.params
+                self.flat = self.regions.params
         self.n_views_total = int(n_views_total or self.V)
         self.grad_scale = 1.0 / self.n_views_total
         self.lr = {**DEFAULT_LR, **(lr or {})}
@@ -102,7 +115,7 @@ class TrainStep:
         self.rf = dict(img=e(V, H, W, 3), den=e(V, H, W))
         self.lo = dict(gimg=e(V, H, W, 3), loss=e(V))
         self.rb = dict(slot_grads=e(V, T, K, ops.SLOT_GRAD_FLOATS), gwb=e(V, T))
-        self.grads = torch.zeros_like(self.flat)
+        self.grads = torch.zeros_like(self.flat) if self.regions is None else self.regions.grads
         self.m = torch.zeros_like(self.flat)
         self.v = torch.zeros_like(self.flat)
         self.step_t = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -113,7 +126,8 @@ class TrainStep:
         self.ws_bin.get(ops.lib().tts_bin_workspace_bytes(G, V, H, W))
         self.ws_loss.get(ops.lib().tts_loss_workspace_bytes(V, H, W))
         self.ws_reloc.get(ops.lib().tts_relocate_workspace_bytes(G) if G >= 2 else 0)
-        self.loss_mean = e(1)
+        self.loss_mean = e(1) if self.regions is None else self.regions.loss
+        self.loss_total = e(1)            # sum over the ranks (peer exchange)
         self.n_moved = torch.zeros(1, dtype=torch.int64, device=dev)
         self.it = 0
         self.graphs = {}
@@ -135,8 +149,17 @@ class TrainStep:
         torch.sum(self.lo["loss"], dim=0, keepdim=True, out=self.loss_mean)
 
     def _update(self, relocate):
-        ops.adam_sgld(self.flat, self.grads, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
-                      noise_lr=self.noise_lr, seed=self.seed)
+        if self.regions is not None:
+            # NVLink exchange: barrier, shard reduce + Adam + broadcast, barrier (replicas equal)
+            ops.peer_barrier(self.regions, 0, self.step_t)
+            ops.adam_peer(self.regions, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
+                          self.loss_total)
+            ops.peer_barrier(self.regions, 1, self.step_t)
+            if self.noise_lr > 0:
+                ops.sgld(self.flat, self.G, self.step_t, self.lr["means"], self.noise_lr, seed=self.seed)
+        else:
+            ops.adam_sgld(self.flat, self.grads, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
+                          noise_lr=self.noise_lr, seed=self.seed)
         if relocate:
             ops.relocate(self.flat, self.m, self.v, self.G, self.step_t, self.dead_thr, self.dead_frac, self.offset,
                          seed=self.seed, ws=self.ws_reloc, out=self.reloc)
@@ -146,7 +169,7 @@ class TrainStep:
         reduce_across_ranks(self.grads, self.loss_mean, self.pg)
 
     def _run(self, relocate):
-        if self.pg is None:
+        if self.pg is None or self.regions is not None:
             self._fwd_bwd()
             self._update(relocate)
         else:
@@ -155,7 +178,7 @@ class TrainStep:
             self._update(relocate)
 
     def _graph_run(self, relocate):
-        if self.pg is None:
+        if self.pg is None or self.regions is not None:
             key = ("all", relocate)
             if key not in self.graphs:
                 g = torch.cuda.CUDAGraph()
@@ -181,10 +204,17 @@ class TrainStep:
             self.graphs[key].replay()
 
     def launches(self, relocate):
-        """Kernels of this library launched by one step (memsets and torch ops excluded)."""
-        n = 13 + 1 + (1 if self.noise_lr > 0 else 0)      # forward/backward chain + Adam (+ SGLD)
+        """Kernels of this library launched by one step (memsets and torch ops excluded):
+        step_begin 1, project 1, bin_pack 4, render_fwd 1, loss 3, render_bwd 1,
+        backward_params 3, then Adam (+ SGLD) or the peer step (2 barriers + Adam + SGLD), and
+        the relocation kernel."""
+        n = 14
+        if self.regions is not None:
+            n += 3 + (1 if self.noise_lr > 0 else 0)
+        else:
+            n += 1 + (1 if self.noise_lr > 0 else 0)
         if relocate:
-            n += 7 + (7 if self.dead_frac > 0 else 0)     # relocation (+ quantile select)
+            n += 1
         return n
 
     def step(self):
@@ -197,11 +227,11 @@ class TrainStep:
         else:
             self._run(relocate)
         self.it += 1
-        return self.loss_mean.view(())
+        return (self.loss_mean if self.regions is None else self.loss_total).view(())
 
     def mean_loss_value(self):
         """Mean photometric loss of the last step (+ the MCMC regulariser when enabled); syncs."""
-        total = float(self.loss_mean.item()) / self.n_views_total
+        total = float((self.loss_mean if self.regions is None else self.loss_total).item()) / self.n_views_total
         if self.lambda_o or self.lambda_s:
             o = torch.sigmoid(view(self.flat, self.G, "opacity_raw"))
             s = torch.exp(view(self.flat, self.G, "log_scales"))
@@ -216,8 +246,16 @@ class TrainStep:
             raise RuntimeError(f"parameter replicas differ across ranks after step {self.it}")
 
     def release(self):
-        """Drop the captured graphs (call before destroying a process group)."""
+        """Drop the captured graphs and, with the peer exchange, hand the model a private copy of
+        its parameters and free the shared regions (call before destroying a process group;
+        every rank calls it)."""
         self.graphs.clear()
+        if self.regions is not None:
+            own = self.flat.clone()
+            self.model.flat.data = own
+            self.flat = own
+            self.regions.close()
+            self.regions = None
 
 
 def fit(model, cameras, gt_images, arm="A", iters=800, lambda_ssim=0.2, lr=None, k=4.0, blur_eps=0.3, near=0.2,
