@@ -291,6 +291,16 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(status, op=dist.ReduceOp.MAX)
     status = int(status.item())
+    # per-rank halves of the step (outside the timed region): the forward/backward chain of this
+    # rank's views, and the exchange + update, which waits for the slowest rank
+    phases = None
+    if world > 1 and st.regions is not None:
+        fb_ms, up_ms = st.phase_times(20)
+        pt = torch.tensor([fb_ms, up_ms], device=dev)
+        allp = [torch.zeros_like(pt) for _ in range(world)]
+        dist.all_gather(allp, pt)
+        phases = {"fwd_bwd_ms": [round(float(x[0]), 4) for x in allp],
+                  "exchange_update_ms": [round(float(x[1]), 4) for x in allp]}
     # the replicated update must leave every rank with the same parameter bits (outside timing)
     replicas_ok = True
     if world > 1:
@@ -342,7 +352,7 @@ def run_ours(args, rank, world, local_rank):
             "roofline_hbm": {"bound": "hbm", "kernel": "adam", "achieved": adam_gbs, "peak": peaks.get("hbm_gbs"),
                              "unit": "GB/s", "frac": adam_gbs / peaks.get("hbm_gbs", 6538.0), "traffic": None,
                              "work": f"28 B x {59 * st.G + 1} parameter elements per launch (read p,g,m,v; write p,m,v)"},
-            "stage_ms": stages, "clocks": clk_s, "replicas_agree": replicas_ok, "device_status": status,
+            "stage_ms": stages, "clocks": clk_s, "replicas_agree": replicas_ok, "device_status": status, "rank_phases": phases,
             "e2e": {"value": args.steps / (ms_e2e / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": launches * args.steps,

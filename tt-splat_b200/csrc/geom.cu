@@ -41,6 +41,25 @@ __device__ __forceinline__ void stage_params(const float* __restrict__ params, i
   }
 }
 
+// The inverse of stage_params: staged rows -> the flat layout, coalesced per field.
+template <int GPB>
+__device__ __forceinline__ void unstage_rows(const float* s_p, int G, int g0, float* __restrict__ dst) {
+  const ParamLayout L{G};
+  const int ng = min(GPB, G - g0);
+  const int offs[6] = {L.means(), L.log_scales(), L.quats(), L.opacity(), L.color_dc(), L.color_rest()};
+  const int width[6] = {3, 3, 4, 1, 3, 45};
+  const int col[6] = {0, 3, 6, 10, 11, 14};
+#pragma unroll
+  for (int f = 0; f < 6; ++f) {
+    const int w = width[f], n = ng * w;
+    float* out = dst + offs[f] + (long long)g0 * w;
+    for (int i = threadIdx.x; i < n; i += GB_THREADS) {
+      const int gg = i / w, c = i - gg * w;
+      out[i] = s_p[gg * PSTRIDE + col[f] + c];
+    }
+  }
+}
+
 __device__ __forceinline__ void load_staged(const float* s, Loaded& x) {
 #pragma unroll
   for (int i = 0; i < 3; i++) {
@@ -126,16 +145,6 @@ __global__ void __launch_bounds__(GB_THREADS)
       cell_rank[(long long)v * G + g] = make_int2(key - v * T, base + __popc(peers & ((1u << lane) - 1u)));
     }
   }
-}
-
-// Address of entry e (0..58) of gaussian g's parameter row in the flat buffer.
-__device__ __forceinline__ long long field_addr(int e, int g, const ParamLayout& L) {
-  if (e < 3) return L.means() + 3LL * g + e;
-  if (e < 6) return L.log_scales() + 3LL * g + (e - 3);
-  if (e < 10) return L.quats() + 4LL * g + (e - 6);
-  if (e < 11) return L.opacity() + (long long)g;
-  if (e < 14) return L.color_dc() + 3LL * g + (e - 11);
-  return L.color_rest() + 45LL * g + (e - 14);
 }
 
 // Sum over the LPG lanes of one gaussian (xor butterfly: every lane ends with the same bits).
@@ -307,11 +316,12 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
   for (int k = 0; k < NB; k++)
 #pragma unroll
     for (int c = 0; c < 3; c++) gco[k][c] = lane_sum<LPG>(gco[k][c]);
-  if (g >= G) return;
-  // the lanes share the writes: lane vl writes the entries e (0..58 of the gaussian's
-  // parameter row) with e % LPG == vl
+  // the gaussian's 59 gradients go to its staged row (lane vl fills the entries e with
+  // e % LPG == vl), then the block writes the rows out field by field, coalesced
+  __syncthreads();                 // every lane is done reading its staged parameters
+  float* row = s_p + gl * PSTRIDE;
   auto put = [&](int e, float val) {
-    if (e % LPG == vl) grads[field_addr(e, g, L)] = val;
+    if (g < G && e % LPG == vl) row[e] = val;
   };
 #pragma unroll
   for (int i = 0; i < 3; i++) {
@@ -327,6 +337,8 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
   for (int k = 1; k < 16; k++)
 #pragma unroll
     for (int c = 0; c < 3; c++) put(14 + 3 * (k - 1) + c, k < NB ? gco[k < NB ? k : 0][c] : 0.f);
+  __syncthreads();
+  unstage_rows<GPB>(s_p, G, g0, grads);
 }
 
 // Deterministic sum of the per-tile w_b partials; grads[59G] = sum * softplus'(w_b_raw).

@@ -203,6 +203,38 @@ class TrainStep:
             self._allreduce()
             self.graphs[key].replay()
 
+    def phase_times(self, steps=20):
+        """Device time of the two halves of a step on this rank, from separately captured graphs:
+        (forward/backward chain ms, exchange + update ms).  With several ranks the second half
+        includes the wait for the slowest rank's first half.  Runs `steps` training steps."""
+        relocate = bool(self.relocate_every) and self.G >= 2
+        if self.pg is not None and self.regions is None:
+            raise RuntimeError("phase_times needs the single-process or peer-exchange step")
+        if "fb" not in self.graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._fwd_bwd()
+            self.graphs["fb"] = g
+        key = ("up", relocate)
+        if key not in self.graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._update(relocate)
+            self.graphs[key] = g
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        fb = up = 0.0
+        for _ in range(steps):
+            ev[0].record()
+            self.graphs["fb"].replay()
+            ev[1].record()
+            self.graphs[key].replay()
+            ev[2].record()
+            torch.cuda.synchronize()
+            fb += ev[0].elapsed_time(ev[1])
+            up += ev[1].elapsed_time(ev[2])
+            self.it += 1
+        return fb / steps, up / steps
+
     def launches(self, relocate):
         """Kernels of this library launched by one step (memsets and torch ops excluded):
         step_begin 1, project 1, bin_pack 4, render_fwd 1, loss 3, render_bwd 1,
