@@ -223,6 +223,18 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ops.read_status()          # clear the device status word before the timed region
     barrier()
+    # Every leg below starts from this state.  SGLD at noise_lr 5e5 on random-noise targets
+    # carries near-transparent gaussians far from the scene (some towards the camera planes,
+    # where the fp32 conic inverse of spike/geometry.py overflows), and a model trained on that
+    # workload for many hundreds of steps produces non-finite pixels, which would change the
+    # work later legs measure.
+    start = [t.clone() for t in (st.flat, st.m, st.v, st.step_t)]
+
+    def restore():
+        for t, c in zip((st.flat, st.m, st.v, st.step_t), start):
+            t.copy_(c)
+        torch.cuda.synchronize()
+        barrier()
 
     # ---- device-timed region: graph replays, inputs resident ---------------------------------
     with ClockSampler(local_rank) as clk:
@@ -241,6 +253,8 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     steps_per_s = args.steps / (ms / 1e3)
+    finite = bool(torch.isfinite(st.flat).all().item())
+    restore()
 
     # ---- end to end through the public API: pinned H2D of the step's targets, D2H of the loss
     # Every step uploads its 8 target images from pinned host memory and reads the loss back.
@@ -308,6 +322,7 @@ def run_ours(args, rank, world, local_rank):
         replicas_ok = replicas_agree(st.flat, pg)
 
     # ---- render MPix/s: forward of the 8-view batch (project + bin + render), device-timed ----
+    restore()
     rend_ms = None
     if rank == 0:
         pj, bp, rf = st.pj, st.bp, st.rf
@@ -346,13 +361,17 @@ def run_ours(args, rank, world, local_rank):
                        "l2": "per-step working set > 126 MB L2 (targets, images, slot rows, SSIM maps)"},
             "render_mpix_s": (V * CONFIG["H"] * CONFIG["W"] / 1e6) / (rend_ms / 1e3) if rend_ms and world == 1 else None,
             "roofline": {"bound": "fp32", "kernel": "render_bwd", "achieved": achieved, "peak": fp32_peak,
-                         "unit": "TFLOP/s", "frac": achieved / fp32_peak, "traffic": None,
+                         "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+                         "traffic": RENDER_BWD_DRAM_PER_VIEW * V if CONFIG["G"] == 100000 else None,
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                         "8-view capture scaled by views per launch)",
                          "peak_source": "nominal FP32 FMA (148 SMs x 128 lanes x 2) at the sampled SM clock",
                          "work": f"44 flops x {pairs} valid (pixel, slot) pairs per launch"},
             "roofline_hbm": {"bound": "hbm", "kernel": "adam", "achieved": adam_gbs, "peak": peaks.get("hbm_gbs"),
-                             "unit": "GB/s", "frac": adam_gbs / peaks.get("hbm_gbs", 6538.0), "traffic": None,
+                             "unit": "GB/s", "frac": adam_gbs / peaks.get("hbm_gbs", 6538.0),
+                             "traffic": ADAM_DRAM if CONFIG["G"] == 100000 else None,
                              "work": f"28 B x {59 * st.G + 1} parameter elements per launch (read p,g,m,v; write p,m,v)"},
-            "stage_ms": stages, "clocks": clk_s, "replicas_agree": replicas_ok, "device_status": status, "rank_phases": phases,
+            "stage_ms": stages, "clocks": clk_s, "replicas_agree": replicas_ok, "device_status": status, "params_finite_after_timed_steps": finite, "rank_phases": phases,
             "e2e": {"value": args.steps / (ms_e2e / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": launches * args.steps,
@@ -456,6 +475,13 @@ def run_config(args, rank, world, local_rank, cid):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# DRAM bytes of one launch, read from an ncu capture of the config-2 train step (8 views per
+# launch; the render backward's traffic is proportional to the views it renders).  The Adam
+# figure under-counts writes that were still in L2 when the kernel ended.
+RENDER_BWD_DRAM_PER_VIEW = (362.3e6 + 88.9e6) / 8
+ADAM_DRAM = 94.4e6 + 16.3e6
 
 
 def cpu_baseline_sample():
