@@ -19,6 +19,15 @@
 namespace tts {
 
 constexpr int LT_W = 64, LT_H = 32, LWIN_MAX = 11, RB = 8;
+// Row passes: each of the IH rows is cut into 6 segments of 11, 11, 11, 11, 10, 10 outputs, so
+// that IH x 6 = 252 items keep the 256 threads busy in one round (segments of RB = 8 would give
+// 336 items: two rounds, the second a third full).
+constexpr int RSEGS = 6, RBR = 11;
+static_assert(4 * 11 + 2 * 10 == LT_W, "row segments cover the tile width");
+__device__ __forceinline__ void row_seg(int s, int& c0, int& width) {
+  c0 = s < 4 ? 11 * s : 44 + 10 * (s - 4);
+  width = s < 4 ? 11 : 10;
+}
 constexpr float SSIM_C1 = 0.01f * 0.01f, SSIM_C2 = 0.03f * 0.03f;
 
 struct Window {
@@ -104,27 +113,30 @@ __global__ void __launch_bounds__(256)
     }
   }
   __syncthreads();
-  // rows: item = (row r, segment of RB outputs); lanes walk down rows (odd stride)
-  for (int it = tid; it < LG::IH * (LT_W / RB); it += 256) {
-    const int r = it % LG::IH, c0 = (it / LG::IH) * RB;
+  // rows: item = (row r, segment of up to RBR outputs); lanes walk down rows (odd stride).  The
+  // last input read of a 10-wide segment is the row's padding column, never used.
+  for (int it = tid; it < LG::IH * RSEGS; it += 256) {
+    const int r = it % LG::IH;
+    int c0, width;
+    row_seg(it / LG::IH, c0, width);
     const f32x2 z = mk2(0.f, 0.f);
-    f32x2 axy[RB], aqq[RB];
-    float a1[RB];
+    f32x2 axy[RBR], aqq[RBR];
+    float a1[RBR];
 #pragma unroll
-    for (int o = 0; o < RB; o++) {
+    for (int o = 0; o < RBR; o++) {
       axy[o] = z;
       aqq[o] = z;
       a1[o] = 0.f;
     }
 #pragma unroll
-    for (int i = 0; i < RB + WIN - 1; i++) {
+    for (int i = 0; i < RBR + WIN - 1; i++) {
       const f32x2 XY = sxy[r * LG::XS + c0 + i];
       const f32x2 QQ = mul2(XY, XY);
       float x, y;
       split2(XY, x, y);
       const float xy = x * y;
 #pragma unroll
-      for (int o = 0; o < RB; o++) {
+      for (int o = 0; o < RBR; o++) {
         const int k = i - o;
         if (k >= 0 && k < WIN) {
           axy[o] = fma2(g2[k], XY, axy[o]);
@@ -134,10 +146,12 @@ __global__ void __launch_bounds__(256)
       }
     }
 #pragma unroll
-    for (int o = 0; o < RB; o++) {
-      hxy[r * LG::HS + c0 + o] = axy[o];
-      hqq[r * LG::HS + c0 + o] = aqq[o];
-      hxy1[r * LG::HS + c0 + o] = a1[o];
+    for (int o = 0; o < RBR; o++) {
+      if (o < width) {
+        hxy[r * LG::HS + c0 + o] = axy[o];
+        hqq[r * LG::HS + c0 + o] = aqq[o];
+        hxy1[r * LG::HS + c0 + o] = a1[o];
+      }
     }
   }
   __syncthreads();
@@ -277,22 +291,24 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
   // transposed row filter: t[r][c] = sum_k g[k] m[r][c + WIN-1 - k]
-  for (int it = tid; it < LG::IH * (LT_W / RB); it += 256) {
-    const int r = it % LG::IH, c0 = (it / LG::IH) * RB;
+  for (int it = tid; it < LG::IH * RSEGS; it += 256) {
+    const int r = it % LG::IH;
+    int c0, width;
+    row_seg(it / LG::IH, c0, width);
     const f32x2 z = mk2(0.f, 0.f);
-    f32x2 a01[RB];
-    float a2[RB];
+    f32x2 a01[RBR];
+    float a2[RBR];
 #pragma unroll
-    for (int o = 0; o < RB; o++) {
+    for (int o = 0; o < RBR; o++) {
       a01[o] = z;
       a2[o] = 0.f;
     }
 #pragma unroll
-    for (int i = 0; i < RB + WIN - 1; i++) {
+    for (int i = 0; i < RBR + WIN - 1; i++) {
       const f32x2 M01 = s01[r * LG::XS + c0 + i];
       const float M2 = s2[r * LG::XS + c0 + i];
 #pragma unroll
-      for (int o = 0; o < RB; o++) {
+      for (int o = 0; o < RBR; o++) {
         const int k = (WIN - 1) - (i - o);
         if (k >= 0 && k < WIN) {
           a01[o] = fma2(g2[k], M01, a01[o]);
@@ -301,9 +317,11 @@ __global__ void __launch_bounds__(256)
       }
     }
 #pragma unroll
-    for (int o = 0; o < RB; o++) {
-      h01[r * LG::HS + c0 + o] = a01[o];
-      h2[r * LG::HS + c0 + o] = a2[o];
+    for (int o = 0; o < RBR; o++) {
+      if (o < width) {
+        h01[r * LG::HS + c0 + o] = a01[o];
+        h2[r * LG::HS + c0 + o] = a2[o];
+      }
     }
   }
   __syncthreads();
