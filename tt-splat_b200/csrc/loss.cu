@@ -86,29 +86,30 @@ __global__ void __launch_bounds__(256)
     g2[k] = mk2(g[k], g[k]);
   }
   {
-    // issue every load of the halo tile before the first shared-memory store
-    constexpr int NL = (LG::IH * LG::IW + 255) / 256;
-    float xv[NL], yv[NL];
+    // issue every load of the halo tile before the first shared-memory store: thread -> one
+    // column and every RPT-th row (no per-element index division)
+    constexpr int RPT = 256 / LG::IW, NR = (LG::IH + RPT - 1) / RPT;
+    const int lc = tid % LG::IW, lr0 = tid / LG::IW;
+    if (lr0 < RPT) {
+      const int xx = ox0 + lc;
+      const long long col = (long long)id.v * H * W + xx;
+      float xv[NR], yv[NR];
 #pragma unroll
-    for (int u = 0; u < NL; ++u) {
-      const int i = tid + 256 * u;
-      const int r = i / LG::IW, c = i % LG::IW;
-      const int yy = oy0 + r, xx = ox0 + c;
-      xv[u] = 0.f;
-      yv[u] = 0.f;
-      if (i < LG::IH * LG::IW && yy < H && xx < W) {
-        const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
-        xv[u] = __ldg(img + q);
-        yv[u] = __ldg(tgt + q);
+      for (int k = 0; k < NR; ++k) {
+        const int r = lr0 + RPT * k, yy = oy0 + r;
+        xv[k] = 0.f;
+        yv[k] = 0.f;
+        if (r < LG::IH && yy < H && xx < W) {
+          const long long q = (col + (long long)yy * W) * 3 + id.ch;
+          xv[k] = __ldg(img + q);
+          yv[k] = __ldg(tgt + q);
+        }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < NL; ++u) {
-      const int i = tid + 256 * u;
-      if (i < LG::IH * LG::IW) {
-        const int r = i / LG::IW, c = i % LG::IW;
+      for (int k = 0; k < NR; ++k) {
+        const int r = lr0 + RPT * k;
         // SSIM sees the inputs clamped to [0, 1] (spike/metrics.py:6-7)
-        sxy[r * LG::XS + c] = mk2(fminf(fmaxf(xv[u], 0.f), 1.f), fminf(fmaxf(yv[u], 0.f), 1.f));
+        if (r < LG::IH) sxy[r * LG::XS + lc] = mk2(fminf(fmaxf(xv[k], 0.f), 1.f), fminf(fmaxf(yv[k], 0.f), 1.f));
       }
     }
   }
@@ -197,7 +198,11 @@ __global__ void __launch_bounds__(256)
       const float sxx = fx2 - mux2, syy = fy2 - muy2, sxy_ = f1[o] - mux * muy;
       const float A1 = 2.f * mux * muy + SSIM_C1, A2 = 2.f * sxy_ + SSIM_C2;
       const float B1 = mux2 + muy2 + SSIM_C1, B2 = sxx + syy + SSIM_C2;
-      const float iD = __frcp_rn(B1 * B2), iB2 = __frcp_rn(B2);
+      // hardware reciprocals (rcp.approx, within 1 ulp): the loss and gradient tolerances are
+      // orders of magnitude wider, and the correctly rounded form costs ~20 instructions more
+      float iD, iB2;
+      asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(iD) : "f"(B1 * B2));
+      asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(iB2) : "f"(B2));
       const float S = (A1 * A2) * iD;
       ssum += S;
       const long long q = (long long)oy * Wo + ox;
@@ -261,31 +266,34 @@ __global__ void __launch_bounds__(256)
     }
   }
   {
-    // map rows [y0-WIN+1, y0+LT_H), cols [x0-WIN+1, x0+LT_W); zero outside the valid region
-    constexpr int NL = (LG::IH * LG::IW + 255) / 256;
-    float av[NL], bv[NL], dv[NL];
+    // map rows [y0-WIN+1, y0+LT_H), cols [x0-WIN+1, x0+LT_W); zero outside the valid region;
+    // thread -> one column and every RPT-th row
+    constexpr int RPT = 256 / LG::IW, NR = (LG::IH + RPT - 1) / RPT;
+    const int lc = tid % LG::IW, lr0 = tid / LG::IW;
+    if (lr0 < RPT) {
+      const int mx = x0 - (WIN - 1) + lc;
+      const bool colok = mx >= 0 && mx < Wo;
+      float av[NR], bv[NR], dv[NR];
 #pragma unroll
-    for (int u = 0; u < NL; ++u) {
-      const int i = tid + 256 * u;
-      const int r = i / LG::IW, c = i % LG::IW;
-      const int my = y0 - (WIN - 1) + r, mx = x0 - (WIN - 1) + c;
-      av[u] = 0.f;
-      bv[u] = 0.f;
-      dv[u] = 0.f;
-      if (i < LG::IH * LG::IW && my >= 0 && my < Ho && mx >= 0 && mx < Wo) {
-        const long long q = (long long)my * Wo + mx;
-        av[u] = __ldg(mbase + q);
-        bv[u] = __ldg(mbase + plane + q);
-        dv[u] = __ldg(mbase + 2 * plane + q);
+      for (int k = 0; k < NR; ++k) {
+        const int r = lr0 + RPT * k, my = y0 - (WIN - 1) + r;
+        av[k] = 0.f;
+        bv[k] = 0.f;
+        dv[k] = 0.f;
+        if (colok && r < LG::IH && my >= 0 && my < Ho) {
+          const long long q = (long long)my * Wo + mx;
+          av[k] = __ldg(mbase + q);
+          bv[k] = __ldg(mbase + plane + q);
+          dv[k] = __ldg(mbase + 2 * plane + q);
+        }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < NL; ++u) {
-      const int i = tid + 256 * u;
-      if (i < LG::IH * LG::IW) {
-        const int r = i / LG::IW, c = i % LG::IW;
-        s01[r * LG::XS + c] = mk2(av[u], bv[u]);
-        s2[r * LG::XS + c] = dv[u];
+      for (int k = 0; k < NR; ++k) {
+        const int r = lr0 + RPT * k;
+        if (r < LG::IH) {
+          s01[r * LG::XS + lc] = mk2(av[k], bv[k]);
+          s2[r * LG::XS + lc] = dv[k];
+        }
       }
     }
   }
