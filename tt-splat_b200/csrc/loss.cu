@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(256)
   // columns: item = (column c, segment of RB output rows); lanes walk along columns
   float ssum = 0.f;
   const long long plane = (long long)Ho * Wo;
-  float* mbase = maps + (long long)vc * 3 * plane;
+  float4* mbase = reinterpret_cast<float4*>(maps) + (long long)vc * plane;   // (M0, M1, M2, 0) per position
   for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
     const int c = it % LT_W, r0 = (it / LT_W) * RB;
     const f32x2 z = mk2(0.f, 0.f);
@@ -206,9 +206,9 @@ __global__ void __launch_bounds__(256)
       const float S = (A1 * A2) * iD;
       ssum += S;
       const long long q = (long long)oy * Wo + ox;
-      mbase[q] = 2.f * iD * (muy * (A2 - A1) - S * mux * (B2 - B1));   // dS/dmu_x
-      mbase[plane + q] = -S * iB2;                                     // dS/d filt(x^2)
-      mbase[2 * plane + q] = 2.f * A1 * iD;                            // dS/d filt(xy)
+      mbase[q] = make_float4(2.f * iD * (muy * (A2 - A1) - S * mux * (B2 - B1)),   // dS/dmu_x
+                             -S * iB2,                                             // dS/d filt(x^2)
+                             2.f * A1 * iD, 0.f);                                  // dS/d filt(xy)
     }
   }
 #pragma unroll
@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(256)
     g2[k] = mk2(g[k], g[k]);
   }
   const long long plane = (long long)Ho * Wo;
-  const float* mbase = maps + (long long)vc * 3 * plane;
+  const float4* mbase = reinterpret_cast<const float4*>(maps) + (long long)vc * plane;
   // the image/target values of this thread's epilogue (one column item per thread: LT_W x LT_H/RB
   // = 256 items) are fetched up front, together with the map halo
   static_assert(LT_W * (LT_H / RB) == 256, "one column item per thread");
@@ -282,9 +282,10 @@ __global__ void __launch_bounds__(256)
         dv[k] = 0.f;
         if (colok && r < LG::IH && my >= 0 && my < Ho) {
           const long long q = (long long)my * Wo + mx;
-          av[k] = __ldg(mbase + q);
-          bv[k] = __ldg(mbase + plane + q);
-          dv[k] = __ldg(mbase + 2 * plane + q);
+          const float4 mm = __ldg(mbase + q);
+          av[k] = mm.x;
+          bv[k] = mm.y;
+          dv[k] = mm.z;
         }
       }
 #pragma unroll
@@ -475,7 +476,7 @@ using namespace tts;
 extern "C" size_t tts_loss_workspace_bytes(int V, int H, int W) {
   if (V < 1 || H < 3 || W < 3) return 0;
   const LossGeom lg = loss_geom(H, W);
-  return a256((size_t)V * 9 * lg.Ho * lg.Wo * 4) + a256((size_t)V * 3 * lg.fbx * lg.fby * 4) +
+  return a256((size_t)V * 12 * lg.Ho * lg.Wo * 4) + a256((size_t)V * 3 * lg.fbx * lg.fby * 4) +
          a256((size_t)V * 3 * lg.bbx * lg.bby * 4);
 }
 
@@ -490,7 +491,7 @@ extern "C" int tts_loss_l1_ssim(const float* img, const float* target, int V, in
   const LossGeom lg = loss_geom(H, W);
   char* p = static_cast<char*>(workspace);
   float* maps = reinterpret_cast<float*>(p);
-  p += a256((size_t)V * 9 * lg.Ho * lg.Wo * 4);
+  p += a256((size_t)V * 12 * lg.Ho * lg.Wo * 4);
   float* spart = reinterpret_cast<float*>(p);
   p += a256((size_t)V * 3 * lg.fbx * lg.fby * 4);
   float* lpart = reinterpret_cast<float*>(p);
