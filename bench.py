@@ -391,8 +391,9 @@ def run_config(args, rank, world, local_rank, cid):
 
     config 3: G = 1M clustered, 1920x1072 (1080 cropped to whole tiles), K = 256, fp32; each rank
               renders one view forward + backward (weak scaling); reports candidate overflow.
-    config 4: G = 3M, 64 views 1264x832 on a seeded spiral, K = 128, forward only; views
-              partitioned over the ranks with no collective (strong scaling); frames/s, MPix/s.
+    config 4: G = 3M, 64 views 1264x832 on a seeded spiral, K = 128, forward only from compact
+              bf16 slot rows; views partitioned over the ranks with no collective (strong
+              scaling); frames/s, MPix/s.
     """
     import torch
     import torch.distributed as dist
@@ -422,9 +423,10 @@ def run_config(args, rank, world, local_rank, cid):
         for ct in cams_t:
             pj = ops.project(flat, G, sh, ct, H, W, out=state.get("pj"))
             state["pj"] = pj
-            bp = ops.bin_pack(pj, G, H, W, 1, K, ws=ws, out=state.get("bp"), with_inv=(cid == 3))
+            bp = ops.bin_pack(pj, G, H, W, 1, K, ws=ws, out=state.get("bp"), with_inv=(cid == 3), bf16=(cid == 4))
             state["bp"] = bp
-            rf = ops.render_fwd(bp["slots"], bp["count"], H, W, flat[59 * G:], c_b, out=state.get("rf"))
+            rf = ops.render_fwd(bp["slots"], bp["count"], H, W, flat[59 * G:], c_b, out=state.get("rf"),
+                                bf16=(cid == 4))
             state["rf"] = rf
             if cid == 3:
                 tg = state.setdefault("tg", torch.rand(rf["img"].shape, device=dev, generator=torch.Generator(dev).manual_seed(5)))
@@ -467,7 +469,8 @@ def run_config(args, rank, world, local_rank, cid):
         line = {"metric": ("fwd+bwd views/s (config 3)" if cid == 3 else "render frames/s (config 4)"),
                 "value": (world if cid == 3 else len(sc["cams"])) / (ms / 1e3), "unit": "views/s" if cid == 3 else "frames/s",
                 "n_gpus": world, "steps": steps, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "weak" if cid == 3 else "strong", "dtype": "f32", "data": "synthetic (seeded)",
+                "scaling": "weak" if cid == 3 else "strong",
+                "dtype": "f32" if cid == 3 else "bf16 slot rows, f32 accumulate", "data": "synthetic (seeded)",
                 "mpix_s": n_views_job * H * W / 1e6 / (ms / 1e3),
                 "config": {"workload": f"config{cid}", "G": G, "H": H, "W": W, "K": K, "sh_degree": sh,
                            "views_per_rank": len(mine)}, **extra}

@@ -20,6 +20,8 @@
  *   count    [V][T] int32 = min(cand, K);  cand [V][T] int32 = candidates (overflow = cand-K)
  *   inv      [V][G][(2R+1)^2] int32 flat slot t*K+k of gaussian g at stencil offset j, or -1
  *   slots    [V][T][K][TTS_SLOT_FLOATS]  theta_u[6] (tile-local), color_o[3], o_col, 0, 0
+ *            or, compact bf16: [V][T][K][TTS_SLOT_BF16] bf16 theta_hi[6], theta_lo[6] (theta_u =
+ *            hi + lo), color_o[3], o_col
  *   img      [V][H][W][3], den [V][H][W], gimg like img
  *   slot_grads [V][T][K][TTS_SLOT_GRAD_FLOATS]  gtheta_u[6], gcolor_o[3], go_col
  */
@@ -41,6 +43,7 @@ extern "C" {
 #define TTS_CAM_FLOATS 20
 #define TTS_PROJ_FLOATS 12
 #define TTS_SLOT_FLOATS 12
+#define TTS_SLOT_BF16 16
 #define TTS_SLOT_GRAD_FLOATS 10
 #define TTS_PARAM_FLOATS 59
 
@@ -66,7 +69,9 @@ int tts_project(const float* params, int G, int sh_degree, const float* cams, in
  * tile*2048 + clamp(long(dist2),0,2047), ties by stencil offset j then gaussian id), plus the
  * inverse table of tools/m9_scatter_oracle.py:20-35 (indexed by stencil offset) and, when
  * proj/slots are given, the operand gather of _operands :207-211 with theta_u_gathered
- * :130-143.  G < 2^31, K <= 256, R <= 3.  inv may be NULL (forward-only rendering). */
+ * :130-143.  G < 2^31, K <= 256, R <= 3.  inv may be NULL (forward-only rendering).
+ * tts_bin_pack writes fp32 slot rows (slot_format 0) or compact bf16 rows (slot_format 1, the
+ * forward-only bf16 path of tts_render_fwd). */
 size_t tts_bin_workspace_bytes(int G, int V, int H, int W);
 int tts_bin_from_mu2d(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W, int R,
                       int K, int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv,
@@ -83,7 +88,8 @@ int tts_bin_from_mu2d_noalloc(const float* mu2d, const uint8_t* keep, int G, int
 int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float* proj,
                  const int32_t* cell_count, const int32_t* cell_rank, int G, int V, int H, int W,
                  int R, int K, float k_poly, int32_t* idx, int32_t* count, int32_t* cand,
-                 int32_t* inv, float* slots, void* workspace, size_t workspace_bytes, void* stream);
+                 int32_t* inv, void* slots, int slot_format, void* workspace,
+                 size_t workspace_bytes, void* stream);
 
 /* ---- operands in the reference layout -> slot rows ---------------------------------------
  * Packs theta_u[V*T,6,K], color_o[V*T,K,3], o_col[V*T,K,1] (the operands of
@@ -98,7 +104,8 @@ int tts_unpack_slot_grads(const float* slot_grads, int VT, int K, float* gtheta_
  * Replaces _DevRenderBinned.forward, tools/m4_train_binned.py:156-166 (= render_binned_cpu
  * :226-230, WSRPolySplatHot.forward spike/backward.py:28-41): Q = Phi.theta_u per tile,
  * w = relu(Q)^2, C = (sum w color_o + w_b c_b) / (sum w o_col + w_b); img[gidx] = C.
- * slots_bf16 != 0 reads slot rows stored as bf16 (bf16 in, fp32 accumulate).
+ * slots_bf16 != 0 reads compact bf16 slot rows (tts_bin_pack slot_format 1; bf16 in, fp32
+ * accumulate).
  * The background weight is read on the device: w_b = softplus(*w_b) when w_b_is_raw != 0
  * (the model's w_b_raw), else *w_b as given (the activated operand of _DevRenderBinned). */
 int tts_render_fwd(const void* slots, int slots_bf16, const int32_t* count, int V, int H, int W,

@@ -28,7 +28,7 @@ SIGNATURES = {
     "tts_bin_workspace_bytes": (SZ, [I, I, I, I]),
     "tts_bin_from_mu2d": (I, [P, P, I, I, I, I, I, I, P, P, P, P, P, SZ, P]),
     "tts_bin_from_mu2d_noalloc": (I, [P, P, I, I, I, I, I, I, P, P, P, P, P]),
-    "tts_bin_pack": (I, [P, P, P, P, P, I, I, I, I, I, I, F, P, P, P, P, P, P, SZ, P]),
+    "tts_bin_pack": (I, [P, P, P, P, P, I, I, I, I, I, I, F, P, P, P, P, P, I, P, SZ, P]),
     "tts_pack_operands": (I, [P, P, P, I, I, P, P]),
     "tts_unpack_slot_grads": (I, [P, I, I, P, P, P, P]),
     "tts_render_fwd": (I, [P, I, P, I, I, I, I, P, I, P, P, P, P]),

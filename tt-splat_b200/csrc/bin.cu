@@ -162,10 +162,10 @@ __device__ __forceinline__ u64 make_key(int j, float4 r, float ctx, float cty) {
 // Writes the outputs of one tile from its sorted keys (threads first, first+step, ... of the
 // caller's group): idx/count/cand, the stencil-indexed inverse table and, with PACK, the slot
 // rows theta_u (tools/m4_train_binned.py:130-143, the reference's fp32 op order) | color_o | keo.
-template <bool PACK>
+template <int PACK>
 __device__ __forceinline__ void emit_tile(const u64* keys, int n, int v, int t, int ntx, int T, int G, int S, int K,
                                           const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
-                                          int* __restrict__ inv, float* __restrict__ slots, int first, int step) {
+                                          int* __restrict__ inv, void* __restrict__ slots, int first, int step) {
   const int cnt = min(n, K);
   const int tx = t % ntx, ty = t / ntx;
   const float ox = (float)(tx * 16), oy = (float)(ty * 16);
@@ -185,12 +185,32 @@ __device__ __forceinline__ void emit_tile(const u64* keys, int n, int v, int t, 
         const float Q = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(a, mux), mux),
                                             __fmul_rn(__fmul_rn(__fmul_rn(2.0f, b), mux), muy)),
                                   __fmul_rn(__fmul_rn(c, muy), muy));
-        float4* dst = reinterpret_cast<float4*>(slots + o * TTS_SLOT_FLOATS);
-        dst[0] = make_float4(__fmul_rn(-a, inv_k), __fmul_rn(-c, inv_k), __fmul_rn(__fmul_rn(-2.0f, b), inv_k),
-                             __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(a, mux), __fmul_rn(b, muy))), inv_k));
-        dst[1] = make_float4(__fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(b, mux), __fmul_rn(c, muy))), inv_k),
-                             __fsub_rn(1.0f, __fmul_rn(Q, inv_k)), p1.y, p1.z);
-        dst[2] = make_float4(p1.w, p2.x, 0.f, 0.f);
+        const float th[6] = {__fmul_rn(-a, inv_k), __fmul_rn(-c, inv_k), __fmul_rn(__fmul_rn(-2.0f, b), inv_k),
+                             __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(a, mux), __fmul_rn(b, muy))), inv_k),
+                             __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(b, mux), __fmul_rn(c, muy))), inv_k),
+                             __fsub_rn(1.0f, __fmul_rn(Q, inv_k))};
+        if (PACK == 1) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(slots) + o * TTS_SLOT_FLOATS);
+          dst[0] = make_float4(th[0], th[1], th[2], th[3]);
+          dst[1] = make_float4(th[4], th[5], p1.y, p1.z);
+          dst[2] = make_float4(p1.w, p2.x, 0.f, 0.f);
+        } else {
+          // compact bf16 row: theta_u as a bf16 (hi, lo) pair (hi + lo carries ~16 significant
+          // bits, which u = Phi.theta needs), colour_o and o_col as bf16
+          __nv_bfloat16 r[16];
+#pragma unroll
+          for (int q = 0; q < 6; ++q) {
+            r[q] = __float2bfloat16_rn(th[q]);
+            r[6 + q] = __float2bfloat16_rn(__fsub_rn(th[q], __bfloat162float(r[q])));
+          }
+          r[12] = __float2bfloat16_rn(p1.y);
+          r[13] = __float2bfloat16_rn(p1.z);
+          r[14] = __float2bfloat16_rn(p1.w);
+          r[15] = __float2bfloat16_rn(p2.x);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(slots) + o * TTS_SLOT_BF16);
+          dst[0] = *reinterpret_cast<const uint4*>(&r[0]);
+          dst[1] = *reinterpret_cast<const uint4*>(&r[8]);
+        }
       }
     } else {
       idx[o] = -1;
@@ -291,11 +311,11 @@ __device__ __forceinline__ void sort_front(u64* keys, int m, int lane) {
 // overflow list for the block kernel).  Keys in per-warp shared memory; when n > K a two-level
 // histogram of q (64 then 32 bins) finds q*, the keys with q <= q* are compacted in place and
 // only those are sorted (warp-synchronous bitonic sort, no block barriers).
-template <bool PACK>
+template <int PACK>
 __global__ void __launch_bounds__(WB_WARPS * 32)
     k_bin_warp(const int* __restrict__ cell_start, const float4* __restrict__ rec, int G, int ntx, int nty, int R,
                int K, int V, const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
-               int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv, float* __restrict__ slots,
+               int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv, void* __restrict__ slots,
                int* __restrict__ ovf_list, int* __restrict__ ovf_count) {
   extern __shared__ u64 wsm[];
   __shared__ int whist[WB_WARPS][64];
@@ -440,12 +460,12 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
   }
 }
 
-template <bool PACK>
+template <int PACK>
 __global__ void __launch_bounds__(BS_THREADS)
     k_bin_select(const int* __restrict__ cell_start, const float4* __restrict__ rec, int G, int ntx, int nty,
                  int R, int K, const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
                  int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv,
-                 float* __restrict__ slots, const int* __restrict__ list, const int* __restrict__ list_count) {
+                 void* __restrict__ slots, const int* __restrict__ list, const int* __restrict__ list_count) {
   __shared__ u64 skeys[BS_CAP];
   __shared__ int shist[2048];
   __shared__ int s_beg[BS_MAXS], s_len[BS_MAXS], s_off[BS_MAXS + 1];
@@ -633,7 +653,7 @@ static BinWorkspace carve(void* ws, int G, int V, int T) {
 
 static int bin_core(const float* mu2d, const int* cell_count, const int2* cell_rank, int G, int V, int ntx,
                     int nty, int R, int K, const float* proj, float inv_k, int* idx, int* count, int* cand,
-                    int* inv, float* slots, BinWorkspace w, cudaStream_t st) {
+                    int* inv, void* slots, int slot_format, BinWorkspace w, cudaStream_t st) {
   const int T = ntx * nty;
   const int S = (2 * R + 1) * (2 * R + 1);
   if (inv) {
@@ -648,22 +668,25 @@ static int bin_core(const float* mu2d, const int* cell_count, const int2* cell_r
   const size_t wsmem = (size_t)WB_WARPS * WCAP * sizeof(u64);
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_bin_warp<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
-    cudaFuncSetAttribute(k_bin_warp<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    cudaFuncSetAttribute(k_bin_warp<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    cudaFuncSetAttribute(k_bin_warp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    cudaFuncSetAttribute(k_bin_warp<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
     attr = true;
   }
   const unsigned bblocks = (unsigned)(tiles < 296 ? tiles : 296);   // two blocks per SM loop over the list
-  if (proj && slots) {
-    k_bin_warp<true><<<wblocks, WB_WARPS * 32, wsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, proj, inv_k,
-                                                            idx, count, cand, inv, slots, w.ovf + 1, w.ovf);
-    k_bin_select<true><<<bblocks, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, proj, inv_k, idx, count,
-                                                       cand, inv, slots, w.ovf + 1, w.ovf);
+#define TTS_BIN_LAUNCH(P, PR, SL)                                                                              \
+  k_bin_warp<P><<<wblocks, WB_WARPS * 32, wsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, PR, inv_k, idx,   \
+                                                       count, cand, inv, SL, w.ovf + 1, w.ovf);                    \
+  k_bin_select<P><<<bblocks, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, PR, inv_k, idx, count,   \
+                                                  cand, inv, SL, w.ovf + 1, w.ovf);
+  if (proj && slots && slot_format == 1) {
+    TTS_BIN_LAUNCH(2, proj, slots)
+  } else if (proj && slots) {
+    TTS_BIN_LAUNCH(1, proj, slots)
   } else {
-    k_bin_warp<false><<<wblocks, WB_WARPS * 32, wsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, nullptr, inv_k,
-                                                             idx, count, cand, inv, nullptr, w.ovf + 1, w.ovf);
-    k_bin_select<false><<<bblocks, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, nullptr, inv_k, idx,
-                                                        count, cand, inv, nullptr, w.ovf + 1, w.ovf);
+    TTS_BIN_LAUNCH(0, nullptr, nullptr)
   }
+#undef TTS_BIN_LAUNCH
   return check_launch("binning");
 }
 
@@ -698,14 +721,15 @@ extern "C" int tts_bin_from_mu2d(const float* mu2d, const uint8_t* keep, int G, 
     k_cell_count<<<dim3((G + 255) / 256, V), 256, 0, st>>>(reinterpret_cast<const float2*>(mu2d), keep, G, ntx, nty,
                                                             w.cell_count, w.cell_rank);
   return bin_core(mu2d, w.cell_count, w.cell_rank, G, V, ntx, nty, R, K, nullptr, 0.f, idx, count, cand, inv, nullptr,
-                  w, st);
+                  0, w, st);
 }
 
 extern "C" int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float* proj, const int32_t* cell_count,
                             const int32_t* cell_rank, int G, int V, int H, int W, int R, int K, float k_poly,
-                            int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv, float* slots, void* workspace,
-                            size_t workspace_bytes, void* stream) {
+                            int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv, void* slots,
+                            int slot_format, void* workspace, size_t workspace_bytes, void* stream) {
   (void)keep;
+  TTS_REQUIRE(slot_format == 0 || slot_format == 1, "slot_format must be 0 (fp32 rows) or 1 (compact bf16 rows)");
   if (int rc = validate(G, V, H, W, R, K)) return rc;
   const int ntx = W / 16, nty = H / 16, T = ntx * nty;
   if (workspace_bytes < bin_workspace_bytes(G, V, T)) return fail(TTS_ERR_CAPACITY, "binning workspace too small");
@@ -714,7 +738,7 @@ extern "C" int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float*
   TTS_REQUIRE(k_poly > 0.f, "k must be positive");
   BinWorkspace w = carve(workspace, G, V, T);
   return bin_core(mu2d, cell_count, reinterpret_cast<const int2*>(cell_rank), G, V, ntx, nty, R, K, proj,
-                  (float)(1.0 / (double)k_poly), idx, count, cand, inv, slots, w, as_stream(stream));
+                  (float)(1.0 / (double)k_poly), idx, count, cand, inv, slots, slot_format, w, as_stream(stream));
 }
 
 // ---- allocation-free binning -------------------------------------------------------------------

@@ -46,8 +46,28 @@ __global__ void __launch_bounds__(FWD_THREADS)
       ok = mbar_wait_bounded(&bar, 0);
     }
   } else {
-    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(slots_) + row0 * TTS_SLOT_FLOATS;
-    for (int i = tid; i < n * TTS_SLOT_FLOATS; i += FWD_THREADS) s_rows[i] = __bfloat162float(src[i]);
+    // compact bf16 rows (32 B: theta hi[6], theta lo[6], color_o[3], o_col) -> fp32 rows in
+    // shared memory, theta_u = hi + lo
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(slots_) + row0 * TTS_SLOT_BF16);
+    for (int sl = tid; sl < n; sl += FWD_THREADS) {
+      const uint4 lo8 = src[2 * sl], hi8 = src[2 * sl + 1];
+      const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&lo8);
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&hi8);
+      float* d = s_rows + sl * TTS_SLOT_FLOATS;
+      // a[0..5] theta hi, a[6..7] + b[0..3] theta lo, b[4..6] color_o, b[7] o_col
+      d[0] = __bfloat162float(a[0]) + __bfloat162float(a[6]);
+      d[1] = __bfloat162float(a[1]) + __bfloat162float(a[7]);
+      d[2] = __bfloat162float(a[2]) + __bfloat162float(b[0]);
+      d[3] = __bfloat162float(a[3]) + __bfloat162float(b[1]);
+      d[4] = __bfloat162float(a[4]) + __bfloat162float(b[2]);
+      d[5] = __bfloat162float(a[5]) + __bfloat162float(b[3]);
+      d[6] = __bfloat162float(b[4]);
+      d[7] = __bfloat162float(b[5]);
+      d[8] = __bfloat162float(b[6]);
+      d[9] = __bfloat162float(b[7]);
+      d[10] = 0.f;
+      d[11] = 0.f;
+    }
     __syncthreads();
   }
   if (!ok) return;   // status recorded; nothing of the tile is written

@@ -10,6 +10,7 @@ from ._lib import call, lib, ptr, stream
 
 SLOT_FLOATS = 12
 SLOT_GRAD_FLOATS = 10
+SLOT_BF16 = 16          # compact bf16 slot row: theta hi[6], theta lo[6], color_o[3], o_col
 PROJ_FLOATS = 12
 
 
@@ -82,25 +83,28 @@ def bin_from_mu2d(mu2d, keep, H, W, R, K, ws=None, with_inv=True):
     return idx, count, cand, inv
 
 
-def bin_pack(pj, G, H, W, R, K, k=4.0, ws=None, out=None, with_inv=True):
+def bin_pack(pj, G, H, W, R, K, k=4.0, ws=None, out=None, with_inv=True, bf16=False):
     """Binning + slot-row pack on the output of ``project`` (``with_inv=False``: no inverse table,
-    for forward-only rendering)."""
+    for forward-only rendering; ``bf16``: compact bf16 slot rows for the bf16 forward)."""
     V = pj["proj"].shape[0]
     _, _, T = tiles(H, W)
     dev = pj["proj"].device
     S = (2 * R + 1) ** 2
     if out is None:
+        slots = (torch.empty(V, T, K, SLOT_BF16, dtype=torch.bfloat16, device=dev) if bf16
+                 else torch.empty(V, T, K, SLOT_FLOATS, device=dev))
         out = dict(idx=torch.empty(V, T, K, dtype=torch.int32, device=dev),
                    count=torch.empty(V, T, dtype=torch.int32, device=dev),
                    cand=torch.empty(V, T, dtype=torch.int32, device=dev),
                    inv=torch.empty(V, G, S, dtype=torch.int32, device=dev) if with_inv else None,
-                   slots=torch.empty(V, T, K, SLOT_FLOATS, device=dev))
+                   slots=slots)
+    fmt = 1 if out["slots"].dtype == torch.bfloat16 else 0
     nbytes = lib().tts_bin_workspace_bytes(G, V, H, W)
     ws = ws or Workspace(dev)
     buf = ws.get(nbytes)
     call("tts_bin_pack", ptr(pj["mu2d"]), ptr(pj["keep"]), ptr(pj["proj"]), ptr(pj["cell_count"]), ptr(pj["cell_rank"]),
          G, V, H, W, R, K, float(k), ptr(out["idx"]), ptr(out["count"]), ptr(out["cand"]), ptr(out["inv"]),
-         ptr(out["slots"]), ptr(buf), nbytes, stream())
+         ptr(out["slots"]), fmt, ptr(buf), nbytes, stream())
     return out
 
 

@@ -26,8 +26,13 @@ class _BinnedRender(torch.autograd.Function):
         flat_d = flat.detach().contiguous()
         need_grad = ctx.needs_input_grad[0]
         pj = ops.project(flat_d, G, sh_degree, cams_t, H, W, blur, near)
-        bp = ops.bin_pack(pj, G, H, W, R, K, k, with_inv=need_grad)
-        slots = bp["slots"].to(torch.bfloat16).contiguous() if bf16 else bp["slots"]
+        if bf16 and not need_grad:
+            bp = ops.bin_pack(pj, G, H, W, R, K, k, with_inv=False, bf16=True)
+            slots = bp["slots"]
+        else:
+            # the backward always works on fp32 slot rows; the bf16 forward gets its own compact rows
+            bp = ops.bin_pack(pj, G, H, W, R, K, k, with_inv=need_grad)
+            slots = ops.bin_pack(pj, G, H, W, R, K, k, with_inv=False, bf16=True)["slots"] if bf16 else bp["slots"]
         rf = ops.render_fwd(slots, bp["count"], H, W, flat_d[59 * G:], c_b, bf16=bf16)
         ctx.save_for_backward(flat_d, cams_t, c_b, bp["slots"], bp["count"], bp["inv"], rf["img"], rf["den"],
                               pj["proj"])
