@@ -178,15 +178,16 @@ int tts_relocate(float* params, float* m, float* v, int G, float dead_thr, float
  * (spike/train.py:27-29 with the views spread over N ranks).  Buffers shared between the
  * ranks of one node are allocated here (tts_peer_alloc: cudaMalloc, zero-filled) and
  * exchanged with CUDA IPC handles (tts_ipc_handle_bytes bytes each; the host moves them).
- * Per step: tts_peer_barrier(phase 0) once every rank's gradient and loss are written;
- * tts_adam_peer: rank `rank` sums the N gradients of its 1/N shard in rank order, updates
- * the shard (and, on rank N-1, w_b_raw) with its moments m, v, and stores the new values into
- * all N parameter buffers; loss_total = sum of the N losses; tts_peer_barrier(phase 1) before
- * the parameters are read again.  params/grads/loss/flags are host arrays of N device
- * pointers (index = rank; this rank's own buffers included); flags point at 2*8 int32 per
- * rank, zero at start; epoch is a device int that grows every step (the step counter).  A
- * barrier that waits too long ORs 4 into the status word (tts_read_status) and returns.
- * N <= 8. */
+ * Per step: tts_peer_signal(phase 0) once this rank's gradient and loss are written;
+ * tts_adam_peer: waits until every rank signalled phase 0, sums the N gradients of this rank's
+ * 1/N shard in rank order, updates the shard (and, on rank N-1, w_b_raw) with its moments m, v,
+ * stores the new values into all N parameter buffers, and its last block to finish signals
+ * phase 1; loss_total = sum of the N losses; then tts_peer_sgld (SGLD after waiting for phase
+ * 1 of every rank) or tts_peer_wait(phase 1) before the parameters are read again.
+ * tts_peer_barrier = signal + wait in one kernel.  params/grads/loss/flags are host arrays of N
+ * device pointers (index = rank; this rank's own buffers included); flags point at 32 int32 per
+ * rank, zero at start; epoch is a device int that grows every step (the step counter).  A wait
+ * that runs too long ORs 4 into the status word (tts_read_status) and gives up.  N <= 8. */
 size_t tts_ipc_handle_bytes(void);
 int tts_peer_alloc(size_t bytes, void** ptr);
 int tts_peer_free(void* ptr);
@@ -195,10 +196,17 @@ int tts_ipc_open(const void* handle, void** ptr_out);
 int tts_ipc_close(void* ptr);
 int tts_peer_barrier(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch,
                      void* stream);
+int tts_peer_signal(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch,
+                    void* stream);
+int tts_peer_wait(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch,
+                  void* stream);
 int tts_adam_peer(float* const* params, const float* const* grads, float* m, float* v, int G,
                   int sh_degree, int rank, int N, const int32_t* step, const double* lr7,
                   double beta1, double beta2, double eps, const float* const* loss,
-                  float* loss_total, void* stream);
+                  float* loss_total, int32_t* const* flags, void* stream);
+int tts_peer_sgld(float* params, int G, double lr_means, float noise_lr, const float* eps_noise,
+                  const int32_t* step, uint64_t seed, int32_t* const* flags, int rank, int N,
+                  void* stream);
 
 /* ---- dense WSR (spike/backward.py:61-63, wsr_polysplat) -----------------------------------
  * C[P,3] from theta_u[G,6], o[G], color[G,3], w_b (device scalar), Phi[P,6], c_b[3], keep[G]

@@ -49,7 +49,10 @@ SIGNATURES = {
     "tts_ipc_open": (I, [P, C.POINTER(P)]),
     "tts_ipc_close": (I, [P]),
     "tts_peer_barrier": (I, [P, I, I, I, P, P]),
-    "tts_adam_peer": (I, [P, P, P, P, I, I, I, I, P, P, D, D, D, P, P, P]),
+    "tts_peer_signal": (I, [P, I, I, I, P, P]),
+    "tts_peer_wait": (I, [P, I, I, I, P, P]),
+    "tts_adam_peer": (I, [P, P, P, P, I, I, I, I, P, P, D, D, D, P, P, P, P]),
+    "tts_peer_sgld": (I, [P, I, D, F, P, P, U64, P, I, I, P]),
     "tts_wsr_dense_fwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P]),
     "tts_wsr_dense_bwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P, P, P, P, P, P]),
 }

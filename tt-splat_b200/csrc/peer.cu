@@ -16,7 +16,7 @@
 #include <algorithm>
 #include <cstring>
 
-#include "common.cuh"
+#include "sgld.cuh"
 
 namespace tts {
 
@@ -33,35 +33,54 @@ struct PeerI {
   int* p[PEER_MAX];
 };
 
-// Flags: flags_r[phase * PEER_MAX + q] on rank r holds the last epoch rank q reached in `phase`.
-__global__ void k_peer_barrier(PeerI flags, int rank, int N, int phase, const int* __restrict__ epoch_ptr) {
-  const int q = threadIdx.x;
-  const int epoch = *epoch_ptr;
-  __threadfence_system();   // this rank's earlier writes (local and peer) before the signal
-  int* mine = flags.p[0];
-  int* dstp = flags.p[0];
+// Flags: flags_r[phase * PEER_MAX + q] on rank r holds the last epoch rank q reached in `phase`;
+// flags_r[2 * PEER_MAX] counts the finished blocks of this rank's Adam kernel.
+constexpr int FLAG_COUNTER = 2 * PEER_MAX;
+
+// Store `epoch` into every rank's flag slot for (phase, rank); the caller has fenced its writes.
+__device__ __forceinline__ void peer_signal(PeerI flags, int rank, int N, int phase, int epoch) {
 #pragma unroll
-  for (int k = 1; k < PEER_MAX; ++k) {
-    if (k == rank) mine = flags.p[k];
-    if (k == q) dstp = flags.p[k];
-  }
-  if (q < N) {
-    volatile int* dst = dstp + phase * PEER_MAX + rank;
-    *dst = epoch;
-  }
-  __syncthreads();
-  if (q < N) {
-    volatile int* src = mine + phase * PEER_MAX + q;
+  for (int q = 0; q < PEER_MAX; ++q)
+    if (q < N) *(volatile int*)(flags.p[q] + phase * PEER_MAX + rank) = epoch;
+}
+
+// Wait (one thread, iteration limit) until all N ranks reached `epoch` in `phase`.
+__device__ __forceinline__ void peer_wait(const int* mine, int N, int phase, int epoch) {
+  for (int q = 0; q < N; ++q) {
+    const volatile int* src = mine + phase * PEER_MAX + q;
     int it = 0;
     while (*src < epoch) {
       if (++it > (1 << 22)) {
         atomicOr(&g_status, STATUS_PEER_TIMEOUT);
-        break;
+        return;
       }
-      __nanosleep(100);
+      __nanosleep(64);
     }
   }
   __threadfence_system();
+}
+
+// Signal and/or wait as a kernel of its own (one thread does it).
+__global__ void k_peer_sync(PeerI flags, int* mine, int rank, int N, int phase, const int* __restrict__ epoch_ptr,
+                            int do_signal, int do_wait) {
+  if (threadIdx.x != 0) return;
+  const int epoch = *epoch_ptr;
+  if (do_signal) {
+    __threadfence_system();   // this rank's earlier writes (local and peer) before the signal
+    peer_signal(flags, rank, N, phase, epoch);
+  }
+  if (do_wait) peer_wait(mine, N, phase, epoch);
+}
+
+// SGLD for every gaussian once all ranks' shards of the update have arrived (phase 1).
+__global__ void __launch_bounds__(256) k_sgld_peer(float* __restrict__ params, int G, double lr_means, float noise_lr,
+                                                    const float* __restrict__ eps_noise, const int* __restrict__ step_ptr,
+                                                    unsigned long long seed, const int* mine, int N) {
+  if (threadIdx.x == 0) peer_wait(mine, N, 1, *step_ptr);
+  __syncthreads();
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= G) return;
+  sgld_one(params, ParamLayout{G}, g, lr_means, noise_lr, eps_noise, *step_ptr, seed);
 }
 
 struct PeerAdamScalars {
@@ -85,10 +104,12 @@ __global__ void __launch_bounds__(256)
     k_adam_peer(PeerF params, PeerCF grads, float* __restrict__ m, float* __restrict__ v, int G, long long lo,
                 long long hi, int N, int rank, int wb_owner, const int* __restrict__ step_ptr,
                 const double* __restrict__ lr7, double beta1, double beta2, double eps, PeerCF loss,
-                float* __restrict__ loss_total) {
+                float* __restrict__ loss_total, PeerI flags, const float* own, int* mine) {
   __shared__ PeerAdamScalars s_a;
   if (threadIdx.x == 0) {
     const int step = *step_ptr;
+    // phase 0: every rank's gradient and loss are written
+    peer_wait(mine, N, 0, step);
     const double bc1 = 1.0 - pow(beta1, (double)step);
     const double bc2 = 1.0 - pow(beta2, (double)step);
     s_a.w1 = (float)(1.0 - beta1);
@@ -102,11 +123,8 @@ __global__ void __launch_bounds__(256)
   const PeerAdamScalars a = s_a;
   const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long stride = (long long)gridDim.x * blockDim.x;
-  // peer loops are unrolled to PEER_MAX with a guard, so the pointer tables stay in registers
-  const float* own = params.p[0];
-#pragma unroll
-  for (int q = 1; q < PEER_MAX; ++q)
-    if (q == rank) own = params.p[q];
+  // peer loops are unrolled to PEER_MAX with a guard (constant indices: the tables stay in the
+  // parameter space); this rank's own buffers come as separate arguments
   auto scalar_update = [&](long long e, float nss) {
     float g = 0.f;
 #pragma unroll
@@ -156,7 +174,19 @@ __global__ void __launch_bounds__(256)
     for (int q = 0; q < PEER_MAX; ++q)
       if (q < N) reinterpret_cast<float4*>(params.p[q])[i] = p4;
   }
-  __threadfence_system();   // the peer stores are visible system-wide before the barrier signals
+  // the block's stores (local and peer) before its count; the barrier orders the other threads'
+  // stores before thread 0's system-scope fence (cumulative), as in a grid barrier
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    // the last block of this rank to finish signals phase 1 to every rank
+    int* ctr = mine + FLAG_COUNTER;
+    if (atomicAdd(ctr, 1) == (int)gridDim.x - 1) {
+      *ctr = 0;
+      __threadfence_system();
+      peer_signal(flags, rank, N, 1, *step_ptr);
+    }
+  }
 }
 
 }  // namespace tts
@@ -200,22 +230,52 @@ extern "C" int tts_ipc_close(void* ptr) {
   return TTS_OK;
 }
 
-extern "C" int tts_peer_barrier(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch, void* stream) {
-  TTS_REQUIRE(flags && epoch && N >= 1 && N <= PEER_MAX && rank >= 0 && rank < N && (phase == 0 || phase == 1),
-              "bad peer barrier arguments");
-  PeerI f = {};
+static int peer_table(int32_t* const* flags, int N, PeerI& f) {
   for (int q = 0; q < N; ++q) {
     TTS_REQUIRE(flags[q], "null peer flag pointer");
     f.p[q] = flags[q];
   }
-  k_peer_barrier<<<1, 32, 0, as_stream(stream)>>>(f, rank, N, phase, epoch);
-  return check_launch("peer_barrier");
+  return TTS_OK;
+}
+
+static int peer_sync(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch, int sig, int wait,
+                     void* stream) {
+  TTS_REQUIRE(flags && epoch && N >= 1 && N <= PEER_MAX && rank >= 0 && rank < N && (phase == 0 || phase == 1),
+              "bad peer barrier arguments");
+  PeerI f = {};
+  if (int rc = peer_table(flags, N, f)) return rc;
+  k_peer_sync<<<1, 32, 0, as_stream(stream)>>>(f, flags[rank], rank, N, phase, epoch, sig, wait);
+  return check_launch("peer_sync");
+}
+
+extern "C" int tts_peer_barrier(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch, void* stream) {
+  return peer_sync(flags, rank, N, phase, epoch, 1, 1, stream);
+}
+
+extern "C" int tts_peer_signal(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch, void* stream) {
+  return peer_sync(flags, rank, N, phase, epoch, 1, 0, stream);
+}
+
+extern "C" int tts_peer_wait(int32_t* const* flags, int rank, int N, int phase, const int32_t* epoch, void* stream) {
+  return peer_sync(flags, rank, N, phase, epoch, 0, 1, stream);
+}
+
+extern "C" int tts_peer_sgld(float* params, int G, double lr_means, float noise_lr, const float* eps_noise,
+                             const int32_t* step, uint64_t seed, int32_t* const* flags, int rank, int N, void* stream) {
+  TTS_REQUIRE(params && step && flags && G >= 1 && N >= 1 && N <= PEER_MAX && rank >= 0 && rank < N,
+              "bad peer SGLD arguments");
+  PeerI f = {};
+  if (int rc = peer_table(flags, N, f)) return rc;
+  k_sgld_peer<<<(G + 255) / 256, 256, 0, as_stream(stream)>>>(params, G, lr_means, noise_lr, eps_noise, step, seed,
+                                                              flags[rank], N);
+  return check_launch("peer_sgld");
 }
 
 extern "C" int tts_adam_peer(float* const* params, const float* const* grads, float* m, float* v, int G, int sh_degree,
                              int rank, int N, const int32_t* step, const double* lr7, double beta1, double beta2,
-                             double eps, const float* const* loss, float* loss_total, void* stream) {
-  TTS_REQUIRE(params && grads && loss && m && v && step && lr7 && loss_total, "null pointer");
+                             double eps, const float* const* loss, float* loss_total, int32_t* const* flags,
+                             void* stream) {
+  TTS_REQUIRE(params && grads && loss && m && v && step && lr7 && loss_total && flags, "null pointer");
   TTS_REQUIRE(N >= 1 && N <= PEER_MAX && rank >= 0 && rank < N && G >= 1, "bad peer Adam arguments");
   PeerF P = {};
   PeerCF Gr = {}, L = {};
@@ -233,8 +293,10 @@ extern "C" int tts_adam_peer(float* const* params, const float* const* grads, fl
   const long long lo = std::min(n, (long long)rank * chunk), hi = std::min(n, lo + chunk);
   cudaStream_t st = as_stream(stream);
   long long blocks = (hi - lo) / 4 / 256 + 1;
-  if (blocks > 148 * 4) blocks = 148 * 4;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  PeerI f = {};
+  if (int rc = peer_table(flags, N, f)) return rc;
   k_adam_peer<<<(unsigned)blocks, 256, 0, st>>>(P, Gr, m, v, G, lo, hi, N, rank, N - 1, step, lr7, beta1, beta2, eps,
-                                                L, loss_total);
+                                                L, loss_total, f, params[rank], flags[rank]);
   return check_launch("adam_peer");
 }

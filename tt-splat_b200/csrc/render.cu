@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(FWD_THREADS)
     k_render_fwd(const void* __restrict__ slots_, const int* __restrict__ count, int ntx, int T, int H, int W, int K,
                  const float* __restrict__ w_b_ptr, int w_b_is_raw, const float* __restrict__ c_b,
                  float* __restrict__ img, float* __restrict__ den_out) {
-  __shared__ __align__(128) float s_rows[KMAX * TTS_SLOT_FLOATS];
+  extern __shared__ __align__(128) float s_rows[];    // K slot rows (sized at launch: more tiles per SM)
   __shared__ __align__(8) uint64_t bar;
   const int t = blockIdx.x, v = blockIdx.y, tid = threadIdx.x;
   const int n = count[(long long)v * T + t];
@@ -252,10 +252,11 @@ extern "C" int tts_render_fwd(const void* slots, int slots_bf16, const int32_t* 
   const int ntx = W / 16, T = ntx * (H / 16);
   dim3 grid(T, V);
   cudaStream_t st = as_stream(stream);
+  const size_t smem = (size_t)K * TTS_SLOT_FLOATS * sizeof(float);
   if (slots_bf16)
-    k_render_fwd<true><<<grid, FWD_THREADS, 0, st>>>(slots, count, ntx, T, H, W, K, w_b, w_b_is_raw, c_b, img, den);
+    k_render_fwd<true><<<grid, FWD_THREADS, smem, st>>>(slots, count, ntx, T, H, W, K, w_b, w_b_is_raw, c_b, img, den);
   else
-    k_render_fwd<false><<<grid, FWD_THREADS, 0, st>>>(slots, count, ntx, T, H, W, K, w_b, w_b_is_raw, c_b, img, den);
+    k_render_fwd<false><<<grid, FWD_THREADS, smem, st>>>(slots, count, ntx, T, H, W, K, w_b, w_b_is_raw, c_b, img, den);
   return check_launch("render_fwd");
 }
 

@@ -254,10 +254,28 @@ def peer_barrier(regions, phase, epoch):
     call("tts_peer_barrier", regions.t_flags, regions.rank, regions.world, int(phase), ptr(epoch), stream())
 
 
+def peer_signal(regions, phase, epoch):
+    _dev(epoch)
+    call("tts_peer_signal", regions.t_flags, regions.rank, regions.world, int(phase), ptr(epoch), stream())
+
+
+def peer_wait(regions, phase, epoch):
+    _dev(epoch)
+    call("tts_peer_wait", regions.t_flags, regions.rank, regions.world, int(phase), ptr(epoch), stream())
+
+
 def adam_peer(regions, m, v, G, sh_degree, step, lr7, loss_total, betas=(0.9, 0.999), eps=1e-8):
-    """tts_adam_peer: this rank's shard of the summed gradient through Adam, broadcast to all."""
+    """tts_adam_peer: waits for every rank's gradient (phase 0), runs this rank's shard of the
+    summed gradient through Adam, broadcasts it and signals phase 1."""
     _dev(m, v, step, lr7, loss_total)
     call("tts_adam_peer", regions.t_params, regions.t_grads, ptr(m), ptr(v), G, sh_degree, regions.rank,
          regions.world, ptr(step), ptr(lr7), float(betas[0]), float(betas[1]), float(eps), regions.t_loss,
-         ptr(loss_total), stream())
+         ptr(loss_total), regions.t_flags, stream())
+
+
+def peer_sgld(regions, flat, G, step, lr_means, noise_lr, eps_noise=None, seed=0):
+    """SGLD once every rank's update has arrived (phase 1)."""
+    _dev(flat, step, eps_noise)
+    call("tts_peer_sgld", ptr(flat), G, float(lr_means), float(noise_lr), ptr(eps_noise), ptr(step),
+         int(seed) & (2 ** 64 - 1), regions.t_flags, regions.rank, regions.world, stream())
 

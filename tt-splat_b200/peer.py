@@ -15,7 +15,7 @@ import torch
 from ._lib import call, lib
 
 _ALIGN = 256
-FLAG_INTS = 16             # 2 phases x 8 ranks
+FLAG_INTS = 32             # 2 phases x 8 ranks, the Adam block counter, padding
 
 
 def _round(n):

@@ -150,13 +150,16 @@ class TrainStep:
 
     def _update(self, relocate):
         if self.regions is not None:
-            # NVLink exchange: barrier, shard reduce + Adam + broadcast, barrier (replicas equal)
-            ops.peer_barrier(self.regions, 0, self.step_t)
+            # NVLink exchange: signal, (wait) shard reduce + Adam + broadcast (signal), (wait) SGLD;
+            # the replicas are bitwise equal afterwards
+            ops.peer_signal(self.regions, 0, self.step_t)
             ops.adam_peer(self.regions, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
                           self.loss_total)
-            ops.peer_barrier(self.regions, 1, self.step_t)
             if self.noise_lr > 0:
-                ops.sgld(self.flat, self.G, self.step_t, self.lr["means"], self.noise_lr, seed=self.seed)
+                ops.peer_sgld(self.regions, self.flat, self.G, self.step_t, self.lr["means"], self.noise_lr,
+                              seed=self.seed)
+            else:
+                ops.peer_wait(self.regions, 1, self.step_t)
         else:
             ops.adam_sgld(self.flat, self.grads, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
                           noise_lr=self.noise_lr, seed=self.seed)
@@ -242,7 +245,7 @@ class TrainStep:
         the relocation kernel."""
         n = 14
         if self.regions is not None:
-            n += 3 + (1 if self.noise_lr > 0 else 0)
+            n += 3                                       # signal, Adam, SGLD or wait
         else:
             n += 1 + (1 if self.noise_lr > 0 else 0)
         if relocate:
