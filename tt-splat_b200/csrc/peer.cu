@@ -37,19 +37,30 @@ struct PeerI {
 // flags_r[2 * PEER_MAX] counts the finished blocks of this rank's Adam kernel.
 constexpr int FLAG_COUNTER = 2 * PEER_MAX;
 
-// Store `epoch` into every rank's flag slot for (phase, rank); the caller has fenced its writes.
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Store `epoch` into every rank's flag slot for (phase, rank) with system-scope release
+// semantics: this thread's earlier writes, and those ordered before them, are visible to any
+// thread that acquires the flag.
 __device__ __forceinline__ void peer_signal(PeerI flags, int rank, int N, int phase, int epoch) {
 #pragma unroll
   for (int q = 0; q < PEER_MAX; ++q)
-    if (q < N) *(volatile int*)(flags.p[q] + phase * PEER_MAX + rank) = epoch;
+    if (q < N) st_release_sys(flags.p[q] + phase * PEER_MAX + rank, epoch);
 }
 
-// Wait (one thread, iteration limit) until all N ranks reached `epoch` in `phase`.
+// Wait (one thread, iteration limit) until all N ranks reached `epoch` in `phase` (acquire).
 __device__ __forceinline__ void peer_wait(const int* mine, int N, int phase, int epoch) {
   for (int q = 0; q < N; ++q) {
-    const volatile int* src = mine + phase * PEER_MAX + q;
+    const int* src = mine + phase * PEER_MAX + q;
     int it = 0;
-    while (*src < epoch) {
+    while (ld_acquire_sys(src) < epoch) {
       if (++it > (1 << 22)) {
         atomicOr(&g_status, STATUS_PEER_TIMEOUT);
         return;
@@ -57,7 +68,6 @@ __device__ __forceinline__ void peer_wait(const int* mine, int N, int phase, int
       __nanosleep(64);
     }
   }
-  __threadfence_system();
 }
 
 // Signal and/or wait as a kernel of its own (one thread does it).
@@ -65,10 +75,7 @@ __global__ void k_peer_sync(PeerI flags, int* mine, int rank, int N, int phase, 
                             int do_signal, int do_wait) {
   if (threadIdx.x != 0) return;
   const int epoch = *epoch_ptr;
-  if (do_signal) {
-    __threadfence_system();   // this rank's earlier writes (local and peer) before the signal
-    peer_signal(flags, rank, N, phase, epoch);
-  }
+  if (do_signal) peer_signal(flags, rank, N, phase, epoch);   // earlier kernels' writes precede it
   if (do_wait) peer_wait(mine, N, phase, epoch);
 }
 
@@ -174,12 +181,12 @@ __global__ void __launch_bounds__(256)
     for (int q = 0; q < PEER_MAX; ++q)
       if (q < N) reinterpret_cast<float4*>(params.p[q])[i] = p4;
   }
-  // the block's stores (local and peer) before its count; the barrier orders the other threads'
-  // stores before thread 0's system-scope fence (cumulative), as in a grid barrier
+  // The block's stores (local and peer) are made visible system-wide before its count (barrier,
+  // then thread 0's system-scope fence, cumulative over the block's stores); the last block to
+  // count publishes phase 1 with release stores.
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
-    // the last block of this rank to finish signals phase 1 to every rank
     int* ctr = mine + FLAG_COUNTER;
     if (atomicAdd(ctr, 1) == (int)gridDim.x - 1) {
       *ctr = 0;
