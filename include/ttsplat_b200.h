@@ -59,10 +59,12 @@ int tts_read_status(int* status_host);      /* synchronous read + clear; diagnos
  * (eval_sh_color on means - camera centre, spike/render.py:22-25) and the activations of
  * _operands, tools/m4_train_binned.py:194-202 (o = sigmoid, keo = keep*o, color_o = keo*colour).
  * Also counts kept gaussians per home cell into cell_count[V][T] (must be zeroed) and writes
- * each gaussian's (cell, rank-in-cell) into cell_rank[V][G][2] for the binning scatter. */
+ * each gaussian's (cell, rank-in-cell) into cell_rank[V][G][2] for the binning scatter.
+ * depth_bt (device float[2] = depth_beta, depth_tau, or NULL) selects arm B (spike/arms.py:34-37):
+ * the opacity is scaled by sigmoid(depth_beta * (depth_tau - z)) of the camera-space z. */
 int tts_project(const float* params, int G, int sh_degree, const float* cams, int V, int H, int W,
                 float blur, float near_plane, float* proj, float* mu2d, uint8_t* keep,
-                int32_t* cell_count, int32_t* cell_rank, void* stream);
+                int32_t* cell_count, int32_t* cell_rank, const float* depth_bt, void* stream);
 
 /* ---- spatial-hash binning ----------------------------------------------------------------
  * Replaces assign_bins, tools/m4_train_binned.py:75-127 (canonical = stable order of its key
@@ -136,15 +138,16 @@ int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W,
  * over the V views in view order; adds the reg_loss gradient (spike/mcmc.py:18-22) and the
  * w_b_raw gradient from the per-tile partials.  grads has the params layout (overwritten).
  * proj is the tts_project output for the same params and cameras (its 2-D means and conics
- * feed the theta-build backward).  The per-(view, gaussian) gathered records go through the
+ * feed the theta-build backward).  Arm B: depth_bt as given to tts_project, and g_depth_bt
+ * (device float[2]) receives d/d depth_beta and d/d depth_tau; both NULL for arm A.  The per-(view, gaussian) gathered records go through the
  * workspace (tts_backward_workspace_bytes). */
 size_t tts_backward_workspace_bytes(int G, int V);
 int tts_backward_params(const float* params, int G, int sh_degree, const float* cams, int V,
                         int H, int W, int R, int K, float k_poly, float blur, float near_plane,
                         const float* proj, const int32_t* inv, const float* slot_grads,
                         const float* gwb_partial,
-                        float lambda_o, float lambda_s, float* grads, void* workspace,
-                        size_t workspace_bytes, void* stream);
+                        float lambda_o, float lambda_s, float* grads, const float* depth_bt,
+                        float* g_depth_bt, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- Adam + SGLD ----------------------------------------------------------------------
  * torch.optim.Adam step (spike/train.py:19,29; groups spike/model.py:82-95) over the flat

@@ -35,13 +35,19 @@ def colour_of(params, sh_degree, cam):
 
 
 def render_view(params, sh_degree, cam, K=128, R=1, k=4.0, blur=0.3, near=0.2, bins=None,
-                c_b=(1.0, 1.0, 1.0)):
-    """Forward for one view; returns a dict with the image and everything the backward needs."""
+                c_b=(1.0, 1.0, 1.0), depth_bt=None):
+    """Forward for one view; returns a dict with the image and everything the backward needs.
+    ``depth_bt`` = (depth_beta, depth_tau) selects arm B (spike/arms.py:34-37): the opacity is
+    scaled by rho = sigmoid(depth_beta (depth_tau - z)) of the camera-space z."""
     conic, mu2d, depth, keep, gcache = geometry.fwd(params["means3d"], params["quats"],
                                                     params["log_scales"], cam, blur, near)
     mu2d32, conic32 = mu2d.astype(F32), conic.astype(F32)
     colour, pre, dirs = colour_of(params, sh_degree, cam)
     o = render.sigmoid(params["opacity_raw"]).astype(F32)
+    rho = np.ones_like(o, dtype=np.float64)
+    if depth_bt is not None:
+        rho = render.sigmoid(float(depth_bt[0]) * (float(depth_bt[1]) - np.asarray(depth, np.float64)))
+        o = (o * rho).astype(F32)
     tm = binning.tile_map(cam["H"], cam["W"])
     if bins is None:
         bins = binning.assign_bins(mu2d32, keep, tm, R, K)
@@ -50,7 +56,8 @@ def render_view(params, sh_degree, cam, K=128, R=1, k=4.0, blur=0.3, near=0.2, b
     img, den, rcache = render.render_fwd(theta, col, oc, w_b, np.asarray(c_b, F32), tm)
     return dict(img=img, den=den, rcache=rcache, bins=bins, tm=tm, theta=theta, col=col, oc=oc,
                 w_b=w_b, mu2d=mu2d32, conic=conic32, keep=keep, depth=depth, gcache=gcache,
-                colour=colour, pre=pre, dirs=dirs, o=o, c_b=np.asarray(c_b, F32), k=k)
+                colour=colour, pre=pre, dirs=dirs, o=render.sigmoid(params["opacity_raw"]).astype(F32), rho=rho,
+                depth_bt=depth_bt, c_b=np.asarray(c_b, F32), k=k, cam=cam)
 
 
 def backward_view(fw, gimg, params, sh_degree):
@@ -65,11 +72,19 @@ def backward_view(fw, gimg, params, sh_degree):
     gm, gq, gs = geometry.bwd(fw["gcache"], g9[:, 0], g9[:, 1], g9[:, 2], g9[:, 3], g9[:, 4])
     keepf = fw["keep"].astype(np.float64)
     o = fw["o"].astype(np.float64)
-    keo = keepf * o
+    rho = fw["rho"]
+    keo = keepf * o * rho
     gcolor_o, go_col = g9[:, 5:8], g9[:, 8]
     gkeo = (gcolor_o * fw["colour"]).sum(-1) + go_col
     gcolour = gcolor_o * keo[:, None]
-    gop = gkeo * keepf * o * (1.0 - o)
+    gop = gkeo * keepf * rho * o * (1.0 - o)
+    gdepth = None
+    if fw["depth_bt"] is not None:
+        beta, tau = float(fw["depth_bt"][0]), float(fw["depth_bt"][1])
+        grho = gkeo * keepf * o * rho * (1.0 - rho)
+        z = np.asarray(fw["depth"], np.float64)
+        gdepth = (float((grho * (tau - z)).sum()), float((grho * beta).sum()))
+        gm = gm + (-grho * beta)[:, None] * np.asarray(fw["cam"]["R_v"], np.float64)[2][None, :]
     grest = np.zeros((G, 15, 3))
     if sh_degree > 0:
         coeffs = np.concatenate([np.asarray(params["color_dc"], np.float64)[:, None, :],
@@ -80,9 +95,12 @@ def backward_view(fw, gimg, params, sh_degree):
         grest[:, :gco.shape[1] - 1] = gco[:, 1:]
     else:
         gdc = gcolour * sh.C0 * (fw["pre"] >= 0.0)
-    return dict(means3d=gm, log_scales=gs * fw["gcache"]["scale"], quats=gq, opacity_raw=gop,
-                color_dc=gdc, color_rest=grest,
-                w_b_raw=float(gw_b) * float(render.sigmoid(params["w_b_raw"])))
+    out = dict(means3d=gm, log_scales=gs * fw["gcache"]["scale"], quats=gq, opacity_raw=gop,
+               color_dc=gdc, color_rest=grest,
+               w_b_raw=float(gw_b) * float(render.sigmoid(params["w_b_raw"])))
+    if gdepth is not None:
+        out["depth_beta"], out["depth_tau"] = gdepth
+    return out
 
 
 def loss_and_grads(params, cams, targets, sh_degree, K=128, R=1, k=4.0, lam=0.2,

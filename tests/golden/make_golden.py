@@ -257,6 +257,37 @@ def gen_render(R, syn, out):
                         **cam_arrays(cam), **p, **res)
 
 
+def gen_arm_b(R, syn, out):
+    """Arm B (spike/arms.py:34-37: o * sigmoid(depth_beta * (depth_tau - depth))) through the
+    reference's dense render (spike/render.py:14-49) on a scene whose tiles do not overflow K = 256
+    and whose gaussians stay inside their 3x3 stencil, so the binned path must agree with it."""
+    from spike import render as ref_render
+    sc = syn.config0(seed=31, G=150, res=64)
+    p, cam, tgt = sc["params"], sc["cams"][0], sc["targets"][0]
+    out_arrays = {}
+    for deg, tag in ((0, "deg0"), (3, "deg3")):
+        model = make_model(p, deg)
+        model.depth_beta = torch.tensor(1.3, requires_grad=True)
+        model.depth_tau = torch.tensor(3.9, requires_grad=True)
+        img = ref_render.render(model, ref_cam(R, cam), "B", sh_degree=deg)
+        wts = torch.from_numpy(np.random.default_rng(32).standard_normal(img.shape).astype(np.float32))
+        (img * wts).sum().backward()
+        out_arrays[f"{tag}__img"] = img.detach().numpy()
+        for k in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc", "color_rest"):
+            gk = getattr(model, k).grad
+            out_arrays[f"{tag}__grad_{k}"] = (gk if gk is not None else torch.zeros_like(getattr(model, k))).numpy()
+        out_arrays[f"{tag}__grad_w_b_raw"] = np.float32(model.w_b_raw.grad)
+        out_arrays[f"{tag}__grad_depth_beta"] = np.float32(model.depth_beta.grad)
+        out_arrays[f"{tag}__grad_depth_tau"] = np.float32(model.depth_tau.grad)
+        out_arrays["wts"] = wts.numpy()
+    with torch.no_grad():
+        mu2d, _, _, keep = project(R, p, cam)
+    cand = cand_of(R, mu2d, keep, cam["H"], cam["W"], 1)
+    assert int(cand.max()) <= 256, int(cand.max())
+    np.savez_compressed(os.path.join(out, "render_arm_b.npz"), depth_beta=np.float32(1.3), depth_tau=np.float32(3.9),
+                        K=256, **cam_arrays(cam), **p, **out_arrays)
+
+
 def gen_geom(R, syn, out):
     sc = syn.config0(seed=5, G=500)
     p, cam = sc["params"], sc["cams"][0]
@@ -370,7 +401,7 @@ def main():
     jobs = dict(bins_scene=lambda: gen_bins_scene(R, syn, HERE), bins_stress=lambda: gen_bins_stress(R, syn, HERE),
                 bins_big=lambda: gen_bins_big(R, syn, HERE), render=lambda: gen_render(R, syn, HERE),
                 geom=lambda: gen_geom(R, syn, HERE), loss=lambda: gen_loss(R, HERE),
-                optim=lambda: gen_optim(R, syn, HERE))
+                optim=lambda: gen_optim(R, syn, HERE), arm_b=lambda: gen_arm_b(R, syn, HERE))
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
             continue

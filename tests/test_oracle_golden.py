@@ -172,6 +172,26 @@ def test_param_grads_vs_reference_autograd(fixture, deg):
     assert abs(g["w_b_raw"] - float(z["grad_w_b_raw"])) < 1e-3 * abs(float(z["grad_w_b_raw"]))
 
 
+@pytest.mark.parametrize("deg", [0, 3])
+def test_arm_b_vs_reference_autograd(deg):
+    """Arm B (opacity x sigmoid(depth_beta (depth_tau - z))) image and gradients, including the
+    two depth parameters, against the reference's dense render + autograd."""
+    z = golden("render_arm_b.npz")
+    cam = cam_from(z)
+    p = params_from(z)
+    bt = (float(z["depth_beta"]), float(z["depth_tau"]))
+    fw = pipeline.render_view(p, deg, cam, K=int(z["K"]), depth_bt=bt)
+    pre = f"deg{deg}__"
+    assert np.abs(fw["img"] - z[pre + "img"]).max() < 1e-4
+    g = pipeline.backward_view(fw, z["wts"].astype(np.float32), p, deg)
+    names = ["means3d", "log_scales", "quats", "opacity_raw", "color_dc"] + (["color_rest"] if deg else [])
+    for n in names:
+        assert rel_l2(g[n], z[pre + "grad_" + n]) < 1e-3, (n, rel_l2(g[n], z[pre + "grad_" + n]))
+    for n in ("w_b_raw", "depth_beta", "depth_tau"):
+        ref = float(z[pre + "grad_" + n])
+        assert abs(g[n] - ref) < 1e-3 * abs(ref), (n, g[n], ref)
+
+
 def test_geometry_bwd_vs_reference():
     z = golden("geom_bwd.npz")
     cam = cam_from(z)

@@ -24,7 +24,7 @@ SIGNATURES = {
     "tts_version": (I, []),
     "tts_last_error": (C.c_char_p, []),
     "tts_read_status": (I, [P]),
-    "tts_project": (I, [P, I, I, P, I, I, I, F, F, P, P, P, P, P, P]),
+    "tts_project": (I, [P, I, I, P, I, I, I, F, F, P, P, P, P, P, P, P]),
     "tts_bin_workspace_bytes": (SZ, [I, I, I, I]),
     "tts_bin_from_mu2d": (I, [P, P, I, I, I, I, I, I, P, P, P, P, P, SZ, P]),
     "tts_bin_from_mu2d_noalloc": (I, [P, P, I, I, I, I, I, I, P, P, P, P, P]),
@@ -36,7 +36,7 @@ SIGNATURES = {
     "tts_loss_workspace_bytes": (SZ, [I, I, I]),
     "tts_loss_l1_ssim": (I, [P, P, I, I, I, F, F, P, P, P, SZ, P]),
     "tts_backward_workspace_bytes": (SZ, [I, I]),
-    "tts_backward_params": (I, [P, I, I, P, I, I, I, I, I, F, F, F, P, P, P, P, F, F, P, P, SZ, P]),
+    "tts_backward_params": (I, [P, I, I, P, I, I, I, I, I, F, F, F, P, P, P, P, F, F, P, P, P, P, SZ, P]),
     "tts_adam_sgld": (I, [P, P, P, P, I, I, P, P, D, D, D, F, P, U64, P]),
     "tts_step_begin": (I, [P, P]),
     "tts_sgld": (I, [P, I, D, F, P, P, U64, P]),

@@ -93,11 +93,16 @@ __device__ __forceinline__ void colour_pre(const float* s, const Loaded& x, cons
   }
 }
 
-template <int DEG, int LPG>
+// Arm B (spike/arms.py:34-37) scales the opacity by the depth weight
+// rho = sigmoid(depth_beta * (depth_tau - z)) of the camera-space z (spike/geometry.py:43).
+__device__ __forceinline__ float depth_weight(const float* bt, float z) { return sigmoidf(bt[0] * (bt[1] - z)); }
+
+template <int DEG, int LPG, bool ARMB>
 __global__ void __launch_bounds__(GB_THREADS)
     k_project(const float* __restrict__ params, int G, const float* __restrict__ cams, int V, int ntx, int nty,
               float blur, float near_plane, float* __restrict__ proj, float* __restrict__ mu2d,
-              uint8_t* __restrict__ keep, int* __restrict__ cell_count, int2* __restrict__ cell_rank) {
+              uint8_t* __restrict__ keep, int* __restrict__ cell_count, int2* __restrict__ cell_rank,
+              const float* __restrict__ depth_bt) {
   constexpr int GPB = GB_THREADS / LPG;
   __shared__ float s_p[GPB * PSTRIDE];
   const int g0 = blockIdx.x * GPB;
@@ -122,7 +127,7 @@ __global__ void __launch_bounds__(GB_THREADS)
       if (DEG > 0) view_dir(x.m, cam, d, nrm);
       float pre[3];
       colour_pre<DEG>(sp, x, d, pre);
-      const float keo = f.keep ? o : 0.f;
+      const float keo = f.keep ? (ARMB ? o * depth_weight(depth_bt, f.mcz) : o) : 0.f;
       const long long o_ = (long long)v * G + g;
       float4* pr = reinterpret_cast<float4*>(proj + o_ * TTS_PROJ_FLOATS);
       pr[0] = make_float4(f.mux, f.muy, f.a, f.b);
@@ -224,11 +229,11 @@ __global__ void __launch_bounds__(256)
 // (tools/operands_manual.py:103-110) and SH backward (coefficients and viewing direction); the
 // lanes' partial sums are combined by a butterfly, then the reg_loss gradient
 // (spike/mcmc.py:18-22) is added and the gaussian's 59 gradients are written.
-template <int DEG, int LPG>
+template <int DEG, int LPG, bool ARMB>
 __global__ void __launch_bounds__(GB_THREADS, 3)
     k_backward(const float* __restrict__ params, int G, const float* __restrict__ cams, int V, float blur,
                float near_plane, const float4* __restrict__ rec, float lambda_o, float lambda_s,
-               float* __restrict__ grads) {
+               float* __restrict__ grads, const float* __restrict__ depth_bt, float2* __restrict__ bt_partial) {
   constexpr int GPB = GB_THREADS / LPG;
   constexpr int NB = (DEG + 1) * (DEG + 1);
   __shared__ float s_p[GPB * PSTRIDE];
@@ -243,6 +248,7 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
   if (g < G) load_staged(sp, x);
   const float o = g < G ? sigmoidf(x.op) : 0.f;
   float gm[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f}, gs[3] = {0.f, 0.f, 0.f}, gop = 0.f;
+  float2 gbt = make_float2(0.f, 0.f);       // arm B: d/d depth_beta, d/d depth_tau of this thread
   float gco[NB][3];
 #pragma unroll
   for (int k = 0; k < NB; k++)
@@ -265,10 +271,20 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
       float pre[3];
       colour_pre<DEG>(sp, x, d, pre);
       const float keepf = f.keep ? 1.f : 0.f;
-      const float keo = keepf * o;
+      const float rho = ARMB ? depth_weight(depth_bt, f.mcz) : 1.f;
+      const float keo = keepf * o * rho;
       const float gkeo =
           gcol[0] * fmaxf(pre[0], 0.f) + gcol[1] * fmaxf(pre[1], 0.f) + gcol[2] * fmaxf(pre[2], 0.f) + goc;
-      gop += gkeo * keepf * o * (1.f - o);
+      gop += gkeo * keepf * rho * o * (1.f - o);
+      if (ARMB) {
+        // keo = keep o rho, rho = sigmoid(beta (tau - z)): d rho = rho (1 - rho) (beta, tau - z, -beta)
+        const float grho = gkeo * keepf * o * rho * (1.f - rho);
+        gbt.x += grho * (depth_bt[1] - f.mcz);
+        gbt.y += grho * depth_bt[0];
+        const float gz = -grho * depth_bt[0];            // z = R_v[2] . means + t_v[2]
+#pragma unroll
+        for (int i = 0; i < 3; i++) gm[i] += gz * cam.R[2 * 3 + i];
+      }
       float gr[3];
 #pragma unroll
       for (int c = 0; c < 3; c++) gr[c] = pre[c] >= 0.f ? gcol[c] * keo : 0.f;   // torch clamp passes at 0
@@ -339,12 +355,42 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
     for (int c = 0; c < 3; c++) put(14 + 3 * (k - 1) + c, k < NB ? gco[k < NB ? k : 0][c] : 0.f);
   __syncthreads();
   unstage_rows<GPB>(s_p, G, g0, grads);
+  if (ARMB) {
+    // this block's (d beta, d tau): warp sums, then the warps in order (deterministic)
+    __shared__ float2 s_bt[GB_THREADS / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      gbt.x += __shfl_xor_sync(0xffffffffu, gbt.x, o);
+      gbt.y += __shfl_xor_sync(0xffffffffu, gbt.y, o);
+    }
+    if ((threadIdx.x & 31) == 0) s_bt[threadIdx.x >> 5] = gbt;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float2 t = s_bt[0];
+      for (int w = 1; w < GB_THREADS / 32; ++w) {
+        t.x += s_bt[w].x;
+        t.y += s_bt[w].y;
+      }
+      bt_partial[blockIdx.x] = t;
+    }
+  }
 }
 
 // Deterministic sum of the per-tile w_b partials; grads[59G] = sum * softplus'(w_b_raw).
 __global__ void __launch_bounds__(1024) k_wb_reduce(const float* __restrict__ part, int n, const float* __restrict__ params,
-                                                     int G, float* __restrict__ grads) {
+                                                     int G, float* __restrict__ grads, const float2* __restrict__ bt_part,
+                                                     int nbt, float* __restrict__ g_depth_bt) {
   __shared__ float red[1024];
+  if (bt_part && threadIdx.x == 0) {
+    // arm B: the blocks' (d beta, d tau) in block order
+    float2 t = make_float2(0.f, 0.f);
+    for (int b = 0; b < nbt; ++b) {
+      t.x += bt_part[b].x;
+      t.y += bt_part[b].y;
+    }
+    g_depth_bt[0] = t.x;
+    g_depth_bt[1] = t.y;
+  }
   float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
   int i = threadIdx.x;
   for (; i + 3 * 1024 < n; i += 4 * 1024) {
@@ -371,22 +417,31 @@ static int lanes_for(int V) { return V >= 8 ? 8 : V >= 4 ? 4 : V >= 2 ? 2 : 1; }
 
 template <int DEG, int LPG>
 static void launch_project(const float* params, int G, const float* cams, int V, int ntx, int nty, float blur,
-                           float near_plane, float* proj, float* mu2d, uint8_t* keep, int* cc, int2* cr, cudaStream_t st) {
+                           float near_plane, float* proj, float* mu2d, uint8_t* keep, int* cc, int2* cr,
+                           const float* depth_bt, cudaStream_t st) {
   constexpr int GPB = GB_THREADS / LPG;
-  k_project<DEG, LPG><<<(G + GPB - 1) / GPB, GB_THREADS, 0, st>>>(params, G, cams, V, ntx, nty, blur, near_plane, proj,
-                                                                   mu2d, keep, cc, cr);
+  const unsigned nb = (G + GPB - 1) / GPB;
+  if (depth_bt)
+    k_project<DEG, LPG, true><<<nb, GB_THREADS, 0, st>>>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d,
+                                                         keep, cc, cr, depth_bt);
+  else
+    k_project<DEG, LPG, false><<<nb, GB_THREADS, 0, st>>>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d,
+                                                          keep, cc, cr, nullptr);
 }
 
 template <int DEG>
 static void project_deg(int lpg, const float* params, int G, const float* cams, int V, int ntx, int nty, float blur,
-                        float near_plane, float* proj, float* mu2d, uint8_t* keep, int* cc, int2* cr, cudaStream_t st) {
+                        float near_plane, float* proj, float* mu2d, uint8_t* keep, int* cc, int2* cr,
+                        const float* bt, cudaStream_t st) {
   switch (lpg) {
-    case 1: launch_project<DEG, 1>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, st); break;
-    case 2: launch_project<DEG, 2>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, st); break;
-    case 4: launch_project<DEG, 4>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, st); break;
-    default: launch_project<DEG, 8>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, st); break;
+    case 1: launch_project<DEG, 1>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, bt, st); break;
+    case 2: launch_project<DEG, 2>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, bt, st); break;
+    case 4: launch_project<DEG, 4>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, bt, st); break;
+    default: launch_project<DEG, 8>(params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cc, cr, bt, st); break;
   }
 }
+
+static size_t a256b(size_t x) { return (x + 255) & ~size_t(255); }
 
 }  // namespace tts
 
@@ -394,7 +449,7 @@ using namespace tts;
 
 extern "C" int tts_project(const float* params, int G, int sh_degree, const float* cams, int V, int H, int W,
                            float blur, float near_plane, float* proj, float* mu2d, uint8_t* keep, int32_t* cell_count,
-                           int32_t* cell_rank, void* stream) {
+                           int32_t* cell_rank, const float* depth_bt, void* stream) {
   TTS_REQUIRE(G >= 0 && V >= 1, "G must be >= 0 and V >= 1");
   TTS_REQUIRE(sh_degree >= 0 && sh_degree <= 3, "sh_degree must be in [0, 3]");
   TTS_REQUIRE(H > 0 && W > 0 && H % 16 == 0 && W % 16 == 0, "H and W must be positive multiples of 16");
@@ -404,29 +459,32 @@ extern "C" int tts_project(const float* params, int G, int sh_degree, const floa
   cudaStream_t st = as_stream(stream);
   const int ntx = W / 16, nty = H / 16, lpg = lanes_for(V);
   int2* cr = reinterpret_cast<int2*>(cell_rank);
+  const float* bt = depth_bt;
   switch (sh_degree) {
-    case 0: project_deg<0>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, st); break;
-    case 1: project_deg<1>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, st); break;
-    case 2: project_deg<2>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, st); break;
-    default: project_deg<3>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, st); break;
+    case 0: project_deg<0>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, bt, st); break;
+    case 1: project_deg<1>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, bt, st); break;
+    case 2: project_deg<2>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, bt, st); break;
+    default: project_deg<3>(lpg, params, G, cams, V, ntx, nty, blur, near_plane, proj, mu2d, keep, cell_count, cr, bt, st); break;
   }
   return check_launch("project");
 }
 
+// gathered records, then (arm B) one (d beta, d tau) partial per backward block (at most G of them)
 extern "C" size_t tts_backward_workspace_bytes(int G, int V) {
-  return (G > 0 && V > 0) ? (size_t)V * G * 48 : 0;   // one gathered 12-float record per (view, gaussian)
+  return (G > 0 && V > 0) ? a256b((size_t)V * G * 48) + a256b((size_t)G * 8) : 0;
 }
 
 extern "C" int tts_backward_params(const float* params, int G, int sh_degree, const float* cams, int V, int H, int W,
                                    int R, int K, float k_poly, float blur, float near_plane, const float* proj,
                                    const int32_t* inv, const float* slot_grads, const float* gwb_partial,
-                                   float lambda_o, float lambda_s, float* grads, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
+                                   float lambda_o, float lambda_s, float* grads, const float* depth_bt,
+                                   float* g_depth_bt, void* workspace, size_t workspace_bytes, void* stream) {
   TTS_REQUIRE(G >= 1 && V >= 1, "G and V must be >= 1");
   TTS_REQUIRE(sh_degree >= 0 && sh_degree <= 3, "sh_degree must be in [0, 3]");
   TTS_REQUIRE(H > 0 && W > 0 && H % 16 == 0 && W % 16 == 0, "H and W must be positive multiples of 16");
   TTS_REQUIRE(R >= 0 && R <= 3 && K >= 1 && K <= 256, "R in [0,3] and K in [1,256]");
   TTS_REQUIRE(params && cams && proj && inv && slot_grads && gwb_partial && grads, "null pointer");
+  TTS_REQUIRE((depth_bt == nullptr) == (g_depth_bt == nullptr), "depth_bt and g_depth_bt go together (arm B)");
   TTS_REQUIRE(((uintptr_t)slot_grads & 7u) == 0, "slot_grads must be 8-byte aligned");
   TTS_REQUIRE(aligned16(proj), "proj must be 16-byte aligned");
   TTS_REQUIRE(workspace && aligned16(workspace), "workspace must be a 16-byte aligned device buffer");
@@ -436,13 +494,20 @@ extern "C" int tts_backward_params(const float* params, int G, int sh_degree, co
   cudaStream_t st = as_stream(stream);
   const int lpg = lanes_for(V);
   float4* rec = static_cast<float4*>(workspace);
+  float2* btp = reinterpret_cast<float2*>(static_cast<char*>(workspace) + a256b((size_t)V * G * 48));
   const long long nvg = (long long)V * G;
   k_slot_gather<<<(unsigned)((nvg + 255) / 256), 256, 0, st>>>(proj, G, V, ntx, ntx * nty, S, K, inv_k, inv,
                                                               slot_grads, rec);
   if (int rc = check_launch("slot_gather")) return rc;
+  int nblk = 0;
 #define TTS_BWD(D, P)                                                                                              \
-  k_backward<D, P><<<(G + GB_THREADS / P - 1) / (GB_THREADS / P), GB_THREADS, 0, st>>>(                           \
-      params, G, cams, V, blur, near_plane, rec, lambda_o, lambda_s, grads);
+  nblk = (G + GB_THREADS / P - 1) / (GB_THREADS / P);                                                              \
+  if (depth_bt)                                                                                                    \
+    k_backward<D, P, true><<<nblk, GB_THREADS, 0, st>>>(params, G, cams, V, blur, near_plane, rec, lambda_o,       \
+                                                        lambda_s, grads, depth_bt, btp);                           \
+  else                                                                                                             \
+    k_backward<D, P, false><<<nblk, GB_THREADS, 0, st>>>(params, G, cams, V, blur, near_plane, rec, lambda_o,      \
+                                                         lambda_s, grads, nullptr, nullptr);
 #define TTS_BWD_DEG(D)            \
   switch (lpg) {                  \
     case 1: TTS_BWD(D, 1) break;  \
@@ -459,6 +524,7 @@ extern "C" int tts_backward_params(const float* params, int G, int sh_degree, co
 #undef TTS_BWD_DEG
 #undef TTS_BWD
   if (int rc = check_launch("backward_params")) return rc;
-  k_wb_reduce<<<1, 1024, 0, st>>>(gwb_partial, V * ntx * nty, params, G, grads);
+  k_wb_reduce<<<1, 1024, 0, st>>>(gwb_partial, V * ntx * nty, params, G, grads, depth_bt ? btp : nullptr, nblk,
+                                  g_depth_bt);
   return check_launch("wb_reduce");
 }

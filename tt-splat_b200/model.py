@@ -81,11 +81,19 @@ class GaussianModel(nn.Module):
         self.flat = nn.Parameter(_flat.to(device=device, dtype=torch.float32).contiguous())
         self.register_buffer("c_b", torch.ones(3, device=device))
         self.depth_tau_init = depth_tau
+        # arm B's global depth weight sigmoid(depth_beta * (depth_tau - z)) (spike/model.py:48-49)
+        self.depth_beta = nn.Parameter(torch.tensor(1.0, device=device))
+        self.depth_tau = nn.Parameter(torch.tensor(float(depth_tau), device=device))
 
     @classmethod
     def from_arrays(cls, params, device="cuda"):
         G = int(np.asarray(params["means3d"]).shape[0])
-        return cls(G, device=device, _flat=pack_arrays(params))
+        m = cls(G, device=device, _flat=pack_arrays(params))
+        with torch.no_grad():
+            for k in ("depth_beta", "depth_tau"):
+                if k in params:
+                    getattr(m, k).fill_(float(np.asarray(params[k])))
+        return m
 
     @property
     def G(self):

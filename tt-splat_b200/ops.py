@@ -42,9 +42,10 @@ class Workspace:
         return self.buf
 
 
-def project(flat, G, sh_degree, cams, H, W, blur=0.3, near=0.2, out=None):
-    """Geometry + SH + activations for V = cams.shape[0] views (also counts home cells)."""
-    _dev(flat, cams)
+def project(flat, G, sh_degree, cams, H, W, blur=0.3, near=0.2, out=None, depth_bt=None):
+    """Geometry + SH + activations for V = cams.shape[0] views (also counts home cells);
+    ``depth_bt`` (device [depth_beta, depth_tau]) selects arm B's depth-weighted opacity."""
+    _dev(flat, cams, depth_bt)
     V = cams.shape[0]
     _, _, T = tiles(H, W)
     dev = flat.device
@@ -56,7 +57,7 @@ def project(flat, G, sh_degree, cams, H, W, blur=0.3, near=0.2, out=None):
     else:
         out["cell_count"].zero_()
     call("tts_project", ptr(flat), G, sh_degree, ptr(cams), V, H, W, float(blur), float(near), ptr(out["proj"]),
-         ptr(out["mu2d"]), ptr(out["keep"]), ptr(out["cell_count"]), ptr(out["cell_rank"]), stream())
+         ptr(out["mu2d"]), ptr(out["keep"]), ptr(out["cell_count"]), ptr(out["cell_rank"]), ptr(depth_bt), stream())
     return out
 
 
@@ -149,20 +150,24 @@ def loss_l1_ssim(img, target, lam=0.2, grad_scale=1.0, ws=None, out=None):
 
 
 def backward_params(flat, G, sh_degree, cams, H, W, R, K, inv, slot_grads, gwb, k=4.0, blur=0.3, near=0.2,
-                    lambda_o=0.0, lambda_s=0.0, out=None, ws=None, proj=None):
+                    lambda_o=0.0, lambda_s=0.0, out=None, ws=None, proj=None, depth_bt=None, g_depth_bt=None):
     """Parameter gradient from the per-slot gradients; ``proj`` is the projection of the same
-    parameters and cameras (recomputed when not given)."""
-    _dev(flat, cams, inv, slot_grads, gwb)
+    parameters and cameras (recomputed when not given).  Arm B: ``depth_bt`` as given to
+    ``project``; d/d(depth_beta, depth_tau) goes to ``g_depth_bt`` (allocated when not given)."""
+    _dev(flat, cams, inv, slot_grads, gwb, depth_bt)
     V = cams.shape[0]
     if proj is None:
-        proj = project(flat, G, sh_degree, cams, H, W, blur, near)["proj"]
+        proj = project(flat, G, sh_degree, cams, H, W, blur, near, depth_bt=depth_bt)["proj"]
+    if depth_bt is not None and g_depth_bt is None:
+        g_depth_bt = torch.empty(2, device=flat.device)
     grads = out if out is not None else torch.empty_like(flat)
     nbytes = lib().tts_backward_workspace_bytes(G, V)
     ws = ws or Workspace(flat.device)
     buf = ws.get(nbytes)
     call("tts_backward_params", ptr(flat), G, sh_degree, ptr(cams), V, H, W, R, K, float(k), float(blur), float(near),
-         ptr(proj), ptr(inv), ptr(slot_grads), ptr(gwb), float(lambda_o), float(lambda_s), ptr(grads), ptr(buf), nbytes, stream())
-    return grads
+         ptr(proj), ptr(inv), ptr(slot_grads), ptr(gwb), float(lambda_o), float(lambda_s), ptr(grads), ptr(depth_bt),
+         ptr(g_depth_bt), ptr(buf), nbytes, stream())
+    return grads if depth_bt is None else (grads, g_depth_bt)
 
 
 def sgld(flat, G, step, lr_means, noise_lr, eps_noise=None, seed=0):

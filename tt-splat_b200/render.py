@@ -7,7 +7,8 @@ the backward runs the fused per-tile backward and the parameter backward kernel,
 gradient of every model parameter.  Rendering is binned (16x16 tiles, radius-R neighbour cells,
 K gaussians per tile, the reference's ``tools/m4_train_binned.py`` operator), which equals the
 dense ``spike.render`` whenever no tile overflows K and no gaussian reaches past its stencil.
-Only arm A (plain weighted-sum rendering) is on this path.
+Arms A (plain weighted-sum rendering) and B (opacity scaled by the depth weight
+sigmoid(depth_beta (depth_tau - z)), spike/arms.py:34-37) are on this path.
 """
 import torch
 
@@ -21,11 +22,12 @@ ARMS = ("A", "B", "C0", "C", "SZ", "RV", "D")
 
 class _BinnedRender(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, flat, cams_t, c_b, cfg):
+    def forward(ctx, flat, depth_bt, cams_t, c_b, cfg):
         G, sh_degree, H, W, R, K, k, blur, near, bf16 = cfg
         flat_d = flat.detach().contiguous()
-        need_grad = ctx.needs_input_grad[0]
-        pj = ops.project(flat_d, G, sh_degree, cams_t, H, W, blur, near)
+        bt = depth_bt.detach().float().contiguous() if depth_bt is not None else None
+        need_grad = ctx.needs_input_grad[0] or (depth_bt is not None and ctx.needs_input_grad[1])
+        pj = ops.project(flat_d, G, sh_degree, cams_t, H, W, blur, near, depth_bt=bt)
         if bf16 and not need_grad:
             bp = ops.bin_pack(pj, G, H, W, R, K, k, with_inv=False, bf16=True)
             slots = bp["slots"]
@@ -37,6 +39,7 @@ class _BinnedRender(torch.autograd.Function):
         ctx.save_for_backward(flat_d, cams_t, c_b, bp["slots"], bp["count"], bp["inv"], rf["img"], rf["den"],
                               pj["proj"])
         ctx.cfg = cfg
+        ctx.bt = bt
         ctx.bins = bp
         return rf["img"]
 
@@ -45,13 +48,17 @@ class _BinnedRender(torch.autograd.Function):
         flat, cams_t, c_b, slots, count, inv, img, den, proj = ctx.saved_tensors
         G, sh_degree, H, W, R, K, k, blur, near, _ = ctx.cfg
         rb = ops.render_bwd(slots, count, H, W, c_b, img, den, gimg.contiguous())
-        grads = ops.backward_params(flat, G, sh_degree, cams_t, H, W, R, K, inv, rb["slot_grads"], rb["gwb"], k, blur, near,
-                                    proj=proj)
-        return grads, None, None, None
+        out = ops.backward_params(flat, G, sh_degree, cams_t, H, W, R, K, inv, rb["slot_grads"], rb["gwb"], k, blur, near,
+                                  proj=proj, depth_bt=ctx.bt)
+        if ctx.bt is None:
+            return out, None, None, None, None
+        grads, gbt = out
+        return grads, gbt, None, None, None
 
 
-def render_views(model, cams, k=4.0, blur_eps=0.3, near=0.2, sh_degree=0, R=1, K=128, bf16=False):
-    """Render V views in one batched launch per stage -> [V, H, W, 3]."""
+def render_views(model, cams, k=4.0, blur_eps=0.3, near=0.2, sh_degree=0, R=1, K=128, bf16=False, arm="A"):
+    """Render V views in one batched launch per stage -> [V, H, W, 3] (arm A, or arm B with the
+    model's depth_beta / depth_tau)."""
     require_cuda()
     cams = [as_camera(c) for c in cams]
     flat = flat_of(model)
@@ -64,13 +71,17 @@ def render_views(model, cams, k=4.0, blur_eps=0.3, near=0.2, sh_degree=0, R=1, K
     c_b = getattr(model, "c_b", None)
     c_b = torch.ones(3, device=flat.device) if c_b is None else c_b.to(flat.device).float().contiguous()
     cfg = (G, int(sh_degree), H, W, int(R), int(K), float(k), float(blur_eps), float(near), bool(bf16))
-    return _BinnedRender.apply(flat, cams_t, c_b, cfg)
+    depth_bt = None
+    if arm == "B":
+        depth_bt = torch.stack([torch.as_tensor(model.depth_beta), torch.as_tensor(model.depth_tau)]).float()
+        depth_bt = depth_bt.to(flat.device)
+    return _BinnedRender.apply(flat, depth_bt, cams_t, c_b, cfg)
 
 
 def render(model, cam, arm="A", k=4.0, blur_eps=0.3, near=0.2, sh_degree=0, R=1, K=128, bf16=False):
     """spike/render.py:14-49 on the B200 path -> [H, W, 3]."""
     if arm not in ARMS:
         raise ValueError(f"unknown arm {arm!r}")
-    if arm != "A":
-        raise NotImplementedError(f"arm {arm!r} is not on the B200 hot path (only arm A, plain WSR)")
-    return render_views(model, [cam], k, blur_eps, near, sh_degree, R, K, bf16)[0]
+    if arm not in ("A", "B"):
+        raise NotImplementedError(f"arm {arm!r} is not on the B200 hot path (arms A and B)")
+    return render_views(model, [cam], k, blur_eps, near, sh_degree, R, K, bf16, arm=arm)[0]
