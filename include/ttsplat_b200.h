@@ -122,6 +122,17 @@ int tts_render_bwd(const float* slots, const int32_t* count, int V, int H, int W
                    const float* c_b, const float* img, const float* den, const float* gimg,
                    float* slot_grads, float* gwb_partial, void* stream);
 
+/* Arm RV (revealage compositing; replaces blend_RV, spike/arms.py:70-83, on the binned path):
+ * W = w_geo * o_col per (pixel, slot), den = sum W + 1e-6, Cavg = sum w_geo color_o / den,
+ * R = exp(sum log1p(-clamp(W, 0, 1 - 1e-4))), C = Cavg (1 - R) + c_b R.  fp32 slot rows only;
+ * writes img, den and aux[V,H,W,4] = (Cavg, R), 16-byte aligned.  The backward takes the same
+ * den/aux and writes slot grads in the arm-A layout and zero w_b partials (w_b is unused). */
+int tts_render_fwd_rv(const float* slots, const int32_t* count, int V, int H, int W, int K,
+                      const float* c_b, float* img, float* den, float* aux, void* stream);
+int tts_render_bwd_rv(const float* slots, const int32_t* count, int V, int H, int W, int K,
+                      const float* c_b, const float* den, const float* aux, const float* gimg,
+                      float* slot_grads, float* gwb_partial, void* stream);
+
 /* ---- photometric loss ------------------------------------------------------------------
  * Replaces metrics.loss_fn, spike/metrics.py:26-28 ((1-l) L1 + l (1-SSIM), SSIM on inputs
  * clamped to [0,1], 11-tap sigma-1.5 window shrunk for small images :15-19) with the manual

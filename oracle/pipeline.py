@@ -35,10 +35,11 @@ def colour_of(params, sh_degree, cam):
 
 
 def render_view(params, sh_degree, cam, K=128, R=1, k=4.0, blur=0.3, near=0.2, bins=None,
-                c_b=(1.0, 1.0, 1.0), depth_bt=None):
+                c_b=(1.0, 1.0, 1.0), depth_bt=None, arm="A"):
     """Forward for one view; returns a dict with the image and everything the backward needs.
     ``depth_bt`` = (depth_beta, depth_tau) selects arm B (spike/arms.py:34-37): the opacity is
-    scaled by rho = sigmoid(depth_beta (depth_tau - z)) of the camera-space z."""
+    scaled by rho = sigmoid(depth_beta (depth_tau - z)) of the camera-space z; ``arm="RV"`` blends
+    with revealage compositing (spike/arms.py:70-83)."""
     conic, mu2d, depth, keep, gcache = geometry.fwd(params["means3d"], params["quats"],
                                                     params["log_scales"], cam, blur, near)
     mu2d32, conic32 = mu2d.astype(F32), conic.astype(F32)
@@ -53,19 +54,26 @@ def render_view(params, sh_degree, cam, K=128, R=1, k=4.0, blur=0.3, near=0.2, b
         bins = binning.assign_bins(mu2d32, keep, tm, R, K)
     theta, col, oc, w_b = render.operands(mu2d32, conic32, keep, colour.astype(F32), o,
                                           params["w_b_raw"], bins, tm, k)
-    img, den, rcache = render.render_fwd(theta, col, oc, w_b, np.asarray(c_b, F32), tm)
+    if arm == "RV":
+        img, den, rcache = render.render_fwd_rv(theta, col, oc, np.asarray(c_b, F32), tm)
+    else:
+        img, den, rcache = render.render_fwd(theta, col, oc, w_b, np.asarray(c_b, F32), tm)
     return dict(img=img, den=den, rcache=rcache, bins=bins, tm=tm, theta=theta, col=col, oc=oc,
                 w_b=w_b, mu2d=mu2d32, conic=conic32, keep=keep, depth=depth, gcache=gcache,
                 colour=colour, pre=pre, dirs=dirs, o=render.sigmoid(params["opacity_raw"]).astype(F32), rho=rho,
-                depth_bt=depth_bt, c_b=np.asarray(c_b, F32), k=k, cam=cam)
+                depth_bt=depth_bt, c_b=np.asarray(c_b, F32), k=k, cam=cam, arm=arm)
 
 
 def backward_view(fw, gimg, params, sh_degree):
     """Manual backward of ``render_view`` for dL/dimg; returns per-parameter grads (float64)."""
     tm, bins = fw["tm"], fw["bins"]
     G = params["means3d"].shape[0]
-    gtheta, gcol, goc, gw_b = render.render_bwd(gimg, fw["theta"], fw["col"], fw["oc"], fw["w_b"],
-                                                fw["c_b"], tm, fw["rcache"])
+    if fw["arm"] == "RV":
+        gtheta, gcol, goc, gw_b = render.render_bwd_rv(gimg, fw["theta"], fw["col"], fw["oc"], fw["c_b"], tm,
+                                                       fw["rcache"])
+    else:
+        gtheta, gcol, goc, gw_b = render.render_bwd(gimg, fw["theta"], fw["col"], fw["oc"], fw["w_b"],
+                                                    fw["c_b"], tm, fw["rcache"])
     conic_t, mu_t = fw["conic"][bins.idx], fw["mu2d"][bins.idx]
     gconic_t, gmu_t = render.theta_bwd(gtheta, conic_t, mu_t, tm.origins, bins.valid, fw["k"])
     g9 = render.scatter_slots(G, bins.idx, bins.valid, gconic_t, gmu_t, gcol, goc)

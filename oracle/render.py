@@ -97,6 +97,54 @@ def render_bwd(gimg, theta, col, oc, w_b, c_b, tm, cache=None):
     return gtheta, gcol, goc, gw_b
 
 
+RV_EPS = F32(1e-6)
+RV_AMAX = F32(1.0 - 1e-4)
+
+
+def render_fwd_rv(theta, col, oc, c_b, tm):
+    """Binned arm RV (blend_RV, spike/arms.py:70-83, on the tile operands) in fp32:
+    W = w oc, den = sum W + eps, Cavg = sum w col / den, R = exp(sum log1p(-clamp(W, 0, 1-1e-4))),
+    C = Cavg (1 - R) + c_b R.  -> img[H,W,3], den[H,W], cache."""
+    u = np.matmul(tm.Phi[None], theta)                          # [T,256,K]
+    relu = np.maximum(u, F32(0.0))
+    w = relu * relu
+    Wm = w * np.transpose(oc, (0, 2, 1))                         # [T,256,K]
+    den = np.matmul(w, oc) + RV_EPS                              # [T,256,1]
+    Cavg = np.matmul(w, col) / den
+    a = np.clip(Wm, F32(0.0), RV_AMAX)
+    R = np.exp(np.sum(np.log1p(-a), -1, keepdims=True))         # [T,256,1]
+    c_b = np.asarray(c_b, F32)
+    C = Cavg * (F32(1.0) - R) + c_b[None, None, :] * R
+    img = np.zeros((tm.H * tm.W, 3), F32)
+    img[tm.gidx] = C.reshape(-1, 3)
+    den_img = np.zeros(tm.H * tm.W, F32)
+    den_img[tm.gidx] = den.reshape(-1)
+    return img.reshape(tm.H, tm.W, 3), den_img.reshape(tm.H, tm.W), (relu, w, Wm, Cavg, den, R)
+
+
+def render_bwd_rv(gimg, theta, col, oc, c_b, tm, cache=None):
+    """Manual backward of ``render_fwd_rv`` (the autograd of blend_RV restated per tile):
+    -> gtheta[T,6,K], gcol[T,K,3], goc[T,K,1], gw_b = 0 (w_b does not enter the blend)."""
+    T = theta.shape[0]
+    if cache is None:
+        _, _, cache = render_fwd_rv(theta, col, oc, c_b, tm)
+    relu, w, Wm, Cavg, den, R = cache
+    c_b = np.asarray(c_b, F32)
+    gC = np.asarray(gimg, F32).reshape(-1, 3)[tm.gidx].reshape(T, 256, 3)
+    f = (F32(1.0) - R) / den
+    gnum = gC * f
+    gden = -np.sum(gC * Cavg, -1, keepdims=True) * f
+    gL = R * np.sum(gC * (c_b[None, None, :] - Cavg), -1, keepdims=True)
+    inside = (Wm >= 0) & (Wm <= RV_AMAX)                          # clamp passes no gradient outside
+    gW = gden - np.where(inside, gL / (F32(1.0) - np.clip(Wm, F32(0.0), RV_AMAX)), F32(0.0))  # [T,256,K]
+    wT = np.transpose(w, (0, 2, 1))
+    gcol = np.matmul(wT, gnum)
+    goc = np.sum(gW * w, 1)[..., None]
+    gw = np.matmul(gnum, np.transpose(col, (0, 2, 1))) + gW * np.transpose(oc, (0, 2, 1))
+    gtheta = np.matmul(tm.Phi.T[None], gw * (relu * F32(2.0)))
+    return gtheta, gcol, goc, F32(0.0)
+
+
 def theta_bwd(gtheta, conic_t, mu_t, origins, valid, k=4.0):
     """_theta_bwd (tools/operands_manual.py:65-80): gtheta[T,6,K] -> gconic_t[T,K,3],
     gmu_t[T,K,2], masked by valid.  Computed in float64."""

@@ -288,6 +288,47 @@ def gen_arm_b(R, syn, out):
                         K=256, **cam_arrays(cam), **p, **out_arrays)
 
 
+def gen_arm_rv(R, syn, out):
+    """Arm RV (revealage compositing, spike/arms.py:70-83) through the reference's dense render on
+    the arm-B scene (tiles within K = 256, gaussians inside their stencil); a few gaussians get an
+    opacity near 1 so that some pixel weights pass the 1 - 1e-4 clamp bound."""
+    from spike import render as ref_render
+    sc = syn.config0(seed=31, G=150, res=64)
+    p, cam = dict(sc["params"]), sc["cams"][0]
+    op = p["opacity_raw"].copy()
+    op[:6] = 14.0
+    p["opacity_raw"] = op
+    # move those six onto pixel centres (x = col + 0.5, y = row + 0.5) at their camera depth, so
+    # that their weight at that pixel is ~o > 1 - 1e-4
+    Rv, tv = np.asarray(cam["R_v"], np.float64), np.asarray(cam["t_v"], np.float64)
+    m = p["means3d"].astype(np.float64).copy()
+    for i in range(6):
+        mc = Rv @ m[i] + tv
+        with torch.no_grad():
+            mu = project(R, dict(p, means3d=m.astype(np.float32)), cam)[0][i].numpy().astype(np.float64)
+        tx, ty = np.floor(mu[0]) + 0.5, np.floor(mu[1]) + 0.5
+        mc[0] = (tx - cam["cx"]) * mc[2] / cam["fx"]
+        mc[1] = (ty - cam["cy"]) * mc[2] / cam["fy"]
+        m[i] = Rv.T @ (mc - tv)
+    p["means3d"] = m.astype(np.float32)
+    out_arrays = {}
+    for deg, tag in ((0, "deg0"), (3, "deg3")):
+        model = make_model(p, deg)
+        img = ref_render.render(model, ref_cam(R, cam), "RV", sh_degree=deg)
+        wts = torch.from_numpy(np.random.default_rng(33).standard_normal(img.shape).astype(np.float32))
+        (img * wts).sum().backward()
+        out_arrays[f"{tag}__img"] = img.detach().numpy()
+        for k in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc", "color_rest"):
+            gk = getattr(model, k).grad
+            out_arrays[f"{tag}__grad_{k}"] = (gk if gk is not None else torch.zeros_like(getattr(model, k))).numpy()
+        out_arrays["wts"] = wts.numpy()
+    with torch.no_grad():
+        mu2d, _, _, keep = project(R, p, cam)
+    cand = cand_of(R, mu2d, keep, cam["H"], cam["W"], 1)
+    assert int(cand.max()) <= 256, int(cand.max())
+    np.savez_compressed(os.path.join(out, "render_arm_rv.npz"), K=256, **cam_arrays(cam), **p, **out_arrays)
+
+
 def gen_geom(R, syn, out):
     sc = syn.config0(seed=5, G=500)
     p, cam = sc["params"], sc["cams"][0]
@@ -401,7 +442,8 @@ def main():
     jobs = dict(bins_scene=lambda: gen_bins_scene(R, syn, HERE), bins_stress=lambda: gen_bins_stress(R, syn, HERE),
                 bins_big=lambda: gen_bins_big(R, syn, HERE), render=lambda: gen_render(R, syn, HERE),
                 geom=lambda: gen_geom(R, syn, HERE), loss=lambda: gen_loss(R, HERE),
-                optim=lambda: gen_optim(R, syn, HERE), arm_b=lambda: gen_arm_b(R, syn, HERE))
+                optim=lambda: gen_optim(R, syn, HERE), arm_b=lambda: gen_arm_b(R, syn, HERE),
+                arm_rv=lambda: gen_arm_rv(R, syn, HERE))
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
             continue

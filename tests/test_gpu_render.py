@@ -106,6 +106,38 @@ def test_arm_b_vs_reference_and_oracle(deg, pkg):
     assert m.depth_beta.grad is None or float(m.depth_beta.grad) == 0.0
 
 
+@pytest.mark.parametrize("deg", [0, 3])
+def test_arm_rv_vs_reference_and_oracle(deg, pkg):
+    """Arm RV (revealage compositing): image and gradients against the reference's dense render +
+    autograd and against the oracle; six pixels carry weights above the clamp bound."""
+    from tt_splat_b200 import camera, render
+    from tt_splat_b200.model import view
+    z = golden("render_arm_rv.npz")
+    cam = cam_from(z)
+    p = params_from(z)
+    K = int(z["K"])
+    m = _model(pkg, p)
+    img = render.render(m, camera.Camera.from_dict(cam), "RV", sh_degree=deg, K=K)
+    fw = pipeline.render_view(p, deg, cam, K=K, arm="RV")
+    pre = f"deg{deg}__"
+    out = img.detach().cpu().numpy()
+    assert np.abs(out - z[pre + "img"]).max() < 1e-3
+    assert np.abs(out - fw["img"]).max() < 1e-3
+    wts = z["wts"].astype(np.float32)
+    (img * torch.from_numpy(wts).to(DEV)).sum().backward()
+    go = pipeline.backward_view(fw, wts, p, deg)
+    G = p["means3d"].shape[0]
+    g = m.flat.grad
+    names = ["means3d", "log_scales", "quats", "opacity_raw", "color_dc"] + (["color_rest"] if deg else [])
+    for n in names:
+        mine = view(g, G, n).cpu().numpy()
+        assert rel_l2(mine, z[pre + "grad_" + n]) < 1e-3, (n, rel_l2(mine, z[pre + "grad_" + n]))
+        assert rel_l2(mine, go[n]) < 1e-3, (n, rel_l2(mine, go[n]))
+    assert float(view(g, G, "w_b_raw")) == 0.0
+    with pytest.raises(NotImplementedError):
+        render.render(m, camera.Camera.from_dict(cam), "RV", sh_degree=deg, K=K, bf16=True)
+
+
 def test_slot_rows_bit_exact_given_projection(pkg):
     """theta_u rows of the pack epilogue are the reference's fp32 expression bit for bit,
     given the device's own mu2d/conic (tools/m4_train_binned.py:130-143)."""

@@ -192,6 +192,24 @@ def test_arm_b_vs_reference_autograd(deg):
         assert abs(g[n] - ref) < 1e-3 * abs(ref), (n, g[n], ref)
 
 
+@pytest.mark.parametrize("deg", [0, 3])
+def test_arm_rv_vs_reference_autograd(deg):
+    """Arm RV (revealage compositing) image and gradients against the reference's dense render +
+    autograd; the fixture has pixel weights above the clamp bound (no gradient there)."""
+    z = golden("render_arm_rv.npz")
+    cam = cam_from(z)
+    p = params_from(z)
+    fw = pipeline.render_view(p, deg, cam, K=int(z["K"]), arm="RV")
+    assert (fw["rcache"][2] > render.RV_AMAX).any()
+    pre = f"deg{deg}__"
+    assert np.abs(fw["img"] - z[pre + "img"]).max() < 1e-4
+    g = pipeline.backward_view(fw, z["wts"].astype(np.float32), p, deg)
+    names = ["means3d", "log_scales", "quats", "opacity_raw", "color_dc"] + (["color_rest"] if deg else [])
+    for n in names:
+        assert rel_l2(g[n], z[pre + "grad_" + n]) < 1e-3, (n, rel_l2(g[n], z[pre + "grad_" + n]))
+    assert g["w_b_raw"] == 0.0
+
+
 def test_geometry_bwd_vs_reference():
     z = golden("geom_bwd.npz")
     cam = cam_from(z)

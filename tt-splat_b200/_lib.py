@@ -33,6 +33,8 @@ SIGNATURES = {
     "tts_unpack_slot_grads": (I, [P, I, I, P, P, P, P]),
     "tts_render_fwd": (I, [P, I, P, I, I, I, I, P, I, P, P, P, P]),
     "tts_render_bwd": (I, [P, P, I, I, I, I, P, P, P, P, P, P, P]),
+    "tts_render_fwd_rv": (I, [P, P, I, I, I, I, P, P, P, P, P]),
+    "tts_render_bwd_rv": (I, [P, P, I, I, I, I, P, P, P, P, P, P, P]),
     "tts_loss_workspace_bytes": (SZ, [I, I, I]),
     "tts_loss_l1_ssim": (I, [P, P, I, I, I, F, F, P, P, P, SZ, P]),
     "tts_backward_workspace_bytes": (SZ, [I, I]),

@@ -207,6 +207,170 @@ __global__ void __launch_bounds__(256)
   out[4] = make_float2(hsum2(gc2), hsum2(goc));
 }
 
+// ---- arm RV: revealage compositing (spike/arms.py:70-83) -------------------------------------
+// Per pixel, over the tile's slots with W = w * o_col (w = relu(u)^2):
+//   den = sum W + eps,  Cavg = sum w color_o / den,  R = exp(sum log1p(-clamp(W, 0, 1 - 1e-4)))
+//   C = Cavg (1 - R) + c_b R          (no w_b: the background enters through R alone)
+// The forward writes den and aux = (Cavg, R) per pixel for the backward.
+constexpr float RV_EPS = 1e-6f;
+constexpr float RV_AMAX = 0.9999f;   // 1 - 1e-4 as the float32 clamp bound
+
+__global__ void __launch_bounds__(FWD_THREADS)
+    k_render_fwd_rv(const float* __restrict__ slots, const int* __restrict__ count, int ntx, int T, int H, int W,
+                    int K, const float* __restrict__ c_b, float* __restrict__ img, float* __restrict__ den_out,
+                    float4* __restrict__ aux) {
+  extern __shared__ __align__(128) float s_rows[];
+  __shared__ __align__(8) uint64_t bar;
+  const int t = blockIdx.x, v = blockIdx.y, tid = threadIdx.x;
+  const int n = count[(long long)v * T + t];
+  const long long row0 = ((long long)v * T + t) * K;
+  if (tid == 0) mbar_init(&bar, 1);
+  __syncthreads();
+  if (n > 0) {
+    if (tid == 0) {
+      const uint32_t bytes = (uint32_t)n * TTS_SLOT_FLOATS * 4u;
+      mbar_expect_tx(&bar, bytes);
+      bulk_g2s(s_rows, slots + row0 * TTS_SLOT_FLOATS, bytes, &bar);
+    }
+    if (!mbar_wait_bounded(&bar, 0)) return;
+  }
+  const int ly = tid >> 2;
+  const int lxa = 2 * (tid & 3), lxb = lxa + 8;
+  const float py = (float)ly + 0.5f;
+  const f32x2 pxa = mk2((float)lxa + 0.5f, (float)lxa + 1.5f);
+  const f32x2 pxb = mk2((float)lxb + 0.5f, (float)lxb + 1.5f);
+  const f32x2 z = mk2(0.f, 0.f);
+  f32x2 a0 = z, a1 = z, a2 = z, a3 = z, b0 = z, b1 = z, b2 = z, b3 = z;
+  float lg[4] = {0.f, 0.f, 0.f, 0.f};
+  const float4* rows = reinterpret_cast<const float4*>(s_rows);
+  for (int s = 0; s < n; ++s) {
+    const float4 A = rows[3 * s + 0];
+    const float4 B = rows[3 * s + 1];
+    const float4 C = rows[3 * s + 2];
+    const float srow = fmaf(A.z, py, A.w);
+    const float rrow = fmaf(fmaf(A.y, py, B.x), py, B.y);
+    const f32x2 t0 = mk2(A.x, A.x), s2 = mk2(srow, srow), r2 = mk2(rrow, rrow);
+    const f32x2 cr = mk2(B.z, B.z), cg = mk2(B.w, B.w), cb = mk2(C.x, C.x), oc = mk2(C.y, C.y);
+    const f32x2 ra = relu2(fma2(fma2(t0, pxa, s2), pxa, r2));
+    const f32x2 rb = relu2(fma2(fma2(t0, pxb, s2), pxb, r2));
+    const f32x2 wa = mul2(ra, ra), wbv = mul2(rb, rb);
+    a0 = fma2(wa, cr, a0); a1 = fma2(wa, cg, a1); a2 = fma2(wa, cb, a2); a3 = fma2(wa, oc, a3);
+    b0 = fma2(wbv, cr, b0); b1 = fma2(wbv, cg, b1); b2 = fma2(wbv, cb, b2); b3 = fma2(wbv, oc, b3);
+    float W4[4];
+    split2(mul2(wa, oc), W4[0], W4[1]);
+    split2(mul2(wbv, oc), W4[2], W4[3]);
+#pragma unroll
+    for (int i = 0; i < 4; i++) lg[i] += log1pf(-fminf(fmaxf(W4[i], 0.f), RV_AMAX));
+  }
+  const int tx = t % ntx, ty = t / ntx;
+  const int gy = ty * 16 + ly;
+  const float cb0 = c_b[0], cb1 = c_b[1], cb2 = c_b[2];
+  float n0[4], n1[4], n2[4], dd[4];
+  split2(a0, n0[0], n0[1]); split2(b0, n0[2], n0[3]);
+  split2(a1, n1[0], n1[1]); split2(b1, n1[2], n1[3]);
+  split2(a2, n2[0], n2[1]); split2(b2, n2[2], n2[3]);
+  split2(a3, dd[0], dd[1]); split2(b3, dd[2], dd[3]);
+  const int lx[4] = {lxa, lxa + 1, lxb, lxb + 1};
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const long long p = ((long long)v * H + gy) * W + tx * 16 + lx[i];
+    const float d = dd[i] + RV_EPS;
+    const float c0 = n0[i] / d, c1 = n1[i] / d, c2 = n2[i] / d;
+    const float R = expf(lg[i]);
+    img[3 * p + 0] = c0 * (1.f - R) + cb0 * R;
+    img[3 * p + 1] = c1 * (1.f - R) + cb1 * R;
+    img[3 * p + 2] = c2 * (1.f - R) + cb2 * R;
+    den_out[p] = d;
+    aux[p] = make_float4(c0, c1, c2, R);
+  }
+}
+
+// Backward of the RV blend per (pixel, slot), with g = dL/dC of the pixel:
+//   gnum = g (1 - R) / den,  gden = -(g . Cavg)(1 - R) / den,  gL = R g . (c_b - Cavg)
+//   dL/dW = gden - gL / (1 - W) [W <= 1 - 1e-4]   (the clamp passes no gradient above its bound)
+// and W = w o_col, so the per-slot sums are those of arm A with gden replaced by dL/dW.
+__global__ void __launch_bounds__(256)
+    k_render_bwd_rv(const float* __restrict__ slots, const int* __restrict__ count, int ntx, int T, int H, int W,
+                    int K, const float* __restrict__ c_b, const float* __restrict__ den, const float4* __restrict__ aux,
+                    const float* __restrict__ gimg, float* __restrict__ slot_grads, float* __restrict__ gwb_partial) {
+  __shared__ __align__(16) float s_g0[256], s_g1[256], s_g2[256], s_gd[256], s_gl[256];
+  const int t = blockIdx.x, v = blockIdx.y, tid = threadIdx.x;
+  const int tx = t % ntx, ty = t / ntx;
+  const int n = count[(long long)v * T + t];
+  const float cb0 = c_b[0], cb1 = c_b[1], cb2 = c_b[2];
+  for (int p = tid; p < 256; p += blockDim.x) {
+    const long long q = ((long long)v * H + ty * 16 + (p >> 4)) * W + tx * 16 + (p & 15);
+    const float g0 = gimg[3 * q], g1 = gimg[3 * q + 1], g2 = gimg[3 * q + 2];
+    const float4 a = aux[q];
+    const float f = (1.f - a.w) / den[q];
+    s_g0[p] = g0 * f;
+    s_g1[p] = g1 * f;
+    s_g2[p] = g2 * f;
+    s_gd[p] = -(g0 * a.x + g1 * a.y + g2 * a.z) * f;
+    s_gl[p] = a.w * (g0 * (cb0 - a.x) + g1 * (cb1 - a.y) + g2 * (cb2 - a.z));
+  }
+  if (tid == 0) gwb_partial[(long long)v * T + t] = 0.f;   // w_b does not enter the RV blend
+  __syncthreads();
+  const int k = tid;
+  if (k >= n) return;
+  const long long o = ((long long)v * T + t) * K + k;
+  const float4* row = reinterpret_cast<const float4*>(slots + o * TTS_SLOT_FLOATS);
+  const float4 A = row[0], B = row[1], C = row[2];
+  const f32x2 t0 = mk2(A.x, A.x);
+  const float t1 = A.y, t2 = A.z, t3 = A.w, t4 = B.x, t5 = B.y;
+  const f32x2 cr = mk2(B.z, B.z), cg = mk2(B.w, B.w), cbb = mk2(C.x, C.x), oc = mk2(C.y, C.y);
+  const f32x2 z = mk2(0.f, 0.f);
+  f32x2 gc0 = z, gc1 = z, gc2 = z, goc = z;
+  float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f, g4 = 0.f, g5 = 0.f;
+  for (int ly = 0; ly < 16; ++ly) {
+    const float py = (float)ly + 0.5f;
+    const float srow = fmaf(t2, py, t3);
+    const float rrow = fmaf(fmaf(t1, py, t4), py, t5);
+    const f32x2 s2 = mk2(srow, srow), r2 = mk2(rrow, rrow);
+    f32x2 a0 = z, a1 = z, a2 = z;
+#pragma unroll
+    for (int lp = 0; lp < 8; ++lp) {
+      const f32x2 px = mk2((float)(2 * lp) + 0.5f, (float)(2 * lp) + 1.5f);
+      const int pi = ly * 16 + 2 * lp;
+      const f32x2 P0 = *reinterpret_cast<const f32x2*>(&s_g0[pi]);
+      const f32x2 P1 = *reinterpret_cast<const f32x2*>(&s_g1[pi]);
+      const f32x2 P2 = *reinterpret_cast<const f32x2*>(&s_g2[pi]);
+      const f32x2 r = relu2(fma2(fma2(t0, px, s2), px, r2));
+      const f32x2 w = mul2(r, r);
+      float wl, wh, gdl, gdh;
+      split2(mul2(w, oc), wl, wh);
+      const float2 gd = *reinterpret_cast<const float2*>(&s_gd[pi]);
+      const float2 gl = *reinterpret_cast<const float2*>(&s_gl[pi]);
+      gdl = wl <= RV_AMAX ? gd.x - gl.x * __frcp_rn(1.f - fmaxf(wl, 0.f)) : gd.x;
+      gdh = wh <= RV_AMAX ? gd.y - gl.y * __frcp_rn(1.f - fmaxf(wh, 0.f)) : gd.y;
+      const f32x2 P3 = mk2(gdl, gdh);
+      gc0 = fma2(w, P0, gc0);
+      gc1 = fma2(w, P1, gc1);
+      gc2 = fma2(w, P2, gc2);
+      goc = fma2(w, P3, goc);
+      const f32x2 gw = fma2(P0, cr, fma2(P1, cg, fma2(P2, cbb, mul2(P3, oc))));
+      const f32x2 gu = mul2(r, gw);
+      a0 = add2(a0, gu);
+      const f32x2 tpx = mul2(gu, px);
+      a1 = add2(a1, tpx);
+      a2 = fma2(tpx, px, a2);
+    }
+    const float s0 = hsum2(a0), s1 = hsum2(a1), s2s = hsum2(a2);
+    g0 += s2s;
+    g1 = fmaf(py * py, s0, g1);
+    g2 = fmaf(py, s1, g2);
+    g3 += s1;
+    g4 = fmaf(py, s0, g4);
+    g5 += s0;
+  }
+  float2* out = reinterpret_cast<float2*>(slot_grads + o * TTS_SLOT_GRAD_FLOATS);
+  out[0] = make_float2(2.f * g0, 2.f * g1);
+  out[1] = make_float2(2.f * g2, 2.f * g3);
+  out[2] = make_float2(2.f * g4, 2.f * g5);
+  out[3] = make_float2(hsum2(gc0), hsum2(gc1));
+  out[4] = make_float2(hsum2(gc2), hsum2(goc));
+}
+
 // theta_u[VT,6,K], color_o[VT,K,3], o_col[VT,K,1] -> slot rows
 __global__ void k_pack_operands(const float* __restrict__ th, const float* __restrict__ col, const float* __restrict__ oc,
                                 int VT, int K, float* __restrict__ slots) {
@@ -272,6 +436,35 @@ extern "C" int tts_render_bwd(const float* slots, const int32_t* count, int V, i
   k_render_bwd<<<grid, threads, 0, as_stream(stream)>>>(slots, count, ntx, T, H, W, K, c_b, img, den, gimg, slot_grads,
                                                          gwb_partial);
   return check_launch("render_bwd");
+}
+
+extern "C" int tts_render_fwd_rv(const float* slots, const int32_t* count, int V, int H, int W, int K,
+                                 const float* c_b, float* img, float* den, float* aux, void* stream) {
+  TTS_REQUIRE(V >= 1 && H > 0 && W > 0 && H % 16 == 0 && W % 16 == 0, "H and W must be positive multiples of 16");
+  TTS_REQUIRE(K >= 1 && K <= KMAX, "K must be in [1, 256]");
+  TTS_REQUIRE(slots && count && c_b && img && den && aux, "null pointer");
+  TTS_REQUIRE(aligned16(slots) && aligned16(aux), "slots and aux must be 16-byte aligned");
+  const int ntx = W / 16, T = ntx * (H / 16);
+  const size_t smem = (size_t)K * TTS_SLOT_FLOATS * sizeof(float);
+  k_render_fwd_rv<<<dim3(T, V), FWD_THREADS, smem, as_stream(stream)>>>(slots, count, ntx, T, H, W, K, c_b, img, den,
+                                                                       reinterpret_cast<float4*>(aux));
+  return check_launch("render_fwd_rv");
+}
+
+extern "C" int tts_render_bwd_rv(const float* slots, const int32_t* count, int V, int H, int W, int K,
+                                 const float* c_b, const float* den, const float* aux, const float* gimg,
+                                 float* slot_grads, float* gwb_partial, void* stream) {
+  TTS_REQUIRE(V >= 1 && H > 0 && W > 0 && H % 16 == 0 && W % 16 == 0, "H and W must be positive multiples of 16");
+  TTS_REQUIRE(K >= 1 && K <= KMAX, "K must be in [1, 256]");
+  TTS_REQUIRE(slots && count && c_b && den && aux && gimg && slot_grads && gwb_partial, "null pointer");
+  TTS_REQUIRE(aligned16(slots) && aligned16(aux) && ((uintptr_t)slot_grads & 7u) == 0,
+              "slots and aux must be 16-byte and slot_grads 8-byte aligned");
+  const int ntx = W / 16, T = ntx * (H / 16);
+  const int threads = ((K + 31) / 32) * 32;
+  k_render_bwd_rv<<<dim3(T, V), threads, 0, as_stream(stream)>>>(slots, count, ntx, T, H, W, K, c_b, den,
+                                                                  reinterpret_cast<const float4*>(aux), gimg,
+                                                                  slot_grads, gwb_partial);
+  return check_launch("render_bwd_rv");
 }
 
 extern "C" int tts_pack_operands(const float* theta_u, const float* color_o, const float* o_col, int VT, int K,

@@ -133,6 +133,30 @@ def render_bwd(slots, count, H, W, c_b, img, den, gimg, out=None):
     return out
 
 
+def render_fwd_rv(slots, count, H, W, c_b, out=None):
+    """Arm RV per-tile forward (fp32 slot rows) -> img, den and aux = (Cavg, R) per pixel."""
+    _dev(slots, count, c_b)
+    V, T, K = slots.shape[0], slots.shape[1], slots.shape[2]
+    dev = slots.device
+    if out is None:
+        out = dict(img=torch.empty(V, H, W, 3, device=dev), den=torch.empty(V, H, W, device=dev),
+                   aux=torch.empty(V, H, W, 4, device=dev))
+    call("tts_render_fwd_rv", ptr(slots), ptr(count), V, H, W, K, ptr(c_b), ptr(out["img"]), ptr(out["den"]),
+         ptr(out["aux"]), stream())
+    return out
+
+
+def render_bwd_rv(slots, count, H, W, c_b, den, aux, gimg, out=None):
+    _dev(slots, count, c_b, den, aux, gimg)
+    V, T, K = slots.shape[0], slots.shape[1], slots.shape[2]
+    dev = slots.device
+    if out is None:
+        out = dict(slot_grads=torch.empty(V, T, K, SLOT_GRAD_FLOATS, device=dev), gwb=torch.empty(V, T, device=dev))
+    call("tts_render_bwd_rv", ptr(slots), ptr(count), V, H, W, K, ptr(c_b), ptr(den), ptr(aux), ptr(gimg),
+         ptr(out["slot_grads"]), ptr(out["gwb"]), stream())
+    return out
+
+
 def loss_l1_ssim(img, target, lam=0.2, grad_scale=1.0, ws=None, out=None):
     _dev(img, target)
     if img.dim() == 3:
