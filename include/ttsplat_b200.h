@@ -170,6 +170,10 @@ int tts_adam_sgld(float* params, const float* grads, float* m, float* v, int G, 
                   const int32_t* step, const double* lr7, double beta1, double beta2, double eps,
                   float noise_lr, const float* eps_noise, uint64_t seed, void* stream);
 int tts_step_begin(int32_t* step, void* stream);
+/* torch.optim.Adam on a vector of n <= 1024 floats with one learning rate: the depth group
+ * (depth_beta, depth_tau) of GaussianModel.param_groups, spike/model.py:93, trained under arm B. */
+int tts_adam_vec(float* p, const float* g, float* m, float* v, int n, const int32_t* step, double lr,
+                 double beta1, double beta2, double eps, void* stream);
 /* add_sgld_noise alone (spike/mcmc.py:25-34) with lr = lr_means; same noise stream/injection. */
 int tts_sgld(float* params, int G, double lr_means, float noise_lr, const float* eps_noise,
              const int32_t* step, uint64_t seed, void* stream);

@@ -112,14 +112,14 @@ def backward_view(fw, gimg, params, sh_degree):
 
 
 def loss_and_grads(params, cams, targets, sh_degree, K=128, R=1, k=4.0, lam=0.2,
-                   lambda_o=0.0, lambda_s=0.0):
+                   lambda_o=0.0, lambda_s=0.0, depth_bt=None, arm="A"):
     """Mean over views of loss_fn (spike/train.py:24-27) + reg_loss (spike/mcmc.py:102); returns
     (total loss, per-view losses, grads dict)."""
     V = len(cams)
     grads = None
     losses = []
     for cam, tgt in zip(cams, targets):
-        fw = render_view(params, sh_degree, cam, K, R, k)
+        fw = render_view(params, sh_degree, cam, K, R, k, depth_bt=depth_bt, arm=arm)
         lv, _, _, gimg = loss_mod.loss_and_grad(fw["img"], tgt, lam)
         losses.append(lv)
         gv = backward_view(fw, (gimg / V).astype(F32), params, sh_degree)

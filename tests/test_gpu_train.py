@@ -37,6 +37,43 @@ def test_one_step_vs_oracle(pkg):
         assert d < 2e-4, (n, d)     # Adam steps are ~lr: a sign flip of a tiny grad moves 2*lr
 
 
+@pytest.mark.parametrize("arm", ["B", "RV"])
+def test_one_step_arms_vs_oracle(arm, pkg):
+    """Arms B and RV through the train step: loss and gradients (the depth pair under B) vs the
+    oracle, and the depth group's Adam update vs torch's formula."""
+    from oracle import optim as ooptim
+    from tt_splat_b200 import camera, model, train
+    sc = _setup(pkg, seed=4)
+    p = sc["params"]
+    m = model.GaussianModel.from_arrays(p, device=DEV)
+    bt = (1.3, 3.9)
+    with torch.no_grad():
+        m.depth_beta.fill_(bt[0])
+        m.depth_tau.fill_(bt[1])
+    st = train.TrainStep(m, [camera.Camera.from_dict(c) for c in sc["cams"]],
+                         [torch.from_numpy(t) for t in sc["targets"]], sh_degree=3, use_graph=False, arm=arm)
+    st.step()
+    total, _, grads = pipeline.loss_and_grads(p, sc["cams"], sc["targets"], 3, depth_bt=bt if arm == "B" else None,
+                                              arm=arm)
+    assert abs(st.mean_loss_value() - total) < 1e-4 * total
+    G = p["means3d"].shape[0]
+    for n in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc", "color_rest"):
+        assert rel_l2(model.view(st.grads, G, n).cpu().numpy(), grads[n]) < 1e-3, n
+    if arm == "RV":
+        assert float(model.view(st.grads, G, "w_b_raw")) == 0.0
+        assert float(model.view(m.flat.data, G, "w_b_raw")) == float(p["w_b_raw"])   # no gradient, no update
+        return
+    g = st.g_dbt.cpu().numpy()
+    ref_g = np.array([grads["depth_beta"], grads["depth_tau"]])
+    assert np.abs(g - ref_g).max() < 1e-3 * np.abs(ref_g).max()
+    pd = np.array(bt, np.float32)
+    ooptim.adam_update(pd, g.astype(np.float32), np.zeros(2, np.float32), np.zeros(2, np.float32), 1,
+                       train.DEFAULT_LR["depth"])
+    assert float(m.depth_beta) == pytest.approx(float(pd[0]), abs=1e-6)
+    assert float(m.depth_tau) == pytest.approx(float(pd[1]), abs=1e-6)
+    assert abs(float(m.depth_beta) - bt[0]) > 1e-3            # the depth pair trained
+
+
 def test_graph_replay_equals_eager(pkg):
     from tt_splat_b200 import camera, model, train
     sc = _setup(pkg, seed=1)

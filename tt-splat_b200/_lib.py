@@ -41,6 +41,7 @@ SIGNATURES = {
     "tts_backward_params": (I, [P, I, I, P, I, I, I, I, I, F, F, F, P, P, P, P, F, F, P, P, P, P, SZ, P]),
     "tts_adam_sgld": (I, [P, P, P, P, I, I, P, P, D, D, D, F, P, U64, P]),
     "tts_step_begin": (I, [P, P]),
+    "tts_adam_vec": (I, [P, P, P, P, I, P, D, D, D, D, P]),
     "tts_sgld": (I, [P, I, D, F, P, P, U64, P]),
     "tts_relocate_workspace_bytes": (SZ, [I]),
     "tts_relocate": (I, [P, P, P, I, F, F, F, P, P, P, U64, P, P, P, SZ, P]),

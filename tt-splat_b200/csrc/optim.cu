@@ -118,6 +118,24 @@ __global__ void __launch_bounds__(256) k_sgld(float* __restrict__ params, int G,
   sgld_one(params, ParamLayout{G}, g, lr_ptr ? lr_ptr[0] : lr_means, noise_lr, eps_noise, *step_ptr, seed);
 }
 
+// torch.optim.Adam on a short vector with one learning rate (the depth group of
+// spike/model.py:93: depth_beta, depth_tau), same arithmetic as k_adam.
+__global__ void k_adam_vec(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                           float* __restrict__ v, int n, const int* __restrict__ step_ptr, double lr, double beta1,
+                           double beta2, double eps) {
+  const int step = *step_ptr;
+  const double bc1 = 1.0 - pow(beta1, (double)step);
+  const double bc2 = 1.0 - pow(beta2, (double)step);
+  AdamScalars a;
+  a.w1 = (float)(1.0 - beta1);
+  a.b2 = (float)beta2;
+  a.w2 = (float)(1.0 - beta2);
+  a.bc2_sqrt = (float)sqrt(bc2);
+  a.eps = (float)eps;
+  const float nss = (float)(-lr / bc1);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) adam_elem(p, g, m, v, i, a, nss);
+}
+
 __global__ void k_step_begin(int* step) { *step += 1; }
 
 }  // namespace tts
@@ -149,6 +167,15 @@ extern "C" int tts_adam_sgld(float* params, const float* grads, float* m, float*
     return check_launch("sgld");
   }
   return TTS_OK;
+}
+
+extern "C" int tts_adam_vec(float* p, const float* g, float* m, float* v, int n, const int32_t* step, double lr,
+                            double beta1, double beta2, double eps, void* stream) {
+  TTS_REQUIRE(n >= 0 && n <= 1024 && p && g && m && v && step, "null pointer or n outside [0, 1024]");
+  TTS_REQUIRE(beta1 >= 0.0 && beta1 < 1.0 && beta2 >= 0.0 && beta2 < 1.0, "betas must be in [0, 1)");
+  if (n == 0) return TTS_OK;
+  k_adam_vec<<<1, ((n + 31) / 32) * 32, 0, as_stream(stream)>>>(p, g, m, v, n, step, lr, beta1, beta2, eps);
+  return check_launch("adam_vec");
 }
 
 extern "C" int tts_sgld(float* params, int G, double lr_means, float noise_lr, const float* eps_noise,

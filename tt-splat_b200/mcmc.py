@@ -75,11 +75,9 @@ def train_mcmc(model, cameras, gt_images, arm="A", iters=600, lr=None, relocate_
                offset=0.005, lambda_o=0.01, lambda_s=0.01, noise_lr=5e5, k=4.0, blur_eps=0.3, near=0.2, log_every=0,
                sh_degree=0, dead_frac=0.0, K=128, R=1, seed=0):
     """spike/mcmc.py:90-114 on the B200 path -> (loss history, total relocations)."""
-    if arm != "A":
-        raise NotImplementedError("only arm A is on the B200 hot path")
     st = TrainStep(model, cameras, gt_images, sh_degree=sh_degree, lr={**DEFAULT_LR, **(lr or {})}, K=K, R=R, k=k,
                    blur=blur_eps, near=near, noise_lr=noise_lr, relocate_every=relocate_every, dead_thr=dead_thr,
-                   dead_frac=dead_frac, offset=offset, lambda_o=lambda_o, lambda_s=lambda_s, seed=seed)
+                   dead_frac=dead_frac, offset=offset, lambda_o=lambda_o, lambda_s=lambda_s, seed=seed, arm=arm)
     hist = []
     for it in range(iters):
         st.step()

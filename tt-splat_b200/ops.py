@@ -200,6 +200,13 @@ def sgld(flat, G, step, lr_means, noise_lr, eps_noise=None, seed=0):
          int(seed) & (2 ** 64 - 1), stream())
 
 
+def adam_vec(p, g, m, v, step, lr, beta1=0.9, beta2=0.999, eps=1e-8):
+    """Adam on a short device vector with one learning rate (the arm-B depth group)."""
+    _dev(p, g, m, v, step)
+    call("tts_adam_vec", ptr(p), ptr(g), ptr(m), ptr(v), p.numel(), ptr(step), float(lr), float(beta1), float(beta2),
+         float(eps), stream())
+
+
 def step_begin(step):
     call("tts_step_begin", ptr(step), stream())
 

@@ -8,6 +8,10 @@ nothing and synchronises nothing with the host:
     -> render backward -> slot->gaussian reduction + parameter backward
     [-> NCCL all-reduce of the gradient across ranks] -> Adam (+ SGLD) [-> relocation]
 
+Arms A, B (depth-weighted opacity; the depth group depth_beta/depth_tau gets its own Adam,
+spike/model.py:93) and RV (revealage compositing; w_b receives no gradient, so Adam leaves it
+where it is, as torch does for a parameter without .grad) train through the same step.
+
 The first step runs eagerly (it also loads the kernels); later steps replay CUDA graphs
 captured from the same launches (one graph per step variant: with or without relocation;
 with a process group, one graph before and one after the all-reduce).  ``step()`` returns the
@@ -64,8 +68,11 @@ class TrainStep:
     def __init__(self, model, cameras, gt_images, sh_degree=0, lambda_ssim=0.2, lr=None, K=128, R=1, k=4.0,
                  blur=0.3, near=0.2, noise_lr=0.0, relocate_every=0, dead_thr=0.005, dead_frac=0.0, offset=0.0,
                  lambda_o=0.0, lambda_s=0.0, seed=0, n_views_total=None, process_group=None, use_graph=True,
-                 exchange="peer"):
+                 exchange="peer", arm="A"):
         require_cuda()
+        if arm not in ("A", "B", "RV"):
+            raise NotImplementedError(f"arm {arm!r} is not on the B200 hot path (arms A, B and RV)")
+        self.arm = arm
         if not isinstance(model, GaussianModel):
             raise TypeError("TrainStep trains a tt_splat_b200.model.GaussianModel (flat device buffer)")
         self.model = model
@@ -95,6 +102,9 @@ class TrainStep:
             if exchange == "peer" and dist.get_world_size(self.pg) > 1:
                 from .peer import PeerRegions
                 # parameters and gradients live in the region the peers write into / read from
+                if arm == "B":
+                    raise NotImplementedError("arm B's depth gradient is reduced by the NCCL exchange: "
+                                              "use exchange='nccl'")
                 self.regions = PeerRegions(self.flat.numel(), dev, self.pg)
                 self.regions.params.copy_(self.flat)
                 model.flat.data = self.regions.params
@@ -113,6 +123,16 @@ class TrainStep:
         self.bp = dict(idx=e(V, T, K, dt=torch.int32), count=e(V, T, dt=torch.int32), cand=e(V, T, dt=torch.int32),
                        inv=e(V, G, S, dt=torch.int32), slots=e(V, T, K, ops.SLOT_FLOATS))
         self.rf = dict(img=e(V, H, W, 3), den=e(V, H, W))
+        if arm == "RV":
+            self.rf["aux"] = e(V, H, W, 4)            # (Cavg, R) per pixel for the RV backward
+        self.dbt = None
+        if arm == "B":
+            # the depth group (depth_beta, depth_tau) in one device vector; the model's two
+            # parameters become views of it so that they follow the training
+            self.dbt = torch.stack([model.depth_beta.detach(), model.depth_tau.detach()]).float().to(dev).contiguous()
+            model.depth_beta.data = self.dbt[0]
+            model.depth_tau.data = self.dbt[1]
+            self.g_dbt, self.m_dbt, self.v_dbt = (torch.zeros(2, device=dev) for _ in range(3))
         self.lo = dict(gimg=e(V, H, W, 3), loss=e(V))
         self.rb = dict(slot_grads=e(V, T, K, ops.SLOT_GRAD_FLOATS), gwb=e(V, T))
         self.grads = torch.zeros_like(self.flat) if self.regions is None else self.regions.grads
@@ -137,15 +157,24 @@ class TrainStep:
     def _fwd_bwd(self):
         G, H, W, R, K = self.G, self.H, self.W, self.R, self.K
         ops.step_begin(self.step_t)
-        ops.project(self.flat, G, self.sh_degree, self.cams_t, H, W, self.blur, self.near, out=self.pj)
+        ops.project(self.flat, G, self.sh_degree, self.cams_t, H, W, self.blur, self.near, out=self.pj,
+                    depth_bt=self.dbt)
         ops.bin_pack(self.pj, G, H, W, R, K, self.k, ws=self.ws_bin, out=self.bp)
-        ops.render_fwd(self.bp["slots"], self.bp["count"], H, W, self.flat[59 * G:], self.model.c_b, out=self.rf)
+        if self.arm == "RV":
+            ops.render_fwd_rv(self.bp["slots"], self.bp["count"], H, W, self.model.c_b, out=self.rf)
+        else:
+            ops.render_fwd(self.bp["slots"], self.bp["count"], H, W, self.flat[59 * G:], self.model.c_b, out=self.rf)
         ops.loss_l1_ssim(self.rf["img"], self.targets, self.lam, self.grad_scale, ws=self.ws_loss, out=self.lo)
-        ops.render_bwd(self.bp["slots"], self.bp["count"], H, W, self.model.c_b, self.rf["img"], self.rf["den"],
-                       self.lo["gimg"], out=self.rb)
+        if self.arm == "RV":
+            ops.render_bwd_rv(self.bp["slots"], self.bp["count"], H, W, self.model.c_b, self.rf["den"], self.rf["aux"],
+                              self.lo["gimg"], out=self.rb)
+        else:
+            ops.render_bwd(self.bp["slots"], self.bp["count"], H, W, self.model.c_b, self.rf["img"], self.rf["den"],
+                           self.lo["gimg"], out=self.rb)
         ops.backward_params(self.flat, G, self.sh_degree, self.cams_t, H, W, R, K, self.bp["inv"],
                             self.rb["slot_grads"], self.rb["gwb"], self.k, self.blur, self.near, self.lambda_o,
-                            self.lambda_s, out=self.grads, ws=self.ws_bwd, proj=self.pj["proj"])
+                            self.lambda_s, out=self.grads, ws=self.ws_bwd, proj=self.pj["proj"], depth_bt=self.dbt,
+                            g_depth_bt=self.g_dbt if self.dbt is not None else None)
         torch.sum(self.lo["loss"], dim=0, keepdim=True, out=self.loss_mean)
 
     def _update(self, relocate):
@@ -163,6 +192,8 @@ class TrainStep:
         else:
             ops.adam_sgld(self.flat, self.grads, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
                           noise_lr=self.noise_lr, seed=self.seed)
+        if self.dbt is not None:
+            ops.adam_vec(self.dbt, self.g_dbt, self.m_dbt, self.v_dbt, self.step_t, self.lr["depth"])
         if relocate:
             ops.relocate(self.flat, self.m, self.v, self.G, self.step_t, self.dead_thr, self.dead_frac, self.offset,
                          seed=self.seed, ws=self.ws_reloc, out=self.reloc)
@@ -170,6 +201,9 @@ class TrainStep:
 
     def _allreduce(self):
         reduce_across_ranks(self.grads, self.loss_mean, self.pg)
+        if self.dbt is not None:
+            import torch.distributed as dist
+            dist.all_reduce(self.g_dbt, group=self.pg)
 
     def _run(self, relocate):
         if self.pg is None or self.regions is not None:
@@ -248,6 +282,8 @@ class TrainStep:
             n += 3                                       # signal, Adam, SGLD or wait
         else:
             n += 1 + (1 if self.noise_lr > 0 else 0)
+        if self.dbt is not None:
+            n += 1                                       # Adam of the depth group (arm B)
         if relocate:
             n += 1
         return n
@@ -296,10 +332,8 @@ class TrainStep:
 def fit(model, cameras, gt_images, arm="A", iters=800, lambda_ssim=0.2, lr=None, k=4.0, blur_eps=0.3, near=0.2,
         log_every=0, sh_degree=0, K=128, R=1):
     """spike/train.py:15-33 on the B200 path: returns the per-iteration mean loss history."""
-    if arm != "A":
-        raise NotImplementedError("only arm A is on the B200 hot path")
     st = TrainStep(model, cameras, gt_images, sh_degree=sh_degree, lambda_ssim=lambda_ssim, lr=lr, K=K, R=R, k=k,
-                   blur=blur_eps, near=near)
+                   blur=blur_eps, near=near, arm=arm)
     hist = []
     for it in range(iters):
         hist.append(st.step().clone())
