@@ -2,9 +2,10 @@
 //
 // Forward (replaces _DevRenderBinned.forward, tools/m4_train_binned.py:156-166): the tile's
 // slot rows (theta_u[6] | color_o[3] | o_col) are staged in shared memory by one bulk copy
-// (cp.async.bulk, completion on an mbarrier); each thread owns two adjacent pixel pairs of one
-// tile row, evaluated with sm_100a packed .f32x2 arithmetic, and loops over the slots with the
-// rows broadcast from shared memory:
+// (cp.async.bulk, completion on an mbarrier); one warp renders the tile, each lane owning eight
+// adjacent pixels of one tile row (four sm_100a packed .f32x2 pairs, so the per-slot row terms
+// are shared by eight pixels), and loops over the slots with the rows broadcast from shared
+// memory:
 //   u = theta . Phi(px, py) = (t0 px + (t2 py + t3)) px + ((t1 py + t4) py + t5)
 //   w = max(u, 0)^2;  num += w color_o;  den += w o_col
 // then C = (num + w_b c_b) / (den + w_b).  The [256 x K] weight matrix never leaves registers.
@@ -19,7 +20,8 @@
 
 namespace tts {
 
-constexpr int FWD_THREADS = 64;   // 4 pixels per thread: two adjacent pairs of one row
+constexpr int FWD_THREADS = 32;   // one warp per tile: 8 pixels per lane (half of one row)
+constexpr int RV_THREADS = 64;    // arm RV forward: 4 pixels per thread (two adjacent pairs of one row)
 constexpr int KMAX = 256;
 
 template <bool BF16>
@@ -29,27 +31,26 @@ __global__ void __launch_bounds__(FWD_THREADS)
                  float* __restrict__ img, float* __restrict__ den_out) {
   extern __shared__ __align__(128) float s_rows[];    // K slot rows (sized at launch: more tiles per SM)
   __shared__ __align__(8) uint64_t bar;
-  const int t = blockIdx.x, v = blockIdx.y, tid = threadIdx.x;
+  const int t = blockIdx.x, v = blockIdx.y, lane = threadIdx.x;
   const int n = count[(long long)v * T + t];
   const long long row0 = ((long long)v * T + t) * K;
-  bool ok = true;
   if (!BF16) {
     const float* src = static_cast<const float*>(slots_) + row0 * TTS_SLOT_FLOATS;
-    if (tid == 0) mbar_init(&bar, 1);
-    __syncthreads();
+    if (lane == 0) mbar_init(&bar, 1);
+    __syncwarp();
     if (n > 0) {
-      if (tid == 0) {
+      if (lane == 0) {
         const uint32_t bytes = (uint32_t)n * TTS_SLOT_FLOATS * 4u;
         mbar_expect_tx(&bar, bytes);
         bulk_g2s(s_rows, src, bytes, &bar);
       }
-      ok = mbar_wait_bounded(&bar, 0);
+      if (!mbar_wait_bounded(&bar, 0)) return;   // status recorded; nothing of the tile is written
     }
   } else {
     // compact bf16 rows (32 B: theta hi[6], theta lo[6], color_o[3], o_col) -> fp32 rows in
     // shared memory, theta_u = hi + lo
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(slots_) + row0 * TTS_SLOT_BF16);
-    for (int sl = tid; sl < n; sl += FWD_THREADS) {
+    for (int sl = lane; sl < n; sl += FWD_THREADS) {
       const uint4 lo8 = src[2 * sl], hi8 = src[2 * sl + 1];
       const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&lo8);
       const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&hi8);
@@ -68,20 +69,21 @@ __global__ void __launch_bounds__(FWD_THREADS)
       d[10] = 0.f;
       d[11] = 0.f;
     }
-    __syncthreads();
+    __syncwarp();
   }
-  if (!ok) return;   // status recorded; nothing of the tile is written
 
   const float wb = w_b_is_raw ? softplusf(*w_b_ptr) : *w_b_ptr;
-  const int ly = tid >> 2;
-  const int lxa = 2 * (tid & 3), lxb = lxa + 8;       // pixels lxa, lxa+1, lxb, lxb+1 of row ly
+  // lane -> row ly, pixels x0 .. x0+7 (four adjacent pairs); one row's srow/rrow serve 8 pixels
+  const int ly = lane >> 1, x0 = 8 * (lane & 1);
   const float py = (float)ly + 0.5f;
-  const f32x2 pxa = mk2((float)lxa + 0.5f, (float)lxa + 1.5f);
-  const f32x2 pxb = mk2((float)lxb + 0.5f, (float)lxb + 1.5f);
+  f32x2 px[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) px[j] = mk2((float)(x0 + 2 * j) + 0.5f, (float)(x0 + 2 * j) + 1.5f);
   const f32x2 z = mk2(0.f, 0.f);
-  f32x2 a0 = z, a1 = z, a2 = z, a3 = z, b0 = z, b1 = z, b2 = z, b3 = z;
+  f32x2 a0[4], a1[4], a2[4], a3[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) a0[j] = a1[j] = a2[j] = a3[j] = z;
   const float4* rows = reinterpret_cast<const float4*>(s_rows);
-#pragma unroll 2
   for (int s = 0; s < n; ++s) {
     const float4 A = rows[3 * s + 0];   // t0 t1 t2 t3
     const float4 B = rows[3 * s + 1];   // t4 t5 cr cg
@@ -90,29 +92,35 @@ __global__ void __launch_bounds__(FWD_THREADS)
     const float rrow = fmaf(fmaf(A.y, py, B.x), py, B.y);
     const f32x2 t0 = mk2(A.x, A.x), s2 = mk2(srow, srow), r2 = mk2(rrow, rrow);
     const f32x2 cr = mk2(B.z, B.z), cg = mk2(B.w, B.w), cb = mk2(C.x, C.x), oc = mk2(C.y, C.y);
-    const f32x2 ra = relu2(fma2(fma2(t0, pxa, s2), pxa, r2));
-    const f32x2 rb = relu2(fma2(fma2(t0, pxb, s2), pxb, r2));
-    const f32x2 wa = mul2(ra, ra), wbv = mul2(rb, rb);
-    a0 = fma2(wa, cr, a0); a1 = fma2(wa, cg, a1); a2 = fma2(wa, cb, a2); a3 = fma2(wa, oc, a3);
-    b0 = fma2(wbv, cr, b0); b1 = fma2(wbv, cg, b1); b2 = fma2(wbv, cb, b2); b3 = fma2(wbv, oc, b3);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const f32x2 r = relu2(fma2(fma2(t0, px[j], s2), px[j], r2));
+      const f32x2 w = mul2(r, r);
+      a0[j] = fma2(w, cr, a0[j]);
+      a1[j] = fma2(w, cg, a1[j]);
+      a2[j] = fma2(w, cb, a2[j]);
+      a3[j] = fma2(w, oc, a3[j]);
+    }
   }
   const int tx = t % ntx, ty = t / ntx;
-  const int gy = ty * 16 + ly;
   const float cb0 = c_b[0], cb1 = c_b[1], cb2 = c_b[2];
-  float n0[4], n1[4], n2[4], dd[4];
-  split2(a0, n0[0], n0[1]); split2(b0, n0[2], n0[3]);
-  split2(a1, n1[0], n1[1]); split2(b1, n1[2], n1[3]);
-  split2(a2, n2[0], n2[1]); split2(b2, n2[2], n2[3]);
-  split2(a3, dd[0], dd[1]); split2(b3, dd[2], dd[3]);
-  const int lx[4] = {lxa, lxa + 1, lxb, lxb + 1};
+  const long long p0 = ((long long)v * H + ty * 16 + ly) * W + tx * 16 + x0;
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const long long p = ((long long)v * H + gy) * W + tx * 16 + lx[i];
-    const float d = dd[i] + wb;
-    img[3 * p + 0] = (n0[i] + wb * cb0) / d;
-    img[3 * p + 1] = (n1[i] + wb * cb1) / d;
-    img[3 * p + 2] = (n2[i] + wb * cb2) / d;
-    den_out[p] = d;
+  for (int j = 0; j < 4; j++) {
+    float n0[2], n1[2], n2[2], dd[2];
+    split2(a0[j], n0[0], n0[1]);
+    split2(a1[j], n1[0], n1[1]);
+    split2(a2[j], n2[0], n2[1]);
+    split2(a3[j], dd[0], dd[1]);
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const long long p = p0 + 2 * j + i;
+      const float d = dd[i] + wb;
+      img[3 * p + 0] = (n0[i] + wb * cb0) / d;
+      img[3 * p + 1] = (n1[i] + wb * cb1) / d;
+      img[3 * p + 2] = (n2[i] + wb * cb2) / d;
+      den_out[p] = d;
+    }
   }
 }
 
@@ -215,7 +223,7 @@ __global__ void __launch_bounds__(256)
 constexpr float RV_EPS = 1e-6f;
 constexpr float RV_AMAX = 0.9999f;   // 1 - 1e-4 as the float32 clamp bound
 
-__global__ void __launch_bounds__(FWD_THREADS)
+__global__ void __launch_bounds__(RV_THREADS)
     k_render_fwd_rv(const float* __restrict__ slots, const int* __restrict__ count, int ntx, int T, int H, int W,
                     int K, const float* __restrict__ c_b, float* __restrict__ img, float* __restrict__ den_out,
                     float4* __restrict__ aux) {
@@ -446,7 +454,7 @@ extern "C" int tts_render_fwd_rv(const float* slots, const int32_t* count, int V
   TTS_REQUIRE(aligned16(slots) && aligned16(aux), "slots and aux must be 16-byte aligned");
   const int ntx = W / 16, T = ntx * (H / 16);
   const size_t smem = (size_t)K * TTS_SLOT_FLOATS * sizeof(float);
-  k_render_fwd_rv<<<dim3(T, V), FWD_THREADS, smem, as_stream(stream)>>>(slots, count, ntx, T, H, W, K, c_b, img, den,
+  k_render_fwd_rv<<<dim3(T, V), RV_THREADS, smem, as_stream(stream)>>>(slots, count, ntx, T, H, W, K, c_b, img, den,
                                                                        reinterpret_cast<float4*>(aux));
   return check_launch("render_fwd_rv");
 }
