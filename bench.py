@@ -480,10 +480,10 @@ def run_config(args, rank, world, local_rank, cid):
         dist.destroy_process_group()
 
 
-# DRAM bytes of one launch, read from an ncu capture of the config-2 train step (8 views per
-# launch; the render backward's traffic is proportional to the views it renders).  The Adam
-# figure under-counts writes that were still in L2 when the kernel ended.
-RENDER_BWD_DRAM_PER_VIEW = (362.3e6 + 88.9e6) / 8
+# DRAM bytes of one launch, read from ncu captures of the config-2 train step (the render
+# backward captured on a 4-view launch; its traffic is proportional to the views it renders).
+# The Adam figure under-counts writes that were still in L2 when the kernel ended.
+RENDER_BWD_DRAM_PER_VIEW = (179.8e6 + 34.7e6) / 4
 ADAM_DRAM = 94.4e6 + 16.3e6
 
 
