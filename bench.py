@@ -364,7 +364,7 @@ def run_ours(args, rank, world, local_rank):
                          "unit": "TFLOP/s", "frac": achieved / fp32_peak,
                          "traffic": RENDER_BWD_DRAM_PER_VIEW * V if CONFIG["G"] == 100000 else None,
                          "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, "
-                                         "8-view capture scaled by views per launch)",
+                                         "4-view capture scaled by views per launch)",
                          "peak_source": "nominal FP32 FMA (148 SMs x 128 lanes x 2) at the sampled SM clock",
                          "work": f"44 flops x {pairs} valid (pixel, slot) pairs per launch"},
             "roofline_hbm": {"bound": "hbm", "kernel": "adam", "achieved": adam_gbs, "peak": peaks.get("hbm_gbs"),

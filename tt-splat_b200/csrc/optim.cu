@@ -34,14 +34,39 @@ __device__ __forceinline__ float lr_of(long long i, long long G, const float nss
   return i < 3 * G ? nss[0] : i < 6 * G ? nss[1] : i < 10 * G ? nss[2] : i < 11 * G ? nss[3] : i < 14 * G ? nss[4] : nss[5];
 }
 
-__global__ void __launch_bounds__(256)
+// One wave of blocks (ADAM_BLOCKS_PER_SM per SM) walks the buffer grid-stride, two 16-byte vectors
+// of each array per thread per pass; the first pass's loads are issued before the block waits for
+// its scalars, so the double-precision bias corrections cost no memory time.
+constexpr int ADAM_BLOCKS_PER_SM = 2;
+
+__global__ void __launch_bounds__(256, ADAM_BLOCKS_PER_SM)
     k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ m,
            float* __restrict__ v, int G, long long n, const int* __restrict__ step_ptr,
            const double* __restrict__ lr7, double beta1, double beta2, double eps) {
-  // scalars in double like the Python-side arithmetic of torch's Adam, cast to fp32 at use;
-  // computed once per block (the double pow is far costlier than the per-element update)
   __shared__ AdamScalars s_a;
   __shared__ float s_nss[7];
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long nv = n / 4, stride = (long long)gridDim.x * blockDim.x;
+  float4* P = reinterpret_cast<float4*>(params);
+  const float4* Gr = reinterpret_cast<const float4*>(grads);
+  float4* M = reinterpret_cast<float4*>(m);
+  float4* Vv = reinterpret_cast<float4*>(v);
+  float4 pa, ga, ma, va, pb, gb, mb, vb;
+  auto load = [&](long long i) {
+    pa = P[i];
+    ma = M[i];
+    va = Vv[i];
+    ga = Gr[i];
+    if (i + stride < nv) {
+      pb = P[i + stride];
+      mb = M[i + stride];
+      vb = Vv[i + stride];
+      gb = Gr[i + stride];
+    }
+  };
+  if (tid < nv) load(tid);
+  // scalars in double like the Python-side arithmetic of torch's Adam, cast to fp32 at use;
+  // computed once per block (the double pow is far costlier than the per-element update)
   if (threadIdx.x == 0) {
     const int step = *step_ptr;
     const double bc1 = 1.0 - pow(beta1, (double)step);
@@ -58,10 +83,7 @@ __global__ void __launch_bounds__(256)
   float nss[6];
 #pragma unroll
   for (int k = 0; k < 6; k++) nss[k] = s_nss[k];
-  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (tid == 0) adam_elem(params, grads, m, v, 59LL * G, a, s_nss[6]);   // w_b_raw
-  // grid-stride over 16-byte vectors, two vectors of each array in flight per thread
-  const long long nv = n / 4, stride = (long long)gridDim.x * blockDim.x;
   auto update4 = [&](long long e0, float4& p4, const float4& g4, float4& m4, float4& v4) {
     float* pp = &p4.x;
     const float* gg = &g4.x;
@@ -78,32 +100,19 @@ __global__ void __launch_bounds__(256)
       vv[j] = vj;
     }
   };
-  float4* P = reinterpret_cast<float4*>(params);
-  const float4* Gr = reinterpret_cast<const float4*>(grads);
-  float4* M = reinterpret_cast<float4*>(m);
-  float4* Vv = reinterpret_cast<float4*>(v);
   for (long long i = tid; i < nv; i += 2 * stride) {
     const long long j = i + stride;
-    const bool two = j < nv;
-    float4 pa = P[i], ma = M[i], va = Vv[i];
-    const float4 ga = Gr[i];
-    float4 pb, mb, vb, gb;
-    if (two) {
-      pb = P[j];
-      mb = M[j];
-      vb = Vv[j];
-      gb = Gr[j];
-    }
     update4(4 * i, pa, ga, ma, va);
     P[i] = pa;
     M[i] = ma;
     Vv[i] = va;
-    if (two) {
+    if (j < nv) {
       update4(4 * j, pb, gb, mb, vb);
       P[j] = pb;
       M[j] = mb;
       Vv[j] = vb;
     }
+    if (i + 2 * stride < nv) load(i + 2 * stride);
   }
   for (long long e = 4 * nv + tid; e < n; e += stride) adam_elem(params, grads, m, v, e, a, lr_of(e, G, nss));
 }
@@ -157,9 +166,9 @@ extern "C" int tts_adam_sgld(float* params, const float* grads, float* m, float*
   cudaStream_t st = as_stream(stream);
   // torch skips parameters without a gradient: the colour rest trains only with SH on
   const long long n = sh_degree > 0 ? 59LL * G : 14LL * G;
-  // two 16-byte vectors per thread per pass; at most 8 blocks of 256 per SM (148 SMs), looping
+  // two 16-byte vectors per thread per pass, one wave of blocks looping over the buffer
   long long blocks = (n + 8 * 256 - 1) / (8 * 256);
-  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks > 148 * ADAM_BLOCKS_PER_SM) blocks = 148 * ADAM_BLOCKS_PER_SM;
   k_adam<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, st>>>(params, grads, m, v, G, n, step, lr7, beta1, beta2, eps);
   if (int rc = check_launch("adam")) return rc;
   if (noise_lr > 0.f && G > 0) {
