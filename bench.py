@@ -266,6 +266,9 @@ def run_ours(args, rank, world, local_rank):
             print(json.dumps({"metric": METRIC, "value": steps_per_s, "unit": "steps/s", "config": CONFIG,
                               "stage_ms": stages}), flush=True)
         st.release()
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
         return
     copy_stream = torch.cuda.Stream()
     staging = [torch.empty_like(st.targets) for _ in range(2)]
