@@ -58,7 +58,7 @@ int tts_read_status(int* status_host);      /* synchronous read + clear; diagnos
  * Replaces spike/geometry.py:10-57 (quat_to_rotmat, cov3d, project_ewa), spike/sh.py:49-72
  * (eval_sh_color on means - camera centre, spike/render.py:22-25) and the activations of
  * _operands, tools/m4_train_binned.py:194-202 (o = sigmoid, keo = keep*o, color_o = keo*colour).
- * Also counts kept gaussians per home cell into cell_count[V][T] (must be zeroed) and writes
+ * Also counts kept gaussians per home cell into cell_count[V][T] (zeroed here first) and writes
  * each gaussian's (cell, rank-in-cell) into cell_rank[V][G][2] for the binning scatter.
  * depth_bt (device float[2] = depth_beta, depth_tau, or NULL) selects arm B (spike/arms.py:34-37):
  * the opacity is scaled by sigmoid(depth_beta * (depth_tau - z)) of the camera-space z. */
@@ -136,10 +136,11 @@ int tts_render_bwd_rv(const float* slots, const int32_t* count, int V, int H, in
 /* ---- photometric loss ------------------------------------------------------------------
  * Replaces metrics.loss_fn, spike/metrics.py:26-28 ((1-l) L1 + l (1-SSIM), SSIM on inputs
  * clamped to [0,1], 11-tap sigma-1.5 window shrunk for small images :15-19) with the manual
- * gradient of tools/loss_manual.py:78-105.  gimg = grad_scale * dloss/dimg; loss[v] written. */
+ * gradient of tools/loss_manual.py:78-105.  gimg = grad_scale * dloss/dimg; loss[v] written,
+ * and, when loss_sum is not NULL, loss_sum[0] = loss[0] + ... + loss[V-1] (view order). */
 size_t tts_loss_workspace_bytes(int V, int H, int W);
 int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W, float lambda,
-                     float grad_scale, float* gimg, float* loss, void* workspace,
+                     float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
                      size_t workspace_bytes, void* stream);
 
 /* ---- slot -> gaussian reduction + geometry/SH/activation backward ------------------------

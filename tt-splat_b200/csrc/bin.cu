@@ -666,13 +666,12 @@ static int bin_core(const float* mu2d, const int* cell_count, const int2* cell_r
   const long long tiles = (long long)V * T;
   const unsigned wblocks = (unsigned)((tiles + WB_WARPS - 1) / WB_WARPS);
   const size_t wsmem = (size_t)WB_WARPS * WCAP * sizeof(u64);
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<unsigned long long> attr_done{0};
+  once_per_device(attr_done, [&] {
     cudaFuncSetAttribute(k_bin_warp<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
     cudaFuncSetAttribute(k_bin_warp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
     cudaFuncSetAttribute(k_bin_warp<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
-    attr = true;
-  }
+  });
   const unsigned bblocks = (unsigned)(tiles < 296 ? tiles : 296);   // two blocks per SM loop over the list
 #define TTS_BIN_LAUNCH(P, PR, SL)                                                                              \
   k_bin_warp<P><<<wblocks, WB_WARPS * 32, wsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, PR, inv_k, idx,   \

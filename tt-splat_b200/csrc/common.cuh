@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <atomic>
 #include <string>
 
 #include "../../include/ttsplat_b200.h"
@@ -20,6 +21,19 @@ int check_launch(const char* what);
   } while (0)
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Runs `set` once per device of this process (kernel attributes such as the dynamic shared memory
+// limit belong to the device context they were set in).
+template <class F>
+inline void once_per_device(std::atomic<unsigned long long>& done, F set) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(done.load() & bit)) {
+    set();
+    done.fetch_or(bit);
+  }
+}
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Device status word (bounded waits that gave up record here instead of trapping).

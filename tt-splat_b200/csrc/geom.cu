@@ -455,9 +455,12 @@ extern "C" int tts_project(const float* params, int G, int sh_degree, const floa
   TTS_REQUIRE(H > 0 && W > 0 && H % 16 == 0 && W % 16 == 0, "H and W must be positive multiples of 16");
   TTS_REQUIRE(aligned16(proj), "proj must be 16-byte aligned");
   TTS_REQUIRE((long long)V * (H / 16) * (W / 16) < (1LL << 31), "V * tiles must fit in 31 bits");
-  if (G == 0) return TTS_OK;
+  TTS_REQUIRE(cell_count, "null cell_count");
   cudaStream_t st = as_stream(stream);
   const int ntx = W / 16, nty = H / 16, lpg = lanes_for(V);
+  if (cudaMemsetAsync(cell_count, 0, (size_t)V * ntx * nty * sizeof(int32_t), st) != cudaSuccess)
+    return check_launch("memset cell counts");
+  if (G == 0) return TTS_OK;
   int2* cr = reinterpret_cast<int2*>(cell_rank);
   const float* bt = depth_bt;
   switch (sh_degree) {

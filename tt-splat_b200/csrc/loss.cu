@@ -65,7 +65,7 @@ __device__ __forceinline__ TileId decode_tile(int tile, int gx, int gy) {
 template <int WIN>
 __global__ void __launch_bounds__(256)
     k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
-               float* __restrict__ maps, float* __restrict__ part) {
+               float* __restrict__ maps, float* __restrict__ part, unsigned* __restrict__ reduce_counter) {
   using LG = LGeom<WIN>;
   extern __shared__ float smem[];
   f32x2* sxy = reinterpret_cast<f32x2*>(smem);                    // [IH][XS] (x, y) clamped
@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(256)
   const int vc = id.v * 3 + id.ch;
   const int ox0 = id.bx * LT_W, oy0 = id.by * LT_H;
   const int tid = threadIdx.x;
+  if (blockIdx.x == 0 && tid == 0) *reduce_counter = 0u;   // for the last-block total of k_loss_reduce
   float g[WIN];
   f32x2 g2[WIN];
 #pragma unroll
@@ -390,8 +391,10 @@ __global__ void __launch_bounds__(256)
 }
 
 __global__ void __launch_bounds__(256) k_loss_reduce(const float* __restrict__ spart, int nsb, const float* __restrict__ lpart,
-                                                     int nlb, int H, int W, int win, float lambda, float* __restrict__ loss) {
+                                                     int nlb, int H, int W, int win, float lambda, float* __restrict__ loss,
+                                                     float* __restrict__ loss_sum, unsigned* __restrict__ counter) {
   __shared__ double rs[256], rl[256];
+  __shared__ bool s_last;
   const int v = blockIdx.x;
   double s = 0.0, l = 0.0;
   for (int i = threadIdx.x; i < 3 * nsb; i += blockDim.x) s += spart[(long long)v * 3 * nsb + i];
@@ -410,6 +413,21 @@ __global__ void __launch_bounds__(256) k_loss_reduce(const float* __restrict__ s
     const double Ns = 3.0 * (double)(H - win + 1) * (double)(W - win + 1);
     const double N = 3.0 * (double)H * (double)W;
     loss[v] = (float)((1.0 - lambda) * rl[0] / N + lambda * (1.0 - rs[0] / Ns));
+  }
+  if (loss_sum == nullptr) return;
+  // the last block to finish adds the V losses in view order
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    __threadfence();
+    const volatile float* lv = loss;
+    float tot = 0.f;
+    for (int i = 0; i < (int)gridDim.x; ++i) tot += lv[i];
+    *loss_sum = tot;
+    *counter = 0u;
   }
 }
 
@@ -451,18 +469,17 @@ static LossGeom loss_geom(int H, int W) {
 template <int WIN>
 static int launch_loss(const float* img, const float* target, int V, int H, int W, float lambda, float grad_scale,
                        const Window& wd, const LossGeom& lg, float* maps, float* spart, float* lpart, float* gimg,
-                       cudaStream_t st) {
+                       unsigned* counter, cudaStream_t st) {
   using LG = LGeom<WIN>;
   const size_t fsm = (size_t)(LG::IH * LG::XS * 2 + LG::IH * LG::HS * 5) * 4;
   const size_t bsm = (size_t)(LG::IH * LG::XS * 3 + (LG::IH * LG::XS & 1) + LG::IH * LG::HS * 3) * 4;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static std::atomic<unsigned long long> attr_done{0};
+  once_per_device(attr_done, [&] {
     cudaFuncSetAttribute(k_ssim_fwd<WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
     cudaFuncSetAttribute(k_ssim_bwd<WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
-    attr_set = true;
-  }
+  });
   k_ssim_fwd<WIN><<<(unsigned)(V * 3 * lg.fbx * lg.fby), 256, fsm, st>>>(img, target, H, W, lg.fbx, lg.fby, wd, maps,
-                                                                        spart);
+                                                                        spart, counter);
   if (int rc = check_launch("ssim_fwd")) return rc;
   k_ssim_bwd<WIN><<<(unsigned)(V * 3 * lg.bbx * lg.bby), 256, bsm, st>>>(img, target, H, W, lg.bbx, lg.bby, wd, lambda,
                                                                         grad_scale, maps, gimg, lpart);
@@ -477,12 +494,12 @@ extern "C" size_t tts_loss_workspace_bytes(int V, int H, int W) {
   if (V < 1 || H < 3 || W < 3) return 0;
   const LossGeom lg = loss_geom(H, W);
   return a256((size_t)V * 12 * lg.Ho * lg.Wo * 4) + a256((size_t)V * 3 * lg.fbx * lg.fby * 4) +
-         a256((size_t)V * 3 * lg.bbx * lg.bby * 4);
+         a256((size_t)V * 3 * lg.bbx * lg.bby * 4) + 256;   // + the reduce counter
 }
 
 extern "C" int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W, float lambda,
-                                float grad_scale, float* gimg, float* loss, void* workspace, size_t workspace_bytes,
-                                void* stream) {
+                                float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
+                                size_t workspace_bytes, void* stream) {
   TTS_REQUIRE(V >= 1 && H >= 3 && W >= 3, "images must be at least 3x3");
   TTS_REQUIRE(img && target && gimg && loss && workspace, "null pointer");
   if (workspace_bytes < tts_loss_workspace_bytes(V, H, W)) return fail(TTS_ERR_CAPACITY, "loss workspace too small");
@@ -495,16 +512,19 @@ extern "C" int tts_loss_l1_ssim(const float* img, const float* target, int V, in
   float* spart = reinterpret_cast<float*>(p);
   p += a256((size_t)V * 3 * lg.fbx * lg.fby * 4);
   float* lpart = reinterpret_cast<float*>(p);
+  p += a256((size_t)V * 3 * lg.bbx * lg.bby * 4);
+  unsigned* counter = reinterpret_cast<unsigned*>(p);
   cudaStream_t st = as_stream(stream);
   int rc;
   switch (wd.win) {
-    case 3: rc = launch_loss<3>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
-    case 5: rc = launch_loss<5>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
-    case 7: rc = launch_loss<7>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
-    case 9: rc = launch_loss<9>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
-    default: rc = launch_loss<11>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, st); break;
+    case 3: rc = launch_loss<3>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    case 5: rc = launch_loss<5>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    case 7: rc = launch_loss<7>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    case 9: rc = launch_loss<9>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    default: rc = launch_loss<11>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
   }
   if (rc) return rc;
-  k_loss_reduce<<<V, 256, 0, st>>>(spart, lg.fbx * lg.fby, lpart, lg.bbx * lg.bby, H, W, lg.win, lambda, loss);
+  k_loss_reduce<<<V, 256, 0, st>>>(spart, lg.fbx * lg.fby, lpart, lg.bbx * lg.bby, H, W, lg.win, lambda, loss,
+                                   loss_sum, counter);
   return check_launch("loss_reduce");
 }

@@ -52,10 +52,8 @@ def project(flat, G, sh_degree, cams, H, W, blur=0.3, near=0.2, out=None, depth_
     if out is None:
         out = dict(proj=torch.empty(V, G, PROJ_FLOATS, device=dev), mu2d=torch.empty(V, G, 2, device=dev),
                    keep=torch.empty(V, G, dtype=torch.uint8, device=dev),
-                   cell_count=torch.zeros(V, T, dtype=torch.int32, device=dev),
+                   cell_count=torch.empty(V, T, dtype=torch.int32, device=dev),
                    cell_rank=torch.empty(V, G, 2, dtype=torch.int32, device=dev))
-    else:
-        out["cell_count"].zero_()
     call("tts_project", ptr(flat), G, sh_degree, ptr(cams), V, H, W, float(blur), float(near), ptr(out["proj"]),
          ptr(out["mu2d"]), ptr(out["keep"]), ptr(out["cell_count"]), ptr(out["cell_rank"]), ptr(depth_bt), stream())
     return out
@@ -169,7 +167,7 @@ def loss_l1_ssim(img, target, lam=0.2, grad_scale=1.0, ws=None, out=None):
     ws = ws or Workspace(dev)
     buf = ws.get(nbytes)
     call("tts_loss_l1_ssim", ptr(img), ptr(target), V, H, W, float(lam), float(grad_scale), ptr(out["gimg"]),
-         ptr(out["loss"]), ptr(buf), nbytes, stream())
+         ptr(out["loss"]), ptr(out.get("loss_sum")), ptr(buf), nbytes, stream())
     return out
 
 

@@ -133,7 +133,7 @@ class TrainStep:
             model.depth_beta.data = self.dbt[0]
             model.depth_tau.data = self.dbt[1]
             self.g_dbt, self.m_dbt, self.v_dbt = (torch.zeros(2, device=dev) for _ in range(3))
-        self.lo = dict(gimg=e(V, H, W, 3), loss=e(V))
+        self.lo = dict(gimg=e(V, H, W, 3), loss=e(V))   # loss_sum (the step's total) bound below
         self.rb = dict(slot_grads=e(V, T, K, ops.SLOT_GRAD_FLOATS), gwb=e(V, T))
         self.grads = torch.zeros_like(self.flat) if self.regions is None else self.regions.grads
         self.m = torch.zeros_like(self.flat)
@@ -147,6 +147,7 @@ class TrainStep:
         self.ws_loss.get(ops.lib().tts_loss_workspace_bytes(V, H, W))
         self.ws_reloc.get(ops.lib().tts_relocate_workspace_bytes(G) if G >= 2 else 0)
         self.loss_mean = e(1) if self.regions is None else self.regions.loss
+        self.lo["loss_sum"] = self.loss_mean   # written by the loss reduction kernel
         self.loss_total = e(1)            # sum over the ranks (peer exchange)
         self.n_moved = torch.zeros(1, dtype=torch.int64, device=dev)
         self.it = 0
@@ -175,7 +176,6 @@ class TrainStep:
                             self.rb["slot_grads"], self.rb["gwb"], self.k, self.blur, self.near, self.lambda_o,
                             self.lambda_s, out=self.grads, ws=self.ws_bwd, proj=self.pj["proj"], depth_bt=self.dbt,
                             g_depth_bt=self.g_dbt if self.dbt is not None else None)
-        torch.sum(self.lo["loss"], dim=0, keepdim=True, out=self.loss_mean)
 
     def _update(self, relocate):
         if self.regions is not None:
