@@ -307,6 +307,8 @@ __device__ __forceinline__ void sort_front(u64* keys, int m, int lane) {
   }
 }
 
+constexpr int KG_UNROLL = 4;   // candidate records in flight per lane during key generation
+
 // One warp per tile for tiles with at most WCAP candidates (tiles with more are appended to the
 // overflow list for the block kernel).  Keys in per-warp shared memory; when n > K a two-level
 // histogram of q (64 then 32 bins) finds q*, the keys with q <= q* are compacted in place and
@@ -356,9 +358,28 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
   }
   const float ctx = __fmul_rn(__fadd_rn((float)tx, 0.5f), 16.0f);
   const float cty = __fmul_rn(__fadd_rn((float)ty, 0.5f), 16.0f);
-  for (int j = 0; j < S; ++j) {
-    const int l = wlen[warp][j], b = wbeg[warp][j], off = woff[warp][j];
-    for (int i = lane; i < l; i += 32) buf[off + i] = make_key(j, rv[b + i], ctx, cty);
+  // candidate c of the tile's concatenated cell lists -> (stencil offset j, record): each lane
+  // issues the loads of KG_UNROLL candidates before keying them, so a tile costs ~n / (32 KG_UNROLL)
+  // round trips to L2 instead of one per cell
+  {
+    int jc = 0;
+    for (int c0 = 0; c0 < n; c0 += 32 * KG_UNROLL) {
+      float4 r[KG_UNROLL];
+      int jj[KG_UNROLL];
+#pragma unroll
+      for (int u = 0; u < KG_UNROLL; ++u) {
+        const int c = c0 + 32 * u + lane;
+        jj[u] = -1;
+        if (c < n) {
+          while (c >= woff[warp][jc + 1]) ++jc;   // c only grows along a lane: empty cells are skipped
+          jj[u] = jc;
+          r[u] = rv[wbeg[warp][jc] + c - woff[warp][jc]];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < KG_UNROLL; ++u)
+        if (jj[u] >= 0) buf[c0 + 32 * u + lane] = make_key(jj[u], r[u], ctx, cty);
+    }
   }
   __syncwarp();
   int m = n;
