@@ -487,7 +487,7 @@ def run_config(args, rank, world, local_rank, cid):
 # backward captured on a 4-view launch; its traffic is proportional to the views it renders).
 # The Adam figure under-counts writes that were still in L2 when the kernel ended.
 RENDER_BWD_DRAM_PER_VIEW = (179.8e6 + 34.7e6) / 4
-ADAM_DRAM = 94.4e6 + 16.3e6
+ADAM_DRAM = 94.4e6 + 15.2e6
 
 
 def cpu_baseline_sample():
