@@ -4,7 +4,8 @@ Workload (benchmark config 2): G = 100,000 gaussians, SH degree 3, a batch of 8 
 radius-4 ring (1264x832, 16x16 tiles, K = 128, R = 1), 0.8*L1 + 0.2*(1-SSIM) loss with the
 11x11 window, fused Adam (lr 1.6e-4 on means, beta 0.9/0.999), MCMC SGLD noise (noise_lr 5e5)
 and relocation of the 1% lowest-opacity gaussians every step, plus the MCMC regulariser.
-Views are split over the ranks; per-gaussian gradients are summed with one NCCL all-reduce.
+Views are split over the ranks; the gradient exchange and the sharded Adam step run over NVLink
+peer memory inside the step's CUDA graph (no library collective on the data path).
 One step = the whole 8-view batch, so ``value`` (steps/s) is a whole-job number and the
 scaling is strong (fixed total work).
 
