@@ -36,6 +36,7 @@ CONFIG = dict(workload="config2: train step, G=100k, 8 views 1264x832, K=128, SH
               H=832, W=1264, K=128, R=1, sh_degree=3)
 METRIC = "train steps/s (G=100k, 8-view batch 1264x832, 1/2/4/8 B200)"
 PEAKS_FILE = os.path.join(REPO, "MEASURED_PEAKS.json")
+REF_BUDGET_S = 90.0   # wall-clock budget of the CPU reference arm's timed samples
 
 
 def load_peaks():
@@ -126,12 +127,19 @@ def run_reference(args, rank, world):
         t2 = time.perf_counter()
         return len(cams) * (t1 - t0) + (t2 - t1)
 
-    for i in range(args.warmup):
+    # one CPU sample takes seconds: at most one warm-up sample, then timed samples until the
+    # requested count or a 90-s budget (at least two), so any --steps finishes within minutes
+    warm = min(args.warmup, 1)
+    for i in range(warm):
         sample(i)
-    times = [sample(args.warmup + i) for i in range(args.steps)]
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < max(args.steps, 1) and (len(times) < 2 or time.perf_counter() - t_start < REF_BUDGET_S):
+        times.append(sample(warm + len(times)))
     step_s = float(np.median(times))
     line = {"impl": "reference", "metric": METRIC, "value": 1.0 / step_s, "unit": "steps/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "steps": len(times), "warmup": warm, "steps_requested": args.steps, "warmup_requested": args.warmup,
+            "ms_per_step": step_s * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 2 shapes)",
             "config": {k: v for k, v in CONFIG.items()},
             "cpu_baseline": {"value": 1.0 / step_s, "unit": "steps/s", "cores": cores, "kind": "port",
