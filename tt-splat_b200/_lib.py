@@ -106,6 +106,14 @@ def stream(device=None):
     return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def on_device(t):
+    """Context selecting a CUDA tensor's device (a no-op for anything else: the ops then raise)."""
+    import contextlib
+    if isinstance(t, torch.Tensor) and t.is_cuda:
+        return torch.cuda.device(t.device)
+    return contextlib.nullcontext()
+
+
 def require_cuda():
     if not torch.cuda.is_available():
         raise RuntimeError("CUDA is not available: tt-splat B200 has no CPU fallback")

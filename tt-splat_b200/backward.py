@@ -6,6 +6,7 @@ differentiable in theta_u, o, color and w_b like ``WSRPolySplatHot``.
 """
 import torch
 
+from ._lib import on_device
 from . import ops
 
 
@@ -44,4 +45,5 @@ class WSRPolySplatHot(torch.autograd.Function):
 
 def wsr_polysplat(theta_u, o, color, w_b, Phi, c_b, keep=None):
     """spike/backward.py:61-63."""
-    return WSRPolySplatHot.apply(theta_u, o, color, w_b, Phi, c_b, keep)
+    with on_device(theta_u):
+        return WSRPolySplatHot.apply(theta_u, o, color, w_b, Phi, c_b, keep)

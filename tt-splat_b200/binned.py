@@ -9,6 +9,7 @@
 """
 import torch
 
+from ._lib import on_device
 from . import forward, ops
 from .camera import as_camera, pack_cameras
 from .model import flat_of
@@ -104,7 +105,8 @@ def _operands(model, cam, tmap, R, K, cached_bins=None, sh_degree=0, blur=0.3, n
     flat = flat_of(model)
     G = model.means3d.shape[0]
     cfg = (G, int(sh_degree), cam.H, cam.W, int(R), int(K), K_POLY, float(blur), float(near))
-    th, col, oc, w_b, idx, valid = _Operands.apply(flat, pack_cameras([cam], flat.device), cfg)
+    with on_device(flat):
+        th, col, oc, w_b, idx, valid = _Operands.apply(flat, pack_cameras([cam], flat.device), cfg)
     return th, col, oc, w_b, (idx, valid)
 
 
@@ -138,4 +140,5 @@ def render_binned_device(model, cam, tmap, R=1, K=128, sh_degree=0):
     """tools/m4_train_binned.py:215-219."""
     thU, col, oc, w_b, _ = _operands(model, cam, tmap, R, K, sh_degree=sh_degree)
     c_b = getattr(model, "c_b", torch.ones(3, device=thU.device))
-    return _DevRenderBinned.apply(thU, col, oc, w_b, tmap.Phi, tmap.gidx, c_b, tmap.H, tmap.W)
+    with on_device(thU):
+        return _DevRenderBinned.apply(thU, col, oc, w_b, tmap.Phi, tmap.gidx, c_b, tmap.H, tmap.W)

@@ -5,6 +5,7 @@ pass; the autograd backward scales the stored gradient.  Images are [H,W,3] (or 
 """
 import torch
 
+from ._lib import on_device
 from . import ops
 
 
@@ -26,7 +27,8 @@ class _LossFn(torch.autograd.Function):
 def loss_fn(pred, gt, lambda_ssim=0.2):
     """(1-l)*L1 + l*(1-SSIM) (spike/metrics.py:26-28); SSIM on [0,1]-clamped inputs, window 11
     shrunk for small images (:15-19).  For a [V,H,W,3] batch, the sum of the per-view losses."""
-    return _LossFn.apply(pred, gt, float(lambda_ssim))
+    with on_device(pred):
+        return _LossFn.apply(pred, gt, float(lambda_ssim))
 
 
 def psnr(pred, gt):

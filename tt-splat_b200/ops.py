@@ -15,12 +15,20 @@ PROJ_FLOATS = 12
 
 
 def _dev(*ts):
+    """CUDA, contiguous, and on the current device (the library launches on the current device's
+    current stream)."""
+    cur = None
     for t in ts:
         if t is not None:
             if not t.is_cuda:
                 raise RuntimeError("tt-splat B200 ops need CUDA tensors (no CPU fallback)")
             if not t.is_contiguous():
                 raise ValueError("tensors must be contiguous")
+            if cur is None:
+                cur = torch.cuda.current_device()
+            if t.device.index != cur:
+                raise ValueError(f"tensor on {t.device} but the current device is cuda:{cur}: "
+                                 "call under torch.cuda.device(...) of the tensors' device")
 
 
 def tiles(H, W):

@@ -14,7 +14,7 @@ C = Cavg (1 - R) + c_b R, spike/arms.py:70-83) are on this path.
 import torch
 
 from . import ops
-from ._lib import require_cuda
+from ._lib import on_device, require_cuda
 from .camera import as_camera, pack_cameras
 from .model import flat_of
 
@@ -86,7 +86,8 @@ def render_views(model, cams, k=4.0, blur_eps=0.3, near=0.2, sh_degree=0, R=1, K
     if arm == "B":
         depth_bt = torch.stack([torch.as_tensor(model.depth_beta), torch.as_tensor(model.depth_tau)]).float()
         depth_bt = depth_bt.to(flat.device)
-    return _BinnedRender.apply(flat, depth_bt, cams_t, c_b, cfg)
+    with on_device(flat):
+        return _BinnedRender.apply(flat, depth_bt, cams_t, c_b, cfg)
 
 
 def render(model, cam, arm="A", k=4.0, blur_eps=0.3, near=0.2, sh_degree=0, R=1, K=128, bf16=False):

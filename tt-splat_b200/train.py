@@ -293,10 +293,11 @@ class TrainStep:
         it = self.it
         relocate = bool(self.relocate_every) and it > 0 and it % self.relocate_every == 0 and self.G >= 2
         self.kernels_per_step = self.launches(relocate)
-        if self.use_graph and it > 0:
-            self._graph_run(relocate)
-        else:
-            self._run(relocate)
+        with torch.cuda.device(self.dev):
+            if self.use_graph and it > 0:
+                self._graph_run(relocate)
+            else:
+                self._run(relocate)
         self.it += 1
         return (self.loss_mean if self.regions is None else self.loss_total).view(())
 
