@@ -329,6 +329,28 @@ def gen_arm_rv(R, syn, out):
     np.savez_compressed(os.path.join(out, "render_arm_rv.npz"), K=256, **cam_arrays(cam), **p, **out_arrays)
 
 
+def gen_sh12(R, syn, out):
+    """Arm A at SH degrees 1 and 2 through the reference's dense render on the arm-B scene (tiles
+    within K = 256, gaussians inside their stencil), with non-zero rest coefficients."""
+    from spike import render as ref_render
+    sc = syn.config0(seed=31, G=150, res=64)
+    p, cam = dict(sc["params"]), sc["cams"][0]
+    p["color_rest"] = (0.3 * np.random.default_rng(34).standard_normal((p["means3d"].shape[0], 15, 3))).astype(np.float32)
+    out_arrays = {}
+    for deg in (1, 2):
+        model = make_model(p, deg)
+        img = ref_render.render(model, ref_cam(R, cam), "A", sh_degree=deg)
+        wts = torch.from_numpy(np.random.default_rng(35).standard_normal(img.shape).astype(np.float32))
+        (img * wts).sum().backward()
+        out_arrays[f"deg{deg}__img"] = img.detach().numpy()
+        for k in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc", "color_rest"):
+            gk = getattr(model, k).grad
+            out_arrays[f"deg{deg}__grad_{k}"] = (gk if gk is not None else torch.zeros_like(getattr(model, k))).numpy()
+        out_arrays[f"deg{deg}__grad_w_b_raw"] = np.float32(model.w_b_raw.grad)
+        out_arrays["wts"] = wts.numpy()
+    np.savez_compressed(os.path.join(out, "render_sh12.npz"), K=256, **cam_arrays(cam), **p, **out_arrays)
+
+
 def gen_geom(R, syn, out):
     sc = syn.config0(seed=5, G=500)
     p, cam = sc["params"], sc["cams"][0]
@@ -443,7 +465,7 @@ def main():
                 bins_big=lambda: gen_bins_big(R, syn, HERE), render=lambda: gen_render(R, syn, HERE),
                 geom=lambda: gen_geom(R, syn, HERE), loss=lambda: gen_loss(R, HERE),
                 optim=lambda: gen_optim(R, syn, HERE), arm_b=lambda: gen_arm_b(R, syn, HERE),
-                arm_rv=lambda: gen_arm_rv(R, syn, HERE))
+                arm_rv=lambda: gen_arm_rv(R, syn, HERE), sh12=lambda: gen_sh12(R, syn, HERE))
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
             continue

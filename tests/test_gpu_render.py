@@ -138,6 +138,27 @@ def test_arm_rv_vs_reference_and_oracle(deg, pkg):
         render.render(m, camera.Camera.from_dict(cam), "RV", sh_degree=deg, K=K, bf16=True)
 
 
+@pytest.mark.parametrize("deg", [1, 2])
+def test_sh_degree_1_2_vs_reference(deg, pkg):
+    """The device path at SH degrees 1 and 2: image and gradients against the reference."""
+    from tt_splat_b200 import camera, render
+    from tt_splat_b200.model import view
+    z = golden("render_sh12.npz")
+    cam = cam_from(z)
+    p = params_from(z)
+    m = _model(pkg, p)
+    img = render.render(m, camera.Camera.from_dict(cam), "A", sh_degree=deg, K=int(z["K"]))
+    pre = f"deg{deg}__"
+    assert np.abs(img.detach().cpu().numpy() - z[pre + "img"]).max() < 1e-3
+    (img * torch.from_numpy(z["wts"].astype(np.float32)).to(DEV)).sum().backward()
+    G = p["means3d"].shape[0]
+    for n in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc", "color_rest"):
+        mine = view(m.flat.grad, G, n).cpu().numpy()
+        assert rel_l2(mine, z[pre + "grad_" + n]) < 1e-3, (n, rel_l2(mine, z[pre + "grad_" + n]))
+    ref = float(z[pre + "grad_w_b_raw"])
+    assert abs(float(view(m.flat.grad, G, "w_b_raw")) - ref) < 1e-3 * abs(ref)
+
+
 def test_slot_rows_bit_exact_given_projection(pkg):
     """theta_u rows of the pack epilogue are the reference's fp32 expression bit for bit,
     given the device's own mu2d/conic (tools/m4_train_binned.py:130-143)."""

@@ -210,6 +210,22 @@ def test_arm_rv_vs_reference_autograd(deg):
     assert g["w_b_raw"] == 0.0
 
 
+@pytest.mark.parametrize("deg", [1, 2])
+def test_sh_degree_1_2_vs_reference_autograd(deg):
+    """Arm A at SH degrees 1 and 2 (the degrees between DC-only and the full 16 coefficients)."""
+    z = golden("render_sh12.npz")
+    cam = cam_from(z)
+    p = params_from(z)
+    fw = pipeline.render_view(p, deg, cam, K=int(z["K"]))
+    pre = f"deg{deg}__"
+    assert np.abs(fw["img"] - z[pre + "img"]).max() < 1e-4
+    g = pipeline.backward_view(fw, z["wts"].astype(np.float32), p, deg)
+    for n in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc", "color_rest"):
+        assert rel_l2(g[n], z[pre + "grad_" + n]) < 1e-3, (n, rel_l2(g[n], z[pre + "grad_" + n]))
+    ref = float(z[pre + "grad_w_b_raw"])
+    assert abs(g["w_b_raw"] - ref) < 1e-3 * abs(ref)
+
+
 def test_geometry_bwd_vs_reference():
     z = golden("geom_bwd.npz")
     cam = cam_from(z)
