@@ -141,9 +141,9 @@ __global__ void __launch_bounds__(256)
     const long long q = ((long long)v * H + ty * 16 + (p >> 4)) * W + tx * 16 + (p & 15);
     const float g0 = gimg[3 * q], g1 = gimg[3 * q + 1], g2 = gimg[3 * q + 2];
     const float c0 = img[3 * q], c1 = img[3 * q + 1], c2 = img[3 * q + 2];
-    const float d = den[q];
-    const float gn0 = g0 / d, gn1 = g1 / d, gn2 = g2 / d;
-    const float gd = -(g0 * c0 + g1 * c1 + g2 * c2) / d;
+    const float inv = __frcp_rn(den[q]);   // one correctly rounded reciprocal instead of four divisions
+    const float gn0 = g0 * inv, gn1 = g1 * inv, gn2 = g2 * inv;
+    const float gd = -(g0 * c0 + g1 * c1 + g2 * c2) * inv;
     s_g0[p] = gn0;
     s_g1[p] = gn1;
     s_g2[p] = gn2;
