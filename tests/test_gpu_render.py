@@ -159,6 +159,31 @@ def test_sh_degree_1_2_vs_reference(deg, pkg):
     assert abs(float(view(m.flat.grad, G, "w_b_raw")) - ref) < 1e-3 * abs(ref)
 
 
+def test_operator_pair_vs_reference(pkg):
+    """The reference's operator pair (_operands + _DevRenderBinned via render_binned_device,
+    tools/m4_train_binned.py:189-219): tables, image and parameter gradients."""
+    from tt_splat_b200 import binned, camera
+    from tt_splat_b200.model import view
+    z = golden("render_config0.npz")
+    cam = cam_from(z)
+    p = params_from(z)
+    m = _model(pkg, p)
+    tmap = binned.TileMap(cam["H"], cam["W"])
+    img, (idx, valid) = binned.render_binned_device(m, camera.Camera.from_dict(cam), tmap, K=int(z["K"]),
+                                                    return_bins=True)
+    v = valid.cpu().numpy()
+    assert np.array_equal(np.where(v, idx.cpu().numpy(), -1), np.where(z["valid"], z["idx"], -1))
+    assert np.abs(img.detach().cpu().numpy() - z["img"]).max() < 1e-3
+    tgt = torch.from_numpy(z["target"]).to(DEV)
+    (img - tgt).abs().mean().backward()
+    G = p["means3d"].shape[0]
+    for n in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc"):
+        mine = view(m.flat.grad, G, n).cpu().numpy()
+        assert rel_l2(mine, z["grad_" + n]) < 1e-3, (n, rel_l2(mine, z["grad_" + n]))
+    with pytest.raises(NotImplementedError):
+        binned.render_binned_device(m, camera.Camera.from_dict(cam), tmap, cached_bins=(idx, valid))
+
+
 def test_slot_rows_bit_exact_given_projection(pkg):
     """theta_u rows of the pack epilogue are the reference's fp32 expression bit for bit,
     given the device's own mu2d/conic (tools/m4_train_binned.py:130-143)."""

@@ -100,6 +100,9 @@ def _operands(model, cam, tmap, R, K, cached_bins=None, sh_degree=0, blur=0.3, n
     """tools/m4_train_binned.py:189-212 -> (theta_u[T,6,K], color_o_t[T,K,3], o_col_t[T,K,1], w_b,
     (idx, valid)).  The colour is the SH colour of degree ``sh_degree`` (0 = the reference's DC)."""
     if cached_bins is not None:
+        # the parameter backward reduces slots to gaussians through the stencil-indexed inverse
+        # table the binning writes; stale tables (gaussians that have since changed cell) have no
+        # such table, and re-binning costs ~23 us per 1264x832 view
         raise NotImplementedError("cached_bins: the device path re-bins every call")
     cam = as_camera(cam)
     flat = flat_of(model)
@@ -136,9 +139,12 @@ class _DevRenderBinned(torch.autograd.Function):
         return gth, gcol, goc, rb["gwb"].sum().reshape(wshape), None, None, None, None, None
 
 
-def render_binned_device(model, cam, tmap, R=1, K=128, sh_degree=0):
-    """tools/m4_train_binned.py:215-219."""
-    thU, col, oc, w_b, _ = _operands(model, cam, tmap, R, K, sh_degree=sh_degree)
+def render_binned_device(model, cam, tmap, R=1, K=128, cached_bins=None, return_bins=False, sh_degree=0):
+    """tools/m4_train_binned.py:215-219: the image [H, W, 3], and with ``return_bins`` the (idx,
+    valid) pair the binning produced.  ``cached_bins`` is not supported (the device path bins every
+    call; see ``_operands``)."""
+    thU, col, oc, w_b, bins = _operands(model, cam, tmap, R, K, cached_bins=cached_bins, sh_degree=sh_degree)
     c_b = getattr(model, "c_b", torch.ones(3, device=thU.device))
     with on_device(thU):
-        return _DevRenderBinned.apply(thU, col, oc, w_b, tmap.Phi, tmap.gidx, c_b, tmap.H, tmap.W)
+        img = _DevRenderBinned.apply(thU, col, oc, w_b, tmap.Phi, tmap.gidx, c_b, tmap.H, tmap.W)
+    return (img, bins) if return_bins else img
