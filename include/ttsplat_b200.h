@@ -51,7 +51,8 @@ int tts_version(void);
 const char* tts_last_error(void);
 
 /* Device status word written by kernels instead of trapping (bounded waits that gave up):
- * 1 = a bulk-copy wait of the forward, 2 = a relocation grid barrier, 4 = a peer barrier. */
+ * 1 = a bulk-copy wait of the forward, 2 = a relocation grid barrier, 4 = a peer barrier;
+ * 8 = a cached binning table that spreads a gaussian over more than its stencil. */
 int tts_read_status(int* status_host);      /* synchronous read + clear; diagnostic only */
 
 /* ---- geometry + SH colour + activations --------------------------------------------------
@@ -92,6 +93,18 @@ int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float* proj,
                  int R, int K, float k_poly, int32_t* idx, int32_t* count, int32_t* cand,
                  int32_t* inv, void* slots, int slot_format, void* workspace,
                  size_t workspace_bytes, void* stream);
+
+/* Operands from cached tables (replaces the cached_bins branch of _operands,
+ * tools/m4_train_binned.py:203-207): idx_in[V][T][K] holds gaussian ids from an earlier binning,
+ * -1 for invalid slots, the valid slots first in each tile.  Writes idx (may alias idx_in),
+ * count[V][T], the fp32 slot rows of the current projection and, when inv is not NULL, an inverse
+ * table: each gaussian's slot in the tile at (dx, dy) of the (2R+1)^2 box that starts at the
+ * smallest tile column and row it occupies.  Tables that spread a gaussian wider than that box
+ * OR 8 into the status word.  Workspace: tts_pack_cached_workspace_bytes. */
+size_t tts_pack_cached_workspace_bytes(int G, int V);
+int tts_pack_cached(const float* proj, int G, int V, int H, int W, int R, int K, float k_poly,
+                    const int32_t* idx_in, int32_t* idx, int32_t* count, int32_t* inv, float* slots,
+                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- operands in the reference layout -> slot rows ---------------------------------------
  * Packs theta_u[V*T,6,K], color_o[V*T,K,3], o_col[V*T,K,1] (the operands of

@@ -180,8 +180,52 @@ def test_operator_pair_vs_reference(pkg):
     for n in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc"):
         mine = view(m.flat.grad, G, n).cpu().numpy()
         assert rel_l2(mine, z["grad_" + n]) < 1e-3, (n, rel_l2(mine, z["grad_" + n]))
-    with pytest.raises(NotImplementedError):
-        binned.render_binned_device(m, camera.Camera.from_dict(cam), tmap, cached_bins=(idx, valid))
+
+
+def test_operator_pair_cached_bins(pkg):
+    """cached_bins (tools/m4_train_binned.py:203-207): the same tables at the same parameters give
+    the same image and gradients; stale tables after the means moved match the oracle driven by
+    those tables."""
+    import types
+    from tt_splat_b200 import binned, camera
+    from tt_splat_b200.model import view
+    z = golden("render_config0.npz")
+    cam = cam_from(z)
+    c = camera.Camera.from_dict(cam)
+    p = params_from(z)
+    K = int(z["K"])
+    G = p["means3d"].shape[0]
+    tmap = binned.TileMap(cam["H"], cam["W"])
+    m = _model(pkg, p)
+    img0, bins = binned.render_binned_device(m, c, tmap, K=K, return_bins=True)
+    img0.sum().backward()
+    g0 = m.flat.grad.clone()
+    m.flat.grad = None
+    img1, bins1 = binned.render_binned_device(m, c, tmap, K=K, cached_bins=bins, return_bins=True)
+    assert bins1 is bins
+    assert torch.equal(img1, img0)
+    img1.sum().backward()
+    assert rel_l2(m.flat.grad.cpu().numpy(), g0.cpu().numpy()) < 1e-6
+    # stale tables: move the means by up to a third of a tile, re-render through the old tables
+    p1 = dict(p)
+    p1["means3d"] = (p["means3d"] + 0.02 * np.random.default_rng(3).standard_normal(p["means3d"].shape)).astype(np.float32)
+    m1 = _model(pkg, p1)
+    img, _ = binned.render_binned_device(m1, c, tmap, K=K, cached_bins=bins, return_bins=True)
+    tb = types.SimpleNamespace(idx=bins[0].cpu().numpy(), valid=bins[1].cpu().numpy())
+    fw = pipeline.render_view(p1, 0, cam, K=K, bins=tb)
+    assert np.abs(img.detach().cpu().numpy() - fw["img"]).max() < 1e-3
+    wts = np.random.default_rng(4).standard_normal(fw["img"].shape).astype(np.float32)
+    (img * torch.from_numpy(wts).to(DEV)).sum().backward()
+    go = pipeline.backward_view(fw, wts, p1, 0)
+    for n in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc"):
+        mine = view(m1.flat.grad, G, n).cpu().numpy()
+        assert rel_l2(mine, go[n]) < 1e-3, (n, rel_l2(mine, go[n]))
+    from tt_splat_b200 import ops
+    assert ops.read_status() == 0
+    bad = (bins[0].clone(), bins[1].clone())
+    bad[1][0, 0] = False                        # a hole before valid slots
+    with pytest.raises(ValueError):
+        binned.render_binned_device(m, c, tmap, K=K, cached_bins=bad)
 
 
 def test_slot_rows_bit_exact_given_projection(pkg):

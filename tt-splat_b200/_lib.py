@@ -26,6 +26,8 @@ SIGNATURES = {
     "tts_read_status": (I, [P]),
     "tts_project": (I, [P, I, I, P, I, I, I, F, F, P, P, P, P, P, P, P]),
     "tts_bin_workspace_bytes": (SZ, [I, I, I, I]),
+    "tts_pack_cached_workspace_bytes": (SZ, [I, I]),
+    "tts_pack_cached": (I, [P, I, I, I, I, I, I, F, P, P, P, P, P, P, SZ, P]),
     "tts_bin_from_mu2d": (I, [P, P, I, I, I, I, I, I, P, P, P, P, P, SZ, P]),
     "tts_bin_from_mu2d_noalloc": (I, [P, P, I, I, I, I, I, I, P, P, P, P, P]),
     "tts_bin_pack": (I, [P, P, P, P, P, I, I, I, I, I, I, F, P, P, P, P, P, I, P, SZ, P]),

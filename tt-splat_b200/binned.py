@@ -63,18 +63,23 @@ def theta_u_gathered(conic_t, mu_t, origins, k):
 
 class _Operands(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, flat, cams_t, cfg):
+    def forward(ctx, flat, cams_t, cached_idx, cfg):
         G, sh_degree, H, W, R, K, k, blur, near = cfg
         flat_d = flat.detach().contiguous()
         pj = ops.project(flat_d, G, sh_degree, cams_t, H, W, blur, near)
-        bp = ops.bin_pack(pj, G, H, W, R, K, k)
-        s = bp["slots"][0]                                           # [T,K,12]
+        if cached_idx is None:
+            bp = ops.bin_pack(pj, G, H, W, R, K, k)
+        else:
+            bp = ops.pack_cached(pj, G, H, W, R, K, cached_idx, k)
+        idx = bp["idx"][0]
+        valid = idx >= 0
+        # the kernels write only the valid slots' rows; the operands are zero elsewhere, like the
+        # reference's products with valid (tools/m4_train_binned.py:209-211)
+        s = torch.where(valid[..., None], bp["slots"][0], torch.zeros((), device=flat_d.device))   # [T,K,12]
         theta_u = s[..., 0:6].transpose(1, 2).contiguous()
         color_o = s[..., 6:9].contiguous()
         o_col = s[..., 9:10].contiguous()
         w_b = torch.nn.functional.softplus(flat_d[59 * G])
-        idx = bp["idx"][0]
-        valid = idx >= 0
         ctx.save_for_backward(flat_d, cams_t, bp["inv"])
         ctx.cfg = cfg
         ctx.mark_non_differentiable(idx, valid)
@@ -93,23 +98,39 @@ class _Operands(torch.autograd.Function):
         if gwb is not None:
             part[0, 0] = gwb
         grads = ops.backward_params(flat, G, sh_degree, cams_t, H, W, R, K, inv, sg, part, k, blur, near)
-        return grads, None, None
+        return grads, None, None, None
+
+
+def _cached_table(cached_bins, G, T, K, device):
+    """The reference's (idx, valid) pair -> int32 [1,T,K] ids with -1 where invalid; the valid
+    slots of a tile must come first (as assign_bins writes them)."""
+    idx, valid = cached_bins
+    idx = torch.as_tensor(idx, device=device)
+    valid = torch.as_tensor(valid, device=device).bool()
+    if tuple(idx.shape) != (T, K) or tuple(valid.shape) != (T, K):
+        raise ValueError(f"cached_bins must be ([{T}, {K}], [{T}, {K}]) tables")
+    if bool((valid[:, 1:] & ~valid[:, :-1]).any()):
+        raise ValueError("cached_bins: the valid slots of a tile must come first")
+    if bool(((idx < 0) | (idx >= G))[valid].any()):
+        raise ValueError("cached_bins: gaussian ids out of range")
+    return torch.where(valid, idx, torch.full_like(idx, -1)).to(torch.int32).contiguous()[None]
 
 
 def _operands(model, cam, tmap, R, K, cached_bins=None, sh_degree=0, blur=0.3, near=0.2):
     """tools/m4_train_binned.py:189-212 -> (theta_u[T,6,K], color_o_t[T,K,3], o_col_t[T,K,1], w_b,
-    (idx, valid)).  The colour is the SH colour of degree ``sh_degree`` (0 = the reference's DC)."""
-    if cached_bins is not None:
-        # the parameter backward reduces slots to gaussians through the stencil-indexed inverse
-        # table the binning writes; stale tables (gaussians that have since changed cell) have no
-        # such table, and re-binning costs ~23 us per 1264x832 view
-        raise NotImplementedError("cached_bins: the device path re-bins every call")
+    (idx, valid)).  The colour is the SH colour of degree ``sh_degree`` (0 = the reference's DC).
+    With ``cached_bins`` (an (idx, valid) pair from an earlier call) the binning is skipped: the
+    operands of the current parameters are gathered through those tables, and the pair is
+    returned as given."""
     cam = as_camera(cam)
     flat = flat_of(model)
     G = model.means3d.shape[0]
     cfg = (G, int(sh_degree), cam.H, cam.W, int(R), int(K), K_POLY, float(blur), float(near))
     with on_device(flat):
-        th, col, oc, w_b, idx, valid = _Operands.apply(flat, pack_cameras([cam], flat.device), cfg)
+        cached = None if cached_bins is None else _cached_table(cached_bins, G, tmap.T, int(K), flat.device)
+        th, col, oc, w_b, idx, valid = _Operands.apply(flat, pack_cameras([cam], flat.device), cached, cfg)
+    if cached_bins is not None:
+        return th, col, oc, w_b, cached_bins
     return th, col, oc, w_b, (idx, valid)
 
 
@@ -141,8 +162,7 @@ class _DevRenderBinned(torch.autograd.Function):
 
 def render_binned_device(model, cam, tmap, R=1, K=128, cached_bins=None, return_bins=False, sh_degree=0):
     """tools/m4_train_binned.py:215-219: the image [H, W, 3], and with ``return_bins`` the (idx,
-    valid) pair the binning produced.  ``cached_bins`` is not supported (the device path bins every
-    call; see ``_operands``)."""
+    valid) pair the binning produced (or ``cached_bins``, which skips the binning)."""
     thU, col, oc, w_b, bins = _operands(model, cam, tmap, R, K, cached_bins=cached_bins, sh_degree=sh_degree)
     c_b = getattr(model, "c_b", torch.ones(3, device=thU.device))
     with on_device(thU):

@@ -718,6 +718,70 @@ static int validate(int G, int V, int H, int W, int R, int K) {
   return TTS_OK;
 }
 
+// ---- operands from cached tables (a (idx, valid) pair returned by an earlier binning) ----------
+// The slot rows are rebuilt from the current projection; the inverse table needs, per gaussian, a
+// slot index j in [0, S) that is distinct for each of its tiles.  An earlier binning put a
+// gaussian only in the D x D tiles around its home cell then, so j is its tile's position in the
+// D x D box starting at the smallest tile column and row it occupies (two atomicMin, independent
+// of their order); tables that spread a gaussian wider are flagged in the status word.
+constexpr int STATUS_TABLE_SPREAD = 8;
+
+__global__ void k_cached_box(const int* __restrict__ idx, long long n, int T, int K, int ntx, int G,
+                             int2* __restrict__ box) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int g = idx[i];
+  if (g < 0 || g >= G) return;
+  const long long vt = i / K;
+  const int v = (int)(vt / T), t = (int)(vt % T);
+  int2* b = box + (long long)v * G + g;
+  atomicMin(&b->x, t % ntx);
+  atomicMin(&b->y, t / ntx);
+}
+
+__global__ void __launch_bounds__(WB_WARPS * 32)
+    k_cached_emit(const int* __restrict__ idx_in, const int2* __restrict__ box, int G, int V, int ntx, int nty, int R,
+                  int K, const float* __restrict__ proj, float inv_k, int* __restrict__ idx, int* __restrict__ count,
+                  int* __restrict__ inv, float* __restrict__ slots) {
+  __shared__ u64 keys[WB_WARPS][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = ntx * nty;
+  const long long gt = (long long)blockIdx.x * WB_WARPS + warp;
+  if (gt >= (long long)V * T) return;
+  const int v = (int)(gt / T), t = (int)(gt % T);
+  const int tx = t % ntx, ty = t / ntx;
+  const int D = 2 * R + 1, S = D * D;
+  const int* in = idx_in + gt * K;
+  // valid slots lead the tile: the count is the first invalid slot
+  int first = K;
+  for (int k = lane; k < K; k += 32)
+    if (in[k] < 0) {
+      first = k;
+      break;
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+  const int n = first;
+  for (int k = lane; k < n; k += 32) {
+    int g = in[k];
+    if (g >= G) {   // not a gaussian of this model (the host validates tables before the launch)
+      atomicOr(&g_status, STATUS_TABLE_SPREAD);
+      g = 0;
+    }
+    const int2 b = box[(long long)v * G + g];
+    const int dx = tx - b.x, dy = ty - b.y;
+    int j = dy * D + dx;
+    if (dx < 0 || dx >= D || dy < 0 || dy >= D) {
+      atomicOr(&g_status, STATUS_TABLE_SPREAD);
+      j = 0;
+    }
+    keys[warp][k] = ((u64)(unsigned)j << 32) | (u64)(unsigned)g;
+  }
+  __syncwarp();
+  if (lane == 0) count[gt] = n;
+  emit_tile<1>(keys[warp], n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
+}
+
 }  // namespace tts
 
 using namespace tts;
@@ -759,6 +823,34 @@ extern "C" int tts_bin_pack(const float* mu2d, const uint8_t* keep, const float*
   BinWorkspace w = carve(workspace, G, V, T);
   return bin_core(mu2d, cell_count, reinterpret_cast<const int2*>(cell_rank), G, V, ntx, nty, R, K, proj,
                   (float)(1.0 / (double)k_poly), idx, count, cand, inv, slots, slot_format, w, as_stream(stream));
+}
+
+extern "C" size_t tts_pack_cached_workspace_bytes(int G, int V) {
+  return (G > 0 && V > 0) ? (size_t)V * G * sizeof(int2) : 0;
+}
+
+extern "C" int tts_pack_cached(const float* proj, int G, int V, int H, int W, int R, int K, float k_poly,
+                               const int32_t* idx_in, int32_t* idx, int32_t* count, int32_t* inv, float* slots,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = validate(G, V, H, W, R, K)) return rc;
+  TTS_REQUIRE(proj && idx_in && idx && count && slots, "null pointer");
+  TTS_REQUIRE(aligned16(proj) && aligned16(slots), "proj and slots must be 16-byte aligned");
+  TTS_REQUIRE(k_poly > 0.f, "k must be positive");
+  if (workspace_bytes < tts_pack_cached_workspace_bytes(G, V))
+    return fail(TTS_ERR_CAPACITY, "cached-table workspace too small");
+  const int ntx = W / 16, nty = H / 16, T = ntx * nty, S = (2 * R + 1) * (2 * R + 1);
+  cudaStream_t st = as_stream(stream);
+  int2* box = static_cast<int2*>(workspace);
+  if (G > 0 && cudaMemsetAsync(box, 0x7f, (size_t)V * G * sizeof(int2), st) != cudaSuccess)
+    return check_launch("memset box");
+  if (inv && cudaMemsetAsync(inv, 0xff, (size_t)V * G * S * 4, st) != cudaSuccess) return check_launch("memset inv");
+  const long long n = (long long)V * T * K;
+  if (G > 0) k_cached_box<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(idx_in, n, T, K, ntx, G, box);
+  if (int rc = check_launch("cached_box")) return rc;
+  const unsigned blocks = (unsigned)(((long long)V * T + WB_WARPS - 1) / WB_WARPS);
+  k_cached_emit<<<blocks, WB_WARPS * 32, 0, st>>>(idx_in, box, G, V, ntx, nty, R, K, proj,
+                                                   (float)(1.0 / (double)k_poly), idx, count, inv, slots);
+  return check_launch("cached_emit");
 }
 
 // ---- allocation-free binning -------------------------------------------------------------------

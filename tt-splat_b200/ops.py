@@ -115,6 +115,26 @@ def bin_pack(pj, G, H, W, R, K, k=4.0, ws=None, out=None, with_inv=True, bf16=Fa
     return out
 
 
+def pack_cached(pj, G, H, W, R, K, idx_in, k=4.0, ws=None):
+    """Slot rows of the current projection for cached tables ``idx_in`` [V,T,K] (int32, -1 =
+    invalid, valid slots first), with the count per tile and the inverse table."""
+    _dev(pj["proj"], idx_in)
+    V = pj["proj"].shape[0]
+    _, _, T = tiles(H, W)
+    if idx_in.dtype != torch.int32 or tuple(idx_in.shape) != (V, T, K):
+        raise ValueError(f"cached idx must be int32 [{V}, {T}, {K}]")
+    dev = pj["proj"].device
+    S = (2 * R + 1) ** 2
+    out = dict(idx=torch.empty_like(idx_in), count=torch.empty(V, T, dtype=torch.int32, device=dev),
+               inv=torch.empty(V, G, S, dtype=torch.int32, device=dev), slots=torch.zeros(V, T, K, SLOT_FLOATS, device=dev))
+    nbytes = lib().tts_pack_cached_workspace_bytes(G, V)
+    ws = ws or Workspace(dev)
+    buf = ws.get(nbytes)
+    call("tts_pack_cached", ptr(pj["proj"]), G, V, H, W, R, K, float(k), ptr(idx_in), ptr(out["idx"]), ptr(out["count"]),
+         ptr(out["inv"]), ptr(out["slots"]), ptr(buf), nbytes, stream())
+    return out
+
+
 def render_fwd(slots, count, H, W, w_b, c_b, bf16=False, out=None, w_b_is_raw=True):
     """Per-tile forward; ``w_b`` is a 1-element device tensor: the model's w_b_raw (softplus
     applied on the device) or, with ``w_b_is_raw=False``, the activated background weight."""
