@@ -12,9 +12,8 @@ scaling is strong (fixed total work).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 ``--impl reference`` times the CPU restatement of the reference path (the oracle port; the
-reference itself is Python and cannot travel to the GPU box) on a bounded sample: one view's
-forward + loss + backward plus the optimizer update over all gaussians, extrapolated to the
-8-view step.
+reference itself is Python and cannot travel to the GPU box): whole 8-view steps, the views'
+forward + loss + backward spread over worker processes on the host cores, for at most 90 s.
 """
 import argparse
 import json
@@ -37,6 +36,9 @@ CONFIG = dict(workload="config2: train step, G=100k, 8 views 1264x832, K=128, SH
 METRIC = "train steps/s (G=100k, 8-view batch 1264x832, 1/2/4/8 B200)"
 PEAKS_FILE = os.path.join(REPO, "MEASURED_PEAKS.json")
 REF_BUDGET_S = 90.0   # wall-clock budget of the CPU reference arm's timed samples
+CPU_SAMPLE = ("one whole step per sample: the 8 views' forward+loss+backward on {workers} worker processes "
+              "(one BLAS thread each), gradients summed in view order, then Adam, SGLD and 1% relocation "
+              "over all 100k gaussians; numpy oracle")
 
 
 def load_peaks():
@@ -94,57 +96,33 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------------------------
 def run_reference(args, rank, world):
-    """The CPU oracle port on a bounded sample (rank 0 only)."""
+    """The CPU restatement of the reference train step (rank 0 only): every step runs all views'
+    forward + loss + backward over worker processes (one BLAS thread each, one view per worker up
+    to the host's cores and memory), sums the gradients and applies Adam, SGLD and relocation."""
     if rank != 0:
         return
-    from oracle import loss as oloss
-    from oracle import optim as ooptim
-    from oracle import pipeline as opipe
+    from oracle.step import CpuStep
     pkg = __graft_entry__.load_package()
-    sc = pkg.synthetic.config2()
-    p, cams, tg = sc["params"], sc["cams"], sc["targets"]
-    lr = {"means": 1.6e-4, "scales": 5e-3, "quats": 1e-3, "opacity": 5e-2, "color": 1e-2, "wb": 1e-2}
-    cores = os.cpu_count()
-    rng = np.random.default_rng(0)
-
-    def sample(i):
-        v = i % len(cams)
-        t0 = time.perf_counter()
-        fw = opipe.render_view(p, 3, cams[v], K=CONFIG["K"])
-        _, _, _, gimg = oloss.loss_and_grad(fw["img"], tg[v], 0.2)
-        g = opipe.backward_view(fw, (gimg / 8).astype(np.float32), p, 3)
-        t1 = time.perf_counter()
-        q = opipe.copy_params(p)
-        opipe.adam_step(q, g, {}, 1, lr, 3)
-        q["means3d"] = ooptim.sgld_noise(q["means3d"], q["log_scales"], q["quats"], q["opacity_raw"],
-                                         rng.standard_normal((p["means3d"].shape[0], 3)), lr["means"]).astype(np.float32)
-        o = 1 / (1 + np.exp(-q["opacity_raw"].astype(np.float64)))
-        thr = ooptim.quantile_threshold(o, 0.01)
-        n_dead = int((o < thr).sum())
-        alive = np.nonzero(o >= thr)[0]
-        tgts = alive[rng.choice(alive.size, n_dead, p=o[alive] / o[alive].sum())]
-        ooptim.relocate(q, thr, tgts)
-        t2 = time.perf_counter()
-        return len(cams) * (t1 - t0) + (t2 - t1)
-
-    # one CPU sample takes seconds: at most one warm-up sample, then timed samples until the
-    # requested count or a 90-s budget (at least two), so any --steps finishes within minutes
-    warm = min(args.warmup, 1)
-    for i in range(warm):
-        sample(i)
-    times = []
-    t_start = time.perf_counter()
-    while len(times) < max(args.steps, 1) and (len(times) < 2 or time.perf_counter() - t_start < REF_BUDGET_S):
-        times.append(sample(warm + len(times)))
+    with CpuStep(pkg.synthetic.config2()) as cs:
+        # one step takes seconds: one warm-up step (it also starts the workers), then timed
+        # steps until the requested count or a 90-s budget (at least two)
+        warm = 1
+        cs.step()
+        times = []
+        t_start = time.perf_counter()
+        while len(times) < max(args.steps, 1) and (len(times) < 2 or time.perf_counter() - t_start < REF_BUDGET_S):
+            t0 = time.perf_counter()
+            cs.step()
+            times.append(time.perf_counter() - t0)
+        workers = cs.workers
     step_s = float(np.median(times))
     line = {"impl": "reference", "metric": METRIC, "value": 1.0 / step_s, "unit": "steps/s", "n_gpus": world,
             "steps": len(times), "warmup": warm, "steps_requested": args.steps, "warmup_requested": args.warmup,
             "ms_per_step": step_s * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 2 shapes)",
             "config": {k: v for k, v in CONFIG.items()},
-            "cpu_baseline": {"value": 1.0 / step_s, "unit": "steps/s", "cores": cores, "kind": "port",
-                             "sample": "per step: one of the 8 views (forward+loss+backward, x8) plus Adam, SGLD and "
-                                       "1% relocation over all 100k gaussians; numpy oracle, BLAS threads = cores"},
+            "cpu_baseline": {"value": 1.0 / step_s, "unit": "steps/s", "cores": workers, "kind": "port",
+                             "sample": CPU_SAMPLE.format(workers=workers)},
             "e2e": {"value": 1.0 / step_s, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -500,24 +478,18 @@ ADAM_DRAM = 94.4e6 + 15.2e6
 
 
 def cpu_baseline_sample():
-    """The oracle port timed on a bounded sample of the workload (one view + optimizer)."""
-    import time as _t
-    from oracle import loss as oloss
-    from oracle import pipeline as opipe
+    """The oracle's whole train step on the host cores (one warm-up step that starts the workers,
+    then one timed step), on the same scene as the device step."""
+    from oracle.step import CpuStep
     pkg = __graft_entry__.load_package()
-    sc = pkg.synthetic.config2()
-    p = sc["params"]
-    t0 = _t.perf_counter()
-    fw = opipe.render_view(p, 3, sc["cams"][0], K=CONFIG["K"])
-    _, _, _, gimg = oloss.loss_and_grad(fw["img"], sc["targets"][0], 0.2)
-    g = opipe.backward_view(fw, (gimg / 8).astype(np.float32), p, 3)
-    t1 = _t.perf_counter()
-    opipe.adam_step(opipe.copy_params(p), g, {}, 1, {"means": 1.6e-4, "scales": 5e-3, "quats": 1e-3, "opacity": 5e-2,
-                                                      "color": 1e-2, "wb": 1e-2}, 3)
-    t2 = _t.perf_counter()
-    step_s = 8 * (t1 - t0) + (t2 - t1)
-    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": "one of the 8 views (forward+loss+backward) x8 + Adam over 100k gaussians; numpy oracle"}
+    with CpuStep(pkg.synthetic.config2()) as cs:
+        cs.step()
+        t0 = time.perf_counter()
+        cs.step()
+        step_s = time.perf_counter() - t0
+        workers = cs.workers
+    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": workers, "kind": "port",
+            "sample": CPU_SAMPLE.format(workers=workers)}
 
 
 def main():

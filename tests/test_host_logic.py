@@ -36,3 +36,32 @@ def test_ops_reject_cpu_tensors(pkg):
     from tt_splat_b200 import ops
     with pytest.raises(RuntimeError):
         ops._dev(torch.zeros(4))
+
+
+def test_cpu_baseline_step_matches_serial_oracle(pkg):
+    """The benchmark's CPU baseline (views over spawned workers, gradients summed in view order)
+    computes the same step as the serial oracle: same loss, same Adam update."""
+    import numpy as np
+    from oracle import loss as oloss
+    from oracle import pipeline as opipe
+    from oracle.step import LR, CpuStep
+    sc = pkg.synthetic.config2(G=3000, H=64, W=96, n_views=3)
+    with CpuStep(sc, workers=2) as cs:
+        loss, q = cs.step()
+    p = sc["params"]
+    g, total = None, 0.0
+    for v in range(3):
+        fw = opipe.render_view(p, 3, sc["cams"][v], K=128)
+        lv, _, _, gimg = oloss.loss_and_grad(fw["img"], sc["targets"][v], 0.2)
+        gv = opipe.backward_view(fw, (gimg / 3).astype(np.float32), p, 3)
+        g = gv if g is None else {k: g[k] + gv[k] for k in g}
+        total += lv
+    assert abs(loss - total / 3) < 1e-12
+    ref = opipe.copy_params(p)
+    opipe.adam_step(ref, g, {}, 1, LR, 3)
+    # SGLD noise and relocation move means and may overwrite relocated rows; the colours of
+    # gaussians that were not relocated are the Adam update alone
+    o = 1 / (1 + np.exp(-ref["opacity_raw"].astype(np.float64)))
+    kept = o >= np.quantile(o, 0.02)
+    np.testing.assert_array_equal(q["color_dc"][kept], ref["color_dc"][kept])
+    assert all(np.isfinite(q[k]).all() for k in opipe.PARAM_NAMES)
