@@ -30,7 +30,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, HERE)
 
-from make_golden_cases import BIG_CASE, STRESS_CASES  # noqa: E402
+from make_golden_cases import BIG_CASE, RADIUS_CASES, STRESS_CASES  # noqa: E402
 
 
 def load_synthetic():
@@ -147,9 +147,9 @@ def gen_bins_scene(R, syn, out):
 
 
 
-def gen_bins_stress(R, syn, out):
+def gen_bins_stress(R, syn, out, cases=STRESS_CASES, fname="bins_stress.npz"):
     arrays = {}
-    for name, seed, G, H, W, Rr, K, kw in STRESS_CASES:
+    for name, seed, G, H, W, Rr, K, kw in cases:
         mu, keep = syn.stress_mu2d(seed, G, H, W, **kw)
         idx_s, valid_s = bins_of(R, torch.from_numpy(mu), torch.from_numpy(keep), H, W, Rr, K, True)
         idx_d, valid_d = bins_of(R, torch.from_numpy(mu), torch.from_numpy(keep), H, W, Rr, K, False)
@@ -157,7 +157,7 @@ def gen_bins_stress(R, syn, out):
         arrays.update({f"{name}__idx_stable": idx_s.astype(np.int32), f"{name}__valid_stable": valid_s,
                        f"{name}__idx_default": idx_d.astype(np.int32), f"{name}__valid_default": valid_d,
                        f"{name}__cand": cand.astype(np.int32)})
-    np.savez_compressed(os.path.join(out, "bins_stress.npz"), **arrays)
+    np.savez_compressed(os.path.join(out, fname), **arrays)
 
 
 def gen_bins_big(R, syn, out):
@@ -462,6 +462,7 @@ def main():
     syn = load_synthetic()
     torch.set_num_threads(os.cpu_count())
     jobs = dict(bins_scene=lambda: gen_bins_scene(R, syn, HERE), bins_stress=lambda: gen_bins_stress(R, syn, HERE),
+                bins_radius=lambda: gen_bins_stress(R, syn, HERE, RADIUS_CASES, "bins_radius.npz"),
                 bins_big=lambda: gen_bins_big(R, syn, HERE), render=lambda: gen_render(R, syn, HERE),
                 geom=lambda: gen_geom(R, syn, HERE), loss=lambda: gen_loss(R, HERE),
                 optim=lambda: gen_optim(R, syn, HERE), arm_b=lambda: gen_arm_b(R, syn, HERE),

@@ -9,5 +9,12 @@ STRESS_CASES = [
     ("allout_k4", 16, 200, 32, 32, 1, 4, dict(n_clusters=2, sigma_px=3.0, frac_drop=1.0)),
 ]
 
+# the largest stencil radius the entry points accept (R = 3: a 7x7 tile neighbourhood per cell)
+RADIUS_CASES = [
+    ("r3_k48", 17, 4000, 80, 112, 3, 48, dict(n_clusters=8, sigma_px=7.0)),
+    ("r3_k8_ties", 18, 1500, 64, 64, 3, 8, dict(n_clusters=3, sigma_px=4.0, quantise=True)),
+    ("r3_k128_sparse", 19, 500, 256, 320, 3, 128, dict(n_clusters=3, sigma_px=6.0, frac_off=0.3)),
+]
+
 BIG_CASE = dict(seed=31, G=1_000_000, H=1072, W=1920, R=1, K=256,
                 kw=dict(n_clusters=64, sigma_px=30.0, frac_off=0.05, frac_drop=0.02))

@@ -55,11 +55,14 @@ def test_bins_config1_digest_and_overflow():
     assert binning.table_digest(b) == str(z["digest"])
 
 
-@pytest.mark.parametrize("case", [c[0] for c in __import__("make_golden_cases").STRESS_CASES])
-def test_bins_stress_bit_exact(case, pkg):
-    import make_golden_cases as mg
-    name, seed, G, H, W, R, K, kw = next(c for c in mg.STRESS_CASES if c[0] == case)
-    z = golden("bins_stress.npz")
+_MG = __import__("make_golden_cases")
+
+
+@pytest.mark.parametrize("fixture,case", [("bins_stress.npz", c[0]) for c in _MG.STRESS_CASES]
+                         + [("bins_radius.npz", c[0]) for c in _MG.RADIUS_CASES])
+def test_bins_stress_bit_exact(fixture, case, pkg):
+    name, seed, G, H, W, R, K, kw = next(c for c in _MG.STRESS_CASES + _MG.RADIUS_CASES if c[0] == case)
+    z = golden(fixture)
     mu, keep = pkg.synthetic.stress_mu2d(seed, G, H, W, **kw)
     tm = binning.tile_map(H, W)
     b = binning.assign_bins(mu, keep, tm, R, K)
