@@ -45,6 +45,18 @@ def test_stress_bit_exact_vs_reference(case, pkg):
     check(idx, count, cand, z[f"{name}__idx_stable"], z[f"{name}__valid_stable"], z[f"{name}__cand"])
 
 
+@pytest.mark.parametrize("case", [c[0] for c in __import__("make_golden_cases").RADIUS_CASES])
+def test_radius3_bit_exact_vs_reference(case, pkg):
+    """Stencil radius 3 (7x7 tile neighbourhood, the largest accepted): overflowing, tied and
+    sparse tiles, bit-exact with the reference's tables."""
+    import make_golden_cases as mg
+    name, seed, G, H, W, R, K, kw = next(c for c in mg.RADIUS_CASES if c[0] == case)
+    z = golden("bins_radius.npz")
+    mu, keep = pkg.synthetic.stress_mu2d(seed, G, H, W, **kw)
+    idx, count, cand, _ = gpu_bins(mu, keep, H, W, R, K)
+    check(idx, count, cand, z[f"{name}__idx_stable"], z[f"{name}__valid_stable"], z[f"{name}__cand"])
+
+
 def test_tables_from_device_geometry(pkg):
     """End to end: the device projection's mu2d (fp32, ulp-level differences from the reference's
     CPU mu2d) binned on the device, against the reference tables.  Tiles can differ only where a
