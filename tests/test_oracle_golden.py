@@ -345,3 +345,56 @@ def test_relocate_vs_reference():
     assert np.array_equal(touched, z["reloc_touched"])
     for k in p:
         assert np.abs(p[k] - z[f"reloc_out_{k}"]).max() < 1e-6, k
+
+
+def _bf16(x):
+    """Round float32 to bfloat16 (nearest, ties to even) and back, by the bit pattern."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
+def test_tile_local_theta_matches_global_quad_form():
+    """spike/tests/test_tile_local.py:22-38 on the oracle's theta_u_gathered: with the tile origin
+    folded into theta, Phi.theta (k = 1) gives 1 - Q of the global quadratic form at every pixel
+    centre of the tile, to float32 rounding (the operand build is float32, as in the reference)."""
+    from oracle.render import theta_u_gathered
+    rng = np.random.default_rng(1)
+    Phi = binning.tile_map(16, 16).Phi.astype(np.float64)
+    lx, ly = Phi[:, 3], Phi[:, 4]
+    for _ in range(20):
+        origin = rng.integers(0, 64, 2).astype(np.float64) * 16.0
+        L = rng.standard_normal((5, 2, 2))
+        M = L @ np.transpose(L, (0, 2, 1)) + 0.1 * np.eye(2)
+        conic = np.stack([M[:, 0, 0], M[:, 0, 1], M[:, 1, 1]], -1)
+        mu = origin + rng.random((5, 2)) * 16.0
+        th = theta_u_gathered(conic[None], mu[None], origin[None], 1.0)[0].astype(np.float64)   # [6, G]
+        q_local = 1.0 - Phi @ th
+        dx = (origin[0] + lx)[:, None] - mu[None, :, 0].astype(np.float32)
+        dy = (origin[1] + ly)[:, None] - mu[None, :, 1].astype(np.float32)
+        a, b, c = (conic[:, i].astype(np.float32) for i in range(3))
+        q_global = a * dx * dx + 2 * b * dx * dy + c * dy * dy
+        scale = np.abs(th).max(0) * 256.0 + 1.0      # largest monomial term per gaussian
+        assert (np.abs(q_local - q_global) <= 1e-7 * scale).all()
+
+
+def test_tile_local_theta_survives_bf16():
+    """spike/tests/test_tile_local.py:41-70: in bfloat16 the tile-local Phi.theta keeps Q within
+    0.1 of the float64 value, while the same product in global pixel coordinates loses it."""
+    from oracle.render import theta_u_gathered
+    origin = np.array([400.0, 400.0])
+    conic = np.array([[0.08, 0.02, 0.05]])
+    mu = origin + np.array([[7.3, 4.6]])
+    Phi = binning.tile_map(16, 16).Phi
+    px, py = origin[0] + Phi[:, 3].astype(np.float64), origin[1] + Phi[:, 4].astype(np.float64)
+    dx, dy = px - mu[0, 0], py - mu[0, 1]
+    q_ref = 0.08 * dx * dx + 2 * 0.02 * dx * dy + 0.05 * dy * dy
+    th_local = theta_u_gathered(conic[None], mu[None], origin[None], 1.0)[0]
+    q_local = 1.0 - (_bf16(Phi).astype(np.float64) @ _bf16(th_local).astype(np.float64))[:, 0]
+    th_global = theta_u_gathered(conic[None], mu[None], np.zeros((1, 2)), 1.0)[0]
+    Phi_g = np.stack([px * px, py * py, px * py, px, py, np.ones_like(px)], -1).astype(np.float32)
+    q_global = 1.0 - (_bf16(Phi_g).astype(np.float64) @ _bf16(th_global).astype(np.float64))[:, 0]
+    err_local = np.abs(q_local - q_ref).max()
+    err_global = np.abs(q_global - q_ref).max()
+    assert err_local < 0.1
+    assert err_global > 1.0 and err_global > 20 * err_local
