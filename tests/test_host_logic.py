@@ -65,3 +65,21 @@ def test_cpu_baseline_step_matches_serial_oracle(pkg):
     kept = o >= np.quantile(o, 0.02)
     np.testing.assert_array_equal(q["color_dc"][kept], ref["color_dc"][kept])
     assert all(np.isfinite(q[k]).all() for k in opipe.PARAM_NAMES)
+
+
+def test_peer_shards_and_region_layout(pkg):
+    """The Adam shards of the peer exchange tile [0, n) in rank order without gaps or overlap,
+    each starting on a 16-byte boundary (the device's float4 loads), and the region's four parts
+    are 256-byte aligned and disjoint."""
+    from tt_splat_b200 import peer
+    for n in (1, 3, 4, 5, 59 * 2000 + 1, 59 * 100000 + 1, 5_900_017):
+        for world in range(1, 9):
+            ranges = [peer.shard_range(n, r, world) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == n
+            for (lo, hi), (lo2, _) in zip(ranges, ranges[1:]):
+                assert lo <= hi == lo2
+            assert all(lo % 4 == 0 for lo, hi in ranges if hi > lo)
+    off_p, off_g, off_l, off_f, size = peer.layout(59 * 100000 + 1)
+    assert all(o % 256 == 0 for o in (off_p, off_g, off_l, off_f, size))
+    assert off_g >= 4 * (59 * 100000 + 1) and off_l >= off_g + 4 * (59 * 100000 + 1)
+    assert off_f >= off_l + 4 and size >= off_f + 4 * peer.FLAG_INTS
