@@ -83,3 +83,27 @@ def test_peer_shards_and_region_layout(pkg):
     assert all(o % 256 == 0 for o in (off_p, off_g, off_l, off_f, size))
     assert off_g >= 4 * (59 * 100000 + 1) and off_l >= off_g + 4 * (59 * 100000 + 1)
     assert off_f >= off_l + 4 and size >= off_f + 4 * peer.FLAG_INTS
+
+
+def test_bench_workload_is_the_baseline_config(pkg):
+    """bench.py's headline workload and the synthetic scene it builds are the configuration the
+    baseline metric is quoted on (G, image size, K, batch of views, SH degree)."""
+    import json
+    import os
+    import re
+    import bench
+    from conftest import REPO
+    path = os.path.join(REPO, "BASELINE.json")
+    if not os.path.exists(path):
+        pytest.skip("no baseline description in this checkout")
+    text = json.load(open(path))["configs"][2]
+    G = int(re.search(r"G=([\d,]+)", text).group(1).replace(",", ""))
+    W, H = map(int, re.search(r"(\d+)\s*[x×]\s*(\d+)", text).groups())
+    K = int(re.search(r"K=(\d+)", text).group(1))
+    views = int(re.search(r"batch of (\d+)", text).group(1))
+    deg = int(re.search(r"SH degree (\d+)", text).group(1))
+    c = bench.CONFIG
+    assert (c["G"], c["W"], c["H"], c["K"], c["views"], c["sh_degree"]) == (G, W, H, K, views, deg)
+    sc = pkg.synthetic.config2(G=1000)     # same cameras and images at a small G
+    assert len(sc["cams"]) == views and sc["targets"][0].shape == (H, W, 3)
+    assert sc["K"] == K and sc["sh_degree"] == deg
