@@ -37,8 +37,8 @@ METRIC = "train steps/s (G=100k, 8-view batch 1264x832, 1/2/4/8 B200)"
 PEAKS_FILE = os.path.join(REPO, "MEASURED_PEAKS.json")
 REF_BUDGET_S = 90.0   # wall-clock budget of the CPU reference arm's timed samples
 CPU_SAMPLE = ("median of whole steps after one warm-up step: the 8 views' forward+loss+backward on "
-              "{workers} worker processes (one BLAS thread each), gradients summed in view order, then "
-              "Adam, SGLD and 1% relocation over all 100k gaussians; numpy oracle")
+              "{workers} worker processes (one per view, one BLAS thread each), gradients summed in view order, "
+              "then Adam, SGLD and 1% relocation over all 100k gaussians; numpy oracle")
 
 
 def load_peaks():

@@ -4,14 +4,22 @@ with the batch's views spread over worker processes.
 The reference trains on a batch of views whose per-view forward + loss + backward are independent
 (``spike/mcmc.py:90-114``: mean of the per-view losses, one optimizer step).  ``CpuStep`` runs
 those per-view passes in parallel, one worker process per view up to the host's cores and
-memory, each numpy process limited to one BLAS thread, then sums the per-view gradients in
-view order and applies Adam, SGLD noise and relocation in the calling process.  It is timed as
-the CPU baseline of the benchmark; it is never part of the product.
+memory, each numpy process limited to one BLAS thread, then sums the per-view gradients in view
+order and applies Adam, SGLD noise and relocation in the calling process.  (Splitting a view's
+tiles over threads of one worker measured slower than one thread: the page faults of the large
+per-tile temporaries contend inside a process.)  It is timed as the CPU baseline of the
+benchmark; it is never part of the product.
 
 Workers are started with ``spawn`` so that a caller that already holds a CUDA context can use it.
+The scene reaches them through a temporary file, so the start-up message each worker reads from
+its pipe stays small: a worker that dies then makes the step raise (``BrokenProcessPool``)
+instead of leaving the parent blocked on a pipe nobody drains.
 """
 import multiprocessing as mp
 import os
+import pickle
+import tempfile
+from concurrent.futures import ProcessPoolExecutor
 
 import numpy as np
 
@@ -26,8 +34,9 @@ _BLAS_VARS = ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")
 _W = {}
 
 
-def _init(params, sh_degree, cams, targets, K, n_views):
-    _W.update(params=params, sh_degree=sh_degree, cams=cams, targets=targets, K=K, n_views=n_views)
+def _init(scene_path):
+    with open(scene_path, "rb") as f:
+        _W.update(pickle.load(f))
 
 
 def _view(v):
@@ -39,9 +48,14 @@ def _view(v):
     return v, float(loss), g
 
 
+def host_cores():
+    """Cores this process may run on."""
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
 def host_workers(n_views, per_view_bytes=VIEW_PEAK_BYTES):
     """Worker count: one per view, bounded by the cores and by 60% of the available memory."""
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    cores = host_cores()
     try:
         import psutil
         avail = psutil.virtual_memory().available
@@ -59,14 +73,20 @@ class CpuStep:
         self.n_views = len(scene["cams"])
         self.workers = workers or host_workers(self.n_views)
         self.rng = np.random.default_rng(seed)
+        fd, self.scene_path = tempfile.mkstemp(prefix="ttsplat_scene_", suffix=".pkl")
         saved = {k: os.environ.get(k) for k in _BLAS_VARS}
-        for k in _BLAS_VARS:
-            os.environ[k] = "1"
         try:
-            self.pool = mp.get_context("spawn").Pool(
-                self.workers, initializer=_init,
-                initargs=(self.p, self.sh_degree, scene["cams"], scene["targets"], scene.get("K", 128),
-                          self.n_views))
+            with os.fdopen(fd, "wb") as f:
+                pickle.dump(dict(params=self.p, sh_degree=self.sh_degree, cams=scene["cams"],
+                                 targets=scene["targets"], K=scene.get("K", 128), n_views=self.n_views),
+                            f, protocol=pickle.HIGHEST_PROTOCOL)
+            for k in _BLAS_VARS:
+                os.environ[k] = "1"
+            self.pool = ProcessPoolExecutor(self.workers, mp_context=mp.get_context("spawn"), initializer=_init,
+                                            initargs=(self.scene_path,))
+        except BaseException:
+            os.unlink(self.scene_path)
+            raise
         finally:
             for k, v in saved.items():
                 if v is None:
@@ -76,7 +96,7 @@ class CpuStep:
 
     def step(self):
         """Run one step; returns (photometric loss, updated parameter copy)."""
-        res = sorted(self.pool.map(_view, range(self.n_views), chunksize=1), key=lambda r: r[0])
+        res = sorted(self.pool.map(_view, range(self.n_views)), key=lambda r: r[0])
         g = {k: np.array(res[0][2][k], copy=True) if k != "w_b_raw" else res[0][2][k] for k in res[0][2]}
         for _, _, gv in res[1:]:
             for k in g:
@@ -95,8 +115,11 @@ class CpuStep:
         return sum(r[1] for r in res) / self.n_views, q
 
     def close(self):
-        self.pool.close()
-        self.pool.join()
+        try:
+            self.pool.shutdown(wait=True, cancel_futures=True)
+        finally:
+            if os.path.exists(self.scene_path):
+                os.unlink(self.scene_path)
 
     def __enter__(self):
         return self
