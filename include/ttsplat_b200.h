@@ -52,8 +52,10 @@ const char* tts_last_error(void);
 
 /* Device status word written by kernels instead of trapping (bounded waits that gave up):
  * 1 = a bulk-copy wait of the forward, 2 = a relocation grid barrier, 4 = a peer barrier;
- * 8 = a cached binning table that spreads a gaussian over more than its stencil. */
-int tts_read_status(int* status_host);      /* synchronous read + clear; diagnostic only */
+ * 8 = a cached binning table that spreads a gaussian over more than its stencil.
+ * Synchronous read + clear.  A non-zero word means a step skipped work: the Python train step
+ * reads it at check_status / check_replicas and at the end of fit / train_mcmc, and raises. */
+int tts_read_status(int* status_host);
 
 /* ---- geometry + SH colour + activations --------------------------------------------------
  * Replaces spike/geometry.py:10-57 (quat_to_rotmat, cov3d, project_ewa), spike/sh.py:49-72
@@ -86,7 +88,10 @@ int tts_bin_from_mu2d(const float* mu2d, const uint8_t* keep, int G, int V, int 
  * in a host runtime that owns the allocator).  Scratch comes from a 16 MiB static device array per
  * GPU, held until exit; problems whose tts_bin_workspace_bytes exceeds 16 MiB are rejected with
  * TTS_ERR_CAPACITY.  The first call on a device looks up that array's address (set-up), so make
- * it before any stream capture.  All calls share the array: calls that overlap on the GPU race. */
+ * it before any stream capture.  All calls share the array: calls that overlap on the GPU race.
+ * The looked-up address is kept for the life of the process and belongs to the device's
+ * context at the time of that first call: after cudaDeviceReset (a new primary context) it is
+ * stale, so do not call this entry point on a device that has been reset. */
 int tts_bin_from_mu2d_noalloc(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W,
                               int R, int K, int32_t* idx, int32_t* count, int32_t* cand,
                               int32_t* inv, void* stream);
@@ -221,7 +226,9 @@ int tts_relocate(float* params, float* m, float* v, int G, float dead_thr, float
  * tts_peer_barrier = signal + wait in one kernel.  params/grads/loss/flags are host arrays of N
  * device pointers (index = rank; this rank's own buffers included); flags point at 32 int32 per
  * rank, zero at start; epoch is a device int that grows every step (the step counter).  A wait
- * that runs too long ORs 4 into the status word (tts_read_status) and gives up.  N <= 8. */
+ * that runs too long ORs 4 into the status word (tts_read_status) and gives up; the Adam and
+ * SGLD blocks whose wait gave up skip their part of the update (no partial gradient sums).
+ * N <= 8. */
 size_t tts_ipc_handle_bytes(void);
 int tts_peer_alloc(size_t bytes, void** ptr);
 int tts_peer_free(void* ptr);

@@ -38,6 +38,26 @@ def test_barrier_times_out_and_reports_status(pkg):
     assert float(x.sum()) == 8.0
 
 
+def test_train_step_raises_after_a_timed_out_wait(pkg):
+    """A peer wait that ran out sets the status word; the train step's status check (called by
+    check_replicas and at the end of fit / train_mcmc) raises naming it, then the word is clear."""
+    from tt_splat_b200 import camera, model, ops, train
+    ops.read_status()                                         # clear
+    sc = pkg.synthetic.config2(seed=5, G=500, H=32, W=48, n_views=1)
+    m = model.GaussianModel.from_arrays(sc["params"], device=DEV)
+    st = train.TrainStep(m, [camera.Camera.from_dict(sc["cams"][0])], sc["targets"], sh_degree=3, use_graph=False)
+    st.step()
+    st.check_status()                                         # a clean step: no error
+    flags = torch.zeros(2, 16, dtype=torch.int32, device=DEV)
+    table = (ctypes.c_void_p * 2)(flags[0].data_ptr(), flags[1].data_ptr())
+    epoch = torch.ones(1, dtype=torch.int32, device=DEV)
+    assert ops.lib().tts_peer_wait(table, 0, 2, 0, ctypes.c_void_p(epoch.data_ptr()),
+                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    with pytest.raises(RuntimeError, match="peer-exchange wait timed out"):
+        st.check_replicas()
+    st.check_status()                                         # read and cleared
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

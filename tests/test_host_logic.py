@@ -107,3 +107,23 @@ def test_bench_workload_is_the_baseline_config(pkg):
     sc = pkg.synthetic.config2(G=1000)     # same cameras and images at a small G
     assert len(sc["cams"]) == views and sc["targets"][0].shape == (H, W, 3)
     assert sc["K"] == K and sc["sh_degree"] == deg
+
+
+def test_status_word_raises_naming_its_bits(pkg, monkeypatch):
+    """A bounded device wait that gave up surfaces as a RuntimeError naming the bit: at
+    TrainStep.check_status / check_replicas and at the end of fit and train_mcmc (the status
+    word is faked here; nothing waits on a device)."""
+    from tt_splat_b200 import ops, train
+    train.raise_on_status(0)
+    with pytest.raises(RuntimeError, match="peer-exchange wait timed out"):
+        train.raise_on_status(4)
+    with pytest.raises(RuntimeError, match="bulk-copy wait") as e:
+        train.raise_on_status(1 | 2 | 64)
+    assert "relocation" in str(e.value) and "unknown bits 0x40" in str(e.value)
+    st = object.__new__(train.TrainStep)       # host state only: no buffers, no device
+    st.dev, st.it, st.pg = torch.device("cpu"), 7, None
+    words = [4, 0]
+    monkeypatch.setattr(ops, "read_status", lambda: words.pop(0))
+    with pytest.raises(RuntimeError, match="iteration 7.*peer-exchange"):
+        st.check_replicas()
+    st.check_replicas()                          # the read cleared the word: no error

@@ -116,6 +116,13 @@ def on_device(t):
     return contextlib.nullcontext()
 
 
+def device_ctx(device):
+    """Context selecting a torch CUDA device (a no-op for any other device)."""
+    import contextlib
+    device = torch.device(device)
+    return torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext()
+
+
 def require_cuda():
     if not torch.cuda.is_available():
         raise RuntimeError("CUDA is not available: tt-splat B200 has no CPU fallback")

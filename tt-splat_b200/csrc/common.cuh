@@ -116,6 +116,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   for (int it = 0; it < (1 << 22); ++it)
     if (mbar_try_wait(bar, parity)) return true;
   atomicOr(&g_status, STATUS_MBAR_TIMEOUT);
+  // A CTA must not exit while its bulk copy may still write into its shared memory (the next
+  // CTA on the SM would receive that memory): wait once more, again with a limit, for the copy
+  // in flight before the caller abandons the tile.
+  for (int it = 0; it < (1 << 22); ++it)
+    if (mbar_try_wait(bar, parity)) break;
   return false;
 }
 

@@ -56,18 +56,20 @@ __device__ __forceinline__ void peer_signal(PeerI flags, int rank, int N, int ph
 }
 
 // Wait (one thread, iteration limit) until all N ranks reached `epoch` in `phase` (acquire).
-__device__ __forceinline__ void peer_wait(const int* mine, int N, int phase, int epoch) {
+// Returns false, after recording the timeout in the status word, when a rank never arrived.
+__device__ __forceinline__ bool peer_wait(const int* mine, int N, int phase, int epoch) {
   for (int q = 0; q < N; ++q) {
     const int* src = mine + phase * PEER_MAX + q;
     int it = 0;
     while (ld_acquire_sys(src) < epoch) {
       if (++it > (1 << 22)) {
         atomicOr(&g_status, STATUS_PEER_TIMEOUT);
-        return;
+        return false;
       }
       __nanosleep(64);
     }
   }
+  return true;
 }
 
 // Signal and/or wait as a kernel of its own (one thread does it).
@@ -83,10 +85,12 @@ __global__ void k_peer_sync(PeerI flags, int* mine, int rank, int N, int phase, 
 __global__ void __launch_bounds__(256) k_sgld_peer(float* __restrict__ params, int G, double lr_means, float noise_lr,
                                                     const float* __restrict__ eps_noise, const int* __restrict__ step_ptr,
                                                     unsigned long long seed, const int* mine, int N) {
-  if (threadIdx.x == 0) peer_wait(mine, N, 1, *step_ptr);
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = peer_wait(mine, N, 1, *step_ptr);
   __syncthreads();
   const int g = blockIdx.x * blockDim.x + threadIdx.x;
-  if (g >= G) return;
+  // a block whose wait gave up adds no noise to parameters whose update may still be arriving
+  if (!s_ok || g >= G) return;
   sgld_one(params, ParamLayout{G}, g, lr_means, noise_lr, eps_noise, *step_ptr, seed);
 }
 
@@ -113,10 +117,12 @@ __global__ void __launch_bounds__(256)
                 const double* __restrict__ lr7, double beta1, double beta2, double eps, PeerCF loss,
                 float* __restrict__ loss_total, PeerI flags, const float* own, int* mine) {
   __shared__ PeerAdamScalars s_a;
+  __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const int step = *step_ptr;
-    // phase 0: every rank's gradient and loss are written
-    peer_wait(mine, N, 0, step);
+    // phase 0: every rank's gradient and loss are written; a block whose wait gave up skips its
+    // part of the update (the status word reports it) rather than sum partial gradients
+    s_ok = peer_wait(mine, N, 0, step);
     const double bc1 = 1.0 - pow(beta1, (double)step);
     const double bc2 = 1.0 - pow(beta2, (double)step);
     s_a.w1 = (float)(1.0 - beta1);
@@ -145,7 +151,7 @@ __global__ void __launch_bounds__(256)
     for (int q = 0; q < PEER_MAX; ++q)
       if (q < N) params.p[q][e] = pn;
   };
-  if (tid == 0) {
+  if (tid == 0 && s_ok) {
     float s = 0.f;
 #pragma unroll
     for (int q = 0; q < PEER_MAX; ++q)
@@ -155,7 +161,7 @@ __global__ void __launch_bounds__(256)
     // the last 1-3 elements of the vector when its length is not a multiple of 4
     for (long long e = hi / 4 * 4; e < hi; ++e) scalar_update(e, lr_seg(e, G, a.nss));
   }
-  for (long long i = lo / 4 + tid; i < hi / 4; i += stride) {
+  for (long long i = lo / 4 + tid; s_ok && i < hi / 4; i += stride) {
     float4 g4 = reinterpret_cast<const float4*>(grads.p[0])[i];
 #pragma unroll
     for (int q = 1; q < PEER_MAX; ++q) {

@@ -84,6 +84,7 @@ def train_mcmc(model, cameras, gt_images, arm="A", iters=600, lr=None, relocate_
         hist.append(st.mean_loss_value() if log_every else st.loss_mean.clone())
         if log_every and (it % log_every == 0 or it == iters - 1):
             print(f"    iter {it:4d}  loss {hist[-1]:.5f}  relocations {int(st.n_moved.item())}")
+    st.check_status()
     if hist and torch.is_tensor(hist[0]):
         hist = (torch.cat(hist) / st.V).cpu().tolist()
     return hist, int(st.n_moved.item())

@@ -21,12 +21,38 @@ import numpy as np
 import torch
 
 from . import ops
-from ._lib import require_cuda
+from ._lib import device_ctx, require_cuda
 from .camera import as_camera, pack_cameras
 from .model import GaussianModel, flat_of, lr_vector, view
 
 DEFAULT_LR = {"means": 5e-3, "scales": 5e-3, "quats": 1e-3, "opacity": 5e-2, "opacity_sh": 5e-2, "color": 1e-2,
               "wb": 1e-2, "depth": 1e-2}   # spike/train.py:9-12
+
+
+# Bits of the device status word (tts_read_status): the bounded waits and the table check that
+# gave up.  A step that set one of them did not do all of its work.
+STATUS_BITS = {
+    1: "a bulk-copy wait of the per-tile forward timed out (that tile's pixels were not written)",
+    2: "a grid barrier of the relocation kernel timed out (the relocation was abandoned)",
+    4: "a peer-exchange wait timed out (a rank's gradient or update never arrived; the waiting "
+       "blocks skipped their part of the update)",
+    8: "a cached binning table spreads a gaussian over more tiles than its stencil box",
+}
+
+
+def status_message(status):
+    """Human-readable description of the bits set in a device status word."""
+    parts = [f"{b}: {msg}" for b, msg in STATUS_BITS.items() if status & b]
+    unknown = status & ~sum(STATUS_BITS)
+    if unknown:
+        parts.append(f"unknown bits {unknown:#x}")
+    return "; ".join(parts)
+
+
+def raise_on_status(status, where="training"):
+    """Raise RuntimeError naming every bit of a non-zero device status word."""
+    if status:
+        raise RuntimeError(f"device status {status:#x} during {where}: {status_message(status)}")
 
 
 def partition_views(n_views, world, rank):
@@ -310,8 +336,16 @@ class TrainStep:
             total += self.lambda_o * float(o.mean()) + self.lambda_s * float(s.mean())
         return total
 
+    def check_status(self):
+        """Read and clear the device status word (synchronises); raise RuntimeError naming the
+        bits when a bounded wait gave up since the last check, i.e. when a step skipped work."""
+        with device_ctx(self.dev):
+            raise_on_status(ops.read_status(), f"the steps up to iteration {self.it}")
+
     def check_replicas(self):
-        """Raise if the ranks' parameter replicas have diverged (a no-op without a process group)."""
+        """Raise if a bounded wait gave up (``check_status``) or the ranks' parameter replicas
+        have diverged (the replica check is a no-op without a process group)."""
+        self.check_status()
         if self.pg is None:
             return
         if not replicas_agree(self.flat, self.pg):
@@ -340,6 +374,7 @@ def fit(model, cameras, gt_images, arm="A", iters=800, lambda_ssim=0.2, lr=None,
         hist.append(st.step().clone())
         if log_every and (it % log_every == 0 or it == iters - 1):
             print(f"    iter {it:4d}  loss {float(hist[-1]) / st.V:.5f}")
+    st.check_status()
     return (torch.stack(hist) / st.V).cpu().tolist() if hist else []
 
 
