@@ -94,13 +94,23 @@ class CpuStep:
                 else:
                     os.environ[k] = v
 
-    def step(self):
-        """Run one step; returns (photometric loss, updated parameter copy)."""
+    def loss_and_grads(self, lambda_o=0.01, lambda_s=0.01):
+        """Mean photometric loss over the views and the summed per-view gradients (view order),
+        plus the MCMC regulariser's gradient (spike/mcmc.py:102, reg_loss :18-22)."""
         res = sorted(self.pool.map(_view, range(self.n_views)), key=lambda r: r[0])
         g = {k: np.array(res[0][2][k], copy=True) if k != "w_b_raw" else res[0][2][k] for k in res[0][2]}
         for _, _, gv in res[1:]:
             for k in g:
                 g[k] = g[k] + gv[k]
+        if lambda_o or lambda_s:
+            gop, gls = optim.reg_loss_grads(self.p["opacity_raw"], self.p["log_scales"], lambda_o, lambda_s)
+            g["opacity_raw"] = g["opacity_raw"] + gop
+            g["log_scales"] = g["log_scales"] + gls
+        return sum(r[1] for r in res) / self.n_views, g
+
+    def step(self):
+        """Run one step; returns (photometric loss, updated parameter copy)."""
+        loss, g = self.loss_and_grads()
         q = pipeline.copy_params(self.p)
         pipeline.adam_step(q, g, {}, 1, LR, self.sh_degree)
         G = self.p["means3d"].shape[0]
@@ -112,7 +122,7 @@ class CpuStep:
         alive = np.nonzero(o >= thr)[0]
         tgts = alive[self.rng.choice(alive.size, n_dead, p=o[alive] / o[alive].sum())]
         optim.relocate(q, thr, tgts)
-        return sum(r[1] for r in res) / self.n_views, q
+        return loss, q
 
     def close(self):
         try:

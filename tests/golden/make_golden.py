@@ -369,6 +369,28 @@ def gen_geom(R, syn, out):
                         gquats=quat.grad.numpy(), glog_scales=logs.grad.numpy(), **cam_arrays(cam))
 
 
+def gen_near_plane(R, syn, out):
+    """Thin gaussians just past the near plane whose means project far off-screen: the reference's
+    fp32 project_ewa (spike/geometry.py:28-57) evaluates det = s00 s11 - s01^2 of a nearly rank-one
+    Sigma2d as rounding noise and clamps it to 1e-12 for some of them (conics of ~1e20), although
+    det(J Sigma J^T + blur I) >= blur^2 exactly.  Seeded needles on the config-2 view-1 camera;
+    kept: every needle whose reference conic exceeds 1e6 (up to 32) and 32 ordinary ones."""
+    cam = syn.config2(G=16, n_views=2)["cams"][1]
+    rng = np.random.default_rng(7)
+    n = 400000
+    d = rng.uniform(0.2, 0.3, n)
+    mc = np.stack([rng.uniform(-12, 12, n) * d, rng.uniform(-12, 12, n) * d, d], 1)
+    means = ((mc - cam["t_v"].astype(np.float64)) @ cam["R_v"].astype(np.float64)).astype(np.float32)
+    ls = np.stack([rng.normal(-8.5, 0.3, n), rng.normal(-8.5, 0.3, n), rng.normal(-1.9, 0.3, n)], 1).astype(np.float32)
+    q = rng.standard_normal((n, 4)).astype(np.float32)
+    mu, conic, depth, keep = project(R, dict(means3d=means, log_scales=ls, quats=q), cam)
+    big = conic.abs().max(1).values.numpy() > 1e6
+    sel = np.concatenate([np.nonzero(big)[0][:32], np.nonzero(~big)[0][:32]])
+    np.savez_compressed(os.path.join(out, "geom_near_plane.npz"), means3d=means[sel], log_scales=ls[sel], quats=q[sel],
+                        ref_mu2d=mu.numpy()[sel], ref_conic=conic.numpy()[sel], ref_depth=depth.numpy()[sel],
+                        ref_keep=keep.numpy()[sel], ref_clamped=big[sel], **cam_arrays(cam))
+
+
 def gen_loss(R, out):
     lm = R.loss_manual
     arrays = {}
@@ -466,7 +488,8 @@ def main():
                 bins_big=lambda: gen_bins_big(R, syn, HERE), render=lambda: gen_render(R, syn, HERE),
                 geom=lambda: gen_geom(R, syn, HERE), loss=lambda: gen_loss(R, HERE),
                 optim=lambda: gen_optim(R, syn, HERE), arm_b=lambda: gen_arm_b(R, syn, HERE),
-                arm_rv=lambda: gen_arm_rv(R, syn, HERE), sh12=lambda: gen_sh12(R, syn, HERE))
+                arm_rv=lambda: gen_arm_rv(R, syn, HERE), sh12=lambda: gen_sh12(R, syn, HERE),
+                near_plane=lambda: gen_near_plane(R, syn, HERE))
     for name, fn in jobs.items():
         if args.only and name not in args.only.split(","):
             continue

@@ -138,6 +138,35 @@ def test_arm_rv_vs_reference_and_oracle(deg, pkg):
         render.render(m, camera.Camera.from_dict(cam), "RV", sh_degree=deg, K=K, bf16=True)
 
 
+def test_near_plane_needles_stay_finite_and_match_float64(pkg):
+    """The near-plane needles of geom_near_plane.npz (the reference's fp32 conic clamps to ~1e20
+    for half of them): the fused projection's conics are within 1e-3 of the float64 oracle, and a
+    1264x832 render of a scene containing them is finite and matches the oracle's binned render."""
+    from tt_splat_b200 import camera, ops, render
+    from tt_splat_b200.model import pack_arrays
+    from oracle import geometry as ogeom
+    z = golden("geom_near_plane.npz")
+    cam = cam_from(z)
+    n = z["means3d"].shape[0]
+    needles = dict(means3d=z["means3d"], log_scales=z["log_scales"], quats=z["quats"],
+                   opacity_raw=np.zeros(n, np.float32), color_dc=np.zeros((n, 3), np.float32),
+                   color_rest=np.zeros((n, 15, 3), np.float32))
+    scene = pkg.synthetic.config2(seed=21, G=3000, n_views=1)["params"]
+    p = {k: np.concatenate([scene[k], needles[k]]) for k in needles}
+    p["w_b_raw"] = scene["w_b_raw"]
+    G = p["means3d"].shape[0]
+    flat = pack_arrays(p).to(DEV)
+    cams_t = camera.pack_cameras([camera.Camera.from_dict(cam)], DEV)
+    pj = ops.project(flat, G, 3, cams_t, cam["H"], cam["W"])
+    dev_conic = pj["proj"][0, G - n:, 2:5].cpu().numpy()
+    conic64, _, _, _, _ = ogeom.fwd(z["means3d"], z["quats"], z["log_scales"], cam)
+    assert np.abs(dev_conic - conic64).max() / np.abs(conic64).max() < 1e-3
+    img = render.render(_model(pkg, p), camera.Camera.from_dict(cam), "A", sh_degree=3).detach().cpu().numpy()
+    assert np.isfinite(img).all()
+    ref = pipeline.render_view(p, 3, cam)["img"]
+    assert np.abs(img - ref).max() < 1e-3
+
+
 @pytest.mark.parametrize("deg", [1, 2])
 def test_sh_degree_1_2_vs_reference(deg, pkg):
     """The device path at SH degrees 1 and 2: image and gradients against the reference."""

@@ -246,6 +246,27 @@ def test_geometry_bwd_vs_reference():
     assert rel_l2(conic_d, conic) < 1e-12 and rel_l2(mu_d, mu2d) < 1e-12
 
 
+def test_near_plane_needles_reference_fp32_clamps_where_float64_is_bounded():
+    """Thin gaussians just past the near plane, projecting far off-screen (fixture written by the
+    reference's fp32 project_ewa, spike/geometry.py:28-57): for half of them the reference's
+    det = s00 s11 - s01^2 cancels to noise and its 1e-12 clamp yields conics of ~1e20, while in
+    float64 every conic is positive definite and bounded by 1/blur (det(J S J^T + blur I) >=
+    blur^2).  The oracle keeps the float64 values, which the device's fused projection matches
+    (tests/test_gpu_render.py)."""
+    z = golden("geom_near_plane.npz")
+    cam = cam_from(z)
+    conic, mu2d, depth, keep, _ = geometry.fwd(z["means3d"], z["quats"], z["log_scales"], cam)
+    clamped = z["ref_clamped"]
+    assert clamped.sum() >= 16 and (~clamped).sum() >= 16
+    assert np.abs(z["ref_conic"][clamped]).max(1).min() > 1e6
+    assert keep.all() and z["ref_keep"].all()
+    assert np.abs(conic).max() <= 1.0 / 0.3 + 1e-9
+    assert (conic[:, 0] > 0).all() and (conic[:, 0] * conic[:, 2] - conic[:, 1] ** 2 > 0).all()
+    # the means are well conditioned in fp32; the conics of these needles are not (even where the
+    # reference's clamp did not fire, its fp32 conic is off by up to order one)
+    assert np.abs(z["ref_mu2d"] - mu2d).max() / np.abs(mu2d).max() < 1e-5
+
+
 def test_geometry_analytic_isotropic():
     """spike/tests/test_geometry_analytic.py:12-35."""
     cam = dict(R_v=np.eye(3), t_v=np.array([0.0, 0.0, 4.0]), fx=178.0, fy=178.0, cx=64.0, cy=64.0)

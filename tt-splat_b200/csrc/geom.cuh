@@ -68,10 +68,29 @@ __device__ __forceinline__ void geom_forward(const float m[3], const float q[4],
   f.J11 = cam.fy * f.zi;
   f.J02 = -cam.fx * f.mcx * f.zi * f.zi;
   f.J12 = -cam.fy * f.mcy * f.zi * f.zi;
-  f.s00 = f.J00 * f.J00 * f.SC00 + 2.f * f.J00 * f.J02 * f.SC02 + f.J02 * f.J02 * f.SC22 + blur;
-  f.s11 = f.J11 * f.J11 * f.SC11 + 2.f * f.J11 * f.J12 * f.SC12 + f.J12 * f.J12 * f.SC22 + blur;
-  f.s01 = f.J00 * f.J11 * f.SC01 + f.J00 * f.J12 * f.SC02 + f.J02 * f.J11 * f.SC12 + f.J02 * f.J12 * f.SC22;
-  const float det = f.s00 * f.s11 - f.s01 * f.s01;
+  // Sigma2d = A A^T + blur I with A = J (R_v R) diag(s) (2x3).  Its entries are sums of squares
+  // and products of A, and its determinant is taken in the Cauchy-Binet form
+  //   det = sum of the squared 2x2 minors of A + blur (tr A A^T) + blur^2,
+  // every term non-negative, so det >= blur^2 as in exact arithmetic.  The textbook
+  // s00 s11 - s01^2 (spike/geometry.py:54) cancels to fp32 rounding noise for thin gaussians just
+  // past the near plane (mean far off-screen, Sigma2d nearly rank one), where the 1e-12 clamp then
+  // yields conics of ~1e20 whose tile-local polynomial overflows the render; the float64 value of
+  // those conics is bounded by 1/blur, and this form stays within fp32 rounding of it.
+  float A0[3], A1[3];
+#pragma unroll
+  for (int k = 0; k < 3; k++) {
+    A0[k] = (f.J00 * f.M[0][k] + f.J02 * f.M[2][k]) * f.s[k];
+    A1[k] = (f.J11 * f.M[1][k] + f.J12 * f.M[2][k]) * f.s[k];
+  }
+  const float p00 = A0[0] * A0[0] + A0[1] * A0[1] + A0[2] * A0[2];
+  const float p11 = A1[0] * A1[0] + A1[1] * A1[1] + A1[2] * A1[2];
+  f.s00 = p00 + blur;
+  f.s11 = p11 + blur;
+  f.s01 = A0[0] * A1[0] + A0[1] * A1[1] + A0[2] * A1[2];
+  const float m01 = A0[0] * A1[1] - A0[1] * A1[0];
+  const float m02 = A0[0] * A1[2] - A0[2] * A1[0];
+  const float m12 = A0[1] * A1[2] - A0[2] * A1[1];
+  const float det = (m01 * m01 + m02 * m02 + m12 * m12) + blur * (p00 + p11) + blur * blur;
   f.dmask = det > 1e-12f ? 1.f : 0.f;
   const float detc = fmaxf(det, 1e-12f);
   f.deti = 1.f / detc;
