@@ -249,6 +249,78 @@ int tts_peer_sgld(float* params, int G, double lr_means, float noise_lr, const f
                   const int32_t* step, uint64_t seed, int32_t* const* flags, int rank, int N,
                   void* stream);
 
+/* ---- the composable spike API: building blocks, forward and backward -------------------------
+ * The reference's differentiable functions of spike/geometry.py, spike/sh.py and
+ * spike/forward.py as standalone kernels, for callers that compose them by hand (the hot path
+ * fuses them into tts_project / tts_backward_params).  dtype 0 = float32, 1 = float64 for every
+ * floating pointer of a call; n counts the leading (batch) elements.  Each *_bwd returns the
+ * gradients of the differentiable inputs for the given output gradients (NULL = zero where
+ * allowed).  Camera poses, intrinsics and pixel grids are constants (never differentiated).
+ * Reductions over pixels write per-chunk partials into a caller workspace of
+ * tts_spike_workspace_bytes(P, G, dtype) bytes and sum them in a fixed order. */
+size_t tts_spike_workspace_bytes(long long P, long long G, int dtype);
+/* quat_to_rotmat, spike/geometry.py:10-19: q[n,4] (w,x,y,z; normalised with the norm clamped at
+ * 1e-12) -> R[n,3,3]. */
+int tts_quat_to_rotmat(const void* q, long long n, void* R, int dtype, void* stream);
+int tts_quat_to_rotmat_bwd(const void* q, const void* gR, long long n, void* gq, int dtype, void* stream);
+/* cov3d, spike/geometry.py:22-25: scales[n,3] (already exponentiated), R[n,3,3] ->
+ * R diag(s^2) R^T [n,3,3]. */
+int tts_cov3d(const void* scales, const void* R, long long n, void* cov, int dtype, void* stream);
+int tts_cov3d_bwd(const void* scales, const void* R, const void* gcov, long long n, void* gscales,
+                  void* gR, int dtype, void* stream);
+/* project_ewa, spike/geometry.py:28-57: means[G,3], cov[G,3,3] (any 3x3), cam16 = host
+ * double[16] {R_v row-major, t_v, fx, fy, cx, cy} -> mu2d[G,2], conic[G,3] (a, b, c of the
+ * inverse of J R_v cov R_v^T J^T + blur I, det clamped at 1e-12 as the reference does),
+ * depth[G] (camera z), keep[G] (uint8, z > near).  Backward: grads of means and cov. */
+int tts_project_ewa(const void* means, const void* cov, long long G, const double* cam16, double blur,
+                    double near_plane, void* mu2d, void* conic, void* depth, uint8_t* keep, int dtype,
+                    void* stream);
+int tts_project_ewa_bwd(const void* means, const void* cov, long long G, const double* cam16,
+                        double blur, double near_plane, const void* gmu2d, const void* gconic,
+                        const void* gdepth, void* gmeans, void* gcov, int dtype, void* stream);
+/* eval_sh_color, spike/sh.py:49-72: coeffs[G,nc,nch] (nc >= (deg+1)^2), dirs[G,3] (normalised
+ * with the norm clamped at 1e-12) -> out[G,nch] = clamp(0.5 + sum_k basis_k coeffs_k, min 0), or
+ * the bare sum when raw != 0.  Backward: grads of coeffs (zero beyond (deg+1)^2) and dirs. */
+int tts_eval_sh(int deg, const void* coeffs, int nc, int nch, const void* dirs, long long G, int raw,
+                void* out, int dtype, void* stream);
+int tts_eval_sh_bwd(int deg, const void* coeffs, int nc, int nch, const void* dirs, long long G,
+                    int raw, const void* gout, void* gcoeffs, void* gdirs, int dtype, void* stream);
+/* color_from_dc, spike/forward.py:69-71: clamp(0.5 + C0 dc, min 0); with gout != NULL writes
+ * the gradient d/d dc instead. */
+int tts_color_from_dc(const void* dc, long long n, const void* gout, void* out, int dtype, void* stream);
+/* phi, spike/forward.py:42-44: px[P], py[P] -> Phi[P,6] = [px^2, py^2, px py, px, py, 1]. */
+int tts_phi(const void* px, const void* py, long long P, void* Phi, int dtype, void* stream);
+int tts_phi_bwd(const void* px, const void* py, const void* gPhi, long long P, void* gpx, void* gpy,
+                int dtype, void* stream);
+/* theta_from_conic, spike/forward.py:23-39: conic[n,3], mu[n,2] (minus origins[i/per][2] when
+ * origins != NULL) -> theta_Q[n,6] and/or theta_u[n,6] = -theta_Q/k + e5 (layout 0), or theta_u
+ * as [n/per,6,per] in the op order of theta_u_gathered, tools/m4_train_binned.py:130-143
+ * (layout 1).  Backward (layout-0 gradients): grads of conic and mu. */
+int tts_theta_from_conic(const void* conic, const void* mu, const void* origins, long long per,
+                         long long n, double k, int layout, void* theta_Q, void* theta_u, int dtype,
+                         void* stream);
+int tts_theta_from_conic_bwd(const void* conic, const void* mu, const void* origins, long long per,
+                             long long n, double k, const void* gtheta_Q, const void* gtheta_u,
+                             void* gconic, void* gmu, int dtype, void* stream);
+/* quad_form, spike/forward.py:13-20: Q[P,G] = a dx^2 + 2 b dx dy + c dy^2, (dx, dy) = pixel -
+ * mean.  Backward: grads of mu2d and conic (pixel sums through the workspace). */
+int tts_quad_form(const void* px, const void* py, const void* mu2d, const void* conic, long long P,
+                  long long G, void* Q, int dtype, void* stream);
+int tts_quad_form_bwd(const void* px, const void* py, const void* mu2d, const void* conic,
+                      const void* gQ, long long P, long long G, void* gmu2d, void* gconic,
+                      void* workspace, size_t workspace_bytes, int dtype, void* stream);
+/* Q = Phi theta^T ([P,6] x [G,6]^T), the GEMM of quad_form_tilelocal, spike/forward.py:47-58.
+ * Backward: gPhi and/or gtheta (either may be NULL; gtheta uses the workspace). */
+int tts_phi_theta(const void* Phi, const void* theta, long long P, long long G, void* Q, int dtype,
+                  void* stream);
+int tts_phi_theta_bwd(const void* Phi, const void* theta, const void* gQ, long long P, long long G,
+                      void* gPhi, void* gtheta, void* workspace, size_t workspace_bytes, int dtype,
+                      void* stream);
+/* poly_splat_wgeo, spike/forward.py:61-66: w[P,G] = max(0, 1 - Q/k)^2 * keep[g] (keep uint8 or
+ * NULL); with gout != NULL writes dL/dQ instead. */
+int tts_poly_splat_wgeo(const void* Q, long long P, long long G, double k, const uint8_t* keep,
+                        const void* gout, void* out, int dtype, void* stream);
+
 /* ---- dense WSR (spike/backward.py:61-63, wsr_polysplat) -----------------------------------
  * C[P,3] from theta_u[G,6], o[G], color[G,3], w_b (device scalar), Phi[P,6], c_b[3], keep[G]
  * (fp32 0/1, may be NULL), and its backward. */

@@ -127,3 +127,46 @@ def test_status_word_raises_naming_its_bits(pkg, monkeypatch):
     with pytest.raises(RuntimeError, match="iteration 7.*peer-exchange"):
         st.check_replicas()
     st.check_replicas()                          # the read cleared the word: no error
+
+
+def test_spike_api_refuses_cpu_tensors(pkg):
+    """The reference-named functions run kernels only: CPU tensors raise (no CPU fallback)."""
+    from tt_splat_b200 import binned, forward, geometry, sh
+    z3, z4, z33 = torch.zeros(4, 3), torch.zeros(4, 4), torch.zeros(4, 3, 3)
+    calls = [lambda: geometry.quat_to_rotmat(z4), lambda: geometry.cov3d(z3, z33),
+             lambda: geometry.project_ewa(z3, z33, torch.eye(3), torch.zeros(3), 1.0, 1.0, 0.0, 0.0),
+             lambda: sh.eval_sh_color(3, torch.zeros(4, 16, 3), z3),
+             lambda: forward.quad_form(torch.zeros(5), torch.zeros(5), torch.zeros(4, 2), z3),
+             lambda: forward.theta_from_conic(z3, torch.zeros(4, 2), 4.0),
+             lambda: forward.phi(torch.zeros(5), torch.zeros(5)),
+             lambda: forward.quad_form_tilelocal(torch.zeros(5), torch.zeros(5), z3, torch.zeros(4, 2), torch.zeros(2)),
+             lambda: forward.poly_splat_wgeo(torch.zeros(5, 4), 4.0),
+             lambda: forward.color_from_dc(z3),
+             lambda: binned.theta_u_gathered(torch.zeros(2, 4, 3), torch.zeros(2, 4, 2), torch.zeros(2, 2), 4.0)]
+    for fn in calls:
+        with pytest.raises(RuntimeError, match="CUDA"):
+            fn()
+
+
+def test_camera_conventions(pkg):
+    """look_at_opencv, pixel_grid and project_point follow spike/camera.py's conventions: the
+    target projects to the principal point, rows are right/down/forward, pixel centres are +0.5
+    in row-major order (the OpenGL -> OpenCV pose conversion is pinned bit for bit by the Blender
+    loader test against the reference's outputs)."""
+    import numpy as np
+    from tt_splat_b200 import camera, synthetic
+    eye = (1.0, 2.0, -3.5)
+    R, t = camera.look_at_opencv(eye, (0.2, -0.1, 0.3))
+    Rn, tn = synthetic.look_at_opencv(eye, (0.2, -0.1, 0.3))
+    assert np.abs(R.numpy() - Rn).max() < 1e-6 and np.abs(t.numpy() - tn).max() < 1e-6
+    assert torch.allclose(R @ R.T, torch.eye(3), atol=1e-6) and abs(float(torch.det(R)) - 1) < 1e-6
+    uv, z = camera.project_point(torch.tensor([0.2, -0.1, 0.3]), R, t, 100.0, 90.0, 32.0, 24.0)
+    assert torch.allclose(uv, torch.tensor([32.0, 24.0]), atol=1e-4) and float(z) > 0
+    uv, _ = camera.project_point(torch.tensor([0.2, -0.1, 0.3]) + R[1], R, t, 100.0, 90.0, 32.0, 24.0)
+    assert float(uv[1]) > 24.0                          # +y of the camera is down the image
+    px, py = camera.pixel_grid(2, 3)
+    assert px.tolist() == [0.5, 1.5, 2.5, 0.5, 1.5, 2.5] and py.tolist() == [0.5, 0.5, 0.5, 1.5, 1.5, 1.5]
+    c2w = torch.eye(4)
+    c2w[:3, 3] = torch.tensor([0.0, 0.0, 4.0])           # OpenGL camera at +4z looking down -z
+    Rv, tv = camera.opengl_c2w_to_opencv_w2c(c2w)
+    assert torch.equal(Rv, torch.diag(torch.tensor([1.0, -1.0, -1.0]))) and torch.equal(tv, torch.tensor([0.0, 0.0, 4.0]))

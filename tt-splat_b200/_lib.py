@@ -19,6 +19,7 @@ F = C.c_float
 D = C.c_double
 SZ = C.c_size_t
 U64 = C.c_uint64
+LL = C.c_longlong
 
 SIGNATURES = {
     "tts_version": (I, []),
@@ -58,6 +59,25 @@ SIGNATURES = {
     "tts_peer_wait": (I, [P, I, I, I, P, P]),
     "tts_adam_peer": (I, [P, P, P, P, I, I, I, I, P, P, D, D, D, P, P, P, P]),
     "tts_peer_sgld": (I, [P, I, D, F, P, P, U64, P, I, I, P]),
+    "tts_spike_workspace_bytes": (SZ, [LL, LL, I]),
+    "tts_quat_to_rotmat": (I, [P, LL, P, I, P]),
+    "tts_quat_to_rotmat_bwd": (I, [P, P, LL, P, I, P]),
+    "tts_cov3d": (I, [P, P, LL, P, I, P]),
+    "tts_cov3d_bwd": (I, [P, P, P, LL, P, P, I, P]),
+    "tts_project_ewa": (I, [P, P, LL, P, D, D, P, P, P, P, I, P]),
+    "tts_project_ewa_bwd": (I, [P, P, LL, P, D, D, P, P, P, P, P, I, P]),
+    "tts_eval_sh": (I, [I, P, I, I, P, LL, I, P, I, P]),
+    "tts_eval_sh_bwd": (I, [I, P, I, I, P, LL, I, P, P, P, I, P]),
+    "tts_color_from_dc": (I, [P, LL, P, P, I, P]),
+    "tts_phi": (I, [P, P, LL, P, I, P]),
+    "tts_phi_bwd": (I, [P, P, P, LL, P, P, I, P]),
+    "tts_theta_from_conic": (I, [P, P, P, LL, LL, D, I, P, P, I, P]),
+    "tts_theta_from_conic_bwd": (I, [P, P, P, LL, LL, D, P, P, P, P, I, P]),
+    "tts_quad_form": (I, [P, P, P, P, LL, LL, P, I, P]),
+    "tts_quad_form_bwd": (I, [P, P, P, P, P, LL, LL, P, P, P, SZ, I, P]),
+    "tts_phi_theta": (I, [P, P, LL, LL, P, I, P]),
+    "tts_phi_theta_bwd": (I, [P, P, P, LL, LL, P, P, P, SZ, I, P]),
+    "tts_poly_splat_wgeo": (I, [P, LL, LL, D, P, P, P, I, P]),
     "tts_wsr_dense_fwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P]),
     "tts_wsr_dense_bwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P, P, P, P, P, P]),
 }

@@ -10,18 +10,6 @@ from ._lib import on_device
 from . import ops
 
 
-def wsr_polysplat_ref(theta_u, o, color, w_b, Phi, c_b, keep=None):
-    """spike/backward.py:11-20 written with torch ops (autograd reference, any device)."""
-    u = Phi @ theta_u.t()
-    w_geo = u.clamp(min=0.0) ** 2
-    if keep is not None:
-        w_geo = w_geo * keep[None, :]
-    w = o[None, :] * w_geo
-    num = w @ color + w_b * c_b[None, :]
-    den = w.sum(1, keepdim=True) + w_b
-    return num / den
-
-
 class WSRPolySplatHot(torch.autograd.Function):
     """Manual forward + backward on the CUDA kernels (spike/backward.py:23-58)."""
 

@@ -1,7 +1,7 @@
 """The binned render operator pair of tools/m4_train_binned.py on the B200 kernels.
 
 - ``TileMap`` (:60-72), ``assign_bins`` (:75-127, canonical stable order, bit-exact),
-  ``theta_u_gathered`` (:130-143, torch expression);
+  ``theta_u_gathered`` (:130-143, the theta kernel in that function's op order, differentiable);
 - ``_operands(model, cam, tmap, R, K)`` (:189-212): geometry, activations, binning and the
   per-tile operand gather, differentiable in the model parameters;
 - ``_DevRenderBinned.apply(theta_u, color_o, o_col, w_b, Phi, gidx, c_b, H, W)`` (:154-186):
@@ -10,7 +10,7 @@
 import torch
 
 from ._lib import on_device
-from . import forward, ops
+from . import ops
 from .camera import as_camera, pack_cameras
 from .model import flat_of
 
@@ -25,7 +25,10 @@ class TileMap:
         self.H, self.W, self.nty, self.ntx = H, W, H // 16, W // 16
         self.T = self.nty * self.ntx
         p = torch.arange(256)
-        self.Phi = forward.phi((p % 16).float() + 0.5, (p // 16).float() + 0.5).to(device)
+        # the monomials [x^2, y^2, x y, x, y, 1] of the 256 tile-local pixel centres (a constant
+        # table of the tile map; the tile kernels generate the same values in registers)
+        lx, ly = (p % 16).float() + 0.5, (p // 16).float() + 0.5
+        self.Phi = torch.stack([lx * lx, ly * ly, lx * ly, lx, ly, torch.ones(256)], dim=1).to(device)
         t = torch.arange(self.T)
         ty, tx = t // self.ntx, t % self.ntx
         self.origins = torch.stack([(tx * 16).float(), (ty * 16).float()], dim=1).to(device)
@@ -50,15 +53,33 @@ def assign_bins(mu2d, keep, tmap, R, K):
     return torch.where(valid, idx, torch.zeros_like(idx)).long(), valid
 
 
+class _ThetaGathered(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, conic_t, mu_t, origins, k):
+        T, K = conic_t.shape[0], conic_t.shape[1]
+        c = conic_t.detach().contiguous().reshape(T * K, 3)
+        m = mu_t.detach().contiguous().reshape(T * K, 2)
+        o = origins.detach().to(c.dtype).contiguous()
+        _, th = ops.theta_from_conic(c, m, k, origins=o, per=K, gathered=True)
+        ctx.save_for_backward(c, m, o)
+        ctx.k, ctx.TK = k, (T, K)
+        return th
+
+    @staticmethod
+    def backward(ctx, g):
+        c, m, o = ctx.saved_tensors
+        T, K = ctx.TK
+        gU = g.transpose(1, 2).contiguous().reshape(T * K, 6)
+        gc, gm = ops.theta_from_conic_bwd(c, m, ctx.k, None, gU, origins=o, per=K)
+        return gc.reshape(T, K, 3), gm.reshape(T, K, 2), None, None
+
+
 def theta_u_gathered(conic_t, mu_t, origins, k):
-    """tools/m4_train_binned.py:130-143 (torch expression, reference op order)."""
-    mu = mu_t - origins[:, None, :]
-    a, b, c = conic_t[..., 0], conic_t[..., 1], conic_t[..., 2]
-    mux, muy = mu[..., 0], mu[..., 1]
-    ik = 1.0 / k
-    Q = a * mux * mux + 2.0 * b * mux * muy + c * muy * muy
-    return torch.stack([-a * ik, -c * ik, -2.0 * b * ik, 2.0 * (a * mux + b * muy) * ik,
-                        2.0 * (b * mux + c * muy) * ik, 1.0 - Q * ik], dim=-1).transpose(1, 2).contiguous()
+    """tools/m4_train_binned.py:130-143: conic_t [T,K,3], mu_t [T,K,2] (global), origins [T,2]
+    -> theta_u [T,6,K] with each tile's origin folded into the means, on the device in the
+    reference function's op order; differentiable in conic_t and mu_t."""
+    with on_device(conic_t):
+        return _ThetaGathered.apply(conic_t, mu_t, origins, float(k))
 
 
 class _Operands(torch.autograd.Function):

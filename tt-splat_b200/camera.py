@@ -1,4 +1,4 @@
-"""OpenCV pinhole cameras (mirrors spike/camera.py:16-70) and their device packing.
+"""OpenCV pinhole cameras (the conventions of spike/camera.py) and their device packing.
 
 ``Camera`` keeps the reference's fields (world->camera ``R_v[3,3]``, ``t_v[3]`` as torch
 tensors, intrinsics, image size) so reference code that builds cameras works unchanged.
@@ -12,20 +12,22 @@ CAM_FLOATS = 20
 
 
 def opengl_c2w_to_opencv_w2c(c2w):
-    """spike/camera.py:16-24."""
+    """OpenGL camera-to-world pose (4x4; camera looks down -z, +y up) -> OpenCV world-to-camera
+    (R_v [3,3], t_v [3]; camera looks down +z, +y down).
+
+    A point's OpenCV camera coordinates are its OpenGL camera coordinates with y and z negated,
+    so R_v is the transpose of the pose's rotation with its last two rows negated, and
+    t_v = -R_v @ (camera position)."""
     c2w = torch.as_tensor(c2w)
-    R_c = c2w[:3, :3]
-    cam_pos = c2w[:3, 3]
-    flip = torch.diag(torch.tensor([1.0, -1.0, -1.0], dtype=c2w.dtype, device=c2w.device))
-    R_v = (R_c @ flip).transpose(-1, -2)
-    return R_v, -R_v @ cam_pos
+    R_v = c2w[:3, :3].transpose(0, 1).clone()
+    R_v[1:] = -R_v[1:]
+    return R_v, -(R_v @ c2w[:3, 3])
 
 
 def project_point(p_world, R_v, t_v, fx, fy, cx, cy):
-    """spike/camera.py:27-33."""
-    p_cam = R_v @ p_world + t_v
-    z = p_cam[2]
-    return torch.stack([fx * p_cam[0] / z + cx, fy * p_cam[1] / z + cy]), z
+    """Pinhole projection of one world point -> (pixel [2], depth z); z > 0 is in front."""
+    x, y, z = R_v @ p_world + t_v
+    return torch.stack([fx * x / z + cx, fy * y / z + cy]), z
 
 
 class Camera:
@@ -76,21 +78,23 @@ def pack_cameras(cams, device):
 
 
 def look_at_opencv(eye, target, up=(0.0, 1.0, 0.0), dtype=torch.float32, device=None):
-    """spike/camera.py:51-63."""
-    eye = torch.as_tensor(eye, dtype=dtype, device=device)
-    target = torch.as_tensor(target, dtype=dtype, device=device)
-    up = torch.as_tensor(up, dtype=dtype, device=device)
-    z = target - eye
-    z = z / z.norm()
-    x = torch.linalg.cross(up, z)
-    x = x / x.norm()
-    y = torch.linalg.cross(z, x)
-    R_v = torch.stack([x, y, z], dim=0)
+    """OpenCV world-to-camera pose (R_v, t_v) of a camera at ``eye`` looking at ``target``: the
+    rows of R_v are the camera's right, down and forward axes in world coordinates, with right
+    = up x forward (normalised) and down = forward x right."""
+    as_vec = lambda v: torch.as_tensor(v, dtype=dtype, device=device)  # noqa: E731
+    eye, target, up = as_vec(eye), as_vec(target), as_vec(up)
+    forward = target - eye
+    forward = forward / forward.norm()
+    right = torch.linalg.cross(up, forward)
+    right = right / right.norm()
+    down = torch.linalg.cross(forward, right)
+    R_v = torch.stack([right, down, forward])
     return R_v, -R_v @ eye
 
 
 def pixel_grid(H, W, dtype=torch.float32, device="cpu"):
-    """spike/camera.py:66-70: row-major pixel centres."""
-    ii, jj = torch.meshgrid(torch.arange(H, dtype=dtype, device=device),
-                            torch.arange(W, dtype=dtype, device=device), indexing="ij")
-    return (jj + 0.5).reshape(-1), (ii + 0.5).reshape(-1)
+    """Pixel centres of an H x W image in row-major order: px [H*W] = column + 0.5,
+    py [H*W] = row + 0.5."""
+    cols = torch.arange(W, dtype=dtype, device=device) + 0.5
+    rows = torch.arange(H, dtype=dtype, device=device) + 0.5
+    return cols.repeat(H), rows.repeat_interleave(W)

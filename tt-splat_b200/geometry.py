@@ -1,47 +1,101 @@
-"""Gaussian geometry (mirrors spike/geometry.py:10-57).
+"""Gaussian geometry on the device: the differentiable functions of spike/geometry.py:10-57.
 
-``project(model, cams)`` is the B200 path: the fused projection kernel (geometry + SH colour +
-activations) for a batch of views.  ``quat_to_rotmat``, ``cov3d`` and ``project_ewa`` keep the
-reference's tensor expressions for callers that compose them by hand.
+``quat_to_rotmat(quats)``, ``cov3d(scales, R)`` and ``project_ewa(means3d, cov3d_w, R_v, t_v,
+fx, fy, cx, cy, blur_eps, near)`` keep the reference's signatures, shapes and clamps (quaternion
+norm and 2-D determinant at 1e-12, depth at ``near``).  Each is a torch autograd Function whose
+forward and backward are kernels of ``libttsplat_b200.so`` (``tts_quat_to_rotmat``,
+``tts_cov3d``, ``tts_project_ewa`` and their ``_bwd``), in float32 or float64; CPU tensors raise
+(there is no CPU fallback).  The camera (R_v, t_v and the intrinsics) is a constant: it receives
+no gradient, as in every training path of the reference.
+
+``project(model, cams)`` is the fused path the renderer and the train step use: geometry, SH
+colour and activations of every gaussian in every view in one kernel.
 """
 import torch
 
 from . import ops
+from ._lib import on_device
 from .camera import as_camera, pack_cameras
 from .model import flat_of
 
 
+def _lead(x, tail, name):
+    if x.dim() < len(tail) or tuple(x.shape[x.dim() - len(tail):]) != tail:
+        raise ValueError(f"{name} must end in {tail}, got {tuple(x.shape)}")
+    return x.contiguous()
+
+
+class _QuatToRotmat(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, quats):
+        q = _lead(quats.detach(), (4,), "quats")
+        ctx.save_for_backward(q)
+        return ops.quat_to_rotmat(q)
+
+    @staticmethod
+    def backward(ctx, gR):
+        (q,) = ctx.saved_tensors
+        return ops.quat_to_rotmat_bwd(q, gR.contiguous())
+
+
+class _Cov3d(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, scales, R):
+        s = _lead(scales.detach(), (3,), "scales")
+        r = _lead(R.detach(), (3, 3), "R")
+        if s.shape[:-1] != r.shape[:-2]:
+            raise ValueError(f"scales {tuple(s.shape)} and R {tuple(r.shape)} must share their leading dims")
+        ctx.save_for_backward(s, r)
+        return ops.cov3d(s, r)
+
+    @staticmethod
+    def backward(ctx, gcov):
+        s, r = ctx.saved_tensors
+        return ops.cov3d_bwd(s, r, gcov.contiguous())
+
+
+class _ProjectEwa(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means3d, cov3d_w, cam16, blur, near):
+        m = _lead(means3d.detach(), (3,), "means3d")
+        c = _lead(cov3d_w.detach(), (3, 3), "cov3d_w")
+        if m.dim() != 2 or c.shape[0] != m.shape[0]:
+            raise ValueError("project_ewa takes means3d [G,3] and cov3d_w [G,3,3]")
+        mu2d, conic, depth, keep = ops.project_ewa(m, c, cam16, blur, near)
+        ctx.save_for_backward(m, c)
+        ctx.args = (cam16, blur, near)
+        ctx.mark_non_differentiable(keep)
+        return mu2d, conic, depth, keep
+
+    @staticmethod
+    def backward(ctx, gmu2d, gconic, gdepth, _gkeep):
+        m, c = ctx.saved_tensors
+        cam16, blur, near = ctx.args
+        f = lambda g: None if g is None else g.contiguous()  # noqa: E731
+        gm, gc = ops.project_ewa_bwd(m, c, cam16, blur, near, f(gmu2d), f(gconic), f(gdepth))
+        return gm, gc, None, None, None
+
+
 def quat_to_rotmat(quats):
-    """spike/geometry.py:10-19."""
-    q = quats / quats.norm(dim=-1, keepdim=True).clamp(min=1e-12)
-    w, x, y, z = q[..., 0], q[..., 1], q[..., 2], q[..., 3]
-    return torch.stack([1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y),
-                        2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x),
-                        2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)],
-                       dim=-1).reshape(*q.shape[:-1], 3, 3)
+    """quats [...,4] (w, x, y, z; normalised, norm clamped at 1e-12) -> R [...,3,3]
+    (spike/geometry.py:10-19)."""
+    with on_device(quats):
+        return _QuatToRotmat.apply(quats)
 
 
 def cov3d(scales, R):
-    """spike/geometry.py:22-25."""
-    s2 = scales * scales
-    return (R * s2[..., None, :]) @ R.transpose(-1, -2)
+    """R diag(scales^2) R^T for scales [...,3] (already exponentiated) and R [...,3,3]
+    (spike/geometry.py:22-25)."""
+    with on_device(scales):
+        return _Cov3d.apply(scales, R)
 
 
 def project_ewa(means3d, cov3d_w, R_v, t_v, fx, fy, cx, cy, blur_eps=0.3, near=0.2):
-    """spike/geometry.py:28-57."""
-    mu_cam = means3d @ R_v.transpose(-1, -2) + t_v
-    depth = mu_cam[:, 2]
-    keep = depth > near
-    z = depth.clamp(min=near)
-    mu2d = torch.stack([fx * mu_cam[:, 0] / z + cx, fy * mu_cam[:, 1] / z + cy], dim=-1)
-    Sigma_cam = torch.einsum('ij,gjk,lk->gil', R_v, cov3d_w, R_v)
-    zero = torch.zeros_like(z)
-    J = torch.stack([torch.stack([fx / z, zero, -fx * mu_cam[:, 0] / (z * z)], dim=-1),
-                     torch.stack([zero, fy / z, -fy * mu_cam[:, 1] / (z * z)], dim=-1)], dim=-2)
-    Sigma2d = torch.einsum('gij,gjk,glk->gil', J, Sigma_cam, J) + blur_eps * torch.eye(2, dtype=J.dtype, device=J.device)
-    s00, s01, s11 = Sigma2d[:, 0, 0], Sigma2d[:, 0, 1], Sigma2d[:, 1, 1]
-    det = (s00 * s11 - s01 * s01).clamp(min=1e-12)
-    return mu2d, torch.stack([s11 / det, -s01 / det, s00 / det], dim=-1), depth, keep
+    """EWA projection (spike/geometry.py:28-57) -> mu2d [G,2], conic_abc [G,3], depth [G],
+    keep [G] (bool).  Differentiable in means3d and cov3d_w."""
+    cam16 = ops._cam16(R_v, t_v, fx, fy, cx, cy)
+    with on_device(means3d):
+        return _ProjectEwa.apply(means3d, cov3d_w, cam16, float(blur_eps), float(near))
 
 
 @torch.no_grad()

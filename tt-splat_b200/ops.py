@@ -341,3 +341,190 @@ def peer_sgld(regions, flat, G, step, lr_means, noise_lr, eps_noise=None, seed=0
     call("tts_peer_sgld", ptr(flat), G, float(lr_means), float(noise_lr), ptr(eps_noise), ptr(step),
          int(seed) & (2 ** 64 - 1), regions.t_flags, regions.rank, regions.world, stream())
 
+
+
+# ---- the composable spike API (spike/geometry.py, spike/sh.py, spike/forward.py) --------------
+# fp32 or fp64 tensors on the current CUDA device; outputs allocated here with the inputs' dtype.
+_SPIKE_DTYPES = {torch.float32: 0, torch.float64: 1}
+
+
+def spike_dtype(*ts):
+    """dtype code (0 float32, 1 float64) shared by the given tensors; raises for CPU tensors,
+    other dtypes or mixed dtypes (the reference's functions compute in their inputs' dtype)."""
+    ts = [t for t in ts if t is not None]
+    _dev(*ts)
+    dt = ts[0].dtype
+    if dt not in _SPIKE_DTYPES or any(t.dtype != dt for t in ts):
+        raise TypeError(f"spike ops take float32 or float64 tensors of one dtype, got {[t.dtype for t in ts]}")
+    return _SPIKE_DTYPES[dt]
+
+
+def _cam16(R_v, t_v, fx, fy, cx, cy):
+    """Host double[16] camera record: R_v (row-major), t_v, fx, fy, cx, cy (constants)."""
+    import ctypes
+    vals = [float(x) for x in torch.as_tensor(R_v).detach().reshape(-1).cpu().tolist()]
+    vals += [float(x) for x in torch.as_tensor(t_v).detach().reshape(-1).cpu().tolist()]
+    vals += [float(torch.as_tensor(x).item()) if torch.is_tensor(x) else float(x) for x in (fx, fy, cx, cy)]
+    if len(vals) != 16:
+        raise ValueError("R_v must be 3x3 and t_v of length 3")
+    return (ctypes.c_double * 16)(*vals)
+
+
+def quat_to_rotmat(q):
+    dt = spike_dtype(q)
+    n = q.numel() // 4
+    R = torch.empty(q.shape[:-1] + (3, 3), dtype=q.dtype, device=q.device)
+    call("tts_quat_to_rotmat", ptr(q), n, ptr(R), dt, stream())
+    return R
+
+
+def quat_to_rotmat_bwd(q, gR):
+    dt = spike_dtype(q, gR)
+    gq = torch.empty_like(q)
+    call("tts_quat_to_rotmat_bwd", ptr(q), ptr(gR), q.numel() // 4, ptr(gq), dt, stream())
+    return gq
+
+
+def cov3d(s, R):
+    dt = spike_dtype(s, R)
+    cov = torch.empty_like(R)
+    call("tts_cov3d", ptr(s), ptr(R), s.numel() // 3, ptr(cov), dt, stream())
+    return cov
+
+
+def cov3d_bwd(s, R, gcov):
+    dt = spike_dtype(s, R, gcov)
+    gs, gR = torch.empty_like(s), torch.empty_like(R)
+    call("tts_cov3d_bwd", ptr(s), ptr(R), ptr(gcov), s.numel() // 3, ptr(gs), ptr(gR), dt, stream())
+    return gs, gR
+
+
+def project_ewa(means, cov, cam16, blur, near):
+    dt = spike_dtype(means, cov)
+    G = means.shape[0]
+    o = lambda *shape: torch.empty(shape, dtype=means.dtype, device=means.device)  # noqa: E731
+    mu2d, conic, depth = o(G, 2), o(G, 3), o(G)
+    keep = torch.empty(G, dtype=torch.uint8, device=means.device)
+    call("tts_project_ewa", ptr(means), ptr(cov), G, cam16, float(blur), float(near), ptr(mu2d), ptr(conic),
+         ptr(depth), ptr(keep), dt, stream())
+    return mu2d, conic, depth, keep.view(torch.bool)
+
+
+def project_ewa_bwd(means, cov, cam16, blur, near, gmu2d, gconic, gdepth):
+    dt = spike_dtype(means, cov, gmu2d, gconic, gdepth)
+    gm, gc = torch.empty_like(means), torch.empty_like(cov)
+    call("tts_project_ewa_bwd", ptr(means), ptr(cov), means.shape[0], cam16, float(blur), float(near), ptr(gmu2d),
+         ptr(gconic), ptr(gdepth), ptr(gm), ptr(gc), dt, stream())
+    return gm, gc
+
+
+def eval_sh(deg, coeffs, dirs, raw=False):
+    dt = spike_dtype(coeffs, dirs)
+    G = dirs.numel() // 3
+    nc, nch = coeffs.shape[-2], coeffs.shape[-1]
+    out = torch.empty(dirs.shape[:-1] + (nch,), dtype=dirs.dtype, device=dirs.device)
+    call("tts_eval_sh", int(deg), ptr(coeffs), nc, nch, ptr(dirs), G, int(bool(raw)), ptr(out), dt, stream())
+    return out
+
+
+def eval_sh_bwd(deg, coeffs, dirs, gout, raw=False):
+    dt = spike_dtype(coeffs, dirs, gout)
+    gco, gd = torch.empty_like(coeffs), torch.empty_like(dirs)
+    call("tts_eval_sh_bwd", int(deg), ptr(coeffs), coeffs.shape[-2], coeffs.shape[-1], ptr(dirs), dirs.numel() // 3,
+         int(bool(raw)), ptr(gout), ptr(gco), ptr(gd), dt, stream())
+    return gco, gd
+
+
+def color_from_dc(dc, gout=None):
+    dt = spike_dtype(dc, gout)
+    out = torch.empty_like(dc)
+    call("tts_color_from_dc", ptr(dc), dc.numel(), ptr(gout), ptr(out), dt, stream())
+    return out
+
+
+def phi(px, py):
+    dt = spike_dtype(px, py)
+    out = torch.empty(px.numel(), 6, dtype=px.dtype, device=px.device)
+    call("tts_phi", ptr(px), ptr(py), px.numel(), ptr(out), dt, stream())
+    return out
+
+
+def phi_bwd(px, py, gPhi):
+    dt = spike_dtype(px, py, gPhi)
+    gx, gy = torch.empty_like(px), torch.empty_like(py)
+    call("tts_phi_bwd", ptr(px), ptr(py), ptr(gPhi), px.numel(), ptr(gx), ptr(gy), dt, stream())
+    return gx, gy
+
+
+def theta_from_conic(conic, mu, k, origins=None, per=1, gathered=False, want_Q=True, want_u=True):
+    """theta_Q / theta_u [n,6] (layout of spike/forward.py:23-39), or with ``gathered`` theta_u
+    as [n/per, 6, per] in the op order of theta_u_gathered (tools/m4_train_binned.py:130-143);
+    the means are taken relative to ``origins[i // per]`` when given."""
+    dt = spike_dtype(conic, mu, origins)
+    n = conic.numel() // 3
+    o = lambda *shape: torch.empty(shape, dtype=conic.dtype, device=conic.device)  # noqa: E731
+    if gathered:
+        thQ, thU = None, o(n // per, 6, per)
+    else:
+        thQ, thU = (o(n, 6) if want_Q else None), (o(n, 6) if want_u else None)
+    call("tts_theta_from_conic", ptr(conic), ptr(mu), ptr(origins), int(per), n, float(k), 1 if gathered else 0,
+         ptr(thQ), ptr(thU), dt, stream())
+    return thQ, thU
+
+
+def theta_from_conic_bwd(conic, mu, k, gQ, gU, origins=None, per=1):
+    dt = spike_dtype(conic, mu, origins, gQ, gU)
+    gc, gm = torch.empty_like(conic), torch.empty_like(mu)
+    call("tts_theta_from_conic_bwd", ptr(conic), ptr(mu), ptr(origins), int(per), conic.numel() // 3, float(k),
+         ptr(gQ), ptr(gU), ptr(gc), ptr(gm), dt, stream())
+    return gc, gm
+
+
+def _spike_ws(P, G, dt, device):
+    nbytes = lib().tts_spike_workspace_bytes(int(P), int(G), int(dt))
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device), nbytes
+
+
+def quad_form(px, py, mu2d, conic):
+    dt = spike_dtype(px, py, mu2d, conic)
+    P, G = px.numel(), mu2d.shape[0]
+    Q = torch.empty(P, G, dtype=px.dtype, device=px.device)
+    call("tts_quad_form", ptr(px), ptr(py), ptr(mu2d), ptr(conic), P, G, ptr(Q), dt, stream())
+    return Q
+
+
+def quad_form_bwd(px, py, mu2d, conic, gQ):
+    dt = spike_dtype(px, py, mu2d, conic, gQ)
+    P, G = px.numel(), mu2d.shape[0]
+    gm, gc = torch.empty_like(mu2d), torch.empty_like(conic)
+    ws, nbytes = _spike_ws(P, G, dt, px.device)
+    call("tts_quad_form_bwd", ptr(px), ptr(py), ptr(mu2d), ptr(conic), ptr(gQ), P, G, ptr(gm), ptr(gc), ptr(ws), nbytes,
+         dt, stream())
+    return gm, gc
+
+
+def phi_theta(Phi, theta):
+    dt = spike_dtype(Phi, theta)
+    P, G = Phi.shape[0], theta.shape[0]
+    Q = torch.empty(P, G, dtype=Phi.dtype, device=Phi.device)
+    call("tts_phi_theta", ptr(Phi), ptr(theta), P, G, ptr(Q), dt, stream())
+    return Q
+
+
+def phi_theta_bwd(Phi, theta, gQ, want_phi=True, want_theta=True):
+    dt = spike_dtype(Phi, theta, gQ)
+    P, G = Phi.shape[0], theta.shape[0]
+    gP = torch.empty_like(Phi) if want_phi else None
+    gT = torch.empty_like(theta) if want_theta else None
+    ws, nbytes = _spike_ws(P, G, dt, Phi.device)
+    call("tts_phi_theta_bwd", ptr(Phi), ptr(theta), ptr(gQ), P, G, ptr(gP), ptr(gT), ptr(ws), nbytes, dt, stream())
+    return gP, gT
+
+
+def poly_splat_wgeo(Q, k, keep=None, gout=None):
+    dt = spike_dtype(Q, gout)
+    _dev(keep)
+    P, G = Q.shape[0], Q.shape[1]
+    out = torch.empty_like(Q)
+    call("tts_poly_splat_wgeo", ptr(Q), P, G, float(k), ptr(keep), ptr(gout), ptr(out), dt, stream())
+    return out

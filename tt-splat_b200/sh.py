@@ -1,8 +1,20 @@
-"""Real spherical harmonics, degrees 0-3 (mirrors spike/sh.py:1-72).
+"""View-dependent colour from real spherical harmonics, degrees 0-3 (spike/sh.py:49-72), on the
+device.
 
-The fused projection kernel evaluates the colour on the device; ``eval_sh_color`` keeps the
-reference's tensor expression for callers that compose it by hand.
+``eval_sh_color(deg, coeffs, dirs)`` keeps the reference's signature: coeffs [G, nc, 3] with
+nc >= (deg+1)^2 (DC first, then the higher bands in the inria/gsplat order), dirs [G, 3]
+(normalised inside, norm clamped at 1e-12); it returns clamp(0.5 + sum_k basis_k coeffs_k,
+min 0) [G, 3].  A torch autograd Function over ``tts_eval_sh`` / ``tts_eval_sh_bwd`` (float32 or
+float64) gives the gradients of the coefficients and of the directions; CPU tensors raise.
+
+The basis constants below are the standard real-SH normalisations (the same numbers every 3DGS
+code uses); the kernels carry their own copy.
 """
+import torch
+
+from . import ops
+from ._lib import on_device
+
 C0 = 0.28209479177387814
 C1 = 0.4886025119029199
 C2 = [1.0925484305920792, -1.0925484305920792, 0.31539156525252005, -1.0925484305920792, 0.5462742152960396]
@@ -10,38 +22,27 @@ C3 = [-0.5900435899266435, 2.890611442640554, -0.4570457994644658, 0.37317633259
       1.445305721320277, -0.5900435899266435]
 
 
-def sh_eval_deg2(coeffs, dirs):
-    """spike/sh.py:20-30."""
-    d = dirs / dirs.norm(dim=-1, keepdim=True).clamp(min=1e-12)
-    x, y, z = d[..., 0], d[..., 1], d[..., 2]
-    r = C0 * coeffs[..., 0]
-    r = r - C1 * y * coeffs[..., 1] + C1 * z * coeffs[..., 2] - C1 * x * coeffs[..., 3]
-    xx, yy, zz, xy, yz, xz = x * x, y * y, z * z, x * y, y * z, x * z
-    return (r + C2[0] * xy * coeffs[..., 4] + C2[1] * yz * coeffs[..., 5] + C2[2] * (2.0 * zz - xx - yy) * coeffs[..., 6]
-            + C2[3] * xz * coeffs[..., 7] + C2[4] * (xx - yy) * coeffs[..., 8])
+class _EvalSH(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, coeffs, dirs, deg):
+        if coeffs.dim() < 2 or dirs.shape[-1] != 3 or coeffs.shape[:-2] != dirs.shape[:-1]:
+            raise ValueError(f"coeffs [...,nc,3] and dirs [...,3] with the same leading dims, got "
+                             f"{tuple(coeffs.shape)} and {tuple(dirs.shape)}")
+        c, d = coeffs.detach().contiguous(), dirs.detach().contiguous()
+        ctx.save_for_backward(c, d)
+        ctx.deg = deg
+        return ops.eval_sh(deg, c, d)
 
-
-def opacity_dc(coeffs):
-    """spike/sh.py:33-35."""
-    return C0 * coeffs[..., 0]
+    @staticmethod
+    def backward(ctx, gout):
+        c, d = ctx.saved_tensors
+        gco, gd = ops.eval_sh_bwd(ctx.deg, c, d, gout.contiguous())
+        return gco, gd, None
 
 
 def eval_sh_color(deg, coeffs, dirs):
-    """spike/sh.py:49-72."""
-    d = dirs / dirs.norm(dim=-1, keepdim=True).clamp(min=1e-12)
-    x, y, z = d[..., 0:1], d[..., 1:2], d[..., 2:3]
-    r = C0 * coeffs[..., 0, :]
-    if deg >= 1:
-        r = r - C1 * y * coeffs[..., 1, :] + C1 * z * coeffs[..., 2, :] - C1 * x * coeffs[..., 3, :]
-    if deg >= 2:
-        xx, yy, zz, xy, yz, xz = x * x, y * y, z * z, x * y, y * z, x * z
-        r = (r + C2[0] * xy * coeffs[..., 4, :] + C2[1] * yz * coeffs[..., 5, :]
-             + C2[2] * (2.0 * zz - xx - yy) * coeffs[..., 6, :] + C2[3] * xz * coeffs[..., 7, :]
-             + C2[4] * (xx - yy) * coeffs[..., 8, :])
-    if deg >= 3:
-        xx, yy, zz = x * x, y * y, z * z
-        r = (r + C3[0] * y * (3 * xx - yy) * coeffs[..., 9, :] + C3[1] * x * y * z * coeffs[..., 10, :]
-             + C3[2] * y * (4 * zz - xx - yy) * coeffs[..., 11, :] + C3[3] * z * (2 * zz - 3 * xx - 3 * yy) * coeffs[..., 12, :]
-             + C3[4] * x * (4 * zz - xx - yy) * coeffs[..., 13, :] + C3[5] * z * (xx - yy) * coeffs[..., 14, :]
-             + C3[6] * x * (xx - 3 * yy) * coeffs[..., 15, :])
-    return (r + 0.5).clamp(min=0.0)
+    """spike/sh.py:49-72 on the device: RGB colour [..., 3] of SH degree ``deg`` (0..3)."""
+    if int(deg) not in (0, 1, 2, 3):
+        raise ValueError(f"SH degree must be 0..3, got {deg}")
+    with on_device(coeffs):
+        return _EvalSH.apply(coeffs, dirs, int(deg))
