@@ -2,8 +2,10 @@
 K=256) and config 4 (3M gaussians, SH degree 3, 1264x832, forward-only novel views).
 
 The device projection feeds both the device binning and the oracle binning, so the tables must
-agree bit for bit (tools/m4_train_binned.py:75-127 restated in oracle/binning.py); the images
-are checked against the oracle's binned forward on the same tables (1e-3 max abs, fp32)."""
+agree bit for bit (tools/m4_train_binned.py:75-127 restated in oracle/binning.py); on the 64
+fullest and 64 random tiles the slot rows must equal the oracle's own theta/colour gather over
+its own tables bit for bit, and the image the oracle's binned forward of those rows (1e-3 max
+abs, fp32)."""
 import numpy as np
 import pytest
 import torch
@@ -50,16 +52,30 @@ def _check_view(pj, bp, v, H, W, K, flat, G):
     assert np.array_equal(idx, np.where(b.valid, b.idx, -1))
     assert np.array_equal(bp["count"][v].cpu().numpy(), b.valid.sum(1))
     assert np.array_equal(cand, b.cand)
-    # forward on the device's own slot rows vs the oracle's binned forward on the same rows, on
-    # the 64 fullest tiles and 64 seeded random ones
+    # on the 64 fullest tiles and 64 seeded random ones: the slot rows the device wrote equal the
+    # oracle's theta_u_gathered / colour gather over the oracle's own tables (same projection
+    # values, tools/m4_train_binned.py:130-143, 207-211), and the device image equals the oracle's
+    # binned forward on those oracle rows
     c_b = torch.ones(3, device=DEV)
     rf = ops.render_fwd(bp["slots"][v:v + 1].contiguous(), bp["count"][v:v + 1].contiguous(), H, W,
                         flat[59 * G:], c_b)
-    rows = bp["slots"][v].cpu().numpy()
     sel = np.unique(np.concatenate([np.argsort(-cand, kind="stable")[:64],
                                     np.random.default_rng(v).integers(0, tm.T, 64)]))
+    proj = pj["proj"][v].cpu().numpy()
+    oidx = np.where(b.valid[sel], b.idx[sel], 0)
+    th = orender.theta_u_gathered(proj[oidx][..., 2:5], proj[oidx][..., 0:2], tm.origins[sel], 4.0)
+    rows = np.zeros((len(sel), K, 12), np.float32)
+    rows[..., 0:6] = np.transpose(th, (0, 2, 1))
+    rows[..., 6:10] = proj[oidx][..., 5:9]
+    vsel = b.valid[sel]
+    dev_rows = bp["slots"][v].cpu().numpy()[sel]
+    assert np.array_equal(dev_rows[..., 0:10][vsel], rows[..., 0:10][vsel])
     w_b = np.float32(orender.softplus(np.float32(flat[59 * G].item())))
-    ref = _oracle_tiles(rows, idx >= 0, w_b, tm, sel)
+    full = np.zeros((tm.T, K, 12), np.float32)
+    full[sel] = rows
+    fvalid = np.zeros((tm.T, K), bool)
+    fvalid[sel] = vsel
+    ref = _oracle_tiles(full, fvalid, w_b, tm, sel)
     got = rf["img"][0].cpu().numpy().reshape(-1, 3)[tm.gidx.reshape(tm.T, -1)[sel]]
     assert np.abs(got - ref).max() < 1e-3
     return cand

@@ -280,18 +280,20 @@ def test_slot_rows_bit_exact_given_projection(pkg):
 
 
 def test_bf16_slot_rows(pkg):
-    """bf16 operands, fp32 accumulation: within 1e-2 relative L2 of the fp32 image (the metric
-    the reference reports for its bf16 device path, tools/m4_train_binned.py:246-248).  The
-    compact rows carry theta_u as a bf16 (hi, lo) pair, colour_o and o_col as bf16."""
+    """bf16 operands, fp32 accumulation, against the oracle's image: north_star's 1e-2 bound
+    (max abs) and the relative-L2 metric the reference reports for its bf16 device path
+    (tools/m4_train_binned.py:246-248).  The compact rows carry theta_u as a bf16 (hi, lo) pair,
+    colour_o and o_col as bf16."""
     from tt_splat_b200 import camera, render
     sc = pkg.synthetic.config1(seed=4, G=3000, res=128)
     m = _model(pkg, sc["params"])
     cam = camera.Camera.from_dict(sc["cams"][0])
-    a = render.render(m, cam, sh_degree=3).detach()
+    ref = pipeline.render_view(sc["params"], 3, sc["cams"][0], K=128)["img"]
     with torch.no_grad():
         b = render.render(m, cam, sh_degree=3, bf16=True)
     c = render.render(m, cam, sh_degree=3, bf16=True)          # with grad: fp32 rows kept for backward
-    assert rel_l2(b.cpu().numpy(), a.cpu().numpy()) < 1e-2
+    assert np.abs(b.cpu().numpy() - ref).max() < 1e-2
+    assert rel_l2(b.cpu().numpy(), ref) < 1e-3
     assert torch.equal(b, c.detach())
 
 

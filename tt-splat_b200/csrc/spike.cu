@@ -32,6 +32,15 @@ unsigned grid_for(long long n) {
   return (unsigned)(b < 1 ? 1 : (b > SP_MAX_BLOCKS ? SP_MAX_BLOCKS : b));
 }
 
+// Individually rounded arithmetic (no FMA contraction): the reference's expressions evaluated
+// in its op order, as torch's CPU kernels do.
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double add_rn(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ float sub_rn(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ double sub_rn(double a, double b) { return __dsub_rn(a, b); }
+
 #define SP_LOOP(i, n) \
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (n); i += (long long)gridDim.x * blockDim.x)
 
@@ -429,37 +438,44 @@ __global__ void __launch_bounds__(SP_THREADS)
 
 // ---- theta from the conic (spike/forward.py:23-39; gathered order tools/m4_train_binned.py:130-143)
 // theta_Q = [a, c, 2b, -2(a mx + b my), -2(b mx + c my), a mx^2 + 2 b mx my + c my^2] over
-// Phi, theta_u = -theta_Q / k + [0,0,0,0,0,1].  The mean is taken relative to origins[i / per]
-// when origins is given.  layout 0 writes [n,6]; layout 1 writes [n/per, 6, per] (the
-// [T,6,K] operand of the binned render), in the op order of theta_u_gathered.
+// Phi, theta_u = (-1/k) theta_Q + [0,0,0,0,0,1].  The mean is taken relative to
+// origins[i / per] when origins is given.  layout 0 writes [n,6]; layout 1 writes theta_u as
+// [n/per, 6, per] (the [T,6,K] operand of the binned render) in the op order of
+// theta_u_gathered, bit-identical to the slot rows of the binning kernel.  1/k is formed in
+// double and rounded to T, as the reference's Python scalar is.
 template <typename T>
 __global__ void __launch_bounds__(SP_THREADS)
     k_theta(const T* __restrict__ conic, const T* __restrict__ mu, const T* __restrict__ origins, long long per,
-            long long n, T k, int layout, T* __restrict__ thQ, T* __restrict__ thU) {
+            long long n, double k, int layout, T* __restrict__ thQ, T* __restrict__ thU) {
+  const T two = T(2);
   SP_LOOP(i, n) {
     const T a = conic[3 * i], b = conic[3 * i + 1], c = conic[3 * i + 2];
     T mx = mu[2 * i], my = mu[2 * i + 1];
     if (origins) {
-      mx -= origins[2 * (i / per)];
-      my -= origins[2 * (i / per) + 1];
+      mx = sub_rn(mx, origins[2 * (i / per)]);
+      my = sub_rn(my, origins[2 * (i / per) + 1]);
     }
     if (layout == 1) {
-      const T ik = T(1) / k;
-      const T Q = a * mx * mx + T(2) * b * mx * my + c * my * my;
-      const T th[6] = {-a * ik, -c * ik, T(-2) * b * ik, T(2) * (a * mx + b * my) * ik, T(2) * (b * mx + c * my) * ik,
-                       T(1) - Q * ik};
+      const T ik = (T)(1.0 / k);
+      const T Q = add_rn(add_rn(mul_rn(mul_rn(a, mx), mx), mul_rn(mul_rn(mul_rn(two, b), mx), my)),
+                         mul_rn(mul_rn(c, my), my));
+      const T th[6] = {mul_rn(-a, ik), mul_rn(-c, ik), mul_rn(mul_rn(T(-2), b), ik),
+                       mul_rn(mul_rn(two, add_rn(mul_rn(a, mx), mul_rn(b, my))), ik),
+                       mul_rn(mul_rn(two, add_rn(mul_rn(b, mx), mul_rn(c, my))), ik), sub_rn(T(1), mul_rn(Q, ik))};
       const long long t = i / per, s = i % per;
 #pragma unroll
       for (int e = 0; e < 6; ++e) thU[(t * 6 + e) * per + s] = th[e];
       continue;
     }
-    const T q[6] = {a, c, T(2) * b, T(-2) * (a * mx + b * my), T(-2) * (b * mx + c * my),
-                    a * mx * mx + T(2) * b * mx * my + c * my * my};
-    const T nk = T(-1) / k;
+    const T q[6] = {a, c, mul_rn(two, b), mul_rn(T(-2), add_rn(mul_rn(a, mx), mul_rn(b, my))),
+                    mul_rn(T(-2), add_rn(mul_rn(b, mx), mul_rn(c, my))),
+                    add_rn(add_rn(mul_rn(mul_rn(a, mx), mx), mul_rn(mul_rn(mul_rn(two, b), mx), my)),
+                           mul_rn(mul_rn(c, my), my))};
+    const T nk = (T)(-1.0 / k);
 #pragma unroll
     for (int e = 0; e < 6; ++e) {
       if (thQ) thQ[6 * i + e] = q[e];
-      if (thU) thU[6 * i + e] = nk * q[e] + (e == 5 ? T(1) : T(0));
+      if (thU) thU[6 * i + e] = add_rn(mul_rn(nk, q[e]), e == 5 ? T(1) : T(0));
     }
   }
 }
@@ -468,7 +484,7 @@ __global__ void __launch_bounds__(SP_THREADS)
 template <typename T>
 __global__ void __launch_bounds__(SP_THREADS)
     k_theta_bwd(const T* __restrict__ conic, const T* __restrict__ mu, const T* __restrict__ origins, long long per,
-                long long n, T k, const T* __restrict__ gQ, const T* __restrict__ gU, T* __restrict__ gconic,
+                long long n, double k, const T* __restrict__ gQ, const T* __restrict__ gU, T* __restrict__ gconic,
                 T* __restrict__ gmu) {
   SP_LOOP(i, n) {
     const T a = conic[3 * i], b = conic[3 * i + 1], c = conic[3 * i + 2];
@@ -478,7 +494,7 @@ __global__ void __launch_bounds__(SP_THREADS)
       my -= origins[2 * (i / per) + 1];
     }
     T g[6];
-    const T nk = T(-1) / k;
+    const T nk = (T)(-1.0 / k);
 #pragma unroll
     for (int e = 0; e < 6; ++e) g[e] = (gQ ? gQ[6 * i + e] : T(0)) + (gU ? nk * gU[6 * i + e] : T(0));
     gconic[3 * i] = g[0] + g[3] * (T(-2) * mx) + g[5] * (mx * mx);
@@ -783,7 +799,7 @@ extern "C" int tts_theta_from_conic(const void* conic, const void* mu, const voi
   if (n == 0) return TTS_OK;
   SP_DISPATCH(dtype, (k_theta<T><<<grid_for(n), SP_THREADS, 0, as_stream(stream)>>>(
                          static_cast<const T*>(conic), static_cast<const T*>(mu), static_cast<const T*>(origins), per,
-                         n, (T)k, layout, static_cast<T*>(theta_Q), static_cast<T*>(theta_u))));
+                         n, k, layout, static_cast<T*>(theta_Q), static_cast<T*>(theta_u))));
   return check_launch("theta_from_conic");
 }
 
@@ -796,7 +812,7 @@ extern "C" int tts_theta_from_conic_bwd(const void* conic, const void* mu, const
   if (n == 0) return TTS_OK;
   SP_DISPATCH(dtype, (k_theta_bwd<T><<<grid_for(n), SP_THREADS, 0, as_stream(stream)>>>(
                          static_cast<const T*>(conic), static_cast<const T*>(mu), static_cast<const T*>(origins), per,
-                         n, (T)k, static_cast<const T*>(gtheta_Q), static_cast<const T*>(gtheta_u),
+                         n, k, static_cast<const T*>(gtheta_Q), static_cast<const T*>(gtheta_u),
                          static_cast<T*>(gconic), static_cast<T*>(gmu))));
   return check_launch("theta_from_conic_bwd");
 }
