@@ -157,7 +157,8 @@ int tts_render_bwd_rv(const float* slots, const int32_t* count, int V, int H, in
  * Replaces metrics.loss_fn, spike/metrics.py:26-28 ((1-l) L1 + l (1-SSIM), SSIM on inputs
  * clamped to [0,1], 11-tap sigma-1.5 window shrunk for small images :15-19) with the manual
  * gradient of tools/loss_manual.py:78-105.  gimg = grad_scale * dloss/dimg; loss[v] written,
- * and, when loss_sum is not NULL, loss_sum[0] = loss[0] + ... + loss[V-1] (view order). */
+ * and, when loss_sum is not NULL, loss_sum[0] = loss[0] + ... + loss[V-1] (view order).
+ * lambda = 0 is the L1 loss alone: one pass over the pixels, no SSIM work. */
 size_t tts_loss_workspace_bytes(int V, int H, int W);
 int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W, float lambda,
                      float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,

@@ -20,15 +20,17 @@ def test_loss_vs_reference_restatement(case, pkg):
     assert rel_l2(out["gimg"][0].cpu().numpy(), z[f"{case}__grad"]) < 1e-3
 
 
+@pytest.mark.parametrize("lam", [0.2, 0.0])
 @pytest.mark.parametrize("H,W", [(64, 96), (832, 1264), (16, 16)])
-def test_loss_with_clamped_inputs_vs_oracle(H, W, pkg):
+def test_loss_with_clamped_inputs_vs_oracle(H, W, lam, pkg):
+    """lambda 0.2 (the train step's loss) and 0 (L1 alone, a pass without SSIM work)."""
     from tt_splat_b200 import ops
     rng = np.random.default_rng(H + W)
     x = rng.uniform(-0.2, 1.2, (2, H, W, 3)).astype(np.float32)
     y = rng.uniform(0, 1, (2, H, W, 3)).astype(np.float32)
-    out = ops.loss_l1_ssim(torch.from_numpy(x).to(DEV), torch.from_numpy(y).to(DEV), 0.2, 0.5)
+    out = ops.loss_l1_ssim(torch.from_numpy(x).to(DEV), torch.from_numpy(y).to(DEV), lam, 0.5)
     for v in range(2):
-        loss, _, _, g = oloss.loss_and_grad(x[v], y[v], 0.2)
+        loss, _, _, g = oloss.loss_and_grad(x[v], y[v], lam)
         assert abs(float(out["loss"][v]) - loss) < 1e-5
         assert rel_l2(out["gimg"][v].cpu().numpy(), 0.5 * g) < 1e-3
 
