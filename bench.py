@@ -32,7 +32,9 @@ sys.path.insert(0, REPO)
 import __graft_entry__  # noqa: E402
 
 CONFIG = dict(workload="config2: train step, G=100k, 8 views 1264x832, K=128, SH3, MCMC", G=100000, views=8,
-              H=832, W=1264, K=128, R=1, sh_degree=3)
+              H=832, W=1264, K=128, R=1, sh_degree=3,
+              l2="inputs larger than L2: the per-step working set (~1 GB: targets, images, slot rows, SSIM maps) "
+                 "exceeds the 126 MB L2")
 METRIC = "train steps/s (G=100k, 8-view batch 1264x832, 1/2/4/8 B200)"
 PEAKS_FILE = os.path.join(REPO, "MEASURED_PEAKS.json")
 REF_BUDGET_S = 90.0   # wall-clock budget of the CPU reference arm's timed samples
@@ -208,6 +210,7 @@ def run_ours(args, rank, world, local_rank):
             t.copy_(c)
         del snap
     torch.cuda.synchronize()
+    fp32_peak = ops.fp32_peak_tflops() if rank == 0 else None
     ops.read_status()          # clear the device status word before the timed region
     barrier()
     # Every leg below starts from this state.  SGLD at noise_lr 5e5 on random-noise targets
@@ -338,29 +341,36 @@ def run_ours(args, rank, world, local_rank):
         bwd_ms = stages["render_bwd"]
         clk_s = clk.summary()
         sm_mhz = clk_s["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
-        fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12        # TFLOP/s at the sampled SM clock
+        fp32_nominal = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12     # TFLOP/s at the sampled SM clock
         achieved = 44.0 * pairs / (bwd_ms * 1e-3) / 1e12
         adam_gbs = 28.0 * (59 * st.G + 1) / (stages["adam"] * 1e-3) / 1e9
+        adam_dram_gbs = ADAM_DRAM / (stages["adam"] * 1e-3) / 1e9
         launches = st.kernels_per_step or 0
         line = {
             "metric": METRIC, "value": steps_per_s, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 2 shapes; random-init model)",
-            "config": {**CONFIG, "views_per_rank": len(mine), "parallelism": (f"view-split x{world} + NVLink peer optimizer step" if st.regions is not None
-                                                     else f"view-split x{world}" + (" + NCCL allreduce" if world > 1 else "")),
-                       "l2": "per-step working set > 126 MB L2 (targets, images, slot rows, SSIM maps)"},
+            "config": dict(CONFIG), "views_per_rank": len(mine),
+            "parallelism": (f"view-split x{world} + NVLink peer optimizer step" if st.regions is not None
+                            else f"view-split x{world}" + (" + NCCL allreduce" if world > 1 else "")),
             "render_mpix_s": (V * CONFIG["H"] * CONFIG["W"] / 1e6) / (rend_ms / 1e3) if rend_ms and world == 1 else None,
             "roofline": {"bound": "fp32", "kernel": "render_bwd", "achieved": achieved, "peak": fp32_peak,
                          "unit": "TFLOP/s", "frac": achieved / fp32_peak,
                          "traffic": RENDER_BWD_DRAM_PER_VIEW * V if CONFIG["G"] == 100000 else None,
                          "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, "
                                          "4-view capture scaled by views per launch)",
-                         "peak_source": "nominal FP32 FMA (148 SMs x 128 lanes x 2) at the sampled SM clock",
+                         "traffic_source": TRAFFIC_SOURCE,
+                         "peak_source": "measured in this run: packed fma.rn.f32x2 probe kernel (tts_fma_probe, best "
+                                        "of 5 launches); MEASURED_PEAKS.json has no FP32 figure",
+                         "peak_nominal": fp32_nominal,
                          "work": f"44 flops x {pairs} valid (pixel, slot) pairs per launch"},
             "roofline_hbm": {"bound": "hbm", "kernel": "adam", "achieved": adam_gbs, "peak": peaks.get("hbm_gbs"),
                              "unit": "GB/s", "frac": adam_gbs / peaks.get("hbm_gbs", 6538.0),
                              "traffic": ADAM_DRAM if CONFIG["G"] == 100000 else None,
-                             "work": f"28 B x {59 * st.G + 1} parameter elements per launch (read p,g,m,v; write p,m,v)"},
+                             "traffic_source": TRAFFIC_SOURCE,
+                             "dram_achieved": adam_dram_gbs, "dram_frac": adam_dram_gbs / peaks.get("hbm_gbs", 6538.0),
+                             "work": f"28 B x {59 * st.G + 1} parameter elements per launch (read p,g,m,v; write p,m,v); "
+                                     "dram_* use the ncu DRAM bytes (part of p, m, v stays in L2)"},
             "stage_ms": stages, "clocks": clk_s, "replicas_agree": replicas_ok, "device_status": status, "params_finite_after_timed_steps": finite, "rank_phases": phases,
             "e2e": {"value": args.steps / (ms_e2e / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4},
@@ -377,8 +387,11 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_config(args, rank, world, local_rank, cid):
-    """Benchmark configs 3 and 4 (extra lines; the headline is config 2).
+    """Benchmark configs 1, 3 and 4 (extra lines; the headline is config 2).
 
+    config 1: G = 10k in 8 clusters, SH 3, one 800x800 view, K = 128: forward + L1 + backward
+              with fp32 slot rows (the line's value), and the bf16-operand forward alone
+              (fwd_bf16_*); every rank runs the same view (replicas).
     config 3: G = 1M clustered, 1920x1072 (1080 cropped to whole tiles), K = 256, fp32; each rank
               renders one view forward + backward (weak scaling); reports candidate overflow.
     config 4: G = 3M, 64 views 1264x832 on a seeded spiral, K = 128, forward only from compact
@@ -392,7 +405,10 @@ def run_config(args, rank, world, local_rank, cid):
     from tt_splat_b200.model import pack_arrays
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if cid == 3:
+    if cid == 1:
+        sc = pkg.synthetic.config1()
+        mine = [0]                               # one view: every rank runs a replica
+    elif cid == 3:
         sc = pkg.synthetic.config3(n_views=max(world, 1))
         mine = [rank]
     else:
@@ -409,19 +425,27 @@ def run_config(args, rank, world, local_rank, cid):
     ws = ops.Workspace(dev)
     state = {}
 
-    def once():
+    def once(fwd_bf16=False):
         for ct in cams_t:
             pj = ops.project(flat, G, sh, ct, H, W, out=state.get("pj"))
             state["pj"] = pj
-            bp = ops.bin_pack(pj, G, H, W, 1, K, ws=ws, out=state.get("bp"), with_inv=(cid == 3), bf16=(cid == 4))
-            state["bp"] = bp
-            rf = ops.render_fwd(bp["slots"], bp["count"], H, W, flat[59 * G:], c_b, out=state.get("rf"),
-                                bf16=(cid == 4))
+            bf16 = cid == 4 or fwd_bf16
+            key = "bp16" if bf16 else "bp"
+            bp = ops.bin_pack(pj, G, H, W, 1, K, ws=ws, out=state.get(key), with_inv=cid in (1, 3) and not bf16,
+                              bf16=bf16)
+            state[key] = bp
+            rf = ops.render_fwd(bp["slots"], bp["count"], H, W, flat[59 * G:], c_b, out=state.get("rf"), bf16=bf16)
             state["rf"] = rf
-            if cid == 3:
-                tg = state.setdefault("tg", torch.rand(rf["img"].shape, device=dev, generator=torch.Generator(dev).manual_seed(5)))
-                lo = ops.loss_l1_ssim(rf["img"], tg, 0.2, 1.0, ws=state.setdefault("wsl", ops.Workspace(dev)),
-                                      out=state.get("lo"))
+            if cid in (1, 3) and not fwd_bf16:
+                if cid == 1:
+                    tg = state.setdefault("tg", torch.from_numpy(sc["targets"][0]).to(dev)[None].contiguous())
+                else:
+                    tg = state.setdefault("tg", torch.rand(rf["img"].shape, device=dev,
+                                                           generator=torch.Generator(dev).manual_seed(5)))
+                # config 1: the L1 loss of its reference run (tools/m4_train_binned.py:238-248);
+                # config 3: the train step's L1 + SSIM
+                lo = ops.loss_l1_ssim(rf["img"], tg, 0.0 if cid == 1 else 0.2, 1.0,
+                                      ws=state.setdefault("wsl", ops.Workspace(dev)), out=state.get("lo"))
                 state["lo"] = lo
                 rb = ops.render_bwd(bp["slots"], bp["count"], H, W, c_b, rf["img"], rf["den"], lo["gimg"],
                                     out=state.get("rb"))
@@ -437,7 +461,7 @@ def run_config(args, rank, world, local_rank, cid):
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    steps = max(1, min(args.steps, 50 if cid == 3 else 10))
+    steps = max(1, min(args.steps, 200 if cid == 1 else 50 if cid == 3 else 10))
     e0.record()
     for _ in range(steps):
         once()
@@ -447,6 +471,18 @@ def run_config(args, rank, world, local_rank, cid):
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
+    fwd16_ms = None
+    if cid == 1:
+        # the bf16-operand forward alone (project + bin with compact rows + render)
+        for _ in range(3):
+            once(fwd_bf16=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            once(fwd_bf16=True)
+        e1.record()
+        torch.cuda.synchronize()
+        fwd16_ms = e0.elapsed_time(e1) / steps
     if cid == 3:
         cand = state["bp"]["cand"].reshape(-1).long()
         over = torch.clamp(cand - K, min=0)
@@ -454,13 +490,18 @@ def run_config(args, rank, world, local_rank, cid):
                  "max_candidates": int(cand.max())}
     else:
         extra = {}
-    n_views_job = world if cid == 3 else len(sc["cams"])
+    n_views_job = world if cid in (1, 3) else len(sc["cams"])
+    if cid == 1:
+        extra = {"overflow_tiles": int((state["bp"]["cand"] > K).sum()),
+                 "fwd_bf16_ms": fwd16_ms, "fwd_bf16_mpix_s": H * W / 1e6 / (fwd16_ms / 1e3),
+                 "loss": "L1 (the reference's config-1 run)", "replicas": "every rank runs the single view"}
     if rank == 0:
-        line = {"metric": ("fwd+bwd views/s (config 3)" if cid == 3 else "render frames/s (config 4)"),
-                "value": (world if cid == 3 else len(sc["cams"])) / (ms / 1e3), "unit": "views/s" if cid == 3 else "frames/s",
+        metric = {1: "fwd+bwd views/s (config 1)", 3: "fwd+bwd views/s (config 3)", 4: "render frames/s (config 4)"}[cid]
+        line = {"metric": metric,
+                "value": n_views_job / (ms / 1e3), "unit": "frames/s" if cid == 4 else "views/s",
                 "n_gpus": world, "steps": steps, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "weak" if cid == 3 else "strong",
-                "dtype": "f32" if cid == 3 else "bf16 slot rows, f32 accumulate", "data": "synthetic (seeded)",
+                "scaling": "strong" if cid == 4 else "weak",
+                "dtype": "bf16 slot rows, f32 accumulate" if cid == 4 else "f32", "data": "synthetic (seeded)",
                 "mpix_s": n_views_job * H * W / 1e6 / (ms / 1e3),
                 "config": {"workload": f"config{cid}", "G": G, "H": H, "W": W, "K": K, "sh_degree": sh,
                            "views_per_rank": len(mine)}, **extra}
@@ -472,9 +513,11 @@ def run_config(args, rank, world, local_rank, cid):
 
 # DRAM bytes of one launch, read from ncu captures of the config-2 train step (the render
 # backward captured on a 4-view launch; its traffic is proportional to the views it renders).
-# The Adam figure under-counts writes that were still in L2 when the kernel ended.
+# The Adam figure under-counts writes that were still in L2 when the kernel ended.  Re-captured
+# whenever those kernels change; the capture is the one TRAFFIC_SOURCE names.
 RENDER_BWD_DRAM_PER_VIEW = (179.8e6 + 34.7e6) / 4
 ADAM_DRAM = 94.4e6 + 15.2e6
+TRAFFIC_SOURCE = "profiles/step_kernels_config2_4views.md (ncu, one launch per kernel, 4-view capture)"
 
 
 def cpu_baseline_sample():
@@ -505,8 +548,8 @@ def main():
     ap.add_argument("--views", type=int, default=CONFIG["views"], help="reduced batch for profiling captures")
     ap.add_argument("--gaussians", type=int, default=CONFIG["G"], help="reduced G for profiling captures")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the end-to-end and render legs (profiling)")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
-                    help="2: the headline train step; 3 / 4: the extra benchmark render configs")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
+                    help="2: the headline train step; 1 / 3 / 4: the other benchmark configs")
     args = ap.parse_args()
     if args.views != CONFIG["views"] or args.gaussians != CONFIG["G"]:
         CONFIG.update(views=args.views, G=args.gaussians,

@@ -333,6 +333,14 @@ int tts_wsr_dense_bwd(const float* theta_u, const float* o, const float* color, 
                       const float* C, const float* den, const float* gC, float* gtheta, float* go,
                       float* gcolor, float* gw_b_partial, void* stream);
 
+/* ---- measurement ----------------------------------------------------------------------------
+ * FP32 FMA-pipe throughput probe (no counterpart in the reference): `blocks` blocks of 256
+ * threads run 8 independent packed fma.rn.f32x2 chains for `iters` rounds and write one float
+ * per thread to out[blocks*256]; tts_fma_probe_flops gives the flops of such a launch.  Timed
+ * by the caller, it is the measured FP32 peak the FP32-bound tile kernels are reported against. */
+long long tts_fma_probe_flops(int blocks, int iters);
+int tts_fma_probe(int blocks, int iters, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

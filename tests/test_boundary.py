@@ -15,7 +15,7 @@ HDR = os.path.join(REPO, "include", "ttsplat_b200.h")
 
 def declared():
     txt = open(HDR).read()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(tts_\w+)\(", txt, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|long long|const char\*)\s+(tts_\w+)\(", txt, re.M)))
 
 
 def test_library_exports_every_declared_symbol(pkg):
@@ -35,7 +35,7 @@ def test_binding_matches_header(pkg):
     assert sorted(_lib.SIGNATURES) == declared()
     txt = open(HDR).read().replace("\n", " ")
     for name, (_, args) in _lib.SIGNATURES.items():
-        m = re.search(rf"(?:int|size_t|char\*|void)\s+\**{name}\(([^)]*)\);", txt)
+        m = re.search(rf"(?:int|size_t|long long|char\*|void)\s+\**{name}\(([^)]*)\);", txt)
         params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(args), name
 

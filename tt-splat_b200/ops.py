@@ -528,3 +528,23 @@ def poly_splat_wgeo(Q, k, keep=None, gout=None):
     out = torch.empty_like(Q)
     call("tts_poly_splat_wgeo", ptr(Q), P, G, float(k), ptr(keep), ptr(gout), ptr(out), dt, stream())
     return out
+
+
+def fp32_peak_tflops(reps=5, iters=4096):
+    """Measured FP32 FMA-pipe peak (TFLOP/s) of the current device: the best of ``reps`` timed
+    launches of the packed-FMA probe kernel (CUDA events on the current stream)."""
+    dev = torch.cuda.current_device()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks = sms * 8
+    out = torch.empty(blocks * 256, device="cuda")
+    flops = lib().tts_fma_probe_flops(blocks, iters)
+    call("tts_fma_probe", blocks, iters, ptr(out), stream())        # warm-up
+    best = 0.0
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call("tts_fma_probe", blocks, iters, ptr(out), stream())
+        e1.record()
+        e1.synchronize()
+        best = max(best, flops / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+    return best
