@@ -9,18 +9,11 @@
 //   k_ssim_fwd : output tile 64x32 of the SSIM map.  Loads the (64+win-1)x(32+win-1) input
 //                halo, filters the five maps x, y, x^2, y^2, xy along rows then columns, and
 //                writes dS/dmu_x, dS/d(filtered x^2), dS/d(filtered xy) plus a per-block
-//                partial of sum(S).  The three dS maps are stored as IEEE half precision (8 B
-//                per position with a pad, half the traffic of fp32): with x, y in [0, 1] they
-//                are bounded by 4 (1/C1 + 1/C2) < 4.5e4, inside the fp16 range, and their
-//                2^-11 relative rounding moves the image gradient by ~5e-5 relative L2 against
-//                the float64 restatement (1e-3 is the gradient bound); S itself, and so the
-//                loss, stays fp32.
+//                partial of sum(S).
 //   k_ssim_bwd : input tile 64x32.  Applies the transposed filter to the three dS maps (zero
 //                outside the valid region), combines them with x and y into the SSIM gradient,
 //                adds the L1 gradient, and writes a per-block partial of sum|x - y|.
 // A one-block-per-view kernel reduces the partials in a fixed order (deterministic).
-#include <cuda_fp16.h>
-
 #include "common.cuh"
 
 namespace tts {
@@ -167,7 +160,7 @@ __global__ void __launch_bounds__(256)
   // columns: item = (column c, segment of RB output rows); lanes walk along columns
   float ssum = 0.f;
   const long long plane = (long long)Ho * Wo;
-  uint2* mbase = reinterpret_cast<uint2*>(maps) + (long long)vc * plane;   // half (M0, M1 | M2, 0) per position
+  float4* mbase = reinterpret_cast<float4*>(maps) + (long long)vc * plane;   // (M0, M1, M2, 0) per position
   for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
     const int c = it % LT_W, r0 = (it / LT_W) * RB;
     const f32x2 z = mk2(0.f, 0.f);
@@ -214,10 +207,9 @@ __global__ void __launch_bounds__(256)
       const float S = (A1 * A2) * iD;
       ssum += S;
       const long long q = (long long)oy * Wo + ox;
-      const __half2 m01 = __floats2half2_rn(2.f * iD * (muy * (A2 - A1) - S * mux * (B2 - B1)),   // dS/dmu_x
-                                            -S * iB2);                                             // dS/d filt(x^2)
-      const __half2 m2 = __floats2half2_rn(2.f * A1 * iD, 0.f);                                  // dS/d filt(xy)
-      mbase[q] = make_uint2(*reinterpret_cast<const unsigned*>(&m01), *reinterpret_cast<const unsigned*>(&m2));
+      mbase[q] = make_float4(2.f * iD * (muy * (A2 - A1) - S * mux * (B2 - B1)),   // dS/dmu_x
+                             -S * iB2,                                             // dS/d filt(x^2)
+                             2.f * A1 * iD, 0.f);                                  // dS/d filt(xy)
     }
   }
 #pragma unroll
@@ -257,7 +249,7 @@ __global__ void __launch_bounds__(256)
     g2[k] = mk2(g[k], g[k]);
   }
   const long long plane = (long long)Ho * Wo;
-  const uint2* mbase = reinterpret_cast<const uint2*>(maps) + (long long)vc * plane;
+  const float4* mbase = reinterpret_cast<const float4*>(maps) + (long long)vc * plane;
   // the image/target values of this thread's epilogue (one column item per thread: LT_W x LT_H/RB
   // = 256 items) are fetched up front, together with the map halo
   static_assert(LT_W * (LT_H / RB) == 256, "one column item per thread");
@@ -291,11 +283,10 @@ __global__ void __launch_bounds__(256)
         dv[k] = 0.f;
         if (colok && r < LG::IH && my >= 0 && my < Ho) {
           const long long q = (long long)my * Wo + mx;
-          const uint2 mm = __ldg(mbase + q);
-          const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&mm.x));
-          av[k] = f01.x;
-          bv[k] = f01.y;
-          dv[k] = __low2float(*reinterpret_cast<const __half2*>(&mm.y));
+          const float4 mm = __ldg(mbase + q);
+          av[k] = mm.x;
+          bv[k] = mm.y;
+          dv[k] = mm.z;
         }
       }
 #pragma unroll
@@ -527,7 +518,7 @@ using namespace tts;
 extern "C" size_t tts_loss_workspace_bytes(int V, int H, int W) {
   if (V < 1 || H < 3 || W < 3) return 0;
   const LossGeom lg = loss_geom(H, W);
-  return a256((size_t)V * 3 * lg.Ho * lg.Wo * 8) + a256((size_t)V * 3 * lg.fbx * lg.fby * 4) +
+  return a256((size_t)V * 12 * lg.Ho * lg.Wo * 4) + a256((size_t)V * 3 * lg.fbx * lg.fby * 4) +
          a256((size_t)V * 3 * lg.bbx * lg.bby * 4) + 256;   // + the reduce counter
 }
 
@@ -542,7 +533,7 @@ extern "C" int tts_loss_l1_ssim(const float* img, const float* target, int V, in
   const LossGeom lg = loss_geom(H, W);
   char* p = static_cast<char*>(workspace);
   float* maps = reinterpret_cast<float*>(p);
-  p += a256((size_t)V * 3 * lg.Ho * lg.Wo * 8);
+  p += a256((size_t)V * 12 * lg.Ho * lg.Wo * 4);
   float* spart = reinterpret_cast<float*>(p);
   p += a256((size_t)V * 3 * lg.fbx * lg.fby * 4);
   float* lpart = reinterpret_cast<float*>(p);
