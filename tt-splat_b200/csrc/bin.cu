@@ -162,78 +162,58 @@ __device__ __forceinline__ u64 make_key(int j, float4 r, float ctx, float cty) {
 // Writes the outputs of one tile from its sorted keys (threads first, first+step, ... of the
 // caller's group): idx/count/cand, the stencil-indexed inverse table and, with PACK, the slot
 // rows theta_u (tools/m4_train_binned.py:130-143, the reference's fp32 op order) | color_o | keo.
-// A thread handles BATCH of its slots at a time: their projection rows are all requested before
-// the first is used, so a tile's epilogue costs one round trip to L2 per batch (the warp kernel
-// batches 4 of a lane's K/32 slots; the block kernel's threads own one slot each).
-
 template <int PACK>
-__device__ __forceinline__ void emit_slot(const float4& p0, const float4& p1, const float4& p2, float ox, float oy,
-                                          float inv_k, long long o, void* __restrict__ slots) {
-  const float mux = __fsub_rn(p0.x, ox), muy = __fsub_rn(p0.y, oy);
-  const float a = p0.z, b = p0.w, c = p1.x;
-  const float Q = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(a, mux), mux), __fmul_rn(__fmul_rn(__fmul_rn(2.0f, b), mux), muy)),
-                            __fmul_rn(__fmul_rn(c, muy), muy));
-  const float th[6] = {__fmul_rn(-a, inv_k), __fmul_rn(-c, inv_k), __fmul_rn(__fmul_rn(-2.0f, b), inv_k),
-                       __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(a, mux), __fmul_rn(b, muy))), inv_k),
-                       __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(b, mux), __fmul_rn(c, muy))), inv_k),
-                       __fsub_rn(1.0f, __fmul_rn(Q, inv_k))};
-  if (PACK == 1) {
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(slots) + o * TTS_SLOT_FLOATS);
-    dst[0] = make_float4(th[0], th[1], th[2], th[3]);
-    dst[1] = make_float4(th[4], th[5], p1.y, p1.z);
-    dst[2] = make_float4(p1.w, p2.x, 0.f, 0.f);
-  } else {
-    // compact bf16 row: theta_u as a bf16 (hi, lo) pair (hi + lo carries ~16 significant bits,
-    // which u = Phi.theta needs), colour_o and o_col as bf16
-    __nv_bfloat16 r[16];
-#pragma unroll
-    for (int q = 0; q < 6; ++q) {
-      r[q] = __float2bfloat16_rn(th[q]);
-      r[6 + q] = __float2bfloat16_rn(__fsub_rn(th[q], __bfloat162float(r[q])));
-    }
-    r[12] = __float2bfloat16_rn(p1.y);
-    r[13] = __float2bfloat16_rn(p1.z);
-    r[14] = __float2bfloat16_rn(p1.w);
-    r[15] = __float2bfloat16_rn(p2.x);
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(slots) + o * TTS_SLOT_BF16);
-    dst[0] = *reinterpret_cast<const uint4*>(&r[0]);
-    dst[1] = *reinterpret_cast<const uint4*>(&r[8]);
-  }
-}
-
-template <int PACK, int BATCH>
 __device__ __forceinline__ void emit_tile(const u64* keys, int n, int v, int t, int ntx, int T, int G, int S, int K,
                                           const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
                                           int* __restrict__ inv, void* __restrict__ slots, int first, int step) {
   const int cnt = min(n, K);
   const int tx = t % ntx, ty = t / ntx;
   const float ox = (float)(tx * 16), oy = (float)(ty * 16);
-  const long long row0 = ((long long)v * T + t) * K;
-  for (int k0 = first; k0 < K; k0 += BATCH * step) {
-    int g[BATCH];
-    float4 p0[BATCH], p1[BATCH], p2[BATCH];
+  for (int k = first; k < K; k += step) {
+    const long long o = ((long long)v * T + t) * K + k;
+    if (k < cnt) {
+      const u64 key = keys[k];
+      const int g = (int)(unsigned)(key & 0xffffffffull);
+      const int j = (int)((key >> 32) & 0xffull);
+      idx[o] = g;
+      if (inv) inv[((long long)v * G + g) * S + j] = t * K + k;
+      if (PACK) {
+        const float4* p = reinterpret_cast<const float4*>(proj + ((long long)v * G + g) * TTS_PROJ_FLOATS);
+        const float4 p0 = p[0], p1 = p[1], p2 = p[2];
+        const float mux = __fsub_rn(p0.x, ox), muy = __fsub_rn(p0.y, oy);
+        const float a = p0.z, b = p0.w, c = p1.x;
+        const float Q = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(a, mux), mux),
+                                            __fmul_rn(__fmul_rn(__fmul_rn(2.0f, b), mux), muy)),
+                                  __fmul_rn(__fmul_rn(c, muy), muy));
+        const float th[6] = {__fmul_rn(-a, inv_k), __fmul_rn(-c, inv_k), __fmul_rn(__fmul_rn(-2.0f, b), inv_k),
+                             __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(a, mux), __fmul_rn(b, muy))), inv_k),
+                             __fmul_rn(__fmul_rn(2.0f, __fadd_rn(__fmul_rn(b, mux), __fmul_rn(c, muy))), inv_k),
+                             __fsub_rn(1.0f, __fmul_rn(Q, inv_k))};
+        if (PACK == 1) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(slots) + o * TTS_SLOT_FLOATS);
+          dst[0] = make_float4(th[0], th[1], th[2], th[3]);
+          dst[1] = make_float4(th[4], th[5], p1.y, p1.z);
+          dst[2] = make_float4(p1.w, p2.x, 0.f, 0.f);
+        } else {
+          // compact bf16 row: theta_u as a bf16 (hi, lo) pair (hi + lo carries ~16 significant
+          // bits, which u = Phi.theta needs), colour_o and o_col as bf16
+          __nv_bfloat16 r[16];
 #pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int k = k0 + u * step;
-      g[u] = -1;
-      if (k < cnt) {
-        const u64 key = keys[k];
-        g[u] = (int)(unsigned)(key & 0xffffffffull);
-        const int j = (int)((key >> 32) & 0xffull);
-        if (inv) inv[((long long)v * G + g[u]) * S + j] = t * K + k;
-        if (PACK) {
-          const float4* p = reinterpret_cast<const float4*>(proj + ((long long)v * G + g[u]) * TTS_PROJ_FLOATS);
-          p0[u] = p[0];
-          p1[u] = p[1];
-          p2[u] = p[2];
+          for (int q = 0; q < 6; ++q) {
+            r[q] = __float2bfloat16_rn(th[q]);
+            r[6 + q] = __float2bfloat16_rn(__fsub_rn(th[q], __bfloat162float(r[q])));
+          }
+          r[12] = __float2bfloat16_rn(p1.y);
+          r[13] = __float2bfloat16_rn(p1.z);
+          r[14] = __float2bfloat16_rn(p1.w);
+          r[15] = __float2bfloat16_rn(p2.x);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(slots) + o * TTS_SLOT_BF16);
+          dst[0] = *reinterpret_cast<const uint4*>(&r[0]);
+          dst[1] = *reinterpret_cast<const uint4*>(&r[8]);
         }
       }
-      if (k < K) idx[row0 + k] = g[u];
-    }
-    if (PACK) {
-#pragma unroll
-      for (int u = 0; u < BATCH; ++u)
-        if (g[u] >= 0) emit_slot<PACK>(p0[u], p1[u], p2[u], ox, oy, inv_k, row0 + k0 + u * step, slots);
+    } else {
+      idx[o] = -1;
     }
   }
 }
@@ -327,7 +307,7 @@ __device__ __forceinline__ void sort_front(u64* keys, int m, int lane) {
   }
 }
 
-constexpr int KG_UNROLL = 8;   // candidate records in flight per lane during key generation
+constexpr int KG_UNROLL = 4;   // candidate records in flight per lane during key generation
 
 // One warp per tile for tiles with at most WCAP candidates (tiles with more are appended to the
 // overflow list for the block kernel).  Keys in per-warp shared memory; when n > K a two-level
@@ -494,7 +474,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
     }
   }
   if (m >= 0 && (m > WCAP / 2 || !bucket_sort(buf, m, lane, hist, wstart[warp]))) sort_front(buf, m, lane);
-  emit_tile<PACK, 4>(buf, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
+  emit_tile<PACK>(buf, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
   if (lane == 0) {
     count[(long long)v * T + t] = min(n, K);
     cand[(long long)v * T + t] = n;
@@ -653,7 +633,7 @@ __global__ void __launch_bounds__(BS_THREADS)
   __syncthreads();
   bitonic_sort(skeys, P);
 
-  emit_tile<PACK, 1>(skeys, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, tid, BS_THREADS);
+  emit_tile<PACK>(skeys, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, tid, BS_THREADS);
   if (tid == 0) {
     count[(long long)v * T + t] = min(n, K);
     cand[(long long)v * T + t] = n;
@@ -799,7 +779,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
   }
   __syncwarp();
   if (lane == 0) count[gt] = n;
-  emit_tile<1, 4>(keys[warp], n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
+  emit_tile<1>(keys[warp], n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
 }
 
 }  // namespace tts
