@@ -190,7 +190,7 @@ def run_ours(args, rank, world, local_rank):
     pg = dist.group.WORLD if world > 1 else None
     st = train.TrainStep(m, cams, list(targets_host), sh_degree=3, lr={"means": 1.6e-4}, K=CONFIG["K"], R=CONFIG["R"],
                          noise_lr=5e5, relocate_every=1, dead_frac=0.01, offset=0.005, lambda_o=0.01, lambda_s=0.01,
-                         seed=1234, n_views_total=V, process_group=pg)
+                         seed=1234, n_views_total=V, process_group=pg, exchange=args.exchange)
 
     def barrier():
         if world > 1:
@@ -548,6 +548,8 @@ def main():
     ap.add_argument("--views", type=int, default=CONFIG["views"], help="reduced batch for profiling captures")
     ap.add_argument("--gaussians", type=int, default=CONFIG["G"], help="reduced G for profiling captures")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the end-to-end and render legs (profiling)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: gradient exchange over NVLink peer memory (default) or an NCCL all-reduce")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
                     help="2: the headline train step; 1 / 3 / 4: the other benchmark configs")
     args = ap.parse_args()
