@@ -333,6 +333,12 @@ int tts_wsr_dense_bwd(const float* theta_u, const float* o, const float* color, 
                       const float* C, const float* den, const float* gC, float* gtheta, float* go,
                       float* gcolor, float* gw_b_partial, void* stream);
 
+/* ---- 8-bit target images ------------------------------------------------------------------
+ * dst[i] = src[i] / 255 (correctly rounded, = numpy's float32(x) / float32(255)): the [0, 1]
+ * floats of 8-bit images as spike/data.py produces them, expanded on the device so that a train
+ * step uploads and holds its targets as uint8.  src 4-byte aligned, dst 16-byte aligned. */
+int tts_unit_from_u8(const uint8_t* src, long long n, float* dst, void* stream);
+
 /* ---- measurement ----------------------------------------------------------------------------
  * FP32 FMA-pipe throughput probe (no counterpart in the reference): `blocks` blocks of 256
  * threads run 8 independent packed fma.rn.f32x2 chains for `iters` rounds and write one float

@@ -111,3 +111,23 @@ def test_training_reduces_loss(pkg):
     hist, moved = mcmc.train_mcmc(m, cams, gts, iters=120, relocate_every=40, noise_lr=50.0, sh_degree=3)
     assert hist[-1] < 0.7 * hist[0], (hist[0], hist[-1])
     assert moved >= 0
+
+
+def test_uint8_targets_equal_float_targets(pkg):
+    """A train step given 8-bit targets (expanded on the device to x / 255, correctly rounded)
+    takes bit-identical steps to one given the float targets numpy computes from them."""
+    from tt_splat_b200 import camera, model, ops, train
+    sc = pkg.synthetic.config2(seed=6, G=2000, H=48, W=64, n_views=2)
+    u8 = torch.from_numpy(np.stack(sc["targets_u8"])).to(DEV)
+    f = ops.unit_from_u8(u8)
+    assert torch.equal(f.cpu(), torch.from_numpy(np.stack(sc["targets"])))
+    cams = [camera.Camera.from_dict(c) for c in sc["cams"]]
+    kw = dict(sh_degree=3, noise_lr=5e5, relocate_every=2, dead_frac=0.01, offset=0.005, seed=2)
+    m1 = model.GaussianModel.from_arrays(sc["params"], device=DEV)
+    m2 = model.GaussianModel.from_arrays(sc["params"], device=DEV)
+    a = train.TrainStep(m1, cams, sc["targets_u8"], **kw)
+    b = train.TrainStep(m2, cams, sc["targets"], **kw)
+    assert a.targets_u8 is not None and b.targets_u8 is None
+    for _ in range(4):
+        assert torch.equal(a.step(), b.step())
+    assert torch.equal(m1.flat, m2.flat)

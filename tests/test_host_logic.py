@@ -170,3 +170,13 @@ def test_camera_conventions(pkg):
     c2w[:3, 3] = torch.tensor([0.0, 0.0, 4.0])           # OpenGL camera at +4z looking down -z
     Rv, tv = camera.opengl_c2w_to_opencv_w2c(c2w)
     assert torch.equal(Rv, torch.diag(torch.tensor([1.0, -1.0, -1.0]))) and torch.equal(tv, torch.tensor([0.0, 0.0, 4.0]))
+
+
+def test_config2_targets_are_8bit(pkg):
+    """The headline scene's targets are 8-bit images: the float targets are exactly x / 255 of
+    the uint8 ones (what the train step computes on the device from the uploaded bytes)."""
+    import numpy as np
+    sc = pkg.synthetic.config2(G=500, H=32, W=48, n_views=2)
+    for f, u in zip(sc["targets"], sc["targets_u8"]):
+        assert u.dtype == np.uint8 and f.dtype == np.float32
+        assert np.array_equal(f, u.astype(np.float32) / np.float32(255.0))

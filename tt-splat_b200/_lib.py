@@ -78,6 +78,7 @@ SIGNATURES = {
     "tts_phi_theta": (I, [P, P, LL, LL, P, I, P]),
     "tts_phi_theta_bwd": (I, [P, P, P, LL, LL, P, P, P, SZ, I, P]),
     "tts_poly_splat_wgeo": (I, [P, LL, LL, D, P, P, P, I, P]),
+    "tts_unit_from_u8": (I, [P, LL, P, P]),
     "tts_fma_probe_flops": (LL, [I, I]),
     "tts_fma_probe": (I, [I, I, P, P]),
     "tts_wsr_dense_fwd": (I, [P, P, P, P, P, P, P, I, I, P, P, P]),

@@ -302,6 +302,17 @@ def wsr_dense_bwd(theta_u, o, color, w_b, Phi, c_b, keep, C, den, gC):
     return gth, go, gcol, gwb
 
 
+def unit_from_u8(src, out=None):
+    """uint8 images -> float32 x / 255 (correctly rounded), same shape, on the device."""
+    _dev(src, out)
+    if src.dtype != torch.uint8:
+        raise TypeError("unit_from_u8 takes a uint8 tensor")
+    if out is None:
+        out = torch.empty(src.shape, dtype=torch.float32, device=src.device)
+    call("tts_unit_from_u8", ptr(src), src.numel(), ptr(out), stream())
+    return out
+
+
 def read_status():
     """Read and clear the device status word (bounded waits that gave up); synchronous."""
     import ctypes

@@ -119,7 +119,9 @@ def ring_cameras(rng, n, H, W, radius=4.0, max_elev=0.35):
 
 def config2(seed=2, G=100000, H=832, W=1264, n_views=8):
     """Config 2 (the headline train step): G=100k uniform in [-1,1]^3, SH deg 3, 8 cameras on a
-    radius-4 ring at seeded elevations, 1264x832 images, K=128, seeded U[0,1] targets."""
+    radius-4 ring at seeded elevations, 1264x832 images, K=128, seeded 8-bit target images
+    (uniform over 0..255; ``targets_u8`` as drawn, ``targets`` = float32(x) / 255, the [0, 1]
+    floats the dataset loaders make of 8-bit frames)."""
     rng = np.random.default_rng(seed)
     means = rng.uniform(-1, 1, (G, 3)).astype(np.float32)
     ls = (-3.5 + 0.3 * rng.standard_normal((G, 3))).astype(np.float32)
@@ -128,9 +130,10 @@ def config2(seed=2, G=100000, H=832, W=1264, n_views=8):
     rgb = rng.uniform(0, 1, (G, 3)).astype(np.float32)
     rest = (0.1 * rng.standard_normal((G, 15, 3))).astype(np.float32)
     cams = ring_cameras(rng, n_views, H, W)
-    targets = [rng.uniform(0, 1, (H, W, 3)).astype(np.float32) for _ in range(n_views)]
+    targets_u8 = [rng.integers(0, 256, (H, W, 3), dtype=np.uint8) for _ in range(n_views)]
+    targets = [t.astype(np.float32) / np.float32(255.0) for t in targets_u8]
     return dict(params=_params(means, ls, q, op, rgb, rest), sh_degree=3, cams=cams,
-                targets=targets, K=128, R=1)
+                targets=targets, targets_u8=targets_u8, K=128, R=1)
 
 
 def config3(seed=3, G=1000000, H=1072, W=1920, n_views=1):
