@@ -163,6 +163,12 @@ size_t tts_loss_workspace_bytes(int V, int H, int W);
 int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W, float lambda,
                      float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
                      size_t workspace_bytes, void* stream);
+/* The same loss with 8-bit target images (uint8 [V][H][W][3], read as x / 255 correctly rounded:
+ * bit-identical to tts_loss_l1_ssim on the float targets numpy's float32(x) / float32(255)
+ * gives), so a train step can hold and upload its targets as bytes. */
+int tts_loss_l1_ssim_u8(const float* img, const uint8_t* target, int V, int H, int W, float lambda,
+                        float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
+                        size_t workspace_bytes, void* stream);
 
 /* ---- slot -> gaussian reduction + geometry/SH/activation backward ------------------------
  * Replaces the index_add of tools/operands_manual.py:94-98 (= build_inv/gather_reduce,
