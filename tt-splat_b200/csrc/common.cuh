@@ -145,6 +145,17 @@ __device__ __forceinline__ U4 philox4x32_10(U4 ctr, uint32_t k0, uint32_t k1) {
   }
   return ctr;
 }
+// x / 255 for a byte x, correctly rounded (the [0, 1] float of an 8-bit pixel, equal to numpy's
+// float32(x) / float32(255)): the product with fp32(1/255) and one Newton-style correction through
+// the exact fma residual, which an exhaustive check over the 256 bytes shows to round correctly
+// (the product alone is off by one ulp for 126 of them).
+__device__ __forceinline__ float unit_from_byte(unsigned x) {
+  const float xf = (float)x, r = 1.0f / 255.0f;
+  const float q = __fmul_rn(xf, r);
+  const float e = __fmaf_rn(-q, 255.0f, xf);
+  return __fmaf_rn(e, r, q);
+}
+
 // Uniform in (0, 1] from 32 random bits (never 0, so log() is finite).
 __device__ __forceinline__ float u01(uint32_t b) { return (float)(b >> 8) * (1.0f / 16777216.0f) + (0.5f / 16777216.0f); }
 // Uniform in [0, 1).

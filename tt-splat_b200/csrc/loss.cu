@@ -33,9 +33,7 @@ constexpr float SSIM_C1 = 0.01f * 0.01f, SSIM_C2 = 0.03f * 0.03f;
 // Target pixels are fp32, or 8-bit images read as x / 255 (correctly rounded: the same floats
 // as numpy's float32(x) / float32(255), so both forms give bit-identical losses and gradients).
 __device__ __forceinline__ float load_target(const float* t, long long q) { return __ldg(t + q); }
-__device__ __forceinline__ float load_target(const uint8_t* t, long long q) {
-  return __fdiv_rn((float)__ldg(t + q), 255.f);
-}
+__device__ __forceinline__ float load_target(const uint8_t* t, long long q) { return unit_from_byte(__ldg(t + q)); }
 
 struct Window {
   float g[LWIN_MAX];

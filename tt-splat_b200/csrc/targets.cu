@@ -10,14 +10,13 @@ __global__ void __launch_bounds__(256) k_unit_from_u8(const uchar4* __restrict__
                                                       float4* __restrict__ dst) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     const uchar4 b = src[i];
-    dst[i] = make_float4(__fdiv_rn((float)b.x, 255.f), __fdiv_rn((float)b.y, 255.f), __fdiv_rn((float)b.z, 255.f),
-                         __fdiv_rn((float)b.w, 255.f));
+    dst[i] = make_float4(unit_from_byte(b.x), unit_from_byte(b.y), unit_from_byte(b.z), unit_from_byte(b.w));
   }
 }
 
 __global__ void k_unit_from_u8_tail(const uint8_t* __restrict__ src, long long beg, long long n, float* __restrict__ dst) {
   const long long i = beg + threadIdx.x;
-  if (i < n) dst[i] = __fdiv_rn((float)src[i], 255.f);
+  if (i < n) dst[i] = unit_from_byte(src[i]);
 }
 
 }  // namespace tts
