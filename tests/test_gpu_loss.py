@@ -64,8 +64,6 @@ def test_loss_u8_targets_equal_float_targets(lam, pkg):
 def test_unit_from_u8_is_correctly_rounded(pkg):
     """Every byte x expands to numpy's float32(x) / float32(255) exactly."""
     from tt_splat_b200 import ops
-    u = torch.arange(256, dtype=torch.uint8).repeat(5)[:1023].to(DEV)       # odd length: the tail path
-    ref = np.arange(256, dtype=np.float32).repeat(1)
-    out = ops.unit_from_u8(u).cpu().numpy()
-    assert np.array_equal(out, (np.tile(np.arange(256), 5)[:1023].astype(np.float32) / np.float32(255.0)))
-    assert ref.size == 256
+    bytes_ = np.tile(np.arange(256), 5)[:1023].astype(np.uint8)            # 1023: the tail path too
+    out = ops.unit_from_u8(torch.from_numpy(bytes_).to(DEV)).cpu().numpy()
+    assert np.array_equal(out, bytes_.astype(np.float32) / np.float32(255.0))
