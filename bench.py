@@ -134,7 +134,7 @@ def stage_times(st, torch, reps=3):
     """Per-stage device times of one eager step (CUDA events on the launching stream, the stages
     queued behind a device-side spin so that host launch latency is excluded)."""
     from tt_splat_b200 import ops
-    names = ["step_begin", "project", "bin_pack", "render_fwd", "loss", "render_bwd", "backward_params", "adam", "sgld",
+    names = ["targets_u8", "project", "bin_pack", "render_fwd", "loss", "render_bwd", "backward_params", "adam", "sgld",
              "relocate"]
     acc = {n: [] for n in names}
     G, H, W, R, K = st.G, st.H, st.W, st.R, st.K
@@ -145,6 +145,8 @@ def stage_times(st, torch, reps=3):
         torch.cuda._sleep(4_000_000)
         ev[0].record()
         ops.step_begin(st.step_t)
+        if st.targets_u8 is not None:
+            ops.unit_from_u8(st.targets_u8, out=st.targets)
         ev[1].record()
         ops.project(st.flat, G, st.sh_degree, st.cams_t, H, W, st.blur, st.near, out=st.pj)
         ev[2].record()
@@ -152,7 +154,7 @@ def stage_times(st, torch, reps=3):
         ev[3].record()
         ops.render_fwd(st.bp["slots"], st.bp["count"], H, W, st.flat[59 * G:], st.model.c_b, out=st.rf)
         ev[4].record()
-        ops.loss_l1_ssim(st.rf["img"], st.loss_targets, st.lam, st.grad_scale, ws=st.ws_loss, out=st.lo)
+        ops.loss_l1_ssim(st.rf["img"], st.targets, st.lam, st.grad_scale, ws=st.ws_loss, out=st.lo)
         ev[5].record()
         ops.render_bwd(st.bp["slots"], st.bp["count"], H, W, st.model.c_b, st.rf["img"], st.rf["den"],
                        st.lo["gimg"], out=st.rb)

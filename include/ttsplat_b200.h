@@ -163,12 +163,6 @@ size_t tts_loss_workspace_bytes(int V, int H, int W);
 int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W, float lambda,
                      float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
                      size_t workspace_bytes, void* stream);
-/* The same loss with 8-bit target images (uint8 [V][H][W][3], read as x / 255 correctly rounded:
- * bit-identical to tts_loss_l1_ssim on the float targets numpy's float32(x) / float32(255)
- * gives), so a train step can hold and upload its targets as bytes. */
-int tts_loss_l1_ssim_u8(const float* img, const uint8_t* target, int V, int H, int W, float lambda,
-                        float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
-                        size_t workspace_bytes, void* stream);
 
 /* ---- slot -> gaussian reduction + geometry/SH/activation backward ------------------------
  * Replaces the index_add of tools/operands_manual.py:94-98 (= build_inv/gather_reduce,
@@ -342,7 +336,7 @@ int tts_wsr_dense_bwd(const float* theta_u, const float* o, const float* color, 
 /* ---- 8-bit target images ------------------------------------------------------------------
  * dst[i] = src[i] / 255 (correctly rounded, = numpy's float32(x) / float32(255)): the [0, 1]
  * floats of 8-bit images as spike/data.py produces them, expanded on the device so that a train
- * step uploads and holds its targets as uint8.  src 4-byte aligned, dst 16-byte aligned. */
+ * step uploads and holds its targets as uint8.  src and dst 16-byte aligned. */
 int tts_unit_from_u8(const uint8_t* src, long long n, float* dst, void* stream);
 
 /* ---- measurement ----------------------------------------------------------------------------

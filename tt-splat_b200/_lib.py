@@ -40,7 +40,6 @@ SIGNATURES = {
     "tts_render_bwd_rv": (I, [P, P, I, I, I, I, P, P, P, P, P, P, P]),
     "tts_loss_workspace_bytes": (SZ, [I, I, I]),
     "tts_loss_l1_ssim": (I, [P, P, I, I, I, F, F, P, P, P, P, SZ, P]),
-    "tts_loss_l1_ssim_u8": (I, [P, P, I, I, I, F, F, P, P, P, P, SZ, P]),
     "tts_backward_workspace_bytes": (SZ, [I, I]),
     "tts_backward_params": (I, [P, I, I, P, I, I, I, I, I, F, F, F, P, P, P, P, F, F, P, P, P, P, SZ, P]),
     "tts_adam_sgld": (I, [P, P, P, P, I, I, P, P, D, D, D, F, P, U64, P]),

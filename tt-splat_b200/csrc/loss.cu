@@ -30,11 +30,6 @@ __device__ __forceinline__ void row_seg(int s, int& c0, int& width) {
 }
 constexpr float SSIM_C1 = 0.01f * 0.01f, SSIM_C2 = 0.03f * 0.03f;
 
-// Target pixels are fp32, or 8-bit images read as x / 255 (correctly rounded: the same floats
-// as numpy's float32(x) / float32(255), so both forms give bit-identical losses and gradients).
-__device__ __forceinline__ float load_target(const float* t, long long q) { return __ldg(t + q); }
-__device__ __forceinline__ float load_target(const uint8_t* t, long long q) { return unit_from_byte(__ldg(t + q)); }
-
 struct Window {
   float g[LWIN_MAX];
   int win;
@@ -67,9 +62,9 @@ __device__ __forceinline__ TileId decode_tile(int tile, int gx, int gy) {
 
 // Packed f32x2 arithmetic on (x, y) and (x^2, y^2): the five filtered maps cost two .f32x2 FMAs
 // and one scalar FMA per tap instead of five FMAs.
-template <int WIN, typename TT>
+template <int WIN>
 __global__ void __launch_bounds__(256)
-    k_ssim_fwd(const float* __restrict__ img, const TT* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
+    k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
                float* __restrict__ maps, float* __restrict__ part, unsigned* __restrict__ reduce_counter) {
   using LG = LGeom<WIN>;
   extern __shared__ float smem[];
@@ -108,7 +103,7 @@ __global__ void __launch_bounds__(256)
         if (r < LG::IH && yy < H && xx < W) {
           const long long q = (col + (long long)yy * W) * 3 + id.ch;
           xv[k] = __ldg(img + q);
-          yv[k] = load_target(tgt, q);
+          yv[k] = __ldg(tgt + q);
         }
       }
 #pragma unroll
@@ -229,9 +224,9 @@ __global__ void __launch_bounds__(256)
 }
 
 // Transposed filter of (dS/dmu_x, dS/d filt(x^2)) as one .f32x2 pair and dS/d filt(xy) alone.
-template <int WIN, typename TT>
+template <int WIN>
 __global__ void __launch_bounds__(256)
-    k_ssim_bwd(const float* __restrict__ img, const TT* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
+    k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
                float lambda, float grad_scale, const float* __restrict__ maps, float* __restrict__ gimg,
                float* __restrict__ part) {
   using LG = LGeom<WIN>;
@@ -268,7 +263,7 @@ __global__ void __launch_bounds__(256)
     if (yy < H && xx < W) {
       const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
       ximg[o] = __ldg(img + q);
-      xtgt[o] = load_target(tgt, q);
+      xtgt[o] = __ldg(tgt + q);
     }
   }
   {
@@ -397,16 +392,15 @@ __global__ void __launch_bounds__(256)
 
 // lambda == 0 (the L1 loss alone, spike/metrics.py:22-23 / loss_fn with lambda_ssim = 0): the
 // L1 gradient grad_scale * sign(x - y) / N and a per-block partial of sum|x - y|, no SSIM pass.
-template <typename TT>
 __global__ void __launch_bounds__(256)
-    k_l1_only(const float* __restrict__ img, const TT* __restrict__ tgt, long long n_per_view, int blocks_per_view,
+    k_l1_only(const float* __restrict__ img, const float* __restrict__ tgt, long long n_per_view, int blocks_per_view,
               float gscale, float* __restrict__ gimg, float* __restrict__ part) {
   __shared__ float red[8];
   const int v = blockIdx.x / blocks_per_view, b = blockIdx.x % blocks_per_view;
   const long long base = (long long)v * n_per_view;
   float l1 = 0.f;
   for (long long i = (long long)b * 256 + threadIdx.x; i < n_per_view; i += (long long)blocks_per_view * 256) {
-    const float d = img[base + i] - load_target(tgt, base + i);
+    const float d = img[base + i] - tgt[base + i];
     l1 += fabsf(d);
     gimg[base + i] = gscale * (d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f));
   }
@@ -497,8 +491,8 @@ static LossGeom loss_geom(int H, int W) {
   return lg;
 }
 
-template <int WIN, typename TT>
-static int launch_loss(const float* img, const TT* target, int V, int H, int W, float lambda, float grad_scale,
+template <int WIN>
+static int launch_loss(const float* img, const float* target, int V, int H, int W, float lambda, float grad_scale,
                        const Window& wd, const LossGeom& lg, float* maps, float* spart, float* lpart, float* gimg,
                        unsigned* counter, cudaStream_t st) {
   using LG = LGeom<WIN>;
@@ -506,13 +500,13 @@ static int launch_loss(const float* img, const TT* target, int V, int H, int W, 
   const size_t bsm = (size_t)(LG::IH * LG::XS * 3 + (LG::IH * LG::XS & 1) + LG::IH * LG::HS * 3) * 4;
   static std::atomic<unsigned long long> attr_done{0};
   once_per_device(attr_done, [&] {
-    cudaFuncSetAttribute(k_ssim_fwd<WIN, TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
-    cudaFuncSetAttribute(k_ssim_bwd<WIN, TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
+    cudaFuncSetAttribute(k_ssim_fwd<WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsm);
+    cudaFuncSetAttribute(k_ssim_bwd<WIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
   });
-  k_ssim_fwd<WIN, TT><<<(unsigned)(V * 3 * lg.fbx * lg.fby), 256, fsm, st>>>(img, target, H, W, lg.fbx, lg.fby, wd, maps,
+  k_ssim_fwd<WIN><<<(unsigned)(V * 3 * lg.fbx * lg.fby), 256, fsm, st>>>(img, target, H, W, lg.fbx, lg.fby, wd, maps,
                                                                         spart, counter);
   if (int rc = check_launch("ssim_fwd")) return rc;
-  k_ssim_bwd<WIN, TT><<<(unsigned)(V * 3 * lg.bbx * lg.bby), 256, bsm, st>>>(img, target, H, W, lg.bbx, lg.bby, wd, lambda,
+  k_ssim_bwd<WIN><<<(unsigned)(V * 3 * lg.bbx * lg.bby), 256, bsm, st>>>(img, target, H, W, lg.bbx, lg.bby, wd, lambda,
                                                                         grad_scale, maps, gimg, lpart);
   return check_launch("ssim_bwd");
 }
@@ -528,10 +522,9 @@ extern "C" size_t tts_loss_workspace_bytes(int V, int H, int W) {
          a256((size_t)V * 3 * lg.bbx * lg.bby * 4) + 256;   // + the reduce counter
 }
 
-template <typename TT>
-static int loss_l1_ssim(const float* img, const TT* target, int V, int H, int W, float lambda, float grad_scale,
-                        float* gimg, float* loss, float* loss_sum, void* workspace, size_t workspace_bytes,
-                        void* stream) {
+extern "C" int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W, float lambda,
+                                float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
+                                size_t workspace_bytes, void* stream) {
   TTS_REQUIRE(V >= 1 && H >= 3 && W >= 3, "images must be at least 3x3");
   TTS_REQUIRE(img && target && gimg && loss && workspace, "null pointer");
   if (workspace_bytes < tts_loss_workspace_bytes(V, H, W)) return fail(TTS_ERR_CAPACITY, "loss workspace too small");
@@ -553,7 +546,7 @@ static int loss_l1_ssim(const float* img, const TT* target, int V, int H, int W,
     const long long want = (npv + 255) / 256 < cap ? (npv + 255) / 256 : cap;
     const int bpv = (int)((want + 2) / 3 * 3);                         // a multiple of 3, <= cap
     if (cudaMemsetAsync(counter, 0, sizeof(unsigned), st) != cudaSuccess) return check_launch("memset loss counter");
-    k_l1_only<TT><<<(unsigned)(V * bpv), 256, 0, st>>>(img, target, npv, bpv, (float)((double)grad_scale / (double)npv),
+    k_l1_only<<<(unsigned)(V * bpv), 256, 0, st>>>(img, target, npv, bpv, (float)((double)grad_scale / (double)npv),
                                                    gimg, lpart);
     if (int rc = check_launch("l1_only")) return rc;
     k_loss_reduce<<<V, 256, 0, st>>>(spart, 0, lpart, bpv / 3, H, W, lg.win, lambda, loss, loss_sum, counter);
@@ -561,28 +554,14 @@ static int loss_l1_ssim(const float* img, const TT* target, int V, int H, int W,
   }
   int rc;
   switch (wd.win) {
-    case 3: rc = launch_loss<3, TT>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
-    case 5: rc = launch_loss<5, TT>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
-    case 7: rc = launch_loss<7, TT>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
-    case 9: rc = launch_loss<9, TT>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
-    default: rc = launch_loss<11, TT>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    case 3: rc = launch_loss<3>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    case 5: rc = launch_loss<5>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    case 7: rc = launch_loss<7>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    case 9: rc = launch_loss<9>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
+    default: rc = launch_loss<11>(img, target, V, H, W, lambda, grad_scale, wd, lg, maps, spart, lpart, gimg, counter, st); break;
   }
   if (rc) return rc;
   k_loss_reduce<<<V, 256, 0, st>>>(spart, lg.fbx * lg.fby, lpart, lg.bbx * lg.bby, H, W, lg.win, lambda, loss,
                                    loss_sum, counter);
   return check_launch("loss_reduce");
-}
-
-extern "C" int tts_loss_l1_ssim(const float* img, const float* target, int V, int H, int W, float lambda,
-                                float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
-                                size_t workspace_bytes, void* stream) {
-  return loss_l1_ssim(img, target, V, H, W, lambda, grad_scale, gimg, loss, loss_sum, workspace, workspace_bytes,
-                      stream);
-}
-
-extern "C" int tts_loss_l1_ssim_u8(const float* img, const uint8_t* target, int V, int H, int W, float lambda,
-                                   float grad_scale, float* gimg, float* loss, float* loss_sum, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
-  return loss_l1_ssim(img, target, V, H, W, lambda, grad_scale, gimg, loss, loss_sum, workspace, workspace_bytes,
-                      stream);
 }

@@ -184,8 +184,8 @@ def render_bwd_rv(slots, count, H, W, c_b, den, aux, gimg, out=None):
 
 
 def loss_l1_ssim(img, target, lam=0.2, grad_scale=1.0, ws=None, out=None):
-    """(1-lam) L1 + lam (1 - SSIM) of img [V,H,W,3] (fp32) against target (fp32, or uint8 8-bit
-    images read as x / 255) -> dict(gimg = grad_scale * dloss/dimg, loss[V])."""
+    """(1-lam) L1 + lam (1 - SSIM) of img [V,H,W,3] against target (both fp32)
+    -> dict(gimg = grad_scale * dloss/dimg, loss[V])."""
     _dev(img, target)
     if img.dim() == 3:
         img, target = img[None], target[None]
@@ -196,9 +196,7 @@ def loss_l1_ssim(img, target, lam=0.2, grad_scale=1.0, ws=None, out=None):
     nbytes = lib().tts_loss_workspace_bytes(V, H, W)
     ws = ws or Workspace(dev)
     buf = ws.get(nbytes)
-    # 8-bit targets are read as x / 255 by the kernels (no float copy of the targets)
-    entry = "tts_loss_l1_ssim_u8" if target.dtype == torch.uint8 else "tts_loss_l1_ssim"
-    call(entry, ptr(img), ptr(target), V, H, W, float(lam), float(grad_scale), ptr(out["gimg"]),
+    call("tts_loss_l1_ssim", ptr(img), ptr(target), V, H, W, float(lam), float(grad_scale), ptr(out["gimg"]),
          ptr(out["loss"]), ptr(out.get("loss_sum")), ptr(buf), nbytes, stream())
     return out
 

@@ -111,16 +111,16 @@ class TrainStep:
         self.H, self.W = cams[0].H, cams[0].W
         ops.tiles(self.H, self.W)
         self.cams_t = pack_cameras(cams, dev)
-        # 8-bit targets (the dataset images' own format) stay uint8 on the device, where the loss
-        # kernels read them as x / 255; float targets are used as given
+        # 8-bit targets (the dataset images' own format) are held and uploaded as uint8 and
+        # expanded to x / 255 by the step's first kernel; float targets are used as given
         gts = [torch.as_tensor(g) for g in gt_images]
+        self.targets_u8 = None
         if all(g.dtype == torch.uint8 for g in gts):
             self.targets_u8 = torch.stack([g.to(dev) for g in gts]).contiguous()
-            self.targets = None
+            self.targets = ops.unit_from_u8(self.targets_u8)
         else:
-            self.targets_u8 = None
             self.targets = torch.stack([g.to(dtype=torch.float32).to(dev) for g in gts]).contiguous()
-        if tuple(self.loss_targets.shape) != (self.V, self.H, self.W, 3):
+        if tuple(self.targets.shape) != (self.V, self.H, self.W, 3):
             raise ValueError(f"gt images must be [H,W,3] = {(self.H, self.W, 3)} each")
         self.sh_degree, self.lam, self.K, self.R, self.k = int(sh_degree), float(lambda_ssim), int(K), int(R), float(k)
         self.blur, self.near = float(blur), float(near)
@@ -188,15 +188,12 @@ class TrainStep:
         self.graphs = {}
         self.kernels_per_step = None
 
-    @property
-    def loss_targets(self):
-        """The target images the loss reads: uint8 [V,H,W,3] (8-bit images) or fp32."""
-        return self.targets_u8 if self.targets_u8 is not None else self.targets
-
     # ---- the launches of one step --------------------------------------------------------
     def _fwd_bwd(self):
         G, H, W, R, K = self.G, self.H, self.W, self.R, self.K
         ops.step_begin(self.step_t)
+        if self.targets_u8 is not None:
+            ops.unit_from_u8(self.targets_u8, out=self.targets)
         ops.project(self.flat, G, self.sh_degree, self.cams_t, H, W, self.blur, self.near, out=self.pj,
                     depth_bt=self.dbt)
         ops.bin_pack(self.pj, G, H, W, R, K, self.k, ws=self.ws_bin, out=self.bp)
@@ -204,7 +201,7 @@ class TrainStep:
             ops.render_fwd_rv(self.bp["slots"], self.bp["count"], H, W, self.model.c_b, out=self.rf)
         else:
             ops.render_fwd(self.bp["slots"], self.bp["count"], H, W, self.flat[59 * G:], self.model.c_b, out=self.rf)
-        ops.loss_l1_ssim(self.rf["img"], self.loss_targets, self.lam, self.grad_scale, ws=self.ws_loss, out=self.lo)
+        ops.loss_l1_ssim(self.rf["img"], self.targets, self.lam, self.grad_scale, ws=self.ws_loss, out=self.lo)
         if self.arm == "RV":
             ops.render_bwd_rv(self.bp["slots"], self.bp["count"], H, W, self.model.c_b, self.rf["den"], self.rf["aux"],
                               self.lo["gimg"], out=self.rb)
@@ -313,10 +310,10 @@ class TrainStep:
 
     def launches(self, relocate):
         """Kernels of this library launched by one step (memsets and torch ops excluded):
-        step_begin 1, project 1, bin_pack 4, render_fwd 1, loss 3, render_bwd 1,
+        step_begin 1, [8-bit target expansion 1], project 1, bin_pack 4, render_fwd 1, loss 3, render_bwd 1,
         backward_params 3, then Adam (+ SGLD) or the peer step (2 barriers + Adam + SGLD), and
         the relocation kernel."""
-        n = 14
+        n = 14 + (1 if self.targets_u8 is not None else 0)
         if self.regions is not None:
             n += 3                                       # signal, Adam, SGLD or wait
         else:
