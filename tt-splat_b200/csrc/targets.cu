@@ -6,16 +6,13 @@
 
 namespace tts {
 
-// 16 bytes per thread and iteration: one 16-byte load, four 16-byte stores.
-__global__ void __launch_bounds__(256) k_unit_from_u8(const uint4* __restrict__ src, long long n16,
+// Four bytes in, one float4 out per thread and iteration: a warp reads 128 contiguous bytes and
+// writes 512 contiguous bytes.
+__global__ void __launch_bounds__(256) k_unit_from_u8(const uchar4* __restrict__ src, long long n4,
                                                       float4* __restrict__ dst) {
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (long long)gridDim.x * blockDim.x) {
-    const uint4 w = __ldg(src + i);
-    const unsigned words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      dst[4 * i + k] = make_float4(unit_from_byte(words[k] & 0xffu), unit_from_byte((words[k] >> 8) & 0xffu),
-                                   unit_from_byte((words[k] >> 16) & 0xffu), unit_from_byte(words[k] >> 24));
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const uchar4 b = __ldg(src + i);
+    dst[i] = make_float4(unit_from_byte(b.x), unit_from_byte(b.y), unit_from_byte(b.z), unit_from_byte(b.w));
   }
 }
 
@@ -33,13 +30,13 @@ extern "C" int tts_unit_from_u8(const uint8_t* src, long long n, float* dst, voi
   TTS_REQUIRE(aligned16(src) && aligned16(dst), "src and dst must be 16-byte aligned");
   if (n == 0) return TTS_OK;
   cudaStream_t st = as_stream(stream);
-  const long long n16 = n / 16;
-  if (n16 > 0) {
-    long long blocks = (n16 + 255) / 256;
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    k_unit_from_u8<<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const uint4*>(src), n16,
+  const long long n4 = n / 4;
+  if (n4 > 0) {
+    long long blocks = (n4 + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    k_unit_from_u8<<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const uchar4*>(src), n4,
                                                      reinterpret_cast<float4*>(dst));
   }
-  if (n % 16) k_unit_from_u8_tail<<<1, 32, 0, st>>>(src, n16 * 16, n, dst);
+  if (n % 4) k_unit_from_u8_tail<<<1, 32, 0, st>>>(src, n4 * 4, n, dst);
   return check_launch("unit_from_u8");
 }
