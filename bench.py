@@ -103,7 +103,7 @@ def run_reference(args, rank, world):
     to the host's cores and memory), sums the gradients and applies Adam, SGLD and relocation."""
     if rank != 0:
         return
-    from oracle.step import CpuStep
+    from oracle.step import CpuStep, host_cores
     pkg = __graft_entry__.load_package()
     with CpuStep(pkg.synthetic.config2()) as cs:
         # one step takes seconds: one warm-up step (it also starts the workers), then timed
@@ -124,6 +124,9 @@ def run_reference(args, rank, world):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 2 shapes)",
             "config": {k: v for k, v in CONFIG.items()},
             "cpu_baseline": {"value": 1.0 / step_s, "unit": "steps/s", "cores": workers, "kind": "port",
+                             "host_cores": host_cores(),
+                             "note": "numpy port of the reference path with min(views, cores) worker processes; "
+                                     "cores beyond the 8 views stay idle",
                              "sample": CPU_SAMPLE.format(workers=workers)},
             "e2e": {"value": 1.0 / step_s, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -540,7 +543,7 @@ TRAFFIC_SOURCE = "profiles/step_kernels_config2_4views.md (ncu, one launch per k
 def cpu_baseline_sample():
     """The oracle's whole train step on the host cores (one warm-up step that starts the workers,
     then the median of three timed steps), on the same scene as the device step."""
-    from oracle.step import CpuStep
+    from oracle.step import CpuStep, host_cores
     pkg = __graft_entry__.load_package()
     with CpuStep(pkg.synthetic.config2()) as cs:
         cs.step()
@@ -551,7 +554,9 @@ def cpu_baseline_sample():
             times.append(time.perf_counter() - t0)
         step_s = float(np.median(times))
         workers = cs.workers
-    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": workers, "kind": "port",
+    return {"value": 1.0 / step_s, "unit": "steps/s", "cores": workers, "kind": "port", "host_cores": host_cores(),
+            "note": "numpy port of the reference path with min(views, cores) worker processes; cores beyond the "
+                    "8 views stay idle",
             "sample": CPU_SAMPLE.format(workers=workers)}
 
 
