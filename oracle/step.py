@@ -4,8 +4,8 @@ with the batch's views spread over worker processes.
 The reference trains on a batch of views whose per-view forward + loss + backward are independent
 (``spike/mcmc.py:90-114``: mean of the per-view losses, one optimizer step).  ``CpuStep`` runs
 those per-view passes in parallel, one worker process per view up to the host's cores and
-memory, each numpy process limited to one BLAS thread, then sums the per-view gradients in view
-order and applies Adam, SGLD noise and relocation in the calling process.  (Splitting a view's
+memory, each numpy process given the host's cores divided by the workers as BLAS threads, then
+sums the per-view gradients in view order and applies Adam, SGLD noise and relocation in the calling process.  (Splitting a view's
 tiles over threads of one worker measured slower than one thread: the page faults of the large
 per-tile temporaries contend inside a process.)  It is timed as the CPU baseline of the
 benchmark; it is never part of the product.
@@ -80,8 +80,11 @@ class CpuStep:
                 pickle.dump(dict(params=self.p, sh_degree=self.sh_degree, cams=scene["cams"],
                                  targets=scene["targets"], K=scene.get("K", 128), n_views=self.n_views),
                             f, protocol=pickle.HIGHEST_PROTOCOL)
+            # the host's cores split over the workers (one BLAS thread each when there are no more
+            # cores than views)
+            self.threads_per_worker = max(1, host_cores() // self.workers)
             for k in _BLAS_VARS:
-                os.environ[k] = "1"
+                os.environ[k] = str(self.threads_per_worker)
             self.pool = ProcessPoolExecutor(self.workers, mp_context=mp.get_context("spawn"), initializer=_init,
                                             initargs=(self.scene_path,))
         except BaseException:
