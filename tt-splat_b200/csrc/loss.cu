@@ -7,9 +7,10 @@
 // (a thread slides an RB-long window along a row, then along a column), with the maps paired in
 // sm_100a .f32x2 FMAs:
 //   k_ssim_fwd : output tile 64x32 of the SSIM map.  Loads the (64+win-1)x(32+win-1) input
-//                halo, filters the five maps x, y, x^2, y^2, xy along rows then columns, and
-//                writes dS/dmu_x, dS/d(filtered x^2), dS/d(filtered xy) plus a per-block
-//                partial of sum(S).
+//                halo, filters the four maps x, y, x^2 + y^2, xy along rows then columns (SSIM
+//                sees the variances only through their sum sigma_x^2 + sigma_y^2, so x^2 and
+//                y^2 are filtered as one map), and writes dS/dmu_x, dS/d(filtered x^2),
+//                dS/d(filtered xy) plus a per-block partial of sum(S).
 //   k_ssim_bwd : input tile 64x32.  Applies the transposed filter to the three dS maps (zero
 //                outside the valid region), combines them with x and y into the SSIM gradient,
 //                adds the L1 gradient, and writes a per-block partial of sum|x - y|.
@@ -60,8 +61,8 @@ __device__ __forceinline__ TileId decode_tile(int tile, int gx, int gy) {
   return t;
 }
 
-// Packed f32x2 arithmetic on (x, y) and (x^2, y^2): the five filtered maps cost two .f32x2 FMAs
-// and one scalar FMA per tap instead of five FMAs.
+// Packed f32x2 arithmetic on (x, y) and (x^2 + y^2, xy): the four filtered maps cost two .f32x2
+// FMAs per tap.
 template <int WIN>
 __global__ void __launch_bounds__(256)
     k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, int H, int W, int gx, int gy, Window wd,
@@ -70,8 +71,7 @@ __global__ void __launch_bounds__(256)
   extern __shared__ float smem[];
   f32x2* sxy = reinterpret_cast<f32x2*>(smem);                    // [IH][XS] (x, y) clamped
   f32x2* hxy = sxy + LG::IH * LG::XS;                             // [IH][HS] row-filtered (x, y)
-  f32x2* hqq = hxy + LG::IH * LG::HS;                             // [IH][HS] row-filtered (x^2, y^2)
-  float* hxy1 = reinterpret_cast<float*>(hqq + LG::IH * LG::HS);  // [IH][HS] row-filtered x*y
+  f32x2* hqp = hxy + LG::IH * LG::HS;                             // [IH][HS] row-filtered (x^2 + y^2, xy)
   __shared__ float red[8];
   const int Ho = H - WIN + 1, Wo = W - WIN + 1;
   const TileId id = decode_tile(blockIdx.x, gx, gy);
@@ -122,28 +122,24 @@ __global__ void __launch_bounds__(256)
     int c0, width;
     row_seg(it / LG::IH, c0, width);
     const f32x2 z = mk2(0.f, 0.f);
-    f32x2 axy[RBR], aqq[RBR];
-    float a1[RBR];
+    f32x2 axy[RBR], aqp[RBR];
 #pragma unroll
     for (int o = 0; o < RBR; o++) {
       axy[o] = z;
-      aqq[o] = z;
-      a1[o] = 0.f;
+      aqp[o] = z;
     }
 #pragma unroll
     for (int i = 0; i < RBR + WIN - 1; i++) {
       const f32x2 XY = sxy[r * LG::XS + c0 + i];
-      const f32x2 QQ = mul2(XY, XY);
       float x, y;
       split2(XY, x, y);
-      const float xy = x * y;
+      const f32x2 QP = mk2(fmaf(x, x, y * y), x * y);
 #pragma unroll
       for (int o = 0; o < RBR; o++) {
         const int k = i - o;
         if (k >= 0 && k < WIN) {
           axy[o] = fma2(g2[k], XY, axy[o]);
-          aqq[o] = fma2(g2[k], QQ, aqq[o]);
-          a1[o] = fmaf(g[k], xy, a1[o]);
+          aqp[o] = fma2(g2[k], QP, aqp[o]);
         }
       }
     }
@@ -151,8 +147,7 @@ __global__ void __launch_bounds__(256)
     for (int o = 0; o < RBR; o++) {
       if (o < width) {
         hxy[r * LG::HS + c0 + o] = axy[o];
-        hqq[r * LG::HS + c0 + o] = aqq[o];
-        hxy1[r * LG::HS + c0 + o] = a1[o];
+        hqp[r * LG::HS + c0 + o] = aqp[o];
       }
     }
   }
@@ -164,26 +159,22 @@ __global__ void __launch_bounds__(256)
   for (int it = tid; it < LT_W * (LT_H / RB); it += 256) {
     const int c = it % LT_W, r0 = (it / LT_W) * RB;
     const f32x2 z = mk2(0.f, 0.f);
-    f32x2 fxy[RB], fqq[RB];
-    float f1[RB];
+    f32x2 fxy[RB], fqp[RB];
 #pragma unroll
     for (int o = 0; o < RB; o++) {
       fxy[o] = z;
-      fqq[o] = z;
-      f1[o] = 0.f;
+      fqp[o] = z;
     }
 #pragma unroll
     for (int i = 0; i < RB + WIN - 1; i++) {
       const f32x2 XY = hxy[(r0 + i) * LG::HS + c];
-      const f32x2 QQ = hqq[(r0 + i) * LG::HS + c];
-      const float P = hxy1[(r0 + i) * LG::HS + c];
+      const f32x2 QP = hqp[(r0 + i) * LG::HS + c];
 #pragma unroll
       for (int o = 0; o < RB; o++) {
         const int k = i - o;
         if (k >= 0 && k < WIN) {
           fxy[o] = fma2(g2[k], XY, fxy[o]);
-          fqq[o] = fma2(g2[k], QQ, fqq[o]);
-          f1[o] = fmaf(g[k], P, f1[o]);
+          fqp[o] = fma2(g2[k], QP, fqp[o]);
         }
       }
     }
@@ -192,13 +183,13 @@ __global__ void __launch_bounds__(256)
     for (int o = 0; o < RB; o++) {
       const int oy = oy0 + r0 + o;
       if (oy >= Ho || ox >= Wo) continue;
-      float mux, muy, fx2, fy2;
+      float mux, muy, fss, fxy1;
       split2(fxy[o], mux, muy);
-      split2(fqq[o], fx2, fy2);
-      const float mux2 = mux * mux, muy2 = muy * muy;
-      const float sxx = fx2 - mux2, syy = fy2 - muy2, sxy_ = f1[o] - mux * muy;
+      split2(fqp[o], fss, fxy1);
+      const float mm = mux * mux + muy * muy;       // mu_x^2 + mu_y^2
+      const float sxy_ = fxy1 - mux * muy;
       const float A1 = 2.f * mux * muy + SSIM_C1, A2 = 2.f * sxy_ + SSIM_C2;
-      const float B1 = mux2 + muy2 + SSIM_C1, B2 = sxx + syy + SSIM_C2;
+      const float B1 = mm + SSIM_C1, B2 = (fss - mm) + SSIM_C2;   // sigma_x^2 + sigma_y^2 + C2
       // hardware reciprocals (rcp.approx, within 1 ulp): the loss and gradient tolerances are
       // orders of magnitude wider, and the correctly rounded form costs ~20 instructions more
       float iD, iB2;
@@ -496,7 +487,7 @@ static int launch_loss(const float* img, const float* target, int V, int H, int 
                        const Window& wd, const LossGeom& lg, float* maps, float* spart, float* lpart, float* gimg,
                        unsigned* counter, cudaStream_t st) {
   using LG = LGeom<WIN>;
-  const size_t fsm = (size_t)(LG::IH * LG::XS * 2 + LG::IH * LG::HS * 5) * 4;
+  const size_t fsm = (size_t)(LG::IH * LG::XS * 2 + LG::IH * LG::HS * 4) * 4;
   const size_t bsm = (size_t)(LG::IH * LG::XS * 3 + (LG::IH * LG::XS & 1) + LG::IH * LG::HS * 3) * 4;
   static std::atomic<unsigned long long> attr_done{0};
   once_per_device(attr_done, [&] {
