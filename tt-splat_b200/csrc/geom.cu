@@ -60,6 +60,28 @@ __device__ __forceinline__ void unstage_rows(const float* s_p, int G, int g0, fl
   }
 }
 
+// The cameras of the first CAM_STAGED views are staged in shared memory with the parameters
+// (one coalesced load per block instead of a dependent camera read per lane after the staging
+// barrier); later views read theirs from global memory.
+constexpr int CAM_STAGED = 16;
+__device__ __forceinline__ void stage_cams(const float* __restrict__ cams, int V, float* s_cam) {
+  const int n = min(V, CAM_STAGED) * TTS_CAM_FLOATS;
+  for (int i = threadIdx.x; i < n; i += GB_THREADS) s_cam[i] = __ldg(cams + i);
+}
+__device__ __forceinline__ Cam cam_at(const float* __restrict__ cams, const float* s_cam, int v) {
+  if (v >= CAM_STAGED) return load_cam(cams, v);
+  const float* p = s_cam + v * TTS_CAM_FLOATS;
+  Cam c;
+#pragma unroll
+  for (int i = 0; i < 9; i++) c.R[i] = p[i];
+#pragma unroll
+  for (int i = 0; i < 3; i++) c.t[i] = p[9 + i];
+  c.fx = p[12]; c.fy = p[13]; c.cx = p[14]; c.cy = p[15];
+#pragma unroll
+  for (int i = 0; i < 3; i++) c.c[i] = p[16 + i];
+  return c;
+}
+
 __device__ __forceinline__ void load_staged(const float* s, Loaded& x) {
 #pragma unroll
   for (int i = 0; i < 3; i++) {
@@ -105,11 +127,13 @@ __global__ void __launch_bounds__(GB_THREADS)
               const float* __restrict__ depth_bt) {
   constexpr int GPB = GB_THREADS / LPG;
   __shared__ float s_p[GPB * PSTRIDE];
+  __shared__ float s_cam[CAM_STAGED * TTS_CAM_FLOATS];
   const int g0 = blockIdx.x * GPB;
-  stage_params<GPB>(params, G, g0, s_p);
-  __syncthreads();
   const int gl = threadIdx.x / LPG, vl = threadIdx.x % LPG;
   const int g = g0 + gl;
+  stage_cams(cams, V, s_cam);
+  stage_params<GPB>(params, G, g0, s_p);
+  __syncthreads();
   const int T = ntx * nty;
   const float* sp = s_p + gl * PSTRIDE;
   Loaded x;
@@ -120,7 +144,7 @@ __global__ void __launch_bounds__(GB_THREADS)
     const int v = vl + it * LPG;
     int key = -1;                          // v * T + home cell of a kept (gaussian, view)
     if (g < G && v < V) {
-      const Cam cam = load_cam(cams, v);
+      const Cam cam = cam_at(cams, s_cam, v);
       GeomFwd f;
       geom_forward(x.m, x.q, x.ls, cam, blur, near_plane, f);
       float d[3] = {0.f, 0.f, 0.f}, nrm;
@@ -237,11 +261,22 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
   constexpr int GPB = GB_THREADS / LPG;
   constexpr int NB = (DEG + 1) * (DEG + 1);
   __shared__ float s_p[GPB * PSTRIDE];
+  __shared__ float s_cam[CAM_STAGED * TTS_CAM_FLOATS];
   const int g0 = blockIdx.x * GPB;
-  stage_params<GPB>(params, G, g0, s_p);
-  __syncthreads();
   const int gl = threadIdx.x / LPG, vl = threadIdx.x % LPG;
   const int g = g0 + gl;
+  // the first view's gathered record is requested before the parameter staging, so that its
+  // latency overlaps it
+  float4 r0 = make_float4(0.f, 0.f, 0.f, 0.f), r1 = r0, r2 = r0;
+  if (g < G && vl < V) {
+    const float4* r = rec + ((long long)vl * G + g) * 3;
+    r0 = __ldg(r);
+    r1 = __ldg(r + 1);
+    r2 = __ldg(r + 2);
+  }
+  stage_cams(cams, V, s_cam);
+  stage_params<GPB>(params, G, g0, s_p);
+  __syncthreads();
   const ParamLayout L{G};
   const float* sp = s_p + gl * PSTRIDE;
   Loaded x;
@@ -256,13 +291,17 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
     for (int c = 0; c < 3; c++) gco[k][c] = 0.f;
   if (g < G) {
     for (int v = vl; v < V; v += LPG) {
-      const float4* r = rec + ((long long)v * G + g) * 3;
-      const float4 r0 = __ldg(r), r1 = __ldg(r + 1), r2 = __ldg(r + 2);
+      if (v != vl) {
+        const float4* r = rec + ((long long)v * G + g) * 3;
+        r0 = __ldg(r);
+        r1 = __ldg(r + 1);
+        r2 = __ldg(r + 2);
+      }
       if (r2.y == 0.f) continue;       // no valid slot in this view
       const float ga = r0.x, gb = r0.y, gc = r0.z, gmx = r0.w, gmy = r1.x;
       const float gcol[3] = {r1.y, r1.z, r1.w};
       const float goc = r2.x;
-      const Cam cam = load_cam(cams, v);
+      const Cam cam = cam_at(cams, s_cam, v);
       GeomFwd f;
       geom_forward(x.m, x.q, x.ls, cam, blur, near_plane, f);
       geom_backward(f, cam, ga, gb, gc, gmx, gmy, gm, gq, gs);
