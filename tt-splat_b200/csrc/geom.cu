@@ -120,7 +120,7 @@ __device__ __forceinline__ void colour_pre(const float* s, const Loaded& x, cons
 __device__ __forceinline__ float depth_weight(const float* bt, float z) { return sigmoidf(bt[0] * (bt[1] - z)); }
 
 template <int DEG, int LPG, bool ARMB>
-__global__ void __launch_bounds__(GB_THREADS)
+__global__ void __launch_bounds__(GB_THREADS, 6)
     k_project(const float* __restrict__ params, int G, const float* __restrict__ cams, int V, int ntx, int nty,
               float blur, float near_plane, float* __restrict__ proj, float* __restrict__ mu2d,
               uint8_t* __restrict__ keep, int* __restrict__ cell_count, int2* __restrict__ cell_rank,
