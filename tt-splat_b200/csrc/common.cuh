@@ -194,6 +194,17 @@ __device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+// max(a * b + c, 0) per lane where the exact result is at most 1: the fused multiply-add
+// saturated to [0, 1] (fma.rn.sat.f32 on each lane; the packed form has no .sat), two issue
+// slots instead of a packed FMA and two max operations.
+__device__ __forceinline__ f32x2 fma_sat2(f32x2 a, f32x2 b, float c) {
+  float alo, ahi, blo, bhi, lo, hi;
+  split2(a, alo, ahi);
+  split2(b, blo, bhi);
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(lo) : "f"(alo), "f"(blo), "f"(c));
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(hi) : "f"(ahi), "f"(bhi), "f"(c));
+  return mk2(lo, hi);
+}
 __device__ __forceinline__ f32x2 relu2(f32x2 a) {
   float lo, hi;
   split2(a, lo, hi);

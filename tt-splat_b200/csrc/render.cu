@@ -8,6 +8,8 @@
 // memory:
 //   u = theta . Phi(px, py) = (t0 px + (t2 py + t3)) px + ((t1 py + t4) py + t5)
 //   w = max(u, 0)^2;  num += w color_o;  den += w o_col
+// u = 1 - Q/k with Q >= 0 for the positive-definite conics the projection produces, so u <= 1
+// and max(u, 0) is the last FMA of u saturated to [0, 1] (both kernels).
 // then C = (num + w_b c_b) / (den + w_b).  The [256 x K] weight matrix never leaves registers.
 //
 // Backward (replaces _DevRenderBinned.backward :169-186 / WSRPolySplatHot.backward,
@@ -90,11 +92,11 @@ __global__ void __launch_bounds__(FWD_THREADS)
     const float4 C = rows[3 * s + 2];   // cb oc 0 0
     const float srow = fmaf(A.z, py, A.w);
     const float rrow = fmaf(fmaf(A.y, py, B.x), py, B.y);
-    const f32x2 t0 = mk2(A.x, A.x), s2 = mk2(srow, srow), r2 = mk2(rrow, rrow);
+    const f32x2 t0 = mk2(A.x, A.x), s2 = mk2(srow, srow);
     const f32x2 cr = mk2(B.z, B.z), cg = mk2(B.w, B.w), cb = mk2(C.x, C.x), oc = mk2(C.y, C.y);
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const f32x2 r = relu2(fma2(fma2(t0, px[j], s2), px[j], r2));
+      const f32x2 r = fma_sat2(fma2(t0, px[j], s2), px[j], rrow);
       const f32x2 w = mul2(r, r);
       a0[j] = fma2(w, cr, a0[j]);
       a1[j] = fma2(w, cg, a1[j]);
@@ -124,7 +126,7 @@ __global__ void __launch_bounds__(FWD_THREADS)
   }
 }
 
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
     k_render_bwd(const float* __restrict__ slots, const int* __restrict__ count, int ntx, int T, int H, int W, int K,
                  const float* __restrict__ c_b, const float* __restrict__ img, const float* __restrict__ den,
                  const float* __restrict__ gimg, float* __restrict__ slot_grads, float* __restrict__ gwb_partial) {
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(256)
     const float py = (float)ly + 0.5f;
     const float srow = fmaf(t2, py, t3);
     const float rrow = fmaf(fmaf(t1, py, t4), py, t5);
-    const f32x2 s2 = mk2(srow, srow), r2 = mk2(rrow, rrow);
+    const f32x2 s2 = mk2(srow, srow);
     f32x2 a0 = z, a1 = z, a2 = z;
 #pragma unroll
     for (int lp = 0; lp < 8; ++lp) {
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(256)
       const f32x2 P1 = *reinterpret_cast<const f32x2*>(&s_g1[pi]);
       const f32x2 P2 = *reinterpret_cast<const f32x2*>(&s_g2[pi]);
       const f32x2 P3 = *reinterpret_cast<const f32x2*>(&s_gd[pi]);
-      const f32x2 r = relu2(fma2(fma2(t0, px, s2), px, r2));
+      const f32x2 r = fma_sat2(fma2(t0, px, s2), px, rrow);
       const f32x2 w = mul2(r, r);
       gc0 = fma2(w, P0, gc0);
       gc1 = fma2(w, P1, gc1);
