@@ -182,6 +182,8 @@ __global__ void __launch_bounds__(256, 3)
 #pragma unroll
     for (int lp = 0; lp < 8; ++lp) {
       const f32x2 px = mk2((float)(2 * lp) + 0.5f, (float)(2 * lp) + 1.5f);
+      const f32x2 pxsq = mk2(((float)(2 * lp) + 0.5f) * ((float)(2 * lp) + 0.5f),
+                             ((float)(2 * lp) + 1.5f) * ((float)(2 * lp) + 1.5f));   // exact
       const int pi = ly * 16 + 2 * lp;
       const f32x2 P0 = *reinterpret_cast<const f32x2*>(&s_g0[pi]);
       const f32x2 P1 = *reinterpret_cast<const f32x2*>(&s_g1[pi]);
@@ -196,9 +198,8 @@ __global__ void __launch_bounds__(256, 3)
       const f32x2 gw = fma2(P0, cr, fma2(P1, cg, fma2(P2, cbb, mul2(P3, oc))));
       const f32x2 gu = mul2(r, gw);
       a0 = add2(a0, gu);
-      const f32x2 tpx = mul2(gu, px);
-      a1 = add2(a1, tpx);
-      a2 = fma2(tpx, px, a2);
+      a1 = fma2(gu, px, a1);
+      a2 = fma2(gu, pxsq, a2);
     }
     const float s0 = hsum2(a0), s1 = hsum2(a1), s2s = hsum2(a2);
     g0 += s2s;
@@ -341,6 +342,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int lp = 0; lp < 8; ++lp) {
       const f32x2 px = mk2((float)(2 * lp) + 0.5f, (float)(2 * lp) + 1.5f);
+      const f32x2 pxsq = mk2(((float)(2 * lp) + 0.5f) * ((float)(2 * lp) + 0.5f),
+                             ((float)(2 * lp) + 1.5f) * ((float)(2 * lp) + 1.5f));   // exact
       const int pi = ly * 16 + 2 * lp;
       const f32x2 P0 = *reinterpret_cast<const f32x2*>(&s_g0[pi]);
       const f32x2 P1 = *reinterpret_cast<const f32x2*>(&s_g1[pi]);
@@ -361,9 +364,8 @@ __global__ void __launch_bounds__(256)
       const f32x2 gw = fma2(P0, cr, fma2(P1, cg, fma2(P2, cbb, mul2(P3, oc))));
       const f32x2 gu = mul2(r, gw);
       a0 = add2(a0, gu);
-      const f32x2 tpx = mul2(gu, px);
-      a1 = add2(a1, tpx);
-      a2 = fma2(tpx, px, a2);
+      a1 = fma2(gu, px, a1);
+      a2 = fma2(gu, pxsq, a2);
     }
     const float s0 = hsum2(a0), s1 = hsum2(a1), s2s = hsum2(a2);
     g0 += s2s;
