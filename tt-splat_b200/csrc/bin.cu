@@ -235,9 +235,10 @@ __device__ __forceinline__ void stencil_range(int j, int R, int tx, int ty, int 
 }
 
 constexpr int WB_WARPS = 4;
-// Keys per warp: 768 (6 KB) keeps seven 4-warp blocks per SM within shared memory; on the config-2
-// workload 0.13 % of the tiles have more candidates (none more than 896) and go to the block kernel.
-constexpr int WCAP = 768;
+// Keys per warp: 896 (7 KB) keeps six 4-warp blocks per SM within shared memory and covers every
+// tile of the config-2 workload (none has more candidates); larger tiles go to the block kernel,
+// whose per-tile latency (~16 µs) would otherwise bound the stage even for a few tiles.
+constexpr int WCAP = 896;
 constexpr int WSORT_MAX = 512;   // the warp's bitonic sort pads to a power of two within WCAP
 constexpr int WTIES = 64;   // ties at the selection boundary resolved by rank (more: sorted with the rest)
 
