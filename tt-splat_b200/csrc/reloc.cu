@@ -32,33 +32,46 @@ __device__ __forceinline__ float opacity_of(const float* params, const ParamLayo
   return sigmoidf(params[L.opacity() + g]);
 }
 
-// Grid-wide barrier for a cooperative launch: the last block to arrive resets the count and
-// bumps the generation; the others wait for the new generation with an iteration limit (on
-// timeout the status word records it and the kernel unwinds: every later barrier also gives up).
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned x) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(x) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_release_gpu(unsigned* p, unsigned x) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(x) : "memory");
+}
+
+// Grid-wide barrier for a cooperative launch: thread 0 of each block arrives with an acq_rel
+// increment (its release covers the block's writes, ordered before it by the block barrier); the
+// last to arrive resets the count and bumps the generation with a release, which the others
+// acquire while they poll, with an iteration limit (on timeout the status word records it and the
+// kernel unwinds: every later barrier also gives up).  The generation is read before arriving, so
+// a fast last arriver cannot bump it unseen.
 __device__ __forceinline__ bool grid_sync(GridBar* bar, unsigned nblocks, int* s_flag) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    volatile unsigned* vgen = &bar->gen;
-    const unsigned gen = *vgen;
-    __threadfence();
-    const unsigned arrived = atomicAdd(&bar->count, 1u);
+    const unsigned gen = ld_acquire_gpu(&bar->gen);
+    const unsigned arrived = atom_add_acq_rel_gpu(&bar->count, 1u);
     int ok = 1;
     if (arrived == nblocks - 1) {
       bar->count = 0u;
-      __threadfence();
-      atomicAdd(&bar->gen, 1u);
+      red_add_release_gpu(&bar->gen, 1u);
     } else {
       int it = 0;
-      while (*vgen == gen) {
+      while (ld_acquire_gpu(&bar->gen) == gen) {
         if (++it > (1 << 24)) {
           ok = 0;
           atomicOr(&g_status, STATUS_GRID_TIMEOUT);
           break;
         }
-        __nanosleep(64);
+        __nanosleep(32);
       }
     }
-    __threadfence();
     *s_flag = ok;
   }
   __syncthreads();
