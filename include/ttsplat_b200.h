@@ -212,6 +212,15 @@ int tts_relocate(float* params, float* m, float* v, int G, float dead_thr, float
                  float offset, const int32_t* targets_in, const float* offset_noise_in,
                  const int32_t* step, uint64_t seed, int32_t* n_dead_out, int32_t* targets_out,
                  void* workspace, size_t workspace_bytes, void* stream);
+/* The SGLD step of tts_sgld (spike/mcmc.py:25-34, the lr of the means at lr7[0]; eps_noise
+ * [G,3] injects its noise, NULL: Philox) followed by tts_relocate, in one launch: the MCMC
+ * order of an iteration that relocates (spike/mcmc.py:97-111), the same results as the two
+ * calls in turn. */
+int tts_sgld_relocate(float* params, float* m, float* v, int G, const double* lr7, float noise_lr,
+                      const float* eps_noise, float dead_thr, float dead_frac, float offset,
+                      const int32_t* targets_in, const float* offset_noise_in, const int32_t* step,
+                      uint64_t seed, int32_t* n_dead_out, int32_t* targets_out, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 /* ---- multi-GPU optimizer step over NVLink peer memory -------------------------------------
  * Replaces the gradient all-reduce + replicated torch.optim.Adam of a view-split batch

@@ -114,3 +114,36 @@ def test_relocation_quantile_threshold_and_sampling(pkg):
     flat2 = _flat(pkg, p)
     out2 = ops.relocate(flat2, torch.zeros_like(flat2), torch.zeros_like(flat2), G, step, 0.0, 0.01, 0.0, seed=7)
     assert torch.equal(out2["targets"][:n], out["targets"][:n]) and torch.equal(flat2, flat)
+
+
+@pytest.mark.parametrize("injected", [False, True])
+def test_sgld_relocate_equals_sgld_then_relocate(injected, pkg):
+    """The one-launch SGLD + relocation of a relocating iteration gives the bits of tts_sgld
+    followed by tts_relocate (Philox draws, and injected SGLD noise + relocation draws)."""
+    from tt_splat_b200 import ops
+    sc = pkg.synthetic.config2(seed=9, G=30000, H=64, W=96, n_views=1)
+    G = 30000
+    flat0 = _flat(pkg, sc["params"])
+    rng = np.random.default_rng(3)
+    m0 = torch.from_numpy(rng.standard_normal(flat0.numel()).astype(np.float32)).to(DEV)
+    v0 = torch.from_numpy(rng.random(flat0.numel()).astype(np.float32)).to(DEV)
+    step = torch.full((1,), 5, dtype=torch.int32, device=DEV)
+    lr7 = torch.tensor([1.6e-4, 5e-3, 1e-3, 5e-2, 2.5e-3, 1.25e-4, 1e-3], dtype=torch.float64, device=DEV)
+    eps = torch.from_numpy(rng.standard_normal((G, 3)).astype(np.float32)).to(DEV) if injected else None
+    kw = dict(dead_thr=0.0, dead_frac=0.01, offset=0.3, seed=11)
+    if injected:
+        # injected targets drawn from the upper half of the opacities (alive: never a dead slot)
+        o = sc["params"]["opacity_raw"].astype(np.float64)
+        alive = np.argsort(o, kind="stable")[G // 2:]
+        kw.update(targets_in=torch.from_numpy(rng.choice(alive, G).astype(np.int32)).to(DEV),
+                  noise_in=torch.from_numpy(rng.standard_normal((G, 3)).astype(np.float32)).to(DEV))
+    a, ma, va = flat0.clone(), m0.clone(), v0.clone()
+    ops.sgld(a, G, step, 1.6e-4, 5e5, eps, seed=11)
+    ra = ops.relocate(a, ma, va, G, step, kw["dead_thr"], kw["dead_frac"], kw["offset"], kw.get("targets_in"),
+                      kw.get("noise_in"), seed=11)
+    b, mb, vb = flat0.clone(), m0.clone(), v0.clone()
+    rb = ops.sgld_relocate(b, mb, vb, G, step, lr7, 5e5, eps, **kw)
+    n = int(ra["n_dead"])
+    assert n == int(rb["n_dead"]) > 0
+    assert torch.equal(ra["targets"][:n], rb["targets"][:n])
+    assert torch.equal(a, b) and torch.equal(ma, mb) and torch.equal(va, vb)

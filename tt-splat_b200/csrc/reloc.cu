@@ -17,7 +17,7 @@
 //      zeroed.
 #include <algorithm>
 
-#include "common.cuh"
+#include "sgld.cuh"
 
 namespace tts {
 
@@ -133,7 +133,10 @@ struct RelocArgs {
   double* bsum;     // [nblocks]
   int* dead_list;   // [G]
   double* cdf;      // [G]
-  int* nat;         // [G], zeroed before the launch
+  int* nat;         // [G], zeroed by the kernel (phase 0)
+  const double* sgld_lr;   // non-null: the SGLD step runs as phase 0 (lr of the means at [0])
+  float noise_lr;
+  const float* sgld_eps;   // injected SGLD noise [G][3], or null for Philox draws
 };
 
 __device__ __forceinline__ long long field_index(const ParamLayout& L, int f, int x) {
@@ -177,6 +180,16 @@ __global__ void __launch_bounds__(RK_THREADS) k_relocate(RelocArgs a) {
   const unsigned nb = gridDim.x;
   const int chunk = (G + (int)nb - 1) / (int)nb;
   const int beg = min(G, (int)blockIdx.x * chunk), end = min(G, beg + chunk);
+  const int step = *a.step_ptr;
+  // ---- 0. the per-target counts of this block's range start at zero; with sgld_lr, the SGLD step
+  // of this block's gaussians (add_sgld_noise right before relocate, spike/mcmc.py:97-111): it
+  // changes only the means, which nothing reads before the copies of phase 4, grid barriers later
+  for (int g = beg + tid; g < end; g += RK_THREADS) a.nat[g] = 0;
+  if (a.sgld_lr) {
+    const double lr_means = a.sgld_lr[0];
+    for (int g = beg + tid; g < end; g += RK_THREADS)
+      sgld_one(a.params, L, g, lr_means, a.noise_lr, a.sgld_eps, step, a.seed);
+  }
   // ---- 1. threshold ----------------------------------------------------------------------------
   float thr = a.dead_thr;
   if (a.dead_frac > 0.f) {
@@ -325,7 +338,6 @@ __global__ void __launch_bounds__(RK_THREADS) k_relocate(RelocArgs a) {
   if (!grid_sync(a.bar, nb, &s_flag)) return;
   // ---- 3. targets: one warp per dead slot; the CDF search splits the range 33 ways per round
   // (32 pivots loaded at once), so a search takes ~log33(G) dependent loads instead of log2(G)
-  const int step = *a.step_ptr;
   const int lane = tid & 31;
   const int nwarps = (int)nb * (RK_THREADS / 32);
   for (int i = blockIdx.x * (RK_THREADS / 32) + (tid >> 5); i < n_dead; i += nwarps) {
@@ -446,10 +458,10 @@ using namespace tts;
 // Sized for up to 1024 blocks, more than any grid reloc_grid() returns.
 extern "C" size_t tts_relocate_workspace_bytes(int G) { return G > 0 ? reloc_bytes(G, 1024, nullptr, nullptr) : 0; }
 
-extern "C" int tts_relocate(float* params, float* m, float* v, int G, float dead_thr, float dead_frac, float offset,
-                            const int32_t* targets_in, const float* offset_noise_in, const int32_t* step, uint64_t seed,
-                            int32_t* n_dead_out, int32_t* targets_out, void* workspace, size_t workspace_bytes,
-                            void* stream) {
+static int relocate_core(float* params, float* m, float* v, int G, float dead_thr, float dead_frac, float offset,
+                         const int32_t* targets_in, const float* offset_noise_in, const int32_t* step, uint64_t seed,
+                         int32_t* n_dead_out, int32_t* targets_out, const double* sgld_lr, float noise_lr,
+                         const float* sgld_eps, void* workspace, size_t workspace_bytes, void* stream) {
   TTS_REQUIRE(G >= 2, "relocation needs G >= 2");
   TTS_REQUIRE(params && m && v && step && n_dead_out && targets_out && workspace, "null pointer");
   TTS_REQUIRE(dead_frac < 1.f, "dead_frac must be < 1");
@@ -470,11 +482,14 @@ extern "C" int tts_relocate(float* params, float* m, float* v, int G, float dead
   a.seed = seed;
   a.n_dead_out = n_dead_out;
   a.targets = targets_out;
+  a.sgld_lr = sgld_lr;
+  a.noise_lr = noise_lr;
+  a.sgld_eps = sgld_eps;
   cudaStream_t st = as_stream(stream);
-  // the barrier word, the digit histograms and the per-target counts start at zero
+  // the barrier word and the digit histograms start at zero (the per-target counts are zeroed by
+  // the kernel)
   const size_t head = reinterpret_cast<char*>(a.bcnt) - static_cast<char*>(workspace);
   if (cudaMemsetAsync(workspace, 0, head, st) != cudaSuccess) return check_launch("memset relocation state");
-  if (cudaMemsetAsync(a.nat, 0, (size_t)G * 4, st) != cudaSuccess) return check_launch("memset nat");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)nblk);
   cfg.blockDim = dim3(RK_THREADS);
@@ -487,4 +502,22 @@ extern "C" int tts_relocate(float* params, float* m, float* v, int G, float dead
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, k_relocate, a) != cudaSuccess) return check_launch("relocate (cooperative launch)");
   return check_launch("relocate");
+}
+
+extern "C" int tts_relocate(float* params, float* m, float* v, int G, float dead_thr, float dead_frac, float offset,
+                            const int32_t* targets_in, const float* offset_noise_in, const int32_t* step, uint64_t seed,
+                            int32_t* n_dead_out, int32_t* targets_out, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  return relocate_core(params, m, v, G, dead_thr, dead_frac, offset, targets_in, offset_noise_in, step, seed,
+                       n_dead_out, targets_out, nullptr, 0.f, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int tts_sgld_relocate(float* params, float* m, float* v, int G, const double* lr7, float noise_lr,
+                                 const float* eps_noise, float dead_thr, float dead_frac, float offset,
+                                 const int32_t* targets_in, const float* offset_noise_in, const int32_t* step,
+                                 uint64_t seed, int32_t* n_dead_out, int32_t* targets_out, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  TTS_REQUIRE(lr7, "null learning-rate table");
+  return relocate_core(params, m, v, G, dead_thr, dead_frac, offset, targets_in, offset_noise_in, step, seed,
+                       n_dead_out, targets_out, lr7, noise_lr, eps_noise, workspace, workspace_bytes, stream);
 }

@@ -262,6 +262,24 @@ def relocate(flat, m, v, G, step, dead_thr=0.005, dead_frac=0.0, offset=0.0, tar
     return out
 
 
+def sgld_relocate(flat, m, v, G, step, lr7, noise_lr, eps_noise=None, dead_thr=0.005, dead_frac=0.0, offset=0.0,
+                  targets_in=None, noise_in=None, seed=0, ws=None, out=None):
+    """sgld(...) then relocate(...) in one launch (the MCMC order of a relocating iteration);
+    ``lr7`` is the device learning-rate table (means first)."""
+    _dev(flat, m, v, step, lr7, eps_noise)
+    dev = flat.device
+    if out is None:
+        out = dict(n_dead=torch.zeros(1, dtype=torch.int32, device=dev),
+                   targets=torch.empty(G, dtype=torch.int32, device=dev))
+    nbytes = lib().tts_relocate_workspace_bytes(G)
+    ws = ws or Workspace(dev)
+    buf = ws.get(nbytes)
+    call("tts_sgld_relocate", ptr(flat), ptr(m), ptr(v), G, ptr(lr7), float(noise_lr), ptr(eps_noise),
+         float(dead_thr), float(dead_frac), float(offset), ptr(targets_in), ptr(noise_in), ptr(step),
+         int(seed) & (2 ** 64 - 1), ptr(out["n_dead"]), ptr(out["targets"]), ptr(buf), nbytes, stream())
+    return out
+
+
 def pack_operands(theta_u, color_o, o_col):
     _dev(theta_u, color_o, o_col)
     VT, K = theta_u.shape[0], theta_u.shape[2]

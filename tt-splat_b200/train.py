@@ -226,13 +226,20 @@ class TrainStep:
             else:
                 ops.peer_wait(self.regions, 1, self.step_t)
         else:
+            # a relocating iteration runs its SGLD step inside the relocation launch
+            fused = relocate and self.noise_lr > 0
             ops.adam_sgld(self.flat, self.grads, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
-                          noise_lr=self.noise_lr, seed=self.seed)
+                          noise_lr=0.0 if fused else self.noise_lr, seed=self.seed)
         if self.dbt is not None:
             ops.adam_vec(self.dbt, self.g_dbt, self.m_dbt, self.v_dbt, self.step_t, self.lr["depth"])
         if relocate:
-            ops.relocate(self.flat, self.m, self.v, self.G, self.step_t, self.dead_thr, self.dead_frac, self.offset,
-                         seed=self.seed, ws=self.ws_reloc, out=self.reloc)
+            if self.regions is None and self.noise_lr > 0:
+                ops.sgld_relocate(self.flat, self.m, self.v, self.G, self.step_t, self.lr7, self.noise_lr,
+                                  dead_thr=self.dead_thr, dead_frac=self.dead_frac, offset=self.offset,
+                                  seed=self.seed, ws=self.ws_reloc, out=self.reloc)
+            else:
+                ops.relocate(self.flat, self.m, self.v, self.G, self.step_t, self.dead_thr, self.dead_frac,
+                             self.offset, seed=self.seed, ws=self.ws_reloc, out=self.reloc)
             self.n_moved.add_(self.reloc["n_dead"])
 
     def _allreduce(self):
@@ -312,12 +319,12 @@ class TrainStep:
         """Kernels of this library launched by one step (memsets and torch ops excluded):
         step_begin 1, [8-bit target expansion 1], project 1, bin_pack 4, render_fwd 1, loss 3, render_bwd 1,
         backward_params 3, then Adam (+ SGLD) or the peer step (2 barriers + Adam + SGLD), and
-        the relocation kernel."""
+        the relocation kernel (on one GPU it also runs the SGLD step of a relocating iteration)."""
         n = 14 + (1 if self.targets_u8 is not None else 0)
         if self.regions is not None:
             n += 3                                       # signal, Adam, SGLD or wait
         else:
-            n += 1 + (1 if self.noise_lr > 0 else 0)
+            n += 1 + (1 if self.noise_lr > 0 and not relocate else 0)
         if self.dbt is not None:
             n += 1                                       # Adam of the depth group (arm B)
         if relocate:
