@@ -34,10 +34,11 @@ __device__ __forceinline__ float lr_of(long long i, long long G, const float nss
   return i < 3 * G ? nss[0] : i < 6 * G ? nss[1] : i < 10 * G ? nss[2] : i < 11 * G ? nss[3] : i < 14 * G ? nss[4] : nss[5];
 }
 
-// One wave of blocks (ADAM_BLOCKS_PER_SM per SM) walks the buffer grid-stride, two 16-byte vectors
-// of each array per thread per pass; the first pass's loads are issued before the block waits for
-// its scalars, so the double-precision bias corrections cost no memory time.
-constexpr int ADAM_BLOCKS_PER_SM = 2;
+// One wave of blocks (ADAM_BLOCKS_PER_SM per SM) walks the buffer grid-stride, one 16-byte vector
+// of each array per thread per pass, with the next pass's four vectors requested before the
+// current one is updated (a register double buffer); the first pass's loads are issued before the
+// block waits for its scalars, so the double-precision bias corrections cost no memory time.
+constexpr int ADAM_BLOCKS_PER_SM = 4;
 
 __global__ void __launch_bounds__(256, ADAM_BLOCKS_PER_SM)
     k_adam(float* __restrict__ params, const float* __restrict__ grads, float* __restrict__ m,
@@ -51,20 +52,14 @@ __global__ void __launch_bounds__(256, ADAM_BLOCKS_PER_SM)
   const float4* Gr = reinterpret_cast<const float4*>(grads);
   float4* M = reinterpret_cast<float4*>(m);
   float4* Vv = reinterpret_cast<float4*>(v);
-  float4 pa, ga, ma, va, pb, gb, mb, vb;
-  auto load = [&](long long i) {
-    pa = P[i];
-    ma = M[i];
-    va = Vv[i];
-    ga = Gr[i];
-    if (i + stride < nv) {
-      pb = P[i + stride];
-      mb = M[i + stride];
-      vb = Vv[i + stride];
-      gb = Gr[i + stride];
-    }
-  };
-  if (tid < nv) load(tid);
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 pa = z4, ga = z4, ma = z4, va = z4;
+  if (tid < nv) {
+    pa = P[tid];
+    ma = M[tid];
+    va = Vv[tid];
+    ga = Gr[tid];
+  }
   // scalars in double like the Python-side arithmetic of torch's Adam, cast to fp32 at use;
   // computed once per block (the double pow is far costlier than the per-element update)
   if (threadIdx.x == 0) {
@@ -100,19 +95,23 @@ __global__ void __launch_bounds__(256, ADAM_BLOCKS_PER_SM)
       vv[j] = vj;
     }
   };
-  for (long long i = tid; i < nv; i += 2 * stride) {
+  for (long long i = tid; i < nv; i += stride) {
     const long long j = i + stride;
+    float4 pb = z4, gb = z4, mb = z4, vb = z4;
+    if (j < nv) {
+      pb = P[j];
+      mb = M[j];
+      vb = Vv[j];
+      gb = Gr[j];
+    }
     update4(4 * i, pa, ga, ma, va);
     P[i] = pa;
     M[i] = ma;
     Vv[i] = va;
-    if (j < nv) {
-      update4(4 * j, pb, gb, mb, vb);
-      P[j] = pb;
-      M[j] = mb;
-      Vv[j] = vb;
-    }
-    if (i + 2 * stride < nv) load(i + 2 * stride);
+    pa = pb;
+    ga = gb;
+    ma = mb;
+    va = vb;
   }
   for (long long e = 4 * nv + tid; e < n; e += stride) adam_elem(params, grads, m, v, e, a, lr_of(e, G, nss));
 }
