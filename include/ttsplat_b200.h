@@ -221,6 +221,14 @@ int tts_sgld_relocate(float* params, float* m, float* v, int G, const double* lr
                       const int32_t* targets_in, const float* offset_noise_in, const int32_t* step,
                       uint64_t seed, int32_t* n_dead_out, int32_t* targets_out, void* workspace,
                       size_t workspace_bytes, void* stream);
+/* The same for one rank of the multi-GPU step: tts_peer_sgld (waits, with an iteration limit,
+ * for every rank's phase-1 flag) followed by tts_relocate, in one launch; flags/rank/N as in
+ * tts_peer_sgld. */
+int tts_peer_sgld_relocate(float* params, float* m, float* v, int G, const double* lr7,
+                           float noise_lr, const float* eps_noise, float dead_thr, float dead_frac,
+                           float offset, const int32_t* step, uint64_t seed, int32_t* n_dead_out,
+                           int32_t* targets_out, int32_t* const* flags, int rank, int N,
+                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- multi-GPU optimizer step over NVLink peer memory -------------------------------------
  * Replaces the gradient all-reduce + replicated torch.optim.Adam of a view-split batch

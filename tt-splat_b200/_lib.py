@@ -49,6 +49,7 @@ SIGNATURES = {
     "tts_relocate_workspace_bytes": (SZ, [I]),
     "tts_relocate": (I, [P, P, P, I, F, F, F, P, P, P, U64, P, P, P, SZ, P]),
     "tts_sgld_relocate": (I, [P, P, P, I, P, F, P, F, F, F, P, P, P, U64, P, P, P, SZ, P]),
+    "tts_peer_sgld_relocate": (I, [P, P, P, I, P, F, P, F, F, F, P, U64, P, P, P, I, I, P, SZ, P]),
     "tts_ipc_handle_bytes": (SZ, []),
     "tts_peer_alloc": (I, [SZ, C.POINTER(P)]),
     "tts_peer_free": (I, [P]),

@@ -17,6 +17,7 @@
 //      zeroed.
 #include <algorithm>
 
+#include "peer.cuh"
 #include "sgld.cuh"
 
 namespace tts {
@@ -137,6 +138,8 @@ struct RelocArgs {
   const double* sgld_lr;   // non-null: the SGLD step runs as phase 0 (lr of the means at [0])
   float noise_lr;
   const float* sgld_eps;   // injected SGLD noise [G][3], or null for Philox draws
+  const int* peer_mine;    // non-null (multi-GPU step): wait for every rank's phase-1 flag first
+  int peer_n;
 };
 
 __device__ __forceinline__ long long field_index(const ParamLayout& L, int f, int x) {
@@ -181,6 +184,14 @@ __global__ void __launch_bounds__(RK_THREADS) k_relocate(RelocArgs a) {
   const int chunk = (G + (int)nb - 1) / (int)nb;
   const int beg = min(G, (int)blockIdx.x * chunk), end = min(G, beg + chunk);
   const int step = *a.step_ptr;
+  if (a.peer_mine) {
+    // multi-GPU step: every rank's shard of the update must have arrived (phase 1) before this
+    // rank's parameters are read; a block whose wait gave up leaves (status recorded), and the
+    // others then give up at the next grid barrier
+    if (tid == 0) s_flag = peer_wait(a.peer_mine, a.peer_n, 1, step) ? 1 : 0;
+    __syncthreads();
+    if (!s_flag) return;
+  }
   // ---- 0. the per-target counts of this block's range start at zero; with sgld_lr, the SGLD step
   // of this block's gaussians (add_sgld_noise right before relocate, spike/mcmc.py:97-111): it
   // changes only the means, which nothing reads before the copies of phase 4, grid barriers later
@@ -461,7 +472,8 @@ extern "C" size_t tts_relocate_workspace_bytes(int G) { return G > 0 ? reloc_byt
 static int relocate_core(float* params, float* m, float* v, int G, float dead_thr, float dead_frac, float offset,
                          const int32_t* targets_in, const float* offset_noise_in, const int32_t* step, uint64_t seed,
                          int32_t* n_dead_out, int32_t* targets_out, const double* sgld_lr, float noise_lr,
-                         const float* sgld_eps, void* workspace, size_t workspace_bytes, void* stream) {
+                         const float* sgld_eps, const int32_t* peer_mine, int peer_n, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   TTS_REQUIRE(G >= 2, "relocation needs G >= 2");
   TTS_REQUIRE(params && m && v && step && n_dead_out && targets_out && workspace, "null pointer");
   TTS_REQUIRE(dead_frac < 1.f, "dead_frac must be < 1");
@@ -485,6 +497,8 @@ static int relocate_core(float* params, float* m, float* v, int G, float dead_th
   a.sgld_lr = sgld_lr;
   a.noise_lr = noise_lr;
   a.sgld_eps = sgld_eps;
+  a.peer_mine = peer_mine;
+  a.peer_n = peer_n;
   cudaStream_t st = as_stream(stream);
   // the barrier word and the digit histograms start at zero (the per-target counts are zeroed by
   // the kernel)
@@ -509,7 +523,8 @@ extern "C" int tts_relocate(float* params, float* m, float* v, int G, float dead
                             int32_t* n_dead_out, int32_t* targets_out, void* workspace, size_t workspace_bytes,
                             void* stream) {
   return relocate_core(params, m, v, G, dead_thr, dead_frac, offset, targets_in, offset_noise_in, step, seed,
-                       n_dead_out, targets_out, nullptr, 0.f, nullptr, workspace, workspace_bytes, stream);
+                       n_dead_out, targets_out, nullptr, 0.f, nullptr, nullptr, 0, workspace, workspace_bytes,
+                       stream);
 }
 
 extern "C" int tts_sgld_relocate(float* params, float* m, float* v, int G, const double* lr7, float noise_lr,
@@ -519,5 +534,17 @@ extern "C" int tts_sgld_relocate(float* params, float* m, float* v, int G, const
                                  size_t workspace_bytes, void* stream) {
   TTS_REQUIRE(lr7, "null learning-rate table");
   return relocate_core(params, m, v, G, dead_thr, dead_frac, offset, targets_in, offset_noise_in, step, seed,
-                       n_dead_out, targets_out, lr7, noise_lr, eps_noise, workspace, workspace_bytes, stream);
+                       n_dead_out, targets_out, lr7, noise_lr, eps_noise, nullptr, 0, workspace, workspace_bytes,
+                       stream);
+}
+
+extern "C" int tts_peer_sgld_relocate(float* params, float* m, float* v, int G, const double* lr7, float noise_lr,
+                                      const float* eps_noise, float dead_thr, float dead_frac, float offset,
+                                      const int32_t* step, uint64_t seed, int32_t* n_dead_out, int32_t* targets_out,
+                                      int32_t* const* flags, int rank, int N, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  TTS_REQUIRE(lr7 && flags && N >= 1 && N <= PEER_MAX && rank >= 0 && rank < N && flags[rank],
+              "bad peer SGLD + relocation arguments");
+  return relocate_core(params, m, v, G, dead_thr, dead_frac, offset, nullptr, nullptr, step, seed, n_dead_out,
+                       targets_out, lr7, noise_lr, eps_noise, flags[rank], N, workspace, workspace_bytes, stream);
 }

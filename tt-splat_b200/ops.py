@@ -366,6 +366,23 @@ def adam_peer(regions, m, v, G, sh_degree, step, lr7, loss_total, betas=(0.9, 0.
          ptr(loss_total), regions.t_flags, stream())
 
 
+def peer_sgld_relocate(regions, flat, m, v, G, step, lr7, noise_lr, eps_noise=None, dead_thr=0.005, dead_frac=0.0,
+                       offset=0.0, seed=0, ws=None, out=None):
+    """peer_sgld(...) then relocate(...) in one launch (waits for phase 1 like peer_sgld)."""
+    _dev(flat, m, v, step, lr7, eps_noise)
+    dev = flat.device
+    if out is None:
+        out = dict(n_dead=torch.zeros(1, dtype=torch.int32, device=dev),
+                   targets=torch.empty(G, dtype=torch.int32, device=dev))
+    nbytes = lib().tts_relocate_workspace_bytes(G)
+    ws = ws or Workspace(dev)
+    buf = ws.get(nbytes)
+    call("tts_peer_sgld_relocate", ptr(flat), ptr(m), ptr(v), G, ptr(lr7), float(noise_lr), ptr(eps_noise),
+         float(dead_thr), float(dead_frac), float(offset), ptr(step), int(seed) & (2 ** 64 - 1), ptr(out["n_dead"]),
+         ptr(out["targets"]), regions.t_flags, regions.rank, regions.world, ptr(buf), nbytes, stream())
+    return out
+
+
 def peer_sgld(regions, flat, G, step, lr_means, noise_lr, eps_noise=None, seed=0):
     """SGLD once every rank's update has arrived (phase 1)."""
     _dev(flat, step, eps_noise)

@@ -220,7 +220,9 @@ class TrainStep:
             ops.peer_signal(self.regions, 0, self.step_t)
             ops.adam_peer(self.regions, self.m, self.v, self.G, self.sh_degree, self.step_t, self.lr7,
                           self.loss_total)
-            if self.noise_lr > 0:
+            if relocate and self.noise_lr > 0:
+                pass                      # the relocation launch waits for phase 1 and runs SGLD
+            elif self.noise_lr > 0:
                 ops.peer_sgld(self.regions, self.flat, self.G, self.step_t, self.lr["means"], self.noise_lr,
                               seed=self.seed)
             else:
@@ -233,7 +235,11 @@ class TrainStep:
         if self.dbt is not None:
             ops.adam_vec(self.dbt, self.g_dbt, self.m_dbt, self.v_dbt, self.step_t, self.lr["depth"])
         if relocate:
-            if self.regions is None and self.noise_lr > 0:
+            if self.regions is not None and self.noise_lr > 0:
+                ops.peer_sgld_relocate(self.regions, self.flat, self.m, self.v, self.G, self.step_t, self.lr7,
+                                       self.noise_lr, dead_thr=self.dead_thr, dead_frac=self.dead_frac,
+                                       offset=self.offset, seed=self.seed, ws=self.ws_reloc, out=self.reloc)
+            elif self.noise_lr > 0:
                 ops.sgld_relocate(self.flat, self.m, self.v, self.G, self.step_t, self.lr7, self.noise_lr,
                                   dead_thr=self.dead_thr, dead_frac=self.dead_frac, offset=self.offset,
                                   seed=self.seed, ws=self.ws_reloc, out=self.reloc)
@@ -304,6 +310,9 @@ class TrainStep:
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         fb = up = 0.0
         for _ in range(steps):
+            # a device-side spin ahead of the two replays lets the host enqueue both before the
+            # GPU reaches them, so the halves are device time, not host graph-launch latency
+            torch.cuda._sleep(2_000_000)
             ev[0].record()
             self.graphs["fb"].replay()
             ev[1].record()
@@ -322,7 +331,7 @@ class TrainStep:
         the relocation kernel (on one GPU it also runs the SGLD step of a relocating iteration)."""
         n = 14 + (1 if self.targets_u8 is not None else 0)
         if self.regions is not None:
-            n += 3                                       # signal, Adam, SGLD or wait
+            n += 2 + (0 if relocate and self.noise_lr > 0 else 1)   # signal, Adam, SGLD or wait
         else:
             n += 1 + (1 if self.noise_lr > 0 and not relocate else 0)
         if self.dbt is not None:
