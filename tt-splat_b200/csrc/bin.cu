@@ -598,6 +598,7 @@ __global__ void __launch_bounds__(BS_THREADS)
     for (int d = 0; d < 5; ++d) {
       const int shift = shifts[d], nb = 1 << bits[d];
       for (int i = tid; i < nb; i += BS_THREADS) shist[i] = 0;
+      if (tid == 0) s_le = n;   // replaced by the bucket's count below (n > BS_CAP: not yet collected)
       __syncthreads();
       const u64 pval = s_pval, pmask = s_pmask;
       for (int j = 0; j < S; ++j) {
@@ -608,27 +609,47 @@ __global__ void __launch_bounds__(BS_THREADS)
         }
       }
       __syncthreads();
-      if (tid == 0) {
-        const int need = K - s_below;
-        int c = 0, b = 0;
-        for (; b < nb - 1; ++b) {
-          if (c + shist[b] >= need) break;
-          c += shist[b];
+      // the bucket holding the need-th key (the first whose cumulative count reaches it): each
+      // thread sums its nb / BS_THREADS consecutive bins, a block scan gives the thread offsets,
+      // and the one thread whose range holds it walks its own bins
+      const int need = K - s_below;
+      const int per = nb / BS_THREADS;
+      int loc = 0;
+      for (int q = 0; q < per; ++q) loc += shist[tid * per + q];
+      const int excl = block_excl_scan(loc, s_scan);
+      if (excl < need && need <= excl + loc) {
+        int c = excl, b = 0;
+        for (; b < per - 1; ++b) {
+          if (c + shist[tid * per + b] >= need) break;
+          c += shist[tid * per + b];
         }
+        const int bucket = tid * per + b;
         s_below += c;
-        s_pval = pval | ((u64)b << shift);
+        s_pval = pval | ((u64)bucket << shift);
         s_pmask = pmask | ((u64)(nb - 1) << shift);
-        s_le = s_below + shist[b];
+        s_le = s_below + shist[bucket];
         s_cnt = 0;
       }
       __syncthreads();
       if (s_le <= BS_CAP) {
+        // collect the keys at or below the bucket: one shared-memory atomic per warp (ballot)
         const u64 upper = s_pval | ((1ull << shift) - 1ull);
+        const int lane = tid & 31;
         for (int j = 0; j < S; ++j) {
           const int len = s_len[j], beg = s_beg[j];
-          for (int i = tid; i < len; i += BS_THREADS) {
-            const u64 key = make_key(j, rv[beg + i], ctx, cty);
-            if (key <= upper) skeys[atomicAdd(&s_cnt, 1)] = key;
+          for (int i0 = 0; i0 < len; i0 += BS_THREADS) {
+            const int i = i0 + tid;
+            u64 key = 0;
+            bool sel = false;
+            if (i < len) {
+              key = make_key(j, rv[beg + i], ctx, cty);
+              sel = key <= upper;
+            }
+            const unsigned bal = __ballot_sync(0xffffffffu, sel);
+            int base = 0;
+            if (lane == 0 && bal) base = atomicAdd(&s_cnt, __popc(bal));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (sel) skeys[base + __popc(bal & ((1u << lane) - 1u))] = key;
           }
         }
         __syncthreads();
