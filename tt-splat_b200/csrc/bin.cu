@@ -17,8 +17,9 @@
 
 namespace tts {
 
-constexpr int BS_THREADS = 256;
-constexpr int BS_CAP = 4096;
+constexpr int BS_THREADS = 512;
+constexpr int BS_CAP = 8192;           // keys held in (dynamic) shared memory: 64 KB
+constexpr int SORT_CAP = 1024;         // keys the block sorts after its radix select
 constexpr int BS_MAXS = 49;  // (2R+1)^2 for R <= 3
 typedef unsigned long long u64;
 
@@ -497,7 +498,7 @@ __global__ void __launch_bounds__(BS_THREADS)
                  int R, int K, const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
                  int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv,
                  void* __restrict__ slots, const int* __restrict__ list, const int* __restrict__ list_count) {
-  __shared__ u64 skeys[BS_CAP];
+  extern __shared__ u64 skeys[];       // [BS_CAP]
   __shared__ int shist[2048];
   __shared__ int s_beg[BS_MAXS], s_len[BS_MAXS], s_off[BS_MAXS + 1];
   __shared__ u64 s_pval, s_pmask;
@@ -540,32 +541,74 @@ __global__ void __launch_bounds__(BS_THREADS)
   if (n <= BS_CAP) {
     for (int j = 0; j < S; ++j) {
       const int len = s_len[j], beg = s_beg[j], off = s_off[j];
+#pragma unroll 4
       for (int i = tid; i < len; i += BS_THREADS) skeys[off + i] = make_key(j, rv[beg + i], ctx, cty);
     }
     nsel = n;
     if (n > K) {
-      // select before sorting: q* = the quantised distance of the K-th smallest key; only keys
-      // with q <= q* can be kept, so only those are sorted
-      for (int i = tid; i < 2048; i += BS_THREADS) shist[i] = 0;
-      __syncthreads();
-      for (int i = tid; i < n; i += BS_THREADS) atomicAdd(&shist[(int)(skeys[i] >> 40)], 1);
-      __syncthreads();
-      int loc = 0;
-#pragma unroll
-      for (int b = 0; b < 8; ++b) loc += shist[tid * 8 + b];
-      const int excl = block_excl_scan(loc, s_scan);
-      if (excl < K && K <= excl + loc) {
-        int c = excl, b = 0;
-        for (; b < 7; ++b) {
-          if (c + shist[tid * 8 + b] >= K) break;
-          c += shist[tid * 8 + b];
-        }
-        s_le = c + shist[tid * 8 + b];      // keys with q <= q*
-        s_pval = (u64)(tid * 8 + b);        // q*
+      // MSB radix select over the keys in shared memory (digits q | j | g of 11/8/11/11/10 bits):
+      // after each digit the bucket holding the K-th smallest key is known; stop once the keys at
+      // or below it fit a small sort (SORT_CAP).  Tiles whose candidates share one quantised
+      // distance (border tiles collect off-screen gaussians, all at q = 2047) are settled by the
+      // stencil and id digits instead of sorting thousands of ties.  Histogram increments are
+      // aggregated per warp over lanes with the same bin (match_any).
+      const int shifts[5] = {40, 32, 21, 10, 0};
+      const int bits[5] = {11, 8, 11, 11, 10};
+      if (tid == 0) {
+        s_pval = 0ull;
+        s_pmask = 0ull;
+        s_below = 0;
       }
       __syncthreads();
-      const unsigned qstar = (unsigned)s_pval;
-      // compact the selected keys to the front: each thread stages its contiguous chunk
+      const int lane = tid & 31;
+      int shift = 0;
+      for (int d = 0; d < 5; ++d) {
+        shift = shifts[d];
+        const int nb = 1 << bits[d];
+        for (int i = tid; i < nb; i += BS_THREADS) shist[i] = 0;
+        if (tid == 0) s_le = n;
+        __syncthreads();
+        const u64 pval = s_pval, pmask = s_pmask;
+        for (int i0 = 0; i0 < n; i0 += BS_THREADS) {
+          const int i = i0 + tid;
+          u64 key = 0;
+          bool act = false;
+          if (i < n) {
+            key = skeys[i];
+            act = (key & pmask) == pval;
+          }
+          const int bin = (int)((key >> shift) & (u64)(nb - 1));
+          const unsigned am = __ballot_sync(0xffffffffu, act);
+          if (act) {
+            const unsigned peers = __match_any_sync(am, bin);
+            if (lane == __ffs(peers) - 1) atomicAdd(&shist[bin], __popc(peers));
+          }
+        }
+        __syncthreads();
+        const int need = K - s_below;
+        const int per = nb >= BS_THREADS ? nb / BS_THREADS : 1;
+        int loc = 0;
+        if (tid * per < nb)
+          for (int q = 0; q < per; ++q) loc += shist[tid * per + q];
+        const int excl = block_excl_scan(loc, s_scan);
+        if (excl < need && need <= excl + loc) {
+          int c = excl, b = 0;
+          for (; b < per - 1; ++b) {
+            if (c + shist[tid * per + b] >= need) break;
+            c += shist[tid * per + b];
+          }
+          const int bucket = tid * per + b;
+          s_below += c;
+          s_pval = pval | ((u64)bucket << shift);
+          s_pmask = pmask | ((u64)(nb - 1) << shift);
+          s_le = s_below + shist[bucket];
+        }
+        __syncthreads();
+        if (s_le <= SORT_CAP) break;   // at the last digit the bucket is the K-th key alone
+      }
+      const u64 upper = s_pval | ((1ull << shift) - 1ull);
+      // compact the keys at or below the bucket to the front: each thread stages its contiguous
+      // chunk in registers first, so no write passes a key not yet read
       const int per = (n + BS_THREADS - 1) / BS_THREADS;   // <= BS_CAP / BS_THREADS = 16
       u64 mine[BS_CAP / BS_THREADS];
       int cnt = 0;
@@ -573,12 +616,12 @@ __global__ void __launch_bounds__(BS_THREADS)
       for (int j = 0; j < BS_CAP / BS_THREADS; ++j) {
         const int i = tid * per + j;
         mine[j] = (j < per && i < n) ? skeys[i] : ~0ull;
-        cnt += (j < per && i < n && (unsigned)(mine[j] >> 40) <= qstar) ? 1 : 0;
+        cnt += (j < per && i < n && mine[j] <= upper) ? 1 : 0;
       }
       const int off = block_excl_scan(cnt, s_scan);
 #pragma unroll
       for (int j = 0, w = off; j < BS_CAP / BS_THREADS; ++j) {
-        if (j < per && tid * per + j < n && (unsigned)(mine[j] >> 40) <= qstar) skeys[w++] = mine[j];
+        if (j < per && tid * per + j < n && mine[j] <= upper) skeys[w++] = mine[j];
       }
       __syncthreads();
       nsel = s_le;
@@ -603,6 +646,7 @@ __global__ void __launch_bounds__(BS_THREADS)
       const u64 pval = s_pval, pmask = s_pmask;
       for (int j = 0; j < S; ++j) {
         const int len = s_len[j], beg = s_beg[j];
+#pragma unroll 4
         for (int i = tid; i < len; i += BS_THREADS) {
           const u64 key = make_key(j, rv[beg + i], ctx, cty);
           if ((key & pmask) == pval) atomicAdd(&shist[(int)((key >> shift) & (u64)(nb - 1))], 1);
@@ -610,12 +654,14 @@ __global__ void __launch_bounds__(BS_THREADS)
       }
       __syncthreads();
       // the bucket holding the need-th key (the first whose cumulative count reaches it): each
-      // thread sums its nb / BS_THREADS consecutive bins, a block scan gives the thread offsets,
-      // and the one thread whose range holds it walks its own bins
+      // thread sums its nb / BS_THREADS consecutive bins (one bin, or none, when nb is smaller),
+      // a block scan gives the thread offsets, and the one thread whose range holds it walks its
+      // own bins
       const int need = K - s_below;
-      const int per = nb / BS_THREADS;
+      const int per = nb >= BS_THREADS ? nb / BS_THREADS : 1;
       int loc = 0;
-      for (int q = 0; q < per; ++q) loc += shist[tid * per + q];
+      if (tid * per < nb)
+        for (int q = 0; q < per; ++q) loc += shist[tid * per + q];
       const int excl = block_excl_scan(loc, s_scan);
       if (excl < need && need <= excl + loc) {
         int c = excl, b = 0;
@@ -723,12 +769,16 @@ static int bin_core(const float* mu2d, const int* cell_count, const int2* cell_r
     cudaFuncSetAttribute(k_bin_warp<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
     cudaFuncSetAttribute(k_bin_warp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
     cudaFuncSetAttribute(k_bin_warp<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    cudaFuncSetAttribute(k_bin_select<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(BS_CAP * sizeof(u64)));
+    cudaFuncSetAttribute(k_bin_select<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(BS_CAP * sizeof(u64)));
+    cudaFuncSetAttribute(k_bin_select<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(BS_CAP * sizeof(u64)));
   });
   const unsigned bblocks = (unsigned)(tiles < 296 ? tiles : 296);   // two blocks per SM loop over the list
+  const size_t bsmem = (size_t)BS_CAP * sizeof(u64);
 #define TTS_BIN_LAUNCH(P, PR, SL)                                                                              \
   k_bin_warp<P><<<wblocks, WB_WARPS * 32, wsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, PR, inv_k, idx,   \
                                                        count, cand, inv, SL, w.ovf + 1, w.ovf);                    \
-  k_bin_select<P><<<bblocks, BS_THREADS, 0, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, PR, inv_k, idx, count,   \
+  k_bin_select<P><<<bblocks, BS_THREADS, bsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, PR, inv_k, idx, count,   \
                                                   cand, inv, SL, w.ovf + 1, w.ovf);
   if (proj && slots && slot_format == 1) {
     TTS_BIN_LAUNCH(2, proj, slots)
