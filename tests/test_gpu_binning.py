@@ -154,3 +154,25 @@ def test_no_kept_gaussians(pkg):
     mu = np.zeros((50, 2), np.float32)
     idx, count, cand, inv = gpu_bins(mu, np.zeros(50, bool), 32, 32, 1, 8)
     assert (idx == -1).all() and (count == 0).all() and (cand == 0).all() and (inv == -1).all()
+
+
+def test_border_ties_bit_exact_vs_oracle(pkg):
+    """Off-screen gaussians are binned into the border cells at the clamped distance q = 2047, as
+    in a trained scene: the left-edge tiles hold hundreds of candidates tied at the K-th distance
+    (the warp kernel narrows among the ties on stencil offset and id), the right-edge tiles fewer
+    (compacted and sorted), the corner tiles thousands (the block kernel); tables and inverse
+    table bit-exact against the oracle."""
+    rng = np.random.default_rng(17)
+    H, W = 832, 1264
+    on = np.stack([rng.uniform(0, W, 12000), rng.uniform(0, H, 12000)], 1)
+    left = np.stack([rng.uniform(-3000, -200, 10000), rng.uniform(0, H, 10000)], 1)
+    right = np.stack([rng.uniform(W + 200, W + 3000, 4000), rng.uniform(0, H, 4000)], 1)
+    corner = np.stack([rng.uniform(-3000, -200, 6000), rng.uniform(-3000, -200, 6000)], 1)
+    mu = np.concatenate([on, left, right, corner]).astype(np.float32)
+    mu = np.ascontiguousarray(mu[rng.permutation(len(mu))])
+    keep = np.ones(len(mu), bool)
+    idx, count, cand, inv = gpu_bins(mu, keep, H, W, 1, 128)
+    r = binning.assign_bins(mu, keep, binning.tile_map(H, W), 1, 128)
+    check(idx, count, cand, r.idx, r.valid, r.cand)
+    assert np.array_equal(inv, binning.stencil_inv(r, len(mu), 1))
+    assert (cand > 896).sum() > 0 and ((cand > 256) & (cand <= 896)).sum() > 0

@@ -240,7 +240,7 @@ constexpr int WB_WARPS = 4;
 // tile of the config-2 workload (none has more candidates); larger tiles go to the block kernel,
 // whose per-tile latency (~16 µs) would otherwise bound the stage even for a few tiles.
 constexpr int WCAP = 896;
-constexpr int WSORT_MAX = 512;   // the warp's bitonic sort pads to a power of two within WCAP
+constexpr int WTIE_NARROW = 256; // above this many keys at or below q*, narrow among the ties
 constexpr int WTIES = 64;   // ties at the selection boundary resolved by rank (more: sorted with the rest)
 
 // Warp bucket sort of keys[0, m) (m <= WCAP/2; the upper half of the warp's buffer is the
@@ -463,13 +463,66 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
       }
       __syncwarp();
       m = -1;    // sorted
-    } else {
-      if (m > WSORT_MAX) {
-        // more than WSORT_MAX keys at or below q* (many ties at q*): the block kernel takes the
-        // tile (nothing of it has been written yet)
-        if (lane == 0) ovf_list[atomicAdd(ovf_count, 1)] = (int)gt;
-        return;
+    } else if (m > WTIE_NARROW) {
+      // Many ties at q* (border tiles collect off-screen gaussians, all at the clamped q = 2047):
+      // narrow among the ties on the key's low 40 bits (stencil offset j, then id g) in 6-bit
+      // digits, with warp-aggregated histogram increments, down to the exact threshold key t*
+      // (the (K - c_lt)-th smallest tie).  The kept keys are those at or below t*: exactly K.
+      int need = K - c_lt;
+      u64 pmask = 0x7FFull << 40, pval = (u64)qstar << 40;
+      const int dsh[7] = {32, 26, 20, 14, 8, 2, 0};
+      const int dwd[7] = {6, 6, 6, 6, 6, 6, 2};
+      for (int d = 0; d < 7; ++d) {
+        const int sh = dsh[d];
+        const u64 dm = (u64)((1 << dwd[d]) - 1);
+        hist[lane] = 0;
+        hist[lane + 32] = 0;
+        __syncwarp();
+        for (int base = 0; base < n; base += 32) {
+          const int i = base + lane;
+          const u64 key = i < n ? buf[i] : 0ull;
+          const bool act = i < n && (key & pmask) == pval;
+          const int bin = (int)((key >> sh) & dm);
+          const unsigned am = __ballot_sync(0xffffffffu, act);
+          if (act) {
+            const unsigned peers = __match_any_sync(am, bin);
+            if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
+          }
+        }
+        __syncwarp();
+        const int g0 = hist[2 * lane], g1 = hist[2 * lane + 1];
+        int gin = g0 + g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, gin, o);
+          if (lane >= o) gin += y;
+        }
+        const int gex = gin - g0 - g1;
+        const bool first = gex + g0 >= need;
+        const int src = __ffs(__ballot_sync(0xffffffffu, gex < need && need <= gin)) - 1;
+        const int bkt = __shfl_sync(0xffffffffu, first ? 2 * lane : 2 * lane + 1, src);
+        const int below = __shfl_sync(0xffffffffu, first ? gex : gex + g0, src);
+        const int inb = __shfl_sync(0xffffffffu, first ? g0 : g1, src);
+        need -= below;
+        pval |= (u64)bkt << sh;
+        pmask |= dm << sh;
+        __syncwarp();
+        if (inb == 1) break;    // the bucket holds t* alone
       }
+      // keys at or below t*: a smaller prefix under pmask (q < q* included), or t* itself
+      int w = 0;
+      for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        const u64 key = i < n ? buf[i] : ~0ull;
+        const bool sel = i < n && (key & pmask) <= pval;
+        const unsigned bal = __ballot_sync(0xffffffffu, sel);
+        __syncwarp();
+        if (sel) buf[w + __popc(bal & lt)] = key;
+        w += __popc(bal);
+        __syncwarp();
+      }
+      m = w;    // = K
+    } else {
       // compact the keys with q <= q* to the front (writes never pass the chunk being read)
       int w = 0;
       for (int base = 0; base < n; base += 32) {
