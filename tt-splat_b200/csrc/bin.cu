@@ -241,7 +241,7 @@ constexpr int WB_WARPS = 4;
 // whose per-tile latency (~16 µs) would otherwise bound the stage even for a few tiles.
 constexpr int WCAP = 896;
 constexpr int WTIE_NARROW = 256; // above this many keys at or below q*, narrow among the ties
-constexpr int WTIES = 64;   // ties at the selection boundary resolved by rank (more: sorted with the rest)
+constexpr int WTIES = 64;   // ties at the selection boundary resolved by rank (more: narrowed or sorted)
 
 // Warp bucket sort of keys[0, m) (m <= WCAP/2; the upper half of the warp's buffer is the
 // scratch): keys are distributed into 64 buckets by the top 6 bits of their 11-bit distance
