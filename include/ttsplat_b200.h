@@ -19,7 +19,9 @@
  *   idx      [V][T][K] int32 gaussian id per slot in canonical order, -1 when unused
  *   count    [V][T] int32 = min(cand, K);  cand [V][T] int32 = candidates (overflow = cand-K)
  *   inv      [V][G][(2R+1)^2] int32 flat slot t*K+k of gaussian g at stencil offset j, or -1
- *   slots    [V][T][K][TTS_SLOT_FLOATS]  theta_u[6] (tile-local), color_o[3], o_col, 0, 0
+ *   slots    [V][T][K][TTS_SLOT_FLOATS]  theta_u[6] (tile-local), color_o[3], o_col, dead, 0
+ *            (dead = 1 when the binning found the slot's weight zero at every pixel of its tile:
+ *            the tile kernels skip it, bit-identically; rows with 0 there are always evaluated) 
  *            or, compact bf16: [V][T][K][TTS_SLOT_BF16] bf16 theta_hi[6], theta_lo[6] (theta_u =
  *            hi + lo), color_o[3], o_col
  *   img      [V][H][W][3], den [V][H][W], gimg like img

@@ -354,3 +354,45 @@ def test_dense_wsr_polysplat_vs_oracle(pkg):
     assert rel_l2(to.grad.cpu().numpy(), go) < 1e-4
     assert rel_l2(tcol.grad.cpu().numpy(), gcol) < 1e-4
     assert abs(float(wb.grad) - gwb) < 1e-4 * abs(gwb)
+
+
+def test_dead_slots_change_no_bits(pkg):
+    """Slots whose weight is zero at every pixel of their tile (u <= 0 everywhere: gaussians
+    binned into neighbouring tiles they never reach) are skipped by the tile kernels.  Removing
+    the clearly dead ones from the tables (max u <= -1e-3) leaves the image, the denominators, the
+    live slots' gradients and the w_b partials bit for bit unchanged, and the removed slots'
+    gradients are exactly zero."""
+    from tt_splat_b200 import ops
+    from tt_splat_b200.model import pack_arrays
+    from tt_splat_b200 import camera
+    sc = pkg.synthetic.config2(seed=13, G=6000, H=96, W=128, n_views=2)
+    G, H, W = 6000, 96, 128
+    flat = pack_arrays(sc["params"]).to(DEV)
+    cams = camera.pack_cameras([camera.Camera.from_dict(c) for c in sc["cams"]], DEV)
+    pj = ops.project(flat, G, 3, cams, H, W)
+    bp = ops.bin_pack(pj, G, H, W, 1, 64)
+    slots, count = bp["slots"], bp["count"]
+    V, T, K, _ = slots.shape
+    c_b = torch.ones(3, device=DEV)
+    p = torch.arange(16, device=DEV, dtype=torch.float32) + 0.5
+    py, px = torch.meshgrid(p, p, indexing="ij")
+    phi = torch.stack([px * px, py * py, px * py, px, py, torch.ones_like(px)], -1).reshape(256, 6)
+    umax = torch.einsum("vtkc,pc->vtkp", slots[..., :6], phi).amax(-1)
+    valid = torch.arange(K, device=DEV)[None, None, :] < count[..., None]
+    keep = valid & (umax > -1e-3)
+    assert int((valid & ~keep).sum()) > 0                      # the scene has dead slots
+    # compacted tables: the kept slots of each tile first, in order
+    order = torch.argsort((~keep).to(torch.int8), dim=-1, stable=True)
+    slots2 = torch.gather(slots, 2, order[..., None].expand(-1, -1, -1, slots.shape[-1])).contiguous()
+    count2 = keep.sum(-1).to(torch.int32).contiguous()
+    a = ops.render_fwd(slots, count, H, W, flat[59 * G:], c_b)
+    b = ops.render_fwd(slots2, count2, H, W, flat[59 * G:], c_b)
+    assert torch.equal(a["img"], b["img"]) and torch.equal(a["den"], b["den"])
+    gimg = torch.randn(a["img"].shape, device=DEV, generator=torch.Generator(DEV).manual_seed(2))
+    ga = ops.render_bwd(slots, count, H, W, c_b, a["img"], a["den"], gimg)
+    gb = ops.render_bwd(slots2, count2, H, W, c_b, b["img"], b["den"], gimg)
+    assert torch.equal(ga["gwb"], gb["gwb"])
+    kept_a = torch.gather(ga["slot_grads"], 2, order[..., None].expand(-1, -1, -1, 10))
+    live2 = torch.arange(K, device=DEV)[None, None, :] < count2[..., None]
+    assert torch.equal(kept_a[live2], gb["slot_grads"][live2])
+    assert (ga["slot_grads"][valid & ~keep] == 0).all()

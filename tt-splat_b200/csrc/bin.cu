@@ -194,7 +194,10 @@ __device__ __forceinline__ void emit_tile(const u64* keys, int n, int v, int t, 
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(slots) + o * TTS_SLOT_FLOATS);
           dst[0] = make_float4(th[0], th[1], th[2], th[3]);
           dst[1] = make_float4(th[4], th[5], p1.y, p1.z);
-          dst[2] = make_float4(p1.w, p2.x, 0.f, 0.f);
+          // field 10 marks a slot whose weight is zero at every pixel of the tile (the tile
+          // kernels skip it; the tables keep it, as the reference's do)
+          const bool dead = slot_dead(th[0], th[1], th[2], th[3], th[4], th[5]);
+          dst[2] = make_float4(p1.w, p2.x, dead ? 1.f : 0.f, 0.f);
         } else {
           // compact bf16 row: theta_u as a bf16 (hi, lo) pair (hi + lo carries ~16 significant
           // bits, which u = Phi.theta needs), colour_o and o_col as bf16

@@ -169,6 +169,28 @@ __device__ __forceinline__ void box_muller(uint32_t a, uint32_t b, float& n0, fl
   n1 = r * s;
 }
 
+// Whether a slot's weight max(u, 0)^2 is exactly zero at every pixel centre of the tile, so that
+// the tile kernels may skip it without changing a bit.  u = theta . Phi is a concave quadratic for
+// the positive-definite conics of the projection; the region u > -m, with m = 1e-6 x the sum of
+// the terms' magnitudes over the tile (far above the rounding of the kernels' fp32 evaluation of u,
+// at most ~3e-7 of that sum), is an ellipse, and when its bounding box misses the box of pixel
+// centres [0.5, 15.5]^2 every evaluated u there is negative.  Evaluated in double; anything else
+// (a degenerate or non-finite row) counts as live.
+__device__ __forceinline__ bool slot_dead(float t0, float t1, float t2, float t3, float t4, float t5) {
+  const double A = t0, B = t1, C = t2, D = t3, E = t4, F = t5;
+  const double det = 4.0 * A * B - C * C;
+  if (!(A < 0.0 && B < 0.0 && det > 0.0)) return false;
+  // the peak (xs, ys) = (XN, YN) / det and everything below scaled by det > 0 (no division)
+  const double XN = C * E - 2.0 * B * D, YN = C * D - 2.0 * A * E;
+  const double M = (fabs(A) + fabs(B) + fabs(C)) * 240.25 + (fabs(D) + fabs(E)) * 15.5 + fabs(F);
+  const double umd = (F + 1e-6 * M) * det + 0.5 * (D * XN + E * YN);   // (peak of u above -m) * det
+  if (!(umd > 0.0)) return umd <= 0.0;
+  const double rx = -4.0 * B * umd, ry = -4.0 * A * umd;   // squared half-extents * det^2
+  const double lo = 0.5 * det, hi = 15.5 * det;
+  return (XN < lo && (lo - XN) * (lo - XN) > rx) || (XN > hi && (XN - hi) * (XN - hi) > rx) ||
+         (YN < lo && (lo - YN) * (lo - YN) > ry) || (YN > hi && (YN - hi) * (YN - hi) > ry);
+}
+
 // ---- packed FP32 pairs (sm_100a .f32x2 arithmetic: two IEEE fp32 lanes per instruction) ----
 typedef unsigned long long f32x2;
 __device__ __forceinline__ f32x2 mk2(float lo, float hi) {

@@ -74,6 +74,38 @@ __global__ void __launch_bounds__(FWD_THREADS)
     __syncwarp();
   }
 
+  // the binning marks a slot whose weight is zero at every pixel of the tile (row field 10, see
+  // slot_dead); the live rows are moved to the front in slot order (the per-pixel sums keep
+  // their order: a dead slot would only add exact zeros).  Each 32-row chunk is read before it is
+  // written, and a row only moves down.  Compact bf16 rows carry no mark.
+  int n_live = n;
+  if (!BF16) {
+    n_live = 0;
+    for (int c0 = 0; c0 < n; c0 += FWD_THREADS) {
+      const int sl = c0 + lane;
+      float4 r0 = make_float4(0.f, 0.f, 0.f, 0.f), r1 = r0, r2 = r0;
+      if (sl < n) {
+        const float4* src = reinterpret_cast<const float4*>(s_rows) + 3 * sl;
+        r0 = src[0];
+        r1 = src[1];
+        r2 = src[2];
+      }
+      const bool live = sl < n && r2.z == 0.f;
+      const unsigned bal = __ballot_sync(0xffffffffu, live);
+      if (bal != (c0 + FWD_THREADS <= n ? 0xffffffffu : (1u << (n - c0)) - 1u) || n_live != c0) {
+        // something to move in this chunk
+        __syncwarp();
+        if (live) {
+          float4* dst = reinterpret_cast<float4*>(s_rows) + 3 * (n_live + __popc(bal & ((1u << lane) - 1u)));
+          dst[0] = r0;
+          dst[1] = r1;
+          dst[2] = r2;
+        }
+      }
+      n_live += __popc(bal);
+    }
+    __syncwarp();
+  }
   const float wb = w_b_is_raw ? softplusf(*w_b_ptr) : *w_b_ptr;
   // lane -> row ly, pixels x0 .. x0+7 (four adjacent pairs); one row's srow/rrow serve 8 pixels
   const int ly = lane >> 1, x0 = 8 * (lane & 1);
@@ -86,7 +118,7 @@ __global__ void __launch_bounds__(FWD_THREADS)
 #pragma unroll
   for (int j = 0; j < 4; j++) a0[j] = a1[j] = a2[j] = a3[j] = z;
   const float4* rows = reinterpret_cast<const float4*>(s_rows);
-  for (int s = 0; s < n; ++s) {
+  for (int s = 0; s < n_live; ++s) {
     const float4 A = rows[3 * s + 0];   // t0 t1 t2 t3
     const float4 B = rows[3 * s + 1];   // t4 t5 cr cg
     const float4 C = rows[3 * s + 2];   // cb oc 0 0
@@ -162,9 +194,19 @@ __global__ void __launch_bounds__(256, 3)
     for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += s_red[i];
     gwb_partial[(long long)v * T + t] = s;
   }
+  // a slot the binning marked dead (zero weight at every pixel: every sum below would be +0)
+  // writes its zero gradient row and leaves; slots are in ascending distance, so the dead ones
+  // gather at the end of the list and whole warps of them skip the pixel loop
   const int k = tid;
   if (k >= n) return;
-  const long long o = ((long long)v * T + t) * K + k;
+  const long long row0 = ((long long)v * T + t) * K;
+  if (slots[(row0 + k) * TTS_SLOT_FLOATS + 10] != 0.f) {
+    float2* out = reinterpret_cast<float2*>(slot_grads + (row0 + k) * TTS_SLOT_GRAD_FLOATS);
+    const float2 z2 = make_float2(0.f, 0.f);
+    out[0] = z2; out[1] = z2; out[2] = z2; out[3] = z2; out[4] = z2;
+    return;
+  }
+  const long long o = row0 + k;
   const float4* row = reinterpret_cast<const float4*>(slots + o * TTS_SLOT_FLOATS);
   const float4 A = row[0], B = row[1], C = row[2];
   const f32x2 t0 = mk2(A.x, A.x);
