@@ -80,7 +80,9 @@ int tts_project(const float* params, int G, int sh_degree, const float* cams, in
  * tts_bin_pack writes fp32 slot rows (slot_format 0) or compact bf16 rows (slot_format 1, the
  * forward-only bf16 path of tts_render_fwd) for the count[t] valid slots of each tile only; the
  * tile kernels read no further, and a caller that hands the rows on as [T,K] operands zeroes the
- * rest itself (the reference's operands are zero in invalid slots). */
+ * rest itself (the reference's operands are zero in invalid slots).  With fp32 slot rows, a slot
+ * marked dead in its row (zero weight at every pixel of the tile) has no inverse entry (-1): its
+ * gradient is zero, and tts_backward_params skips it. */
 size_t tts_bin_workspace_bytes(int G, int V, int H, int W);
 int tts_bin_from_mu2d(const float* mu2d, const uint8_t* keep, int G, int V, int H, int W, int R,
                       int K, int32_t* idx, int32_t* count, int32_t* cand, int32_t* inv,

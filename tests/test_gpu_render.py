@@ -396,3 +396,36 @@ def test_dead_slots_change_no_bits(pkg):
     live2 = torch.arange(K, device=DEV)[None, None, :] < count2[..., None]
     assert torch.equal(kept_a[live2], gb["slot_grads"][live2])
     assert (ga["slot_grads"][valid & ~keep] == 0).all()
+
+
+def test_dead_slots_without_inverse_entries_change_no_bits(pkg):
+    """With fp32 slot rows the binning leaves dead slots out of the inverse table; the parameter
+    backward through it equals, bit for bit, the one through the complete table of the same
+    binning, and the entries left out are exactly the dead-marked slots'."""
+    from tt_splat_b200 import camera, ops
+    from tt_splat_b200.model import pack_arrays
+    sc = pkg.synthetic.config2(seed=14, G=6000, H=96, W=128, n_views=2)
+    G, H, W, K = 6000, 96, 128, 64
+    flat = pack_arrays(sc["params"]).to(DEV)
+    cams = camera.pack_cameras([camera.Camera.from_dict(c) for c in sc["cams"]], DEV)
+    pj = ops.project(flat, G, 3, cams, H, W)
+    bp = ops.bin_pack(pj, G, H, W, 1, K)
+    full = ops.bin_from_mu2d(pj["mu2d"], pj["keep"], H, W, 1, K)       # no rows: complete table
+    assert torch.equal(bp["idx"], full[0])
+    inv_p, inv_f = bp["inv"], full[3]
+    dead = bp["slots"][..., 10] != 0
+    valid = bp["idx"] >= 0
+    assert int((dead & valid).sum()) > 0
+    flatpos = torch.arange(bp["idx"][0].numel(), device=DEV).reshape(bp["idx"].shape[1:])
+    for v in range(2):
+        dead_pos = set(flatpos[dead[v] & valid[v]].tolist())
+        missing = (inv_f[v] >= 0) & (inv_p[v] < 0)
+        assert set(inv_f[v][missing].tolist()) == dead_pos
+        assert torch.equal(inv_p[v][inv_p[v] >= 0], inv_f[v][inv_p[v] >= 0])
+    c_b = torch.ones(3, device=DEV)
+    rf = ops.render_fwd(bp["slots"], bp["count"], H, W, flat[59 * G:], c_b)
+    gimg = torch.randn(rf["img"].shape, device=DEV, generator=torch.Generator(DEV).manual_seed(4))
+    rb = ops.render_bwd(bp["slots"], bp["count"], H, W, c_b, rf["img"], rf["den"], gimg)
+    ga = ops.backward_params(flat, G, 3, cams, H, W, 1, K, inv_p, rb["slot_grads"], rb["gwb"], proj=pj["proj"])
+    gb = ops.backward_params(flat, G, 3, cams, H, W, 1, K, inv_f, rb["slot_grads"], rb["gwb"], proj=pj["proj"])
+    assert torch.equal(ga, gb)

@@ -177,7 +177,10 @@ __device__ __forceinline__ void emit_tile(const u64* keys, int n, int v, int t, 
       const int g = (int)(unsigned)(key & 0xffffffffull);
       const int j = (int)((key >> 32) & 0xffull);
       idx[o] = g;
-      if (inv) inv[((long long)v * G + g) * S + j] = t * K + k;
+      // a slot the fp32 packing marks dead gets no inverse entry: its gradient row is zero, so
+      // the slot->gaussian gather may skip it (and a view where all of a gaussian's slots are
+      // dead drops out of its parameter backward) without changing a bit
+      if (inv && PACK != 1) inv[((long long)v * G + g) * S + j] = t * K + k;
       if (PACK) {
         const float4* p = reinterpret_cast<const float4*>(proj + ((long long)v * G + g) * TTS_PROJ_FLOATS);
         const float4 p0 = p[0], p1 = p[1], p2 = p[2];
@@ -198,6 +201,7 @@ __device__ __forceinline__ void emit_tile(const u64* keys, int n, int v, int t, 
           // kernels skip it; the tables keep it, as the reference's do)
           const bool dead = slot_dead(th[0], th[1], th[2], th[3], th[4], th[5]);
           dst[2] = make_float4(p1.w, p2.x, dead ? 1.f : 0.f, 0.f);
+          if (inv && !dead) inv[((long long)v * G + g) * S + j] = t * K + k;
         } else {
           // compact bf16 row: theta_u as a bf16 (hi, lo) pair (hi + lo carries ~16 significant
           // bits, which u = Phi.theta needs), colour_o and o_col as bf16
