@@ -156,21 +156,26 @@ def test_no_kept_gaussians(pkg):
     assert (idx == -1).all() and (count == 0).all() and (cand == 0).all() and (inv == -1).all()
 
 
-def test_border_ties_bit_exact_vs_oracle(pkg):
+@pytest.mark.parametrize("n_unkept", [0, 110000])
+def test_border_ties_bit_exact_vs_oracle(n_unkept, pkg):
     """Off-screen gaussians are binned into the border cells at the clamped distance q = 2047, as
     in a trained scene: the left-edge tiles hold hundreds of candidates tied at the K-th distance
     (the warp kernel narrows among the ties on stencil offset and id), the right-edge tiles fewer
     (compacted and sorted), the corner tiles thousands (the block kernel); tables and inverse
-    table bit-exact against the oracle."""
+    table bit-exact against the oracle.  With 110000 gaussians more that are not kept, G exceeds
+    2^17 and the warp kernel keys with 64 bits instead of 32 (ids spread over the whole range)."""
     rng = np.random.default_rng(17)
     H, W = 832, 1264
     on = np.stack([rng.uniform(0, W, 12000), rng.uniform(0, H, 12000)], 1)
     left = np.stack([rng.uniform(-3000, -200, 10000), rng.uniform(0, H, 10000)], 1)
     right = np.stack([rng.uniform(W + 200, W + 3000, 4000), rng.uniform(0, H, 4000)], 1)
     corner = np.stack([rng.uniform(-3000, -200, 6000), rng.uniform(-3000, -200, 6000)], 1)
-    mu = np.concatenate([on, left, right, corner]).astype(np.float32)
-    mu = np.ascontiguousarray(mu[rng.permutation(len(mu))])
-    keep = np.ones(len(mu), bool)
+    pad = np.stack([rng.uniform(0, W, n_unkept), rng.uniform(0, H, n_unkept)], 1)
+    mu = np.concatenate([on, left, right, corner, pad]).astype(np.float32)
+    keep = np.arange(len(mu)) < len(mu) - n_unkept
+    perm = rng.permutation(len(mu))
+    mu, keep = np.ascontiguousarray(mu[perm]), np.ascontiguousarray(keep[perm])
+    assert (len(mu) > 2 ** 17) == (n_unkept > 0)
     idx, count, cand, inv = gpu_bins(mu, keep, H, W, 1, 128)
     r = binning.assign_bins(mu, keep, binning.tile_map(H, W), 1, 128)
     check(idx, count, cand, r.idx, r.valid, r.cand)

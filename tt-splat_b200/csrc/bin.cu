@@ -4,9 +4,10 @@
 // tile gathers the candidates of its (2R+1)^2 neighbour cells, keys them exactly as the
 // reference (tile-local key q = clamp(long(dist2), 0, 2047) with dist2 in fp32, no FMA
 // contraction), and keeps the K smallest of (q, stencil offset j, gaussian id) in ascending
-// order — the stable order of the reference's packed sort key.  Per tile, candidates up to
-// BS_CAP are sorted in shared memory; larger candidate sets first run an MSB radix select over
-// the 51-bit key (digits q | j | g) until at most BS_CAP keys remain below the threshold.
+// order — the stable order of the reference's packed sort key.  A warp per tile selects and
+// sorts up to WCAP candidates in shared memory (32-bit keys when ids and stencil offsets fit
+// them, else 64-bit); a block per tile takes larger candidate sets, with an MSB radix select
+// over the 51-bit key (digits q | j | g) until at most SORT_CAP keys remain to sort.
 // The epilogue writes idx/count/cand, the stencil-indexed inverse table used by the
 // deterministic slot->gaussian reduction, and (optionally) the packed slot rows
 // theta_u[6] | color_o[3] | o_col of _operands (:207-211, theta_u_gathered :130-143).
@@ -149,33 +150,61 @@ __device__ __forceinline__ void bitonic_sort(u64* s, int P) {
   }
 }
 
+// Packed sort keys (q, stencil offset j, gaussian id g), compared as unsigned integers: the
+// 64-bit form q<<40 | j<<32 | g holds any problem; the 32-bit form q<<21 | j<<17 | g holds
+// G <= 2^17 and S <= 16 stencil offsets (R <= 1) in the same order, and halves the warp's key
+// buffer and its compare and shuffle work.  dsh/dwd: shift and width of the digits of the bits
+// below q (j, then g) that the tie narrowing walks, most significant first.
+template <class KT>
+struct KeyBits;
+template <>
+struct KeyBits<u64> {
+  static constexpr int QS = 40, JS = 32, ND = 7;
+  static constexpr u64 GM = 0xffffffffull, JM = 0xffull;
+  // digits 32, 26, 20, 14, 8, 2 (6 bits) and 0 (2 bits)
+  __device__ static int dsh(int d) { return d < 6 ? 32 - 6 * d : 0; }
+  __device__ static int dwd(int d) { return d < 6 ? 6 : 2; }
+};
+template <>
+struct KeyBits<unsigned> {
+  static constexpr int QS = 21, JS = 17, ND = 4;
+  static constexpr unsigned GM = 0x1ffffu, JM = 0xfu;
+  // digits 15, 9, 3 (6 bits) and 0 (3 bits)
+  __device__ static int dsh(int d) { return d < 3 ? 15 - 6 * d : 0; }
+  __device__ static int dwd(int d) { return d < 3 ? 6 : 3; }
+};
+constexpr int KEY32_MAX_G = 1 << 17, KEY32_MAX_S = 16;
+
 // Quantised distance of the reference: clamp(long(dist2), 0, 2047), torch's INT64_MIN for
 // non-finite or >= 2^63 values clamping to 0.
-__device__ __forceinline__ u64 make_key(int j, float4 r, float ctx, float cty) {
+template <class KT = u64>
+__device__ __forceinline__ KT make_key(int j, float4 r, float ctx, float cty) {
   const float dx = __fsub_rn(r.y, ctx);
   const float dy = __fsub_rn(r.z, cty);
   const float d2 = __fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy));
   unsigned q = 0;
   if (d2 >= 0.0f && d2 < 9.223372036854775808e18f) q = d2 >= 2047.0f ? 2047u : (unsigned)d2;
-  return ((u64)q << 40) | ((u64)(unsigned)j << 32) | (u64)(unsigned)__float_as_int(r.x);
+  using KB = KeyBits<KT>;
+  return ((KT)q << KB::QS) | ((KT)(unsigned)j << KB::JS) | (KT)(unsigned)__float_as_int(r.x);
 }
 
 // Writes the outputs of one tile from its sorted keys (threads first, first+step, ... of the
 // caller's group): idx/count/cand, the stencil-indexed inverse table and, with PACK, the slot
 // rows theta_u (tools/m4_train_binned.py:130-143, the reference's fp32 op order) | color_o | keo.
-template <int PACK>
-__device__ __forceinline__ void emit_tile(const u64* keys, int n, int v, int t, int ntx, int T, int G, int S, int K,
+template <int PACK, class KT = u64>
+__device__ __forceinline__ void emit_tile(const KT* keys, int n, int v, int t, int ntx, int T, int G, int S, int K,
                                           const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
                                           int* __restrict__ inv, void* __restrict__ slots, int first, int step) {
+  using KB = KeyBits<KT>;
   const int cnt = min(n, K);
   const int tx = t % ntx, ty = t / ntx;
   const float ox = (float)(tx * 16), oy = (float)(ty * 16);
   for (int k = first; k < K; k += step) {
     const long long o = ((long long)v * T + t) * K + k;
     if (k < cnt) {
-      const u64 key = keys[k];
-      const int g = (int)(unsigned)(key & 0xffffffffull);
-      const int j = (int)((key >> 32) & 0xffull);
+      const KT key = keys[k];
+      const int g = (int)(unsigned)(key & KB::GM);
+      const int j = (int)((key >> KB::JS) & KB::JM);
       idx[o] = g;
       // a slot the fp32 packing marks dead gets no inverse entry: its gradient row is zero, so
       // the slot->gaussian gather may skip it (and a view where all of a gaussian's slots are
@@ -256,12 +285,14 @@ constexpr int WTIES = 64;   // ties at the selection boundary resolved by rank (
 // among the bucket's keys (keys are unique: one stencil offset per gaussian and tile).  Buckets
 // beyond 64 keys would make the ranking quadratic: the caller then falls back to the bitonic
 // sort.  Returns false (keys untouched) in that case.
-__device__ __forceinline__ bool bucket_sort(u64* keys, int m, int lane, int* hist, int* start) {
-  u64* tmp = keys + WCAP / 2;
+template <class KT>
+__device__ __forceinline__ bool bucket_sort(KT* keys, int m, int lane, int* hist, int* start) {
+  constexpr int BS = KeyBits<KT>::QS + 5;
+  KT* tmp = keys + WCAP / 2;
   hist[lane] = 0;
   hist[lane + 32] = 0;
   __syncwarp();
-  for (int i = lane; i < m; i += 32) atomicAdd(&hist[(int)((keys[i] >> 45) & 63ull)], 1);
+  for (int i = lane; i < m; i += 32) atomicAdd(&hist[(int)((keys[i] >> BS) & 63u)], 1);
   __syncwarp();
   const int h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
   if (__any_sync(0xffffffffu, h0 > 64 || h1 > 64)) return false;
@@ -279,13 +310,13 @@ __device__ __forceinline__ bool bucket_sort(u64* keys, int m, int lane, int* his
   if (lane == 31) start[64] = incl;
   __syncwarp();
   for (int i = lane; i < m; i += 32) {
-    const u64 k = keys[i];
-    tmp[atomicAdd(&hist[(int)((k >> 45) & 63ull)], 1)] = k;
+    const KT k = keys[i];
+    tmp[atomicAdd(&hist[(int)((k >> BS) & 63u)], 1)] = k;
   }
   __syncwarp();
   for (int i = lane; i < m; i += 32) {
-    const u64 k = tmp[i];
-    const int b = (int)((k >> 45) & 63ull);
+    const KT k = tmp[i];
+    const int b = (int)((k >> BS) & 63u);
     const int s = start[b], e = start[b + 1];
     int r = 0;
     for (int t = s; t < e; ++t) r += tmp[t] < k;
@@ -297,10 +328,11 @@ __device__ __forceinline__ bool bucket_sort(u64* keys, int m, int lane, int* his
 
 // Warp-synchronous bitonic sort of keys[0, m) in place (padded with ~0 up to the next power of
 // two, which must fit the buffer).
-__device__ __forceinline__ void sort_front(u64* keys, int m, int lane) {
+template <class KT>
+__device__ __forceinline__ void sort_front(KT* keys, int m, int lane) {
   int P = 1;
   while (P < m) P <<= 1;
-  for (int i = m + lane; i < P; i += 32) keys[i] = ~0ull;
+  for (int i = m + lane; i < P; i += 32) keys[i] = ~(KT)0;
   __syncwarp();
   for (int size = 2; size <= P; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
@@ -308,7 +340,7 @@ __device__ __forceinline__ void sort_front(u64* keys, int m, int lane) {
         const int lo = 2 * i - (i & (stride - 1));
         const int hi = lo + stride;
         const bool asc = (lo & size) == 0;
-        const u64 a = keys[lo], b = keys[hi];
+        const KT a = keys[lo], b = keys[hi];
         if ((a > b) == asc) {
           keys[lo] = b;
           keys[hi] = a;
@@ -325,16 +357,17 @@ constexpr int KG_UNROLL = 4;   // candidate records in flight per lane during ke
 // overflow list for the block kernel).  Keys in per-warp shared memory; when n > K a two-level
 // histogram of q (64 then 32 bins) finds q*, the keys with q <= q* are compacted in place and
 // only those are sorted (warp-synchronous bitonic sort, no block barriers).
-template <int PACK>
+template <int PACK, class KT>
 __global__ void __launch_bounds__(WB_WARPS * 32)
     k_bin_warp(const int* __restrict__ cell_start, const float4* __restrict__ rec, int G, int ntx, int nty, int R,
                int K, int V, const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
                int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv, void* __restrict__ slots,
                int* __restrict__ ovf_list, int* __restrict__ ovf_count) {
-  extern __shared__ u64 wsm[];
+  using KB = KeyBits<KT>;
+  extern __shared__ __align__(8) unsigned char wsm_raw[];
   __shared__ int whist[WB_WARPS][64];
   __shared__ int wstart[WB_WARPS][65];
-  __shared__ u64 wties[WB_WARPS][WTIES];
+  __shared__ KT wties[WB_WARPS][WTIES];
   __shared__ int wbeg[WB_WARPS][BS_MAXS], wlen[WB_WARPS][BS_MAXS], woff[WB_WARPS][BS_MAXS + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T = ntx * nty;
@@ -343,7 +376,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
   const int v = (int)(gt / T), t = (int)(gt % T);
   const int tx = t % ntx, ty = t / ntx;
   const int D = 2 * R + 1, S = D * D;
-  u64* buf = wsm + (size_t)warp * WCAP;
+  KT* buf = reinterpret_cast<KT*>(wsm_raw) + (size_t)warp * WCAP;
   int* hist = whist[warp];
   const int* cs = cell_start + (long long)v * (T + 1);
   const float4* rv = rec + (long long)v * G;
@@ -390,7 +423,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
       }
 #pragma unroll
       for (int u = 0; u < KG_UNROLL; ++u)
-        if (jj[u] >= 0) buf[c0 + 32 * u + lane] = make_key(jj[u], r[u], ctx, cty);
+        if (jj[u] >= 0) buf[c0 + 32 * u + lane] = make_key<KT>(jj[u], r[u], ctx, cty);
     }
   }
   __syncwarp();
@@ -400,7 +433,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
     hist[lane] = 0;
     hist[lane + 32] = 0;
     __syncwarp();
-    for (int i = lane; i < n; i += 32) atomicAdd(&hist[(int)((buf[i] >> 45) & 63ull)], 1);
+    for (int i = lane; i < n; i += 32) atomicAdd(&hist[(int)((buf[i] >> (KB::QS + 5)) & 63u)], 1);
     __syncwarp();
     const int h0 = hist[2 * lane], h1 = hist[2 * lane + 1];
     int incl = h0 + h1;
@@ -421,7 +454,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
     hist[lane] = 0;
     __syncwarp();
     for (int i = lane; i < n; i += 32) {
-      const unsigned q = (unsigned)(buf[i] >> 40);
+      const unsigned q = (unsigned)(buf[i] >> KB::QS);
       if ((int)(q >> 5) == b1) atomicAdd(&hist[q & 31u], 1);
     }
     __syncwarp();
@@ -445,12 +478,12 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
       // side list; each tie's rank among the ties (by stencil offset, then id: unique per tile)
       // places the K - c_lt smallest directly behind the sorted front, so only c_lt < K keys
       // need sorting.
-      u64* ties = wties[warp];
+      KT* ties = wties[warp];
       int w = 0, tw = 0;
       for (int base = 0; base < n; base += 32) {
         const int i = base + lane;
-        const u64 key = i < n ? buf[i] : ~0ull;
-        const unsigned q = (unsigned)(key >> 40);
+        const KT key = i < n ? buf[i] : ~(KT)0;
+        const unsigned q = (unsigned)(key >> KB::QS);
         const bool lo = i < n && q < qstar, eq = i < n && q == qstar;
         const unsigned bl = __ballot_sync(0xffffffffu, lo), be = __ballot_sync(0xffffffffu, eq);
         __syncwarp();
@@ -463,7 +496,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
       if (c_lt > WCAP / 2 || !bucket_sort(buf, c_lt, lane, hist, wstart[warp])) sort_front(buf, c_lt, lane);
       const int need = K - c_lt;
       for (int i = lane; i < hq; i += 32) {
-        const u64 key = ties[i];
+        const KT key = ties[i];
         int rank = 0;
         for (int t2 = 0; t2 < hq; ++t2) rank += ties[t2] < key;
         if (rank < need) buf[c_lt + rank] = key;
@@ -476,18 +509,16 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
       // digits, with warp-aggregated histogram increments, down to the exact threshold key t*
       // (the (K - c_lt)-th smallest tie).  The kept keys are those at or below t*: exactly K.
       int need = K - c_lt;
-      u64 pmask = 0x7FFull << 40, pval = (u64)qstar << 40;
-      const int dsh[7] = {32, 26, 20, 14, 8, 2, 0};
-      const int dwd[7] = {6, 6, 6, 6, 6, 6, 2};
-      for (int d = 0; d < 7; ++d) {
-        const int sh = dsh[d];
-        const u64 dm = (u64)((1 << dwd[d]) - 1);
+      KT pmask = (KT)0x7FF << KB::QS, pval = (KT)qstar << KB::QS;
+      for (int d = 0; d < KB::ND; ++d) {
+        const int sh = KB::dsh(d);
+        const KT dm = (KT)((1 << KB::dwd(d)) - 1);
         hist[lane] = 0;
         hist[lane + 32] = 0;
         __syncwarp();
         for (int base = 0; base < n; base += 32) {
           const int i = base + lane;
-          const u64 key = i < n ? buf[i] : 0ull;
+          const KT key = i < n ? buf[i] : (KT)0;
           const bool act = i < n && (key & pmask) == pval;
           const int bin = (int)((key >> sh) & dm);
           const unsigned am = __ballot_sync(0xffffffffu, act);
@@ -511,7 +542,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
         const int below = __shfl_sync(0xffffffffu, first ? gex : gex + g0, src);
         const int inb = __shfl_sync(0xffffffffu, first ? g0 : g1, src);
         need -= below;
-        pval |= (u64)bkt << sh;
+        pval |= (KT)bkt << sh;
         pmask |= dm << sh;
         __syncwarp();
         if (inb == 1) break;    // the bucket holds t* alone
@@ -520,7 +551,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
       int w = 0;
       for (int base = 0; base < n; base += 32) {
         const int i = base + lane;
-        const u64 key = i < n ? buf[i] : ~0ull;
+        const KT key = i < n ? buf[i] : ~(KT)0;
         const bool sel = i < n && (key & pmask) <= pval;
         const unsigned bal = __ballot_sync(0xffffffffu, sel);
         __syncwarp();
@@ -534,8 +565,8 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
       int w = 0;
       for (int base = 0; base < n; base += 32) {
         const int i = base + lane;
-        const u64 key = i < n ? buf[i] : ~0ull;
-        const bool sel = i < n && (unsigned)(key >> 40) <= qstar;
+        const KT key = i < n ? buf[i] : ~(KT)0;
+        const bool sel = i < n && (unsigned)(key >> KB::QS) <= qstar;
         const unsigned bal = __ballot_sync(0xffffffffu, sel);
         __syncwarp();
         if (sel) buf[w + __popc(bal & lt)] = key;
@@ -545,7 +576,7 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
     }
   }
   if (m >= 0 && (m > WCAP / 2 || !bucket_sort(buf, m, lane, hist, wstart[warp]))) sort_front(buf, m, lane);
-  emit_tile<PACK>(buf, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
+  emit_tile<PACK, KT>(buf, n, v, t, ntx, T, G, S, K, proj, inv_k, idx, inv, slots, lane, 32);
   if (lane == 0) {
     count[(long long)v * T + t] = min(n, K);
     cand[(long long)v * T + t] = n;
@@ -823,12 +854,17 @@ static int bin_core(const float* mu2d, const int* cell_count, const int2* cell_r
   if (cudaMemsetAsync(w.ovf, 0, 4, st) != cudaSuccess) return check_launch("memset overflow count");
   const long long tiles = (long long)V * T;
   const unsigned wblocks = (unsigned)((tiles + WB_WARPS - 1) / WB_WARPS);
-  const size_t wsmem = (size_t)WB_WARPS * WCAP * sizeof(u64);
+  // 32-bit keys when the id and the stencil offset fit them (same order, half the shared memory)
+  const bool key32 = G <= KEY32_MAX_G && S <= KEY32_MAX_S;
+  const size_t wsmem64 = (size_t)WB_WARPS * WCAP * sizeof(u64), wsmem32 = (size_t)WB_WARPS * WCAP * sizeof(unsigned);
   static std::atomic<unsigned long long> attr_done{0};
   once_per_device(attr_done, [&] {
-    cudaFuncSetAttribute(k_bin_warp<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
-    cudaFuncSetAttribute(k_bin_warp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
-    cudaFuncSetAttribute(k_bin_warp<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    cudaFuncSetAttribute(k_bin_warp<0, u64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem64);
+    cudaFuncSetAttribute(k_bin_warp<1, u64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem64);
+    cudaFuncSetAttribute(k_bin_warp<2, u64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem64);
+    cudaFuncSetAttribute(k_bin_warp<0, unsigned>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem32);
+    cudaFuncSetAttribute(k_bin_warp<1, unsigned>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem32);
+    cudaFuncSetAttribute(k_bin_warp<2, unsigned>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem32);
     cudaFuncSetAttribute(k_bin_select<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(BS_CAP * sizeof(u64)));
     cudaFuncSetAttribute(k_bin_select<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(BS_CAP * sizeof(u64)));
     cudaFuncSetAttribute(k_bin_select<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(BS_CAP * sizeof(u64)));
@@ -836,8 +872,13 @@ static int bin_core(const float* mu2d, const int* cell_count, const int2* cell_r
   const unsigned bblocks = (unsigned)(tiles < 296 ? tiles : 296);   // two blocks per SM loop over the list
   const size_t bsmem = (size_t)BS_CAP * sizeof(u64);
 #define TTS_BIN_LAUNCH(P, PR, SL)                                                                              \
-  k_bin_warp<P><<<wblocks, WB_WARPS * 32, wsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, PR, inv_k, idx,   \
-                                                       count, cand, inv, SL, w.ovf + 1, w.ovf);                    \
+  if (key32)                                                                                                   \
+    k_bin_warp<P, unsigned><<<wblocks, WB_WARPS * 32, wsmem32, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, PR, \
+                                                                     inv_k, idx, count, cand, inv, SL, w.ovf + 1,   \
+                                                                     w.ovf);                                        \
+  else                                                                                                         \
+    k_bin_warp<P, u64><<<wblocks, WB_WARPS * 32, wsmem64, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, V, PR,      \
+                                                                inv_k, idx, count, cand, inv, SL, w.ovf + 1, w.ovf); \
   k_bin_select<P><<<bblocks, BS_THREADS, bsmem, st>>>(w.cell_start, w.rec, G, ntx, nty, R, K, PR, inv_k, idx, count,   \
                                                   cand, inv, SL, w.ovf + 1, w.ovf);
   if (proj && slots && slot_format == 1) {
