@@ -147,3 +147,34 @@ def test_sgld_relocate_equals_sgld_then_relocate(injected, pkg):
     assert n == int(rb["n_dead"]) > 0
     assert torch.equal(ra["targets"][:n], rb["targets"][:n])
     assert torch.equal(a, b) and torch.equal(ma, mb) and torch.equal(va, vb)
+
+
+@pytest.mark.parametrize("n_bucket", [3000, 10000])
+def test_relocation_quantile_inside_one_bucket(n_bucket, pkg):
+    """The 1% quantile lies among n_bucket opacities that share the select's first (11-bit) digit,
+    spaced ~13 ulps apart: with 3000 members the last two digits are selected among them in
+    shared memory, with 10000 (over the list capacity) by the grid-wide passes.  Either way the
+    threshold falls between the 500th and 501st smallest opacity: the relocation is bit-identical
+    to one given a threshold between those two values."""
+    from tt_splat_b200 import ops
+    G = 50000
+    p = dict(pkg.synthetic.config0(seed=8, G=G)["params"])
+    rng = np.random.default_rng(5)
+    o = np.concatenate([0.0832 + 1e-7 * np.arange(n_bucket), rng.uniform(0.5, 0.95, G - n_bucket)])
+    perm = rng.permutation(G)
+    o = o[perm]
+    p["opacity_raw"] = np.log(o / (1.0 - o)).astype(np.float32)
+    flat0 = _flat(pkg, p)
+    low = np.sort(o)[:501]
+    assert low[-1] < 0.09375 and low[0] >= 0.078125          # one 11-bit bucket of the fp32 bits
+    mid = float(0.5 * (low[499] + low[500]))
+    step = torch.ones(1, dtype=torch.int32, device=DEV)
+    outs = []
+    for thr, frac in ((0.0, 0.01), (mid, 0.0)):
+        flat = flat0.clone()
+        m, v = torch.ones_like(flat), torch.ones_like(flat)
+        r = ops.relocate(flat, m, v, G, step, thr, frac, 0.2, seed=21)
+        outs.append((int(r["n_dead"]), r["targets"][:500].clone(), flat, m, v))
+    (na, ta, fa, ma, va), (nb, tb, fb, mb, vb) = outs
+    assert na == nb == 500
+    assert torch.equal(ta, tb) and torch.equal(fa, fb) and torch.equal(ma, mb) and torch.equal(va, vb)

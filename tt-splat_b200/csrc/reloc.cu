@@ -5,16 +5,17 @@
 //   1. threshold: dead_thr, or the torch.quantile of the opacities at dead_frac, found by an
 //      exact MSB radix select (11/11/10-bit digits of the fp32 bit pattern, order-preserving
 //      for the non-negative opacities) of the two bracketing order statistics; every block
-//      reads the merged digit histogram and picks the same bucket;
+//      reads the merged digit histogram and picks the same bucket; the members of the first
+//      digit's buckets (up to SEL_CAP) are then listed once, and every block selects the last two
+//      digits among them in shared memory;
 //   2. per-block dead counts and alive opacity sums; each block sums its predecessors in block
 //      order and writes its part of the ascending dead list and of the inclusive opacity CDF
 //      over the alive set (float64, one fixed summation order);
 //   3. one target per dead slot, drawn with replacement proportional to opacity (binary search
 //      of a Philox uniform in the CDF) or injected; per-target occurrence counts n;
 //   4. dead slots take the target's parameters (+ offset * N(0,1) on the means) and the split
-//      opacity logit(o_t / (n_t + 1)); then targets get the same split (after a barrier, so the
-//      dead slots read the targets' old opacity); Adam moments of every touched gaussian are
-//      zeroed.
+//      opacity logit(o_t / (n_t + 1)), from the target's logit saved in phase 3; in the same
+//      phase the targets get the same split; Adam moments of every touched gaussian are zeroed.
 #include <algorithm>
 
 #include "peer.cuh"
@@ -23,6 +24,10 @@
 namespace tts {
 
 constexpr int RK_THREADS = 512;
+// Members of the buckets that the first (11-bit) digit of the quantile select picks, held in
+// shared memory so that the last two digits need no grid barrier; more members take the
+// grid-wide passes.
+constexpr int SEL_CAP = 6144;
 constexpr int STATUS_GRID_TIMEOUT = 2;
 
 struct GridBar {
@@ -130,11 +135,14 @@ struct RelocArgs {
   int* targets;
   GridBar* bar;
   int* hist;        // [3 passes][2 selections][2048]
+  int* sel_count;   // members of the first digit's buckets (zeroed with the histograms)
+  unsigned* sel_list;   // [SEL_CAP] their opacity bit patterns
   int* bcnt;        // [nblocks]
   double* bsum;     // [nblocks]
   int* dead_list;   // [G]
   double* cdf;      // [G]
   int* nat;         // [G], zeroed by the kernel (phase 0)
+  float* old_logit;  // [G] target opacity logit of each dead slot before the split
   const double* sgld_lr;   // non-null: the SGLD step runs as phase 0 (lr of the means at [0])
   float noise_lr;
   const float* sgld_eps;   // injected SGLD noise [G][3], or null for Philox draws
@@ -178,6 +186,7 @@ __global__ void __launch_bounds__(RK_THREADS) k_relocate(RelocArgs a) {
   __shared__ unsigned s_pval[2], s_pmask[2];
   __shared__ int s_need[2];
   __shared__ int s_pick[2][2];     // (bucket, rank consumed before it) per selection
+  __shared__ unsigned s_list[SEL_CAP];
   const ParamLayout L{a.G};
   const int G = a.G, tid = threadIdx.x;
   const unsigned nb = gridDim.x;
@@ -214,52 +223,116 @@ __global__ void __launch_bounds__(RK_THREADS) k_relocate(RelocArgs a) {
       s_need[tid] = (tid == 0 ? lo : hi) + 1;
     }
     const int shifts[3] = {21, 10, 0}, bits[3] = {11, 11, 10};
+    int m_list = -1;   // >= 0: the last two digits select among the s_list members
     for (int d = 0; d < 3; ++d) {
       const int nbins = 1 << bits[d];
       for (int i = tid; i < 2 * 2048; i += RK_THREADS) sh[i >> 11][i & 2047] = 0;
       __syncthreads();
       const unsigned pv0 = s_pval[0], pm0 = s_pmask[0], pv1 = s_pval[1], pm1 = s_pmask[1];
-      for (int g = beg + tid; g < end; g += RK_THREADS) {
-        const unsigned b = __float_as_uint(opacity_of(a.params, L, g));
-        const unsigned dg = (b >> shifts[d]) & (unsigned)(nbins - 1);
-        if ((b & pm0) == pv0) atomicAdd(&sh[0][dg], 1);
-        if ((b & pm1) == pv1) atomicAdd(&sh[1][dg], 1);
+      const int* h0 = &sh[0][0];
+      const int* h1 = &sh[1][0];
+      if (m_list >= 0) {
+        // every block histograms the same member list in its own shared memory
+        for (int i = tid; i < m_list; i += RK_THREADS) {
+          const unsigned b = s_list[i];
+          const unsigned dg = (b >> shifts[d]) & (unsigned)(nbins - 1);
+          if ((b & pm0) == pv0) atomicAdd(&sh[0][dg], 1);
+          if ((b & pm1) == pv1) atomicAdd(&sh[1][dg], 1);
+        }
+        __syncthreads();
+      } else {
+        for (int g = beg + tid; g < end; g += RK_THREADS) {
+          const unsigned b = __float_as_uint(opacity_of(a.params, L, g));
+          const unsigned dg = (b >> shifts[d]) & (unsigned)(nbins - 1);
+          if ((b & pm0) == pv0) atomicAdd(&sh[0][dg], 1);
+          if ((b & pm1) == pv1) atomicAdd(&sh[1][dg], 1);
+        }
+        __syncthreads();
+        int* gh = a.hist + d * 2 * 2048;
+        for (int i = tid; i < 2 * nbins; i += RK_THREADS) {
+          const int w = i / nbins, bin = i - w * nbins;
+          const int c = sh[w][bin];
+          if (c) atomicAdd(gh + w * 2048 + bin, c);
+        }
+        if (!grid_sync(a.bar, nb, &s_flag)) return;
+        h0 = gh;
+        h1 = gh + 2048;
       }
-      __syncthreads();
-      int* gh = a.hist + d * 2 * 2048;
-      for (int i = tid; i < 2 * nbins; i += RK_THREADS) {
-        const int w = i / nbins, bin = i - w * nbins;
-        const int c = sh[w][bin];
-        if (c) atomicAdd(gh + w * 2048 + bin, c);
-      }
-      if (!grid_sync(a.bar, nb, &s_flag)) return;
-      // every block picks the same buckets from the merged histogram
-      for (int w = 0; w < 2; ++w) {
-        const int need = s_need[w];
+      // every block picks the same buckets from the merged histogram: both selections in one
+      // block scan (the second one's counts carried exactly in the scan's double)
+      {
         const int per = nbins / RK_THREADS;        // 4 or 2 bins per thread
-        int loc = 0;
-        for (int q = 0; q < per; ++q) loc += __ldcg(gh + w * 2048 + tid * per + q);
+        const bool glob = m_list < 0;
+        int c0[4], c1[4], loc0 = 0, loc1 = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          c0[q] = q < per ? (glob ? __ldcg(h0 + tid * per + q) : h0[tid * per + q]) : 0;
+          c1[q] = q < per ? (glob ? __ldcg(h1 + tid * per + q) : h1[tid * per + q]) : 0;
+          loc0 += c0[q];
+          loc1 += c1[q];
+        }
         int ci;
         double si;
-        block_incl_scan(loc, 0.0, ci, si, s_w);
-        const int excl = ci - loc;
-        if (excl < need && need <= ci) {
-          int c = excl, q = 0;
-          for (; q < per - 1; ++q) {
-            const int h = __ldcg(gh + w * 2048 + tid * per + q);
-            if (c + h >= need) break;
-            c += h;
+        block_incl_scan(loc0, (double)loc1, ci, si, s_w);
+        const int incl[2] = {ci, (int)si}, loc[2] = {loc0, loc1};
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          const int need = s_need[w], excl = incl[w] - loc[w];
+          if (excl < need && need <= incl[w]) {
+            // the first of this thread's bins that reaches need (unrolled: the counts stay in
+            // registers)
+            int c = excl, q = 0;
+            bool found = false;
+#pragma unroll
+            for (int qq = 0; qq < 3; ++qq) {
+              if (!found && qq < per - 1) {
+                const int h = w ? c1[qq] : c0[qq];
+                if (c + h >= need) {
+                  found = true;
+                } else {
+                  c += h;
+                  q = qq + 1;
+                }
+              }
+            }
+            s_pick[w][0] = tid * per + q;
+            s_pick[w][1] = c;
           }
-          s_pick[w][0] = tid * per + q;
-          s_pick[w][1] = c;
         }
         __syncthreads();
-        if (tid == 0) {
-          s_need[w] = need - s_pick[w][1];
-          s_pval[w] |= (unsigned)s_pick[w][0] << shifts[d];
-          s_pmask[w] |= (unsigned)(nbins - 1) << shifts[d];
+        if (tid < 2) {
+          s_need[tid] -= s_pick[tid][1];
+          s_pval[tid] |= (unsigned)s_pick[tid][0] << shifts[d];
+          s_pmask[tid] |= (unsigned)(nbins - 1) << shifts[d];
         }
         __syncthreads();
+      }
+      if (d == 0) {
+        // the members of the two chosen buckets go to one list (opacity bits; the order of the
+        // appends does not matter, the selection depends only on the values)
+        const unsigned qv0 = s_pval[0], qm0 = s_pmask[0], qv1 = s_pval[1], qm1 = s_pmask[1];
+        const int lane = tid & 31;
+        for (int base = beg; base < end; base += RK_THREADS) {
+          const int g = base + tid;
+          unsigned b = 0u;
+          bool mem = false;
+          if (g < end) {
+            b = __float_as_uint(opacity_of(a.params, L, g));
+            mem = (b & qm0) == qv0 || (b & qm1) == qv1;
+          }
+          const unsigned bal = __ballot_sync(0xffffffffu, mem);
+          int pos = 0;
+          if (lane == 0 && bal) pos = atomicAdd(a.sel_count, __popc(bal));
+          pos = __shfl_sync(0xffffffffu, pos, 0) + __popc(bal & ((1u << lane) - 1u));
+          if (mem && pos < SEL_CAP) a.sel_list[pos] = b;
+        }
+        if (!grid_sync(a.bar, nb, &s_flag)) return;
+        const int mc = __ldcg(a.sel_count);   // the same in every block
+        if (mc <= SEL_CAP) {
+          for (int i = tid; i < mc; i += RK_THREADS) s_list[i] = __ldcg(a.sel_list + i);
+          m_list = mc;
+          __syncthreads();
+        }
       }
     }
     const float olo = __uint_as_float(s_pval[0]), ohi = __uint_as_float(s_pval[1]);
@@ -379,11 +452,14 @@ __global__ void __launch_bounds__(RK_THREADS) k_relocate(RelocArgs a) {
     }
     if (lane == 0) {
       a.targets[i] = t;
+      a.old_logit[i] = a.params[L.opacity() + t];   // before any split of this launch
       atomicAdd(a.nat + t, 1);
     }
   }
   if (!grid_sync(a.bar, nb, &s_flag)) return;
-  // ---- 4a. dead slots: one warp per slot copies the target's 59 parameters --------------------
+  // ---- 4. dead slots and targets in one phase (disjoint gaussians: targets are alive) ----------
+  // 4a. dead slots: one warp per slot copies the target's 59 parameters, the opacity split from
+  // the target's logit saved in phase 3 (4b may already have split the target's own)
   for (int i = blockIdx.x * (RK_THREADS / 32) + (tid >> 5); i < n_dead; i += nwarps) {
     const int d = __ldcg(a.dead_list + i), t = __ldcg(a.targets + i);
     float e = 0.f;
@@ -404,15 +480,14 @@ __global__ void __launch_bounds__(RK_THREADS) k_relocate(RelocArgs a) {
       const long long src = field_index(L, f, t), dst = field_index(L, f, d);
       float val;
       if (f < 3) val = a.params[src] + a.offset * e;
-      else if (f == 10) val = split_logit(opacity_of(a.params, L, t), nt + 1);
+      else if (f == 10) val = split_logit(sigmoidf(__ldcg(a.old_logit + i)), nt + 1);
       else val = a.params[src];
       a.params[dst] = val;
       a.m[dst] = 0.f;
       a.v[dst] = 0.f;
     }
   }
-  if (!grid_sync(a.bar, nb, &s_flag)) return;
-  // ---- 4b. targets: split opacity, zero moments ------------------------------------------------
+  // 4b. targets: split opacity, zero moments
   for (int g = beg + tid; g < end; g += RK_THREADS) {
     const int n = __ldcg(a.nat + g);
     if (n == 0) continue;
@@ -444,15 +519,20 @@ static size_t reloc_bytes(int G, int nblk, RelocArgs* w, char* base) {
     return p;
   };
   char* p0 = take(sizeof(GridBar));
-  char* p1 = take(3 * 2 * 2048 * 4);
+  char* p1 = take(3 * 2 * 2048 * 4 + 4);    // + the bucket-member count
+  char* p7 = take((size_t)SEL_CAP * 4);
   char* p2 = take((size_t)nblk * 4);
   char* p3 = take((size_t)nblk * 8);
   char* p4 = take((size_t)G * 4);
   char* p5 = take((size_t)G * 8);
   char* p6 = take((size_t)G * 4);
+  char* p8 = take((size_t)G * 4);
   if (w) {
     w->bar = reinterpret_cast<GridBar*>(p0);
     w->hist = reinterpret_cast<int*>(p1);
+    w->sel_count = reinterpret_cast<int*>(p1) + 3 * 2 * 2048;
+    w->sel_list = reinterpret_cast<unsigned*>(p7);
+    w->old_logit = reinterpret_cast<float*>(p8);
     w->bcnt = reinterpret_cast<int*>(p2);
     w->bsum = reinterpret_cast<double*>(p3);
     w->dead_list = reinterpret_cast<int*>(p4);
@@ -500,9 +580,9 @@ static int relocate_core(float* params, float* m, float* v, int G, float dead_th
   a.peer_mine = peer_mine;
   a.peer_n = peer_n;
   cudaStream_t st = as_stream(stream);
-  // the barrier word and the digit histograms start at zero (the per-target counts are zeroed by
-  // the kernel)
-  const size_t head = reinterpret_cast<char*>(a.bcnt) - static_cast<char*>(workspace);
+  // the barrier word, the digit histograms and the bucket-member count start at zero (the
+  // per-target counts are zeroed by the kernel)
+  const size_t head = reinterpret_cast<char*>(a.sel_list) - static_cast<char*>(workspace);
   if (cudaMemsetAsync(workspace, 0, head, st) != cudaSuccess) return check_launch("memset relocation state");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)nblk);
