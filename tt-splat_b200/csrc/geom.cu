@@ -251,10 +251,14 @@ __global__ void __launch_bounds__(256)
 // Parameter backward, one gaussian per LPG lanes, each lane over its views: from the gathered
 // record, the geometry backward (tools/geom_bwd.py:67-152), activation backward
 // (tools/operands_manual.py:103-110) and SH backward (coefficients and viewing direction); the
-// lanes' partial sums are combined by a butterfly, then the reg_loss gradient
-// (spike/mcmc.py:18-22) is added and the gaussian's 59 gradients are written.
+// lanes' geometry sums are combined by a butterfly, the colour-coefficient sums through a
+// per-round shared-memory exchange of each view's SH basis and colour gradient (each lane sums
+// the entries it writes), then the reg_loss gradient (spike/mcmc.py:18-22) is added and the
+// gaussian's 59 gradients are written.
+// Four blocks per SM (128 registers) when a gaussian has 4 or 8 lanes: the colour-coefficient
+// sums live in shared memory, not in 48 registers per lane; one or two lanes keep three blocks.
 template <int DEG, int LPG, bool ARMB>
-__global__ void __launch_bounds__(GB_THREADS, 3)
+__global__ void __launch_bounds__(GB_THREADS, LPG >= 4 ? 4 : 3)
     k_backward(const float* __restrict__ params, int G, const float* __restrict__ cams, int V, float blur,
                float near_plane, const float4* __restrict__ rec, float lambda_o, float lambda_s,
                float* __restrict__ grads, const float* __restrict__ depth_bt, float2* __restrict__ bt_partial) {
@@ -284,79 +288,106 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
   const float o = g < G ? sigmoidf(x.op) : 0.f;
   float gm[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f}, gs[3] = {0.f, 0.f, 0.f}, gop = 0.f;
   float2 gbt = make_float2(0.f, 0.f);       // arm B: d/d depth_beta, d/d depth_tau of this thread
-  float gco[NB][3];
+  // colour-coefficient gradients: lane vl owns the entries e = 11 + 3k + c with e % LPG == vl (the
+  // ones it writes out) and sums them over the views, in view order, from the per-view SH basis b
+  // and colour gradient gr that every lane publishes in shared memory each round
+  constexpr int NX = NB + 3, NOWN = (3 * NB + LPG - 1) / LPG;
+  __shared__ float s_x[GPB * LPG * NX];
+  float* xs = s_x + gl * LPG * NX;
+  const int e0 = 11 + ((vl - 11) % LPG + LPG) % LPG;
+  float gco[NOWN];
 #pragma unroll
-  for (int k = 0; k < NB; k++)
+  for (int i = 0; i < NOWN; i++) gco[i] = 0.f;
+  const int nr = (V + LPG - 1) / LPG;       // the same in every lane: the rounds are warp-uniform
+  for (int rd = 0; rd < nr; ++rd) {
+    const int v = rd * LPG + vl;
+    float bx[NB], grx[3] = {0.f, 0.f, 0.f};  // zero: no contribution of this lane in this round
 #pragma unroll
-    for (int c = 0; c < 3; c++) gco[k][c] = 0.f;
-  if (g < G) {
-    for (int v = vl; v < V; v += LPG) {
-      if (v != vl) {
+    for (int k = 0; k < NB; k++) bx[k] = 0.f;
+    if (g < G && v < V) {
+      if (rd > 0) {
         const float4* r = rec + ((long long)v * G + g) * 3;
         r0 = __ldg(r);
         r1 = __ldg(r + 1);
         r2 = __ldg(r + 2);
       }
-      if (r2.y == 0.f) continue;       // no valid slot in this view
-      const float ga = r0.x, gb = r0.y, gc = r0.z, gmx = r0.w, gmy = r1.x;
-      const float gcol[3] = {r1.y, r1.z, r1.w};
-      const float goc = r2.x;
-      const Cam cam = cam_at(cams, s_cam, v);
-      GeomFwd f;
-      geom_forward(x.m, x.q, x.ls, cam, blur, near_plane, f);
-      geom_backward(f, cam, ga, gb, gc, gmx, gmy, gm, gq, gs);
-      float d[3] = {0.f, 0.f, 0.f}, nrm = 1.f;
-      if (DEG > 0) view_dir(x.m, cam, d, nrm);
-      float pre[3];
-      colour_pre<DEG>(sp, x, d, pre);
-      const float keepf = f.keep ? 1.f : 0.f;
-      const float rho = ARMB ? depth_weight(depth_bt, f.mcz) : 1.f;
-      const float keo = keepf * o * rho;
-      const float gkeo =
-          gcol[0] * fmaxf(pre[0], 0.f) + gcol[1] * fmaxf(pre[1], 0.f) + gcol[2] * fmaxf(pre[2], 0.f) + goc;
-      gop += gkeo * keepf * rho * o * (1.f - o);
-      if (ARMB) {
-        // keo = keep o rho, rho = sigmoid(beta (tau - z)): d rho = rho (1 - rho) (beta, tau - z, -beta)
-        const float grho = gkeo * keepf * o * rho * (1.f - rho);
-        gbt.x += grho * (depth_bt[1] - f.mcz);
-        gbt.y += grho * depth_bt[0];
-        const float gz = -grho * depth_bt[0];            // z = R_v[2] . means + t_v[2]
-#pragma unroll
-        for (int i = 0; i < 3; i++) gm[i] += gz * cam.R[2 * 3 + i];
-      }
-      float gr[3];
-#pragma unroll
-      for (int c = 0; c < 3; c++) gr[c] = pre[c] >= 0.f ? gcol[c] * keo : 0.f;   // torch clamp passes at 0
-      float b[16];
-      sh_basis(DEG, d[0], d[1], d[2], b);
-#pragma unroll
-      for (int k = 0; k < NB; k++)
-#pragma unroll
-        for (int c = 0; c < 3; c++) gco[k][c] += b[k] * gr[c];
-      if (DEG > 0) {
-        // direction gradient through the normalisation d = dirs / max(|dirs|, 1e-12)
-        float gd[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = 1; k < NB; k++) {
-          float dx, dy, dz;
-          sh_basis_grad(k, d[0], d[1], d[2], dx, dy, dz);
-          float w = 0.f;
-#pragma unroll
-          for (int c = 0; c < 3; c++) w += sp[14 + 3 * (k - 1) + c] * gr[c];
-          gd[0] += w * dx;
-          gd[1] += w * dy;
-          gd[2] += w * dz;
+      if (r2.y != 0.f) {               // else no valid slot in this view
+        const float ga = r0.x, gb = r0.y, gc = r0.z, gmx = r0.w, gmy = r1.x;
+        const float gcol[3] = {r1.y, r1.z, r1.w};
+        const float goc = r2.x;
+        const Cam cam = cam_at(cams, s_cam, v);
+        GeomFwd f;
+        geom_forward(x.m, x.q, x.ls, cam, blur, near_plane, f);
+        geom_backward(f, cam, ga, gb, gc, gmx, gmy, gm, gq, gs);
+        float d[3] = {0.f, 0.f, 0.f}, nrm = 1.f;
+        if (DEG > 0) view_dir(x.m, cam, d, nrm);
+        float pre[3];
+        colour_pre<DEG>(sp, x, d, pre);
+        const float keepf = f.keep ? 1.f : 0.f;
+        const float rho = ARMB ? depth_weight(depth_bt, f.mcz) : 1.f;
+        const float keo = keepf * o * rho;
+        const float gkeo =
+            gcol[0] * fmaxf(pre[0], 0.f) + gcol[1] * fmaxf(pre[1], 0.f) + gcol[2] * fmaxf(pre[2], 0.f) + goc;
+        gop += gkeo * keepf * rho * o * (1.f - o);
+        if (ARMB) {
+          // keo = keep o rho, rho = sigmoid(beta (tau - z)): d rho = rho (1 - rho) (beta, tau - z, -beta)
+          const float grho = gkeo * keepf * o * rho * (1.f - rho);
+          gbt.x += grho * (depth_bt[1] - f.mcz);
+          gbt.y += grho * depth_bt[0];
+          const float gz = -grho * depth_bt[0];            // z = R_v[2] . means + t_v[2]
+  #pragma unroll
+          for (int i = 0; i < 3; i++) gm[i] += gz * cam.R[2 * 3 + i];
         }
-        if (nrm > 1e-12f) {
-          const float dd = d[0] * gd[0] + d[1] * gd[1] + d[2] * gd[2];
-#pragma unroll
-          for (int i = 0; i < 3; i++) gm[i] += (gd[i] - d[i] * dd) / nrm;
-        } else {
-#pragma unroll
-          for (int i = 0; i < 3; i++) gm[i] += gd[i] / 1e-12f;
+        float gr[3];
+  #pragma unroll
+        for (int c = 0; c < 3; c++) gr[c] = pre[c] >= 0.f ? gcol[c] * keo : 0.f;   // torch clamp passes at 0
+        float b[16];
+        sh_basis(DEG, d[0], d[1], d[2], b);
+  #pragma unroll
+        for (int k = 0; k < NB; k++) bx[k] = b[k];
+  #pragma unroll
+        for (int c = 0; c < 3; c++) grx[c] = gr[c];
+        if (DEG > 0) {
+          // direction gradient through the normalisation d = dirs / max(|dirs|, 1e-12)
+          float gd[3] = {0.f, 0.f, 0.f};
+  #pragma unroll
+          for (int k = 1; k < NB; k++) {
+            float dx, dy, dz;
+            sh_basis_grad(k, d[0], d[1], d[2], dx, dy, dz);
+            float w = 0.f;
+  #pragma unroll
+            for (int c = 0; c < 3; c++) w += sp[14 + 3 * (k - 1) + c] * gr[c];
+            gd[0] += w * dx;
+            gd[1] += w * dy;
+            gd[2] += w * dz;
+          }
+          if (nrm > 1e-12f) {
+            const float dd = d[0] * gd[0] + d[1] * gd[1] + d[2] * gd[2];
+  #pragma unroll
+            for (int i = 0; i < 3; i++) gm[i] += (gd[i] - d[i] * dd) / nrm;
+          } else {
+  #pragma unroll
+            for (int i = 0; i < 3; i++) gm[i] += gd[i] / 1e-12f;
+          }
         }
       }
     }
+    float* mine = xs + vl * NX;
+#pragma unroll
+    for (int k = 0; k < NB; k++) mine[k] = bx[k];
+#pragma unroll
+    for (int c = 0; c < 3; c++) mine[NB + c] = grx[c];
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < NOWN; i++) {
+      const int e = e0 + i * LPG;
+      if (e < 11 + 3 * NB) {
+        const int kk = (e - 11) / 3, c = (e - 11) % 3;
+#pragma unroll
+        for (int l = 0; l < LPG; l++) gco[i] += xs[l * NX + kk] * xs[l * NX + NB + c];
+      }
+    }
+    __syncwarp();                        // the next round overwrites the exchange
   }
   // combine the lanes (all lanes of the warp take part: the shuffles are warp-wide)
 #pragma unroll
@@ -367,10 +398,6 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
 #pragma unroll
   for (int i = 0; i < 4; i++) gq[i] = lane_sum<LPG>(gq[i]);
   gop = lane_sum<LPG>(gop);
-#pragma unroll
-  for (int k = 0; k < NB; k++)
-#pragma unroll
-    for (int c = 0; c < 3; c++) gco[k][c] = lane_sum<LPG>(gco[k][c]);
   // the gaussian's 59 gradients go to its staged row (lane vl fills the entries e with
   // e % LPG == vl), then the block writes the rows out field by field, coalesced
   __syncthreads();                 // every lane is done reading its staged parameters
@@ -383,15 +410,16 @@ __global__ void __launch_bounds__(GB_THREADS, 3)
     const float s = expf(x.ls[i]);
     put(i, gm[i]);
     put(3 + i, gs[i] * s + lambda_s / (3.f * (float)G) * s);
-    put(11 + i, gco[0][i]);
   }
 #pragma unroll
   for (int i = 0; i < 4; i++) put(6 + i, gq[i]);
   put(10, gop + lambda_o / (float)G * o * (1.f - o));
 #pragma unroll
-  for (int k = 1; k < 16; k++)
-#pragma unroll
-    for (int c = 0; c < 3; c++) put(14 + 3 * (k - 1) + c, k < NB ? gco[k < NB ? k : 0][c] : 0.f);
+  for (int i = 0; i < NOWN; i++) {
+    const int e = e0 + i * LPG;
+    if (e < 11 + 3 * NB) put(e, gco[i]);
+  }
+  for (int e = 11 + 3 * NB; e < 59; e++) put(e, 0.f);   // SH coefficients above the degree
   __syncthreads();
   unstage_rows<GPB>(s_p, G, g0, grads);
   if (ARMB) {
