@@ -535,10 +535,10 @@ def run_config(args, rank, world, local_rank, cid):
 # backward captured on a 4-view launch; its traffic is proportional to the views it renders).
 # The Adam figure under-counts writes that were still in L2 when the kernel ended.  Re-captured
 # whenever those kernels change; the capture is the one TRAFFIC_SOURCE names.
-RENDER_BWD_DRAM_PER_VIEW = (179.9e6 + 35.3e6) / 4
+RENDER_BWD_DRAM_PER_VIEW = (179.9e6 + 36.1e6) / 4
 ADAM_DRAM = 94.4e6 + 14.5e6
 TRAFFIC_SOURCE = ("profiles/step_kernels_config2_4views.md (ncu, one launch per kernel, 4-view capture "
-                  "at commit 547699c)")
+                  "at commit 99b1f18)")
 
 
 def cpu_baseline_sample():
