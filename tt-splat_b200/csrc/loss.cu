@@ -93,17 +93,20 @@ __global__ void __launch_bounds__(256)
     const int lc = tid % LG::IW, lr0 = tid / LG::IW;
     if (lr0 < RPT) {
       const int xx = ox0 + lc;
-      const long long col = (long long)id.v * H * W + xx;
+      // this thread's rows lr0, lr0 + RPT, ... inside both the halo tile and the image: the
+      // first kn of them (bounds hoisted out of the loads)
+      const int rows = min(LG::IH, H - oy0);
+      const int kn = xx < W ? (rows - lr0 + RPT - 1) / RPT : 0;
+      const long long base = (((long long)id.v * H + oy0 + lr0) * W + xx) * 3 + id.ch;
+      const int step = 3 * W * RPT;
       float xv[NR], yv[NR];
 #pragma unroll
       for (int k = 0; k < NR; ++k) {
-        const int r = lr0 + RPT * k, yy = oy0 + r;
         xv[k] = 0.f;
         yv[k] = 0.f;
-        if (r < LG::IH && yy < H && xx < W) {
-          const long long q = (col + (long long)yy * W) * 3 + id.ch;
-          xv[k] = __ldg(img + q);
-          yv[k] = __ldg(tgt + q);
+        if (k < kn) {
+          xv[k] = __ldg(img + base + k * step);
+          yv[k] = __ldg(tgt + base + k * step);
         }
       }
 #pragma unroll
@@ -179,10 +182,11 @@ __global__ void __launch_bounds__(256)
       }
     }
     const int ox = ox0 + c;
+    const int on = ox < Wo ? min(RB, Ho - oy0 - r0) : 0;     // outputs of this item in the map
+    float4* mp = mbase + (long long)(oy0 + r0) * Wo + ox;
 #pragma unroll
     for (int o = 0; o < RB; o++) {
-      const int oy = oy0 + r0 + o;
-      if (oy >= Ho || ox >= Wo) continue;
+      if (o >= on) continue;
       float mux, muy, fss, fxy1;
       split2(fxy[o], mux, muy);
       split2(fqp[o], fss, fxy1);
@@ -197,8 +201,7 @@ __global__ void __launch_bounds__(256)
       asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(iB2) : "f"(B2));
       const float S = (A1 * A2) * iD;
       ssum += S;
-      const long long q = (long long)oy * Wo + ox;
-      mbase[q] = make_float4(2.f * iD * (muy * (A2 - A1) - S * mux * (B2 - B1)),   // dS/dmu_x
+      mp[o * Wo] = make_float4(2.f * iD * (muy * (A2 - A1) - S * mux * (B2 - B1)),   // dS/dmu_x
                              -S * iB2,                                             // dS/d filt(x^2)
                              2.f * A1 * iD, 0.f);                                  // dS/d filt(xy)
     }
@@ -245,16 +248,17 @@ __global__ void __launch_bounds__(256)
   // = 256 items) are fetched up front, together with the map halo
   static_assert(LT_W * (LT_H / RB) == 256, "one column item per thread");
   const int ec = tid % LT_W, er0 = (tid / LT_W) * RB;
+  // rows of this item inside the image, and the image offset of its first pixel
+  const int en = x0 + ec < W ? min(RB, H - y0 - er0) : 0;
+  const long long eb = (((long long)id.v * H + y0 + er0) * W + x0 + ec) * 3 + id.ch;
   float ximg[RB], xtgt[RB];
 #pragma unroll
   for (int o = 0; o < RB; o++) {
-    const int yy = y0 + er0 + o, xx = x0 + ec;
     ximg[o] = 0.f;
     xtgt[o] = 0.f;
-    if (yy < H && xx < W) {
-      const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
-      ximg[o] = __ldg(img + q);
-      xtgt[o] = __ldg(tgt + q);
+    if (o < en) {
+      ximg[o] = __ldg(img + eb + o * 3 * W);
+      xtgt[o] = __ldg(tgt + eb + o * 3 * W);
     }
   }
   {
@@ -265,16 +269,19 @@ __global__ void __launch_bounds__(256)
     if (lr0 < RPT) {
       const int mx = x0 - (WIN - 1) + lc;
       const bool colok = mx >= 0 && mx < Wo;
+      // this thread's rows lr0 + RPT k with map row my in [0, Ho) and r < IH: k in [klo, khi)
+      const int m0 = y0 - (WIN - 1) + lr0;                       // map row of k = 0
+      const int klo = m0 >= 0 ? 0 : (-m0 + RPT - 1) / RPT;
+      const int khi = colok ? min((LG::IH - lr0 + RPT - 1) / RPT, (Ho - m0 + RPT - 1) / RPT) : 0;
+      const long long mb0 = (long long)m0 * Wo + mx;
       float av[NR], bv[NR], dv[NR];
 #pragma unroll
       for (int k = 0; k < NR; ++k) {
-        const int r = lr0 + RPT * k, my = y0 - (WIN - 1) + r;
         av[k] = 0.f;
         bv[k] = 0.f;
         dv[k] = 0.f;
-        if (colok && r < LG::IH && my >= 0 && my < Ho) {
-          const long long q = (long long)my * Wo + mx;
-          const float4 mm = __ldg(mbase + q);
+        if (k >= klo && k < khi) {
+          const float4 mm = __ldg(mbase + (mb0 + (long long)k * RPT * Wo));
           av[k] = mm.x;
           bv[k] = mm.y;
           dv[k] = mm.z;
@@ -352,12 +359,10 @@ __global__ void __launch_bounds__(256)
         }
       }
     }
-    const int xx = x0 + c;
 #pragma unroll
     for (int o = 0; o < RB; o++) {
-      const int yy = y0 + r0 + o;
-      if (yy >= H || xx >= W) continue;
-      const long long q = (((long long)id.v * H + yy) * W + xx) * 3 + id.ch;
+      if (o >= en) continue;
+      const long long q = eb + o * 3 * W;
       const float xr = ximg[o], yr = xtgt[o];
       const float x = fminf(fmaxf(xr, 0.f), 1.f), y = fminf(fmaxf(yr, 0.f), 1.f);
       const float mask = (xr >= 0.f && xr <= 1.f) ? 1.f : 0.f;
