@@ -180,3 +180,23 @@ def test_config2_targets_are_8bit(pkg):
     for f, u in zip(sc["targets"], sc["targets_u8"]):
         assert u.dtype == np.uint8 and f.dtype == np.float32
         assert np.array_equal(f, u.astype(np.float32) / np.float32(255.0))
+
+
+def test_32bit_binning_keys_order_like_the_64bit_keys():
+    """The warp binning keys (q, stencil offset j, id g) as q<<21 | j<<17 | g when G <= 2^17 and
+    (2R+1)^2 <= 16 sort exactly as q<<40 | j<<32 | g, the reference's packed key order (ties in q
+    broken by j, then g); every field stays inside its bits."""
+    import numpy as np
+    rng = np.random.default_rng(0)
+    n = 100000
+    q = rng.integers(0, 2048, n, dtype=np.uint64)
+    q[: n // 4] = 2047                                   # border tiles: many keys tied at the clamp
+    j = rng.integers(0, 9, n, dtype=np.uint64)
+    g = rng.permutation(1 << 17)[:n].astype(np.uint64)   # unique ids below 2^17
+    k64 = (q << np.uint64(40)) | (j << np.uint64(32)) | g
+    k32 = ((q << np.uint64(21)) | (j << np.uint64(17)) | g).astype(np.uint32)
+    assert int(k32.max()) < 2 ** 32 - 1                 # below the ~0 padding of the warp sort
+    assert np.array_equal(np.argsort(k64, kind="stable"), np.argsort(k32, kind="stable"))
+    assert np.array_equal(k32 >> np.uint32(21), q.astype(np.uint32))
+    assert np.array_equal((k32 >> np.uint32(17)) & np.uint32(15), j.astype(np.uint32))
+    assert np.array_equal(k32 & np.uint32((1 << 17) - 1), g.astype(np.uint32))
