@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(GB_THREADS, LPG >= 4 ? 4 : 3)
 __global__ void __launch_bounds__(1024) k_wb_reduce(const float* __restrict__ part, int n, const float* __restrict__ params,
                                                      int G, float* __restrict__ grads, const float2* __restrict__ bt_part,
                                                      int nbt, float* __restrict__ g_depth_bt) {
-  __shared__ float red[1024];
+  __shared__ float red[32];
   if (bt_part && threadIdx.x == 0) {
     // arm B: the blocks' (d beta, d tau) in block order
     float2 t = make_float2(0.f, 0.f);
@@ -467,15 +467,17 @@ __global__ void __launch_bounds__(1024) k_wb_reduce(const float* __restrict__ pa
     a3 += part[i + 3072];
   }
   for (; i < n; i += 1024) a0 += part[i];
-  red[threadIdx.x] = (a0 + a1) + (a2 + a3);
+  // fixed order: each warp's xor butterfly, then the 32 warp sums in warp order
+  float r = (a0 + a1) + (a2 + a3);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = r;
   __syncthreads();
-  for (int s = blockDim.x >> 1; s > 0; s >>= 1) {
-    if ((int)threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
-    __syncthreads();
-  }
   if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
     const ParamLayout L{G};
-    grads[L.w_b_raw()] = red[0] * softplus_grad(params[L.w_b_raw()]);
+    grads[L.w_b_raw()] = t * softplus_grad(params[L.w_b_raw()]);
   }
 }
 

@@ -414,26 +414,44 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256) k_loss_reduce(const float* __restrict__ spart, int nsb, const float* __restrict__ lpart,
                                                      int nlb, int H, int W, int win, float lambda, float* __restrict__ loss,
                                                      float* __restrict__ loss_sum, unsigned* __restrict__ counter) {
-  __shared__ double rs[256], rl[256];
+  __shared__ double rs[8], rl[8];
   __shared__ bool s_last;
-  const int v = blockIdx.x;
-  double s = 0.0, l = 0.0;
-  for (int i = threadIdx.x; i < 3 * nsb; i += blockDim.x) s += spart[(long long)v * 3 * nsb + i];
-  for (int i = threadIdx.x; i < 3 * nlb; i += blockDim.x) l += lpart[(long long)v * 3 * nlb + i];
-  rs[threadIdx.x] = s;
-  rl[threadIdx.x] = l;
-  __syncthreads();
-  for (int st = blockDim.x >> 1; st > 0; st >>= 1) {
-    if ((int)threadIdx.x < st) {
-      rs[threadIdx.x] += rs[threadIdx.x + st];
-      rl[threadIdx.x] += rl[threadIdx.x + st];
+  const int v = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  // fixed-order sums (deterministic): four independent partials per thread, then the warps'
+  // xor butterflies, then the 8 warp sums in warp order
+  auto part_sum = [&](const float* p, int n) {
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    int i = tid;
+    for (; i + 768 < n; i += 1024) {
+      a0 += p[i];
+      a1 += p[i + 256];
+      a2 += p[i + 512];
+      a3 += p[i + 768];
     }
-    __syncthreads();
+    for (; i < n; i += 256) a0 += p[i];
+    return (a0 + a1) + (a2 + a3);
+  };
+  double s = part_sum(spart + (long long)v * 3 * nsb, 3 * nsb);
+  double l = part_sum(lpart + (long long)v * 3 * nlb, 3 * nlb);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    l += __shfl_xor_sync(0xffffffffu, l, o);
   }
-  if (threadIdx.x == 0) {
+  if (lane == 0) {
+    rs[wid] = s;
+    rl[wid] = l;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double S = 0.0, Lt = 0.0;
+    for (int w = 0; w < 8; ++w) {
+      S += rs[w];
+      Lt += rl[w];
+    }
     const double Ns = 3.0 * (double)(H - win + 1) * (double)(W - win + 1);
     const double N = 3.0 * (double)H * (double)W;
-    loss[v] = (float)((1.0 - lambda) * rl[0] / N + lambda * (1.0 - rs[0] / Ns));
+    loss[v] = (float)((1.0 - lambda) * Lt / N + lambda * (1.0 - S / Ns));
   }
   if (loss_sum == nullptr) return;
   // the last block to finish adds the V losses in view order
