@@ -443,37 +443,54 @@ def run_config(args, rank, world, local_rank, cid):
     groups = [mine[i:i + chunk] for i in range(0, len(mine), chunk)]
     cams_t = [camera.pack_cameras([camera.Camera.from_dict(sc["cams"][i]) for i in gv], dev) for gv in groups]
     ws = ops.Workspace(dev)
-    state = {}
+    state = {"wsl": ops.Workspace(dev), "wsb": ops.Workspace(dev)}
+    # the loss target stays resident: config 1's seeded target image, config 3's seeded uniform
+    # image (one view of H x W x 3)
+    if cid == 1:
+        state["tg"] = torch.from_numpy(sc["targets"][0]).to(dev)[None].contiguous()
+    elif cid == 3:
+        state["tg"] = torch.rand((len(groups[0]), H, W, 3), device=dev, generator=torch.Generator(dev).manual_seed(5))
 
-    def once(fwd_bf16=False):
-        for ct in cams_t:
+    def once(fwd_bf16=False, marks=None):
+        # marks: a list that receives (stage, recorded CUDA event) pairs for the first view group
+        def tick(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((name, ev))
+
+        for gi, ct in enumerate(cams_t):
+            if marks is not None and gi > 0:
+                break
+            tick("start")
             pj = ops.project(flat, G, sh, ct, H, W, out=state.get("pj"))
             state["pj"] = pj
+            tick("project")
             bf16 = cid == 4 or fwd_bf16
             key = "bp16" if bf16 else "bp"
             bp = ops.bin_pack(pj, G, H, W, 1, K, ws=ws, out=state.get(key), with_inv=cid in (1, 3) and not bf16,
                               bf16=bf16)
             state[key] = bp
+            tick("bin_pack")
             rf = ops.render_fwd(bp["slots"], bp["count"], H, W, flat[59 * G:], c_b, out=state.get("rf"), bf16=bf16)
             state["rf"] = rf
+            tick("render_fwd")
             if cid in (1, 3) and not fwd_bf16:
-                if cid == 1:
-                    tg = state.setdefault("tg", torch.from_numpy(sc["targets"][0]).to(dev)[None].contiguous())
-                else:
-                    tg = state.setdefault("tg", torch.rand(rf["img"].shape, device=dev,
-                                                           generator=torch.Generator(dev).manual_seed(5)))
+                tg = state["tg"]
                 # config 1: the L1 loss of its reference run (tools/m4_train_binned.py:238-248);
                 # config 3: the train step's L1 + SSIM
-                lo = ops.loss_l1_ssim(rf["img"], tg, 0.0 if cid == 1 else 0.2, 1.0,
-                                      ws=state.setdefault("wsl", ops.Workspace(dev)), out=state.get("lo"))
+                lo = ops.loss_l1_ssim(rf["img"], tg, 0.0 if cid == 1 else 0.2, 1.0, ws=state["wsl"],
+                                      out=state.get("lo"))
                 state["lo"] = lo
+                tick("loss")
                 rb = ops.render_bwd(bp["slots"], bp["count"], H, W, c_b, rf["img"], rf["den"], lo["gimg"],
                                     out=state.get("rb"))
                 state["rb"] = rb
+                tick("render_bwd")
                 state["grads"] = ops.backward_params(flat, G, sh, ct, H, W, 1, K, bp["inv"], rb["slot_grads"],
-                                                     rb["gwb"], out=state.get("grads"),
-                                                     ws=state.setdefault("wsb", ops.Workspace(dev)),
+                                                     rb["gwb"], out=state.get("grads"), ws=state["wsb"],
                                                      proj=pj["proj"])
+                tick("backward_params")
 
     for _ in range(max(args.warmup, 3)):
         once()
@@ -503,6 +520,15 @@ def run_config(args, rank, world, local_rank, cid):
         e1.record()
         torch.cuda.synchronize()
         fwd16_ms = e0.elapsed_time(e1) / steps
+    # per-stage device time of one launch of the first view group (CUDA events between the
+    # stages, mean of five passes)
+    stage_ms = {}
+    for _ in range(5):
+        marks = []
+        once(marks=marks)
+        torch.cuda.synchronize()
+        for (_, a), (name, b) in zip(marks, marks[1:]):
+            stage_ms[name] = stage_ms.get(name, 0.0) + a.elapsed_time(b) / 5
     if cid == 3:
         cand = state["bp"]["cand"].reshape(-1).long()
         over = torch.clamp(cand - K, min=0)
@@ -524,7 +550,8 @@ def run_config(args, rank, world, local_rank, cid):
                 "dtype": "bf16 slot rows, f32 accumulate" if cid == 4 else "f32", "data": "synthetic (seeded)",
                 "mpix_s": n_views_job * H * W / 1e6 / (ms / 1e3),
                 "config": {"workload": f"config{cid}", "G": G, "H": H, "W": W, "K": K, "sh_degree": sh,
-                           "views_per_rank": len(mine)}, **extra}
+                           "views_per_rank": len(mine)},
+                "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()}, "stage_views": len(groups[0]), **extra}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

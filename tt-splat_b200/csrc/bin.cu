@@ -583,8 +583,13 @@ __global__ void __launch_bounds__(WB_WARPS * 32)
   }
 }
 
+// Two blocks per SM (64 registers, no spills; 2 x ~73 KB of shared memory): the 296-block grid
+// is one resident wave, so both blocks of an SM walk the tile list at once and one block's
+// barrier waits hide behind the other's work.  Unbounded, the kernel took ~118 registers, one
+// block fitted per SM and the second half of the grid started only after the first had walked
+// its whole share of the list.
 template <int PACK>
-__global__ void __launch_bounds__(BS_THREADS)
+__global__ void __launch_bounds__(BS_THREADS, 2)
     k_bin_select(const int* __restrict__ cell_start, const float4* __restrict__ rec, int G, int ntx, int nty,
                  int R, int K, const float* __restrict__ proj, float inv_k, int* __restrict__ idx,
                  int* __restrict__ count, int* __restrict__ cand, int* __restrict__ inv,
