@@ -256,9 +256,11 @@ __global__ void __launch_bounds__(256)
 // the entries it writes), then the reg_loss gradient (spike/mcmc.py:18-22) is added and the
 // gaussian's 59 gradients are written.
 // Four blocks per SM (128 registers) when a gaussian has 4 or 8 lanes: the colour-coefficient
-// sums live in shared memory, not in 48 registers per lane; one or two lanes keep three blocks.
+// sums live in shared memory, not in 48 registers per lane.  One or two lanes keep three blocks
+// at SH degree 2 and 3 (four would spill 100-500 B per thread); degrees 0 and 1 fit four blocks
+// without spills at any lane count (one view at 1M gaussians, SH 0: 0.318 -> 0.276 ms).
 template <int DEG, int LPG, bool ARMB>
-__global__ void __launch_bounds__(GB_THREADS, LPG >= 4 ? 4 : 3)
+__global__ void __launch_bounds__(GB_THREADS, (LPG >= 4 || DEG <= 1) ? 4 : 3)
     k_backward(const float* __restrict__ params, int G, const float* __restrict__ cams, int V, float blur,
                float near_plane, const float4* __restrict__ rec, float lambda_o, float lambda_s,
                float* __restrict__ grads, const float* __restrict__ depth_bt, float2* __restrict__ bt_partial) {
