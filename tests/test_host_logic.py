@@ -1,4 +1,6 @@
 """Host-side logic that needs no GPU: cached binning tables, device guards, view partitions."""
+import math
+
 import pytest
 import torch
 
@@ -170,6 +172,35 @@ def test_camera_conventions(pkg):
     c2w[:3, 3] = torch.tensor([0.0, 0.0, 4.0])           # OpenGL camera at +4z looking down -z
     Rv, tv = camera.opengl_c2w_to_opencv_w2c(c2w)
     assert torch.equal(Rv, torch.diag(torch.tensor([1.0, -1.0, -1.0]))) and torch.equal(tv, torch.tensor([0.0, 0.0, 4.0]))
+
+
+def test_reference_camera_cases(pkg):
+    """spike/tests/test_camera.py:16-62 in float64: an OpenGL camera at the origin looks down -z
+    (a point in front has z > 0 and lands on the principal point, +x goes right, a point behind
+    has z < 0); a camera moved to +4z sees the origin at depth 4; a rotated and translated pose
+    gives an orthonormal R_v with determinant 1."""
+    from tt_splat_b200 import camera
+    f = lambda x: torch.tensor(x, dtype=torch.float64)  # noqa: E731
+    fx = fy = 100.0
+    cx = cy = 64.0
+    R_v, t_v = camera.opengl_c2w_to_opencv_w2c(torch.eye(4, dtype=torch.float64))
+    pix, z = camera.project_point(f([0.0, 0.0, -5.0]), R_v, t_v, fx, fy, cx, cy)
+    assert z.item() > 0 and torch.allclose(pix, f([cx, cy]), atol=1e-9)
+    pix, z = camera.project_point(f([1.0, 0.0, -5.0]), R_v, t_v, fx, fy, cx, cy)
+    assert abs(pix[0].item() - (fx / 5.0 + cx)) < 1e-9 and z.item() > 0
+    assert camera.project_point(f([0.0, 0.0, 5.0]), R_v, t_v, fx, fy, cx, cy)[1].item() < 0
+    c2w = torch.eye(4, dtype=torch.float64)
+    c2w[2, 3] = 4.0
+    R_v, t_v = camera.opengl_c2w_to_opencv_w2c(c2w)
+    pix, z = camera.project_point(f([0.0, 0.0, 0.0]), R_v, t_v, fx, fy, cx, cy)
+    assert abs(z.item() - 4.0) < 1e-9 and torch.allclose(pix, f([cx, cy]), atol=1e-9)
+    th = 0.5
+    c2w = torch.eye(4, dtype=torch.float64)
+    c2w[:3, :3] = f([[math.cos(th), 0.0, math.sin(th)], [0.0, 1.0, 0.0], [-math.sin(th), 0.0, math.cos(th)]])
+    c2w[:3, 3] = f([1.0, 2.0, 3.0])
+    R_v, _ = camera.opengl_c2w_to_opencv_w2c(c2w)
+    assert torch.allclose(R_v @ R_v.T, torch.eye(3, dtype=torch.float64), atol=1e-9)
+    assert abs(torch.det(R_v).item() - 1.0) < 1e-9
 
 
 def test_config2_targets_are_8bit(pkg):
