@@ -5,7 +5,8 @@ shrunk for tiny images) on top of the reference's SSIM restatement ``tools/loss_
 11-tap sigma-1.5 Gaussian window (``gauss_1d`` :28-31), valid separable filtering (``filt`` :44-49
 and its transpose ``filt_T`` :52-55), ``ssim_fwd`` :58-75 and the manual gradient of
 ``loss_manual`` :78-105.  float64.  The clamp's gradient follows torch (passes at the bounds).
-Parity against the third-party pytorch_msssim itself is unpinned (it is not installed).
+pytorch_msssim 1.0.0, the third-party package the reference calls, is not installed: its SSIM
+is pinned through an independent restatement of its published algorithm (tests), not run.
 """
 import numpy as np
 

@@ -319,6 +319,52 @@ def test_loss_vs_reference_restatement(case):
     assert rel_l2(grad, z[f"{case}__grad"]) < 1e-10
 
 
+def _ssim_published(pred, gt, win_size=11):
+    """SSIM as pytorch_msssim 1.0.0 publishes it, restated independently of the oracle, for
+    spike/metrics.py:15-19's call ssim(clamp(pred), clamp(gt), data_range=1, win_size=w): a
+    normalised 1-D Gaussian of sigma 1.5 over arange(w) - w // 2, applied without padding along
+    H then along W (scipy correlation, mode "valid"), K = (0.01, 0.03), the map
+    ((2 mu1 mu2 + C1) / (mu1^2 + mu2^2 + C1)) * ((2 s12 + C2) / (s1^2 + s2^2 + C2)) averaged per
+    channel, then over the channels."""
+    from scipy.signal import correlate
+    H, W = pred.shape[:2]
+    w = min(win_size, H, W)
+    w = max(w - 1 if w % 2 == 0 else w, 3)
+    c = np.arange(w, dtype=np.float64) - w // 2
+    g = np.exp(-(c ** 2) / (2 * 1.5 ** 2))
+    g = g / g.sum()
+
+    def blur(m):
+        return correlate(correlate(m, g[:, None], mode="valid"), g[None, :], mode="valid")
+
+    C1, C2 = 0.01 ** 2, 0.03 ** 2
+    per_channel = []
+    for ch in range(3):
+        X = np.clip(np.asarray(pred[..., ch], np.float64), 0.0, 1.0)
+        Y = np.clip(np.asarray(gt[..., ch], np.float64), 0.0, 1.0)
+        mu1, mu2 = blur(X), blur(Y)
+        s1 = blur(X * X) - mu1 * mu1
+        s2 = blur(Y * Y) - mu2 * mu2
+        s12 = blur(X * Y) - mu1 * mu2
+        cs = (2 * s12 + C2) / (s1 + s2 + C2)
+        per_channel.append((((2 * mu1 * mu2 + C1) / (mu1 * mu1 + mu2 * mu2 + C1)) * cs).mean())
+    return float(np.mean(per_channel))
+
+
+@pytest.mark.parametrize("shape", [(40, 56), (17, 23), (8, 12), (6, 6)])
+def test_oracle_ssim_equals_the_published_algorithm(shape):
+    """The oracle's SSIM (restated from tools/loss_manual.py) equals an independent restatement
+    of pytorch_msssim's published algorithm, including the shrunken odd window of small images
+    and the [0, 1] clamp of the inputs; the loss then follows as (1 - l) L1 + l (1 - SSIM)."""
+    rng = np.random.default_rng(sum(shape))
+    pred = rng.uniform(-0.2, 1.2, shape + (3,))
+    gt = rng.uniform(0.0, 1.0, shape + (3,))
+    loss, ssim, l1, _ = oloss.loss_and_grad(pred, gt, 0.2)
+    ref = _ssim_published(pred, gt)
+    assert abs(ssim - ref) < 1e-12, (ssim, ref)
+    assert abs(loss - (0.8 * np.abs(pred - gt).mean() + 0.2 * (1.0 - ref))) < 1e-12
+
+
 def test_loss_clamp_gradient_finite_difference():
     rng = np.random.default_rng(5)
     x = rng.uniform(-0.3, 1.3, (20, 22, 3))
