@@ -231,3 +231,58 @@ def test_32bit_binning_keys_order_like_the_64bit_keys():
     assert np.array_equal(k32 >> np.uint32(21), q.astype(np.uint32))
     assert np.array_equal((k32 >> np.uint32(17)) & np.uint32(15), j.astype(np.uint32))
     assert np.array_equal(k32 & np.uint32((1 << 17) - 1), g.astype(np.uint32))
+
+
+def _scene_fixture():
+    import numpy as np
+    from conftest import golden
+    z = golden("scene.npz")
+    return np, z
+
+
+@pytest.mark.parametrize("case", [("m_g40", 40, 0.6, 5, True, 0.05), ("m_fresh150", 150, 0.7, 2, False, 0.05),
+                                  ("m_gt30", 30, 0.5, 1, True, 0.08), ("m_default4", 4, 1.3, 3, False, 0.05)])
+def test_model_draws_equal_the_reference(case, pkg):
+    """GaussianModel(G, extent, seed, gt, init_scale) draws the reference's model bit for bit
+    (spike/model.py:16-51; tests/golden/make_golden_scene.py)."""
+    from tt_splat_b200 import model
+    np, z = _scene_fixture()
+    name, G, extent, seed, gt, init_scale = case
+    m = model.GaussianModel(G, extent=extent, seed=seed, gt=gt, init_scale=init_scale, device="cpu")
+    for f in ("means3d", "log_scales", "quats", "opacity_raw", "color_dc"):
+        assert np.array_equal(getattr(m, f).detach().numpy(), z[f"{name}__{f}"]), (name, f)
+
+
+def test_scene_helpers_match_the_reference(pkg):
+    """synthetic.make_orbit_cameras and make_gt_model (spike/synthetic.py:16-30): the same camera
+    poses and intrinsics as the reference (to float32 rounding), and make_gt_model is the
+    reference's gt model."""
+    from tt_splat_b200 import synthetic
+    np, z = _scene_fixture()
+    for name, kw in (("o_default48", dict(n=4, res=48)),
+                     ("o_custom", dict(n=3, radius=3.0, elevation=0.2, res=32, fov=0.9))):
+        cams = synthetic.make_orbit_cameras(**kw)
+        assert np.abs(np.stack([c.R_v.numpy() for c in cams]) - z[f"{name}__R"]).max() < 1e-6
+        assert np.abs(np.stack([c.t_v.numpy() for c in cams]) - z[f"{name}__t"]).max() < 1e-5
+        k = np.array([[c.fx, c.fy, c.cx, c.cy, c.H, c.W] for c in cams], np.float64)
+        assert np.allclose(k, z[f"{name}__k"], rtol=1e-12, atol=0)
+    gt = synthetic.make_gt_model(device="cpu")
+    assert np.array_equal(gt.means3d.detach().numpy(), z["m_gt30__means3d"])
+    assert np.array_equal(gt.color_dc.detach().numpy(), z["m_gt30__color_dc"])
+    with pytest.raises(TypeError):
+        synthetic.make_gt_model(dtype=torch.float64, device="cpu")
+
+
+@pytest.mark.parametrize("case", [("p_subset", 500, 200, 11, 7), ("p_pad", 50, 120, 12, 3)])
+def test_init_from_points_equals_the_reference(case, pkg):
+    """GaussianModel.init_from_points (spike/model.py:55-79) on a seeded cloud with more points
+    than gaussians (random subset) and with fewer (jittered copies): means, log-scales and DC
+    colours bit for bit."""
+    from make_golden_scene import point_cloud
+    from tt_splat_b200 import model
+    np, z = _scene_fixture()
+    name, P, G, cseed, iseed = case
+    xyz, rgb = point_cloud(P, cseed)
+    m = model.GaussianModel(G, seed=0, device="cpu").init_from_points(xyz, rgb, seed=iseed)
+    for f in ("means3d", "log_scales", "color_dc"):
+        assert np.array_equal(getattr(m, f).detach().numpy(), z[f"{name}__{f}"]), (name, f)

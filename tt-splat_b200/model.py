@@ -104,6 +104,42 @@ class GaussianModel(nn.Module):
             return view(self._parameters["flat"], self.G_, name)
         return super().__getattr__(name)
 
+    @torch.no_grad()
+    def init_from_points(self, xyz, rgb, seed=0):
+        """Start the gaussians from a point cloud (e.g. ``data.load_colmap_points``), as
+        spike/model.py:55-79 does: xyz[P,3], rgb[P,3] in [0, 1] (numpy or torch).
+
+        With at least G points, G of them are taken in the order of a random permutation; with
+        fewer, every point is kept and the missing G - P are copies of random points, moved by
+        Gaussian noise of 1 % of the cloud's bounding-box diagonal.  Every gaussian gets the same
+        isotropic log-scale, the log of the median nearest-neighbour distance among up to 4000
+        of them (at least 1e-4), and the colour whose DC term renders as the point's rgb.  The
+        draws come from a CPU generator seeded with ``seed`` in the reference's order (the
+        permutation or the copy indices and noise, then the subset permutation), so a seed
+        gives the reference's model; opacities, rotations and SH rest stay as they were."""
+        G = self.G_
+        gen = torch.Generator().manual_seed(int(seed))
+        xyz = torch.as_tensor(xyz, dtype=torch.float32).cpu()
+        rgb = torch.as_tensor(rgb, dtype=torch.float32).cpu()
+        P = xyz.shape[0]
+        if P >= G:
+            pick = torch.randperm(P, generator=gen)[:G]
+            pts, cols = xyz[pick], rgb[pick]
+        else:
+            src = torch.randint(0, P, (G - P,), generator=gen)
+            diag = (xyz.max(0).values - xyz.min(0).values).norm() * 0.01
+            pts = torch.cat([xyz, xyz[src] + torch.randn(G - P, 3, generator=gen) * diag], 0)
+            cols = torch.cat([rgb, rgb[src]], 0)
+        probe = pts[torch.randperm(G, generator=gen)[:min(G, 4000)]]
+        dist = torch.cdist(probe, probe)
+        dist.fill_diagonal_(float("inf"))
+        nn_dist = dist.min(1).values.median().clamp(min=1e-4)
+        dev = self.flat.device
+        self.means3d.copy_(pts.to(dev))
+        self.log_scales.fill_(float(torch.log(nn_dist)))
+        self.color_dc.copy_(((cols - 0.5) / C0).to(dev))
+        return self
+
     def to_arrays(self):
         f = self.flat.detach().cpu()
         out = {n: view(f, self.G_, n).numpy().copy() for n in NAMES}

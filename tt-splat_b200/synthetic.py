@@ -1,4 +1,5 @@
-"""Seeded synthetic scenes for the five benchmark configurations.
+"""Seeded synthetic scenes for the five benchmark configurations, and the reference's data-free
+self-consistency scene (``make_scene`` and its parts, ``spike/synthetic.py``).
 
 The reference measures on synthetic scenes only (no dataset ships with it), so every
 scene here is drawn from a seeded ``numpy.random.Generator(PCG64)`` in float32.  The
@@ -209,3 +210,49 @@ def stress_mu2d(seed, G, H, W, n_clusters=16, sigma_px=6.0, frac_off=0.1, frac_d
             mu[p, i % 2] = specials[i % len(specials)]
             keep[p] = True
     return mu, keep
+
+
+# ---- the reference's data-free self-consistency scene (spike/synthetic.py:16-48) ---------------
+# A known gaussian set rendered from orbit cameras gives ground-truth images that a fresh model
+# must recover.  Same names, arguments and draws as the reference; images come from the device
+# render.  The default image size is 48 (the reference's 40 rounded up to whole 16-pixel tiles,
+# which the binned path needs).
+
+def make_gt_model(seed=1, G=30, extent=0.5, dtype=None, device="cuda"):
+    """The known scene: ``GaussianModel(G, extent, seed, gt=True, init_scale=0.08)``."""
+    import torch
+
+    from .model import GaussianModel
+    if dtype not in (None, torch.float32):
+        raise TypeError("the device path keeps gaussians in float32")
+    return GaussianModel(G, extent=extent, seed=seed, gt=True, init_scale=0.08, device=device)
+
+
+def make_orbit_cameras(n=4, radius=2.5, elevation=0.6, res=48, fov=0.7, dtype=None, device=None):
+    """n square res x res pinhole cameras (field of view ``fov`` radians, principal point at the
+    image centre) at azimuths 2 pi i / n on a ring of the given radius and height, looking at the
+    origin.  Cameras stay on the host; the render moves them to the model's device."""
+    from .camera import Camera, look_at_opencv as look_at
+    f = 0.5 * res / math.tan(0.5 * fov)
+    cams = []
+    for i in range(n):
+        th = 2.0 * math.pi * i / n
+        R_v, t_v = look_at((radius * math.cos(th), elevation, radius * math.sin(th)), (0.0, 0.0, 0.0))
+        cams.append(Camera(R_v, t_v, f, f, res / 2.0, res / 2.0, res, res))
+    return cams
+
+
+def render_gt_images(gt_model, cameras, arm="A", **kw):
+    """One device render per camera, without gradients."""
+    import torch
+
+    from .render import render
+    with torch.no_grad():
+        return [render(gt_model, cam, arm, **kw).detach() for cam in cameras]
+
+
+def make_scene(arm="A", seed=1, G_gt=30, n_views=4, res=48, device="cuda"):
+    """(gt_model, cameras, gt_images) of the self-consistency scene for one arm."""
+    gt = make_gt_model(seed=seed, G=G_gt, device=device)
+    cams = make_orbit_cameras(n=n_views, res=res)
+    return gt, cams, render_gt_images(gt, cams, arm)
