@@ -286,3 +286,18 @@ def test_init_from_points_equals_the_reference(case, pkg):
     m = model.GaussianModel(G, seed=0, device="cpu").init_from_points(xyz, rgb, seed=iseed)
     for f in ("means3d", "log_scales", "color_dc"):
         assert np.array_equal(getattr(m, f).detach().numpy(), z[f"{name}__{f}"]), (name, f)
+
+
+def test_default_device_is_cuda_or_raises(pkg, monkeypatch):
+    """device.default_device (spike/device.py:13-23): CUDA or an error, never a CPU fallback."""
+    from tt_splat_b200 import device
+    with pytest.raises(ValueError):
+        device.default_device("cpu")
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    with pytest.raises(RuntimeError):
+        device.default_device()
+    with pytest.raises(RuntimeError):
+        device.default_device("cuda:0")
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    assert device.default_device() == torch.device("cuda")
+    assert device.default_device("cuda:1") == torch.device("cuda", 1)

@@ -9,7 +9,7 @@ There is no CPU fallback: the ops raise when the library or a CUDA device is mis
 from . import synthetic  # noqa: F401  (numpy only)
 
 __all__ = ["synthetic", "camera", "model", "geometry", "sh", "forward", "backward", "render",
-           "binned", "train", "mcmc", "metrics", "plyio", "data", "peer"]
+           "binned", "train", "mcmc", "metrics", "plyio", "data", "peer", "device"]
 
 
 def __getattr__(name):
